@@ -1,0 +1,185 @@
+/*
+ * tensoros_nn_gpu.h - B200 (sm_100a) drop-in for TensorOS runtime/nn's GGUF
+ * decode path.
+ *
+ * Every operator the reference keeps file-static in runtime/nn/llm.c has a
+ * host-pointer twin here with the same arguments and the same results (bit
+ * for bit): a hosted llm.c links against these names instead of its static
+ * functions.  Behind them the work runs on the GPU through hand-written
+ * sm_100a kernels; there is no CPU fallback: without a usable GPU every call
+ * fails with TOS_ENODEV and the void drop-ins leave their zero-filled result.
+ *
+ * Ownership: the caller owns every buffer.  Weights passed by host pointer
+ * are uploaded and repacked once and cached by (pointer, shape, type), as the
+ * reference uses GGUF tensors in place (runtime/nn/gguf.c:301-313); call
+ * tos_weight_cache_clear() after changing such memory.  Device-pointer
+ * variants (*_dev) are asynchronous on the given CUDA stream (NULL = the
+ * library's stream) and never synchronise.
+ *
+ * Errors: functions returning int return a tos_status_t.  The void / float
+ * drop-ins mirror the reference's void signatures; their status is kept in a
+ * thread-local slot read by tos_last_status().  As in the reference
+ * (llm.c:285-287, 359-360, 406-408), an unsupported ggml type yields zeros.
+ *
+ * Threading: calls are serialised per library instance on one stream; a model
+ * (tos_model_t) must be used by one host thread at a time.
+ */
+#ifndef TENSOROS_NN_GPU_H
+#define TENSOROS_NN_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+typedef enum {
+    TOS_OK = 0,
+    TOS_EINVAL = -1,    /* bad argument (shape, type, pointer) */
+    TOS_ENOMEM = -2,    /* device or host allocation failed */
+    TOS_ECUDA = -3,     /* CUDA runtime error */
+    TOS_ENCCL = -4,     /* collective error */
+    TOS_ETIMEOUT = -5,  /* a bounded device-side wait ran out */
+    TOS_ENOTSUP = -6,   /* valid but unsupported configuration */
+    TOS_ENODEV = -7     /* no usable CUDA device */
+} tos_status_t;
+
+/* ggml_type_t numeric values, verbatim from runtime/nn/gguf.h:38-58 */
+enum {
+    TOS_TYPE_F32 = 0,
+    TOS_TYPE_F16 = 1,
+    TOS_TYPE_Q4_0 = 2,
+    TOS_TYPE_Q8_0 = 8
+};
+
+/* attention numerics */
+enum {
+    TOS_ATTN_EXACT = 0, /* reference order, bit-identical */
+    TOS_ATTN_FAST = 1   /* split-position partial sums; max rel. error 1e-4 */
+};
+
+const char *tos_status_string(int status);
+int tos_last_status(void);
+
+/* ------------------------------------------------------------ library */
+/* Select the device and create the library stream (idempotent). */
+int tos_init(int device);
+int tos_shutdown(void);
+int tos_device_count(void);
+int tos_synchronize(void);
+/* The library's CUDA stream (cudaStream_t as void*). */
+void *tos_stream(void);
+
+/* ------------------------------------------------- registered weights */
+/* A quantised matrix [out_dim][in_dim/32 blocks] (Q4_0 or Q8_0) held on the
+ * device in plane layout.  Replaces the zero-copy GGUF pointer of llm.c. */
+typedef struct tos_weight tos_weight_t;
+int tos_weight_create(tos_weight_t **w, const void *host_blocks, int out_dim, int in_dim, int type);
+int tos_weight_create_dev(tos_weight_t **w, const void *dev_blocks, int out_dim, int in_dim,
+                          int type, void *stream);
+void tos_weight_destroy(tos_weight_t *w);
+size_t tos_weight_device_bytes(const tos_weight_t *w);
+void tos_weight_cache_clear(void);
+
+/* ---------------------------------------- device-pointer operators */
+/* out = W x  (llm_gemv, llm.c:329-349), x/out device pointers */
+int tos_gemv_dev(const tos_weight_t *w, const float *x, float *out, void *stream);
+/* out = W rmsnorm(x, norm_w, eps): fused llm_rmsnorm + llm_gemv */
+int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
+                      float *out, void *stream);
+/* per-block values q4_0_dot32 / q8_0_dot32 (llm.c:148-216) for n_blocks
+ * consecutive GGUF blocks against x[32*n_blocks] */
+int tos_block_dots_dev(const void *blocks, int type, const float *x, int n_blocks, float *out,
+                       void *stream);
+int tos_rmsnorm_dev(float *out, const float *x, const void *w, int wtype, int dim, float eps,
+                    void *stream);
+int tos_rope_dev(float *vec, int n_vec, int pos, int head_dim, float base, void *stream);
+int tos_softmax_dev(float *x, int n, void *stream);
+int tos_silu_dev(float *x, int n, void *stream);
+int tos_vadd_dev(float *dst, const float *src, int n, void *stream);
+int tos_vmul_dev(float *dst, const float *src, int n, void *stream);
+int tos_axpy_dev(float *dst, float s, const float *src, int n, void *stream);
+int tos_dot_dev(const float *a, const float *b, int n, float *out, void *stream);
+int tos_embed_dev(float *out, const void *embd, int type, int dim, int token, void *stream);
+int tos_argmax_dev(const float *x, int n, int *out_index, void *stream);
+
+/* Single-query attention over a KV cache [ctx][n_kv*head_dim] (kv_type F32 or
+ * F16) for query heads q[n_heads*head_dim] at position pos (attends t<=pos),
+ * llm.c:683-714.  workspace: tos_attention_workspace_bytes(n_heads, max_ctx)
+ * bytes of device memory. */
+size_t tos_attention_workspace_bytes(int n_heads, int max_ctx);
+int tos_attention_dev(float *out, const float *q, const void *k_cache, const void *v_cache,
+                      int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,
+                      int mode, void *workspace, size_t workspace_bytes, void *stream);
+
+/* --------------------- host-pointer drop-ins for runtime/nn/llm.c statics */
+void tos_gemv(float *out, const void *weight, const float *x, int out_dim, int in_dim, int type); /* llm.c:329 */
+float tos_vec_dot(const void *weight, const float *x, int n, int type);                           /* llm.c:221 */
+float tos_q4_0_dot32(const void *block, const float *x);                                          /* llm.c:148 */
+float tos_q8_0_dot32(const void *block, const float *x);                                          /* llm.c:187 */
+void tos_embed(float *out, const void *embd, int type, int dim, int token);                       /* llm.c:365 */
+void tos_rmsnorm(float *out, const float *x, const void *w, int dim, int wtype);                  /* llm.c:416 */
+void tos_rope(float *vec, int pos, int head_dim, float base);                                     /* llm.c:460 */
+void tos_softmax(float *x, int n);                                                                /* llm.c:506 */
+void tos_silu(float *x, int n);                                                                   /* llm.c:538 */
+float tos_dot_f32(const float *a, const float *b, int n);                                         /* llm.c:551 */
+void tos_axpy_f32(float *dst, float scale, const float *src, int n);                              /* llm.c:580 */
+void tos_vadd_f32(float *dst, const float *src, int n);                                           /* llm.c:599 */
+void tos_vmul_f32(float *dst, const float *src, int n);                                           /* llm.c:617 */
+int tos_argmax(const float *logits, int n);                                                       /* llm.c:1129 */
+/* quantize4.h:64-67: fp32-scale 20-byte Q4 blocks */
+float tos_q4_dot_block(const void *block20, const float *x);
+void tos_q4_gemv(float *out, const void *blocks20, const float *x, int out_dim, int in_dim);
+
+/* ------------------------------------------------------------- model */
+/* Mirrors llm_model_t (llm.h:44-115): architecture parameters and the GGUF
+ * tensor pointers (host memory, GGUF block layout).  Layer arrays hold
+ * n_layers pointers each.  Norm weights are F32 [dim]. */
+typedef struct {
+    int dim, n_layers, n_heads, n_kv_heads, ff_dim, vocab_size, max_seq;
+    float rope_base;
+    float norm_eps;          /* the reference hard-codes 1e-6f (llm.c:431) */
+    int kv_type;             /* TOS_TYPE_F32 (reference) or TOS_TYPE_F16 */
+    int attn_mode;           /* TOS_ATTN_EXACT or TOS_ATTN_FAST */
+    int wtype;               /* type of every projection matrix: Q4_0 / Q8_0 */
+    int embd_type;           /* token_embd type: Q4_0 / Q8_0 / F16 / F32 */
+    int out_type;            /* output.weight type (Q4_0 / Q8_0) */
+    const void *token_embd;
+    const void *output_weight;   /* NULL: tied to token_embd (llm.c:740-742) */
+    const float *output_norm;
+    const float *const *attn_norm;
+    const float *const *ffn_norm;
+    const void *const *wq;
+    const void *const *wk;
+    const void *const *wv;
+    const void *const *wo;
+    const void *const *wgate;
+    const void *const *wup;
+    const void *const *wdown;
+} tos_model_desc_t;
+
+typedef struct tos_model tos_model_t;
+
+int tos_model_create(tos_model_t **m, const tos_model_desc_t *desc);
+void tos_model_destroy(tos_model_t *m);
+/* llm_reset_cache (llm.c:2042-2053): zero the KV cache */
+int tos_model_reset(tos_model_t *m);
+/* llm_forward_token (llm.c:641-743): logits (host, vocab_size floats) may be
+ * NULL to skip the copy-out. */
+int tos_model_forward_token(tos_model_t *m, float *logits, int token, int pos);
+/* forward + llm_argmax on the device; *next receives the greedy token */
+int tos_model_forward_argmax(tos_model_t *m, int token, int pos, int *next);
+/* llm_generate with temperature 0 and no text stops (llm.c:1279-1347):
+ * prefill the prompt token by token, then n_gen greedy tokens into out.
+ * Returns the number generated or a negative status. */
+int tos_model_generate_greedy(tos_model_t *m, const int *prompt, int n_prompt, int n_gen, int *out);
+/* device pointer of the last logits (vocab_size floats) */
+const float *tos_model_logits_dev(const tos_model_t *m);
+size_t tos_model_device_bytes(const tos_model_t *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

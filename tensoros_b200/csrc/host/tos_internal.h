@@ -1,0 +1,35 @@
+/*
+ * tos_internal.h - shared state of the C11 host runtime (not installed).
+ */
+#ifndef TOS_INTERNAL_H
+#define TOS_INTERNAL_H
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+
+#include "tensoros_nn_gpu.h"
+#include "tos_kernels.h"
+
+struct tos_weight {
+    tosk_qmat_t m;
+};
+
+typedef struct {
+    int inited;
+    int device;
+    cudaStream_t stream;
+    int *err_dev;           /* device-side error word of bounded waits */
+    void *scratch;          /* device scratch for the host-pointer drop-ins */
+    size_t scratch_bytes;
+} tos_lib_t;
+
+extern tos_lib_t tos_g;
+
+int tos_set_status(int st);
+int tos_from_cuda(int cuda_err);
+int tos_ensure_init(void);
+void *tos_scratch(size_t bytes);
+int tos_check_device_error(void);
+cudaStream_t tos_pick_stream(void *s);
+
+#endif

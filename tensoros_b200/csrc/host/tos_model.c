@@ -1,0 +1,357 @@
+/*
+ * tos_model.c - device-resident decoder mirroring llm_forward_token
+ * (runtime/nn/llm.c:641-743) and the greedy generate loop (llm.c:1255-1347).
+ *
+ * Per token the stream runs 5 kernels per layer plus 3:
+ *   embed (llm.c:650)
+ *   per layer: [rmsnorm + q|k|v GEMV + RoPE + KV store]   llm.c:657-681
+ *              [attention scores] [softmax + PV]            llm.c:683-714
+ *              [o GEMV + residual]                          llm.c:717-718
+ *              [rmsnorm + gate|up GEMV + SiLU*up]           llm.c:723-729
+ *              [down GEMV + residual]                       llm.c:732-733
+ *   [rmsnorm + LM-head GEMV] [argmax]                       llm.c:737-742, 1129
+ * Every launch uses programmatic dependent launch, so a GEMV's weight
+ * prefetch overlaps the tail of the kernel before it, and the whole sequence
+ * is captured once into a CUDA graph.  The token and position live in device
+ * memory (4+4 bytes copied in per call) so the same graph serves every step.
+ *
+ * Weights are uploaded from the caller's GGUF buffers and repacked into the
+ * GEMV plane layout: q|k|v rows concatenated, gate/up rows interleaved
+ * (row 2i = gate i, row 2i+1 = up i) so the SiLU*up epilogue sees both.
+ */
+#include <stdlib.h>
+#include <string.h>
+
+#include "tos_internal.h"
+
+struct tos_model {
+    tos_model_desc_t d;
+    int hd, kv_dim, q_dim, esz;
+    tosk_qmat_t *wqkv, *wo, *wgu, *wdown;
+    tosk_qmat_t lm;
+    void *embd;
+    float *norms;             /* [n_layers][2][dim], then output norm [dim] */
+    void *kc, *vc;            /* [n_layers][max_seq][kv_dim] */
+    float *x, *q, *att, *h, *logits;
+    float2 *rope;             /* [max_seq][hd/2] */
+    void *ws;
+    size_t ws_bytes;
+    int *io;                  /* device: token, pos, next, err */
+    int *io_host;             /* pinned mirror */
+    cudaStream_t st;
+    cudaGraphExec_t gexec;
+    int have_graph;
+    size_t dev_bytes;
+};
+
+static size_t qrow_bytes(int cols, int type)
+{
+    return (size_t)(cols / 32) * (type == TOS_TYPE_Q4_0 ? 18 : 34);
+}
+
+static size_t embd_row_bytes(int dim, int type)
+{
+    switch (type) {
+    case TOS_TYPE_Q4_0: return (size_t)(dim / 32) * 18;
+    case TOS_TYPE_Q8_0: return (size_t)(dim / 32) * 34;
+    case TOS_TYPE_F16: return (size_t)dim * 2;
+    default: return (size_t)dim * 4;
+    }
+}
+
+static int dmalloc(tos_model_t *m, void **p, size_t bytes)
+{
+    int e = cudaMalloc(p, bytes);
+    if (e == cudaSuccess) m->dev_bytes += bytes;
+    return e;
+}
+
+/* Upload n host GGUF matrices (rows[i] x cols, same type) through the staging
+ * buffer and repack them into one plane matrix. */
+static int upload_qmat(tos_model_t *m, tosk_qmat_t *dst, const void *const *hsrc, const int *rows,
+                       int n, int interleave, int type, int cols, void *stage)
+{
+    int total = 0;
+    for (int i = 0; i < n; i++) total += rows[i];
+    int e = tosk_qmat_alloc(dst, type, total, cols);
+    if (e) return e;
+    m->dev_bytes += dst->bytes;
+    const void *dsrc[4];
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+        size_t b = qrow_bytes(cols, type) * (size_t)rows[i];
+        dsrc[i] = (char *)stage + off;
+        e = cudaMemcpyAsync((char *)stage + off, hsrc[i], b, cudaMemcpyHostToDevice, m->st);
+        if (e) return e;
+        off += (b + 255) & ~(size_t)255;
+    }
+    e = tosk_qmat_repack(dst, dsrc, rows, n, interleave, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);   /* staging is reused next */
+    return e;
+}
+
+void tos_model_destroy(tos_model_t *m)
+{
+    if (!m) return;
+    if (m->st) cudaStreamSynchronize(m->st);
+    if (m->have_graph) cudaGraphExecDestroy(m->gexec);
+    for (int L = 0; m->wqkv && L < m->d.n_layers; L++) {
+        tosk_qmat_free(&m->wqkv[L]);
+        tosk_qmat_free(&m->wo[L]);
+        tosk_qmat_free(&m->wgu[L]);
+        tosk_qmat_free(&m->wdown[L]);
+    }
+    free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
+    tosk_qmat_free(&m->lm);
+    void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
+                    m->rope, m->ws, m->io};
+    for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
+        if (bufs[i]) cudaFree(bufs[i]);
+    if (m->io_host) cudaFreeHost(m->io_host);
+    if (m->st) cudaStreamDestroy(m->st);
+    free(m);
+}
+
+static int validate(const tos_model_desc_t *d)
+{
+    if (!d || d->dim <= 0 || d->n_layers <= 0 || d->n_heads <= 0 || d->n_kv_heads <= 0 ||
+        d->ff_dim <= 0 || d->vocab_size <= 0 || d->max_seq <= 0)
+        return TOS_EINVAL;
+    if (d->dim % d->n_heads || d->n_heads % d->n_kv_heads) return TOS_EINVAL;
+    int hd = d->dim / d->n_heads;
+    if (hd & 1) return TOS_EINVAL;
+    if (d->dim % 32 || d->ff_dim % 32) return TOS_ENOTSUP;
+    if (d->wtype != TOS_TYPE_Q4_0 && d->wtype != TOS_TYPE_Q8_0) return TOS_ENOTSUP;
+    if (d->kv_type != TOS_TYPE_F32 && d->kv_type != TOS_TYPE_F16) return TOS_ENOTSUP;
+    if (d->attn_mode != TOS_ATTN_EXACT && d->attn_mode != TOS_ATTN_FAST) return TOS_EINVAL;
+    const void *head = d->output_weight ? d->output_weight : d->token_embd;
+    int ht = d->output_weight ? d->out_type : d->embd_type;
+    if (!head || (ht != TOS_TYPE_Q4_0 && ht != TOS_TYPE_Q8_0)) return TOS_ENOTSUP;
+    if (!d->token_embd || !d->output_norm || !d->attn_norm || !d->ffn_norm || !d->wq || !d->wk ||
+        !d->wv || !d->wo || !d->wgate || !d->wup || !d->wdown)
+        return TOS_EINVAL;
+    return TOS_OK;
+}
+
+int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
+{
+    if (!out) return tos_set_status(TOS_EINVAL);
+    *out = NULL;
+    int rc = validate(d);
+    if (rc) return tos_set_status(rc);
+    rc = tos_ensure_init();
+    if (rc) return tos_set_status(rc);
+    tos_model_t *m = (tos_model_t *)calloc(1, sizeof(*m));
+    if (!m) return tos_set_status(TOS_ENOMEM);
+    m->d = *d;
+    const int L = d->n_layers, dim = d->dim, ff = d->ff_dim;
+    m->hd = dim / d->n_heads;
+    m->q_dim = d->n_heads * m->hd;
+    m->kv_dim = d->n_kv_heads * m->hd;
+    m->esz = d->kv_type == TOS_TYPE_F16 ? 2 : 4;
+    int e = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking);
+    m->wqkv = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
+    m->wo = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
+    m->wgu = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
+    m->wdown = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
+    if (!m->wqkv || !m->wo || !m->wgu || !m->wdown) { tos_model_destroy(m); return tos_set_status(TOS_ENOMEM); }
+
+    const int wt = d->wtype;
+    const void *head = d->output_weight ? d->output_weight : d->token_embd;
+    const int ht = d->output_weight ? d->out_type : d->embd_type;
+    /* staging holds the GGUF sources of one plane matrix, each 256-aligned */
+#define AL256(v) (((v) + 255) & ~(size_t)255)
+    size_t stage_b = 0, t;
+    t = AL256(qrow_bytes(dim, wt) * (size_t)m->q_dim) + 2 * AL256(qrow_bytes(dim, wt) * (size_t)m->kv_dim);
+    if (t > stage_b) stage_b = t;
+    t = 2 * AL256(qrow_bytes(dim, wt) * (size_t)ff); if (t > stage_b) stage_b = t;
+    t = AL256(qrow_bytes(ff, wt) * (size_t)dim); if (t > stage_b) stage_b = t;
+    t = AL256(qrow_bytes(m->q_dim, wt) * (size_t)dim); if (t > stage_b) stage_b = t;
+    t = AL256(qrow_bytes(dim, ht) * (size_t)d->vocab_size); if (t > stage_b) stage_b = t;
+#undef AL256
+    void *stage = NULL;
+    if (!e) e = cudaMalloc(&stage, stage_b);
+
+    for (int l = 0; !e && l < L; l++) {
+        const void *qkv[3] = {d->wq[l], d->wk[l], d->wv[l]};
+        int rq[3] = {m->q_dim, m->kv_dim, m->kv_dim};
+        e = upload_qmat(m, &m->wqkv[l], qkv, rq, 3, 0, wt, dim, stage);
+        if (!e) { const void *s1[1] = {d->wo[l]}; int r1[1] = {dim}; e = upload_qmat(m, &m->wo[l], s1, r1, 1, 0, wt, m->q_dim, stage); }
+        if (!e) { const void *gu[2] = {d->wgate[l], d->wup[l]}; int r2[2] = {ff, ff}; e = upload_qmat(m, &m->wgu[l], gu, r2, 2, 1, wt, dim, stage); }
+        if (!e) { const void *s1[1] = {d->wdown[l]}; int r1[1] = {dim}; e = upload_qmat(m, &m->wdown[l], s1, r1, 1, 0, wt, ff, stage); }
+    }
+    if (!e) { const void *s1[1] = {head}; int r1[1] = {d->vocab_size}; e = upload_qmat(m, &m->lm, s1, r1, 1, 0, ht, dim, stage); }
+    if (stage) cudaFree(stage);
+
+    size_t eb = embd_row_bytes(dim, d->embd_type) * (size_t)d->vocab_size;
+    if (!e) e = dmalloc(m, &m->embd, eb);
+    if (!e) e = cudaMemcpy(m->embd, d->token_embd, eb, cudaMemcpyHostToDevice);
+    size_t nb = ((size_t)L * 2 + 1) * (size_t)dim * 4;
+    if (!e) e = dmalloc(m, (void **)&m->norms, nb);
+    for (int l = 0; !e && l < L; l++) {
+        e = cudaMemcpy(m->norms + (size_t)(2 * l) * dim, d->attn_norm[l], (size_t)dim * 4, cudaMemcpyHostToDevice);
+        if (!e) e = cudaMemcpy(m->norms + (size_t)(2 * l + 1) * dim, d->ffn_norm[l], (size_t)dim * 4, cudaMemcpyHostToDevice);
+    }
+    if (!e) e = cudaMemcpy(m->norms + (size_t)2 * L * dim, d->output_norm, (size_t)dim * 4, cudaMemcpyHostToDevice);
+
+    size_t kvb = (size_t)L * d->max_seq * m->kv_dim * m->esz;
+    if (!e) e = dmalloc(m, &m->kc, kvb);
+    if (!e) e = dmalloc(m, &m->vc, kvb);
+    if (!e) e = cudaMemset(m->kc, 0, kvb);
+    if (!e) e = cudaMemset(m->vc, 0, kvb);
+    int mx = dim > ff ? dim : ff;
+    if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->q, (size_t)mx * 4);
+    if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
+    if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
+    if (!e) e = dmalloc(m, (void **)&m->logits, (size_t)d->vocab_size * 4);
+    if (!e) e = dmalloc(m, (void **)&m->rope, (size_t)d->max_seq * (m->hd / 2) * sizeof(float2));
+    if (!e) e = tosk_rope_table(m->rope, d->max_seq, m->hd, d->rope_base, m->st);
+    m->ws_bytes = tosk_attention_ws_bytes(d->n_heads, d->max_seq);
+    if (!e) e = dmalloc(m, &m->ws, m->ws_bytes);
+    if (!e) e = dmalloc(m, (void **)&m->io, 4 * sizeof(int));
+    if (!e) e = cudaMemset(m->io, 0, 4 * sizeof(int));
+    if (!e) e = cudaMallocHost((void **)&m->io_host, 4 * sizeof(int));
+    if (!e) e = cudaStreamSynchronize(m->st);
+    if (e) {
+        tos_model_destroy(m);
+        return tos_set_status(tos_from_cuda(e));
+    }
+    *out = m;
+    return tos_set_status(TOS_OK);
+}
+
+size_t tos_model_device_bytes(const tos_model_t *m) { return m ? m->dev_bytes : 0; }
+const float *tos_model_logits_dev(const tos_model_t *m) { return m ? m->logits : NULL; }
+
+int tos_model_reset(tos_model_t *m)
+{
+    if (!m) return tos_set_status(TOS_EINVAL);
+    size_t kvb = (size_t)m->d.n_layers * m->d.max_seq * m->kv_dim * m->esz;
+    int e = cudaMemsetAsync(m->kc, 0, kvb, m->st);
+    if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);
+    return tos_set_status(tos_from_cuda(e));
+}
+
+/* Enqueue one token step; reads token from io[0] and position from io[1],
+ * leaves the greedy next token in io[2]. */
+static int enqueue_token(tos_model_t *m)
+{
+    const tos_model_desc_t *d = &m->d;
+    cudaStream_t st = m->st;
+    int *err = m->io + 3;
+    const int pdl = 1;
+    const int dim = d->dim;
+    size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
+    int e = tosk_embed(m->x, m->embd, d->embd_type, dim, m->io, 0, pdl, st);
+    for (int l = 0; !e && l < d->n_layers; l++) {
+        tosk_norm_t n1 = {m->norms + (size_t)(2 * l) * dim, d->norm_eps};
+        tosk_epi_t qkv;
+        memset(&qkv, 0, sizeof(qkv));
+        qkv.kind = TOSK_EPI_QKV;
+        qkv.rope_cs = m->rope;
+        qkv.pos = m->io + 1;
+        qkv.hd = m->hd;
+        qkv.q_rows = m->q_dim;
+        qkv.kv_rows = m->kv_dim;
+        qkv.kv_type = d->kv_type;
+        qkv.k_cache = (char *)m->kc + kv_layer * l;
+        qkv.v_cache = (char *)m->vc + kv_layer * l;
+        e = tosk_gemv(&m->wqkv[l], m->x, &n1, m->q, &qkv, err, pdl, st);
+        if (!e) e = tosk_attention(m->att, m->q, qkv.k_cache, qkv.v_cache, d->kv_type, d->n_heads,
+                                   d->n_kv_heads, m->hd, m->io + 1, 0, d->max_seq, d->attn_mode, m->ws,
+                                   m->ws_bytes, err, pdl, st);
+        tosk_epi_t res;
+        memset(&res, 0, sizeof(res));
+        res.kind = TOSK_EPI_RESID;
+        res.resid = m->x;
+        if (!e) e = tosk_gemv(&m->wo[l], m->att, NULL, m->x, &res, err, pdl, st);
+        tosk_norm_t n2 = {m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps};
+        tosk_epi_t sw;
+        memset(&sw, 0, sizeof(sw));
+        sw.kind = TOSK_EPI_SWIGLU;
+        if (!e) e = tosk_gemv(&m->wgu[l], m->x, &n2, m->h, &sw, err, pdl, st);
+        if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x, &res, err, pdl, st);
+    }
+    tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps};
+    if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, err, pdl, st);
+    if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
+    return e;
+}
+
+static int run_token(tos_model_t *m, int token, int pos)
+{
+    if (token < 0 || token >= m->d.vocab_size || pos < 0 || pos >= m->d.max_seq) return TOS_EINVAL;
+    m->io_host[0] = token;
+    m->io_host[1] = pos;
+    int e = cudaMemcpyAsync(m->io, m->io_host, 2 * sizeof(int), cudaMemcpyHostToDevice, m->st);
+    if (e) return tos_from_cuda(e);
+    if (!m->have_graph) {
+        /* first step runs eagerly (sets kernel attributes), then capture */
+        e = enqueue_token(m);
+        if (!e) e = cudaStreamSynchronize(m->st);
+        if (e) return tos_from_cuda(e);
+        cudaGraph_t g = NULL;
+        if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            int ce = enqueue_token(m);
+            int ee = cudaStreamEndCapture(m->st, &g);
+            if (!ce && !ee && g && cudaGraphInstantiate(&m->gexec, g, 0) == cudaSuccess) m->have_graph = 1;
+            if (g) cudaGraphDestroy(g);
+        }
+        cudaGetLastError();
+    } else {
+        e = cudaGraphLaunch(m->gexec, m->st);
+        if (e) return tos_from_cuda(e);
+    }
+    return TOS_OK;
+}
+
+static int finish(tos_model_t *m, float *logits, int *next)
+{
+    int e = cudaMemcpyAsync(m->io_host + 2, m->io + 2, 2 * sizeof(int), cudaMemcpyDeviceToHost, m->st);
+    if (!e && logits)
+        e = cudaMemcpyAsync(logits, m->logits, (size_t)m->d.vocab_size * 4, cudaMemcpyDeviceToHost, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);
+    if (e) return tos_from_cuda(e);
+    if (m->io_host[3] != 0) {
+        cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
+        cudaStreamSynchronize(m->st);
+        return TOS_ETIMEOUT;
+    }
+    if (next) *next = m->io_host[2];
+    return TOS_OK;
+}
+
+int tos_model_forward_token(tos_model_t *m, float *logits, int token, int pos)
+{
+    if (!m) return tos_set_status(TOS_EINVAL);
+    int rc = run_token(m, token, pos);
+    if (!rc) rc = finish(m, logits, NULL);
+    return tos_set_status(rc);
+}
+
+int tos_model_forward_argmax(tos_model_t *m, int token, int pos, int *next)
+{
+    if (!m || !next) return tos_set_status(TOS_EINVAL);
+    int rc = run_token(m, token, pos);
+    if (!rc) rc = finish(m, NULL, next);
+    return tos_set_status(rc);
+}
+
+int tos_model_generate_greedy(tos_model_t *m, const int *prompt, int n_prompt, int n_gen, int *out)
+{
+    if (!m || n_prompt < 0 || n_gen < 0 || (n_prompt && !prompt) || (n_gen && !out))
+        return tos_set_status(TOS_EINVAL);
+    if (n_prompt == 0) return tos_set_status(TOS_EINVAL);
+    int pos = 0, next = 0, rc = TOS_OK;
+    for (int i = 0; i < n_prompt && !rc; i++) rc = tos_model_forward_argmax(m, prompt[i], pos++, &next);
+    int g = 0;
+    for (; !rc && g < n_gen && pos < m->d.max_seq; g++) {
+        out[g] = next;
+        rc = tos_model_forward_argmax(m, next, pos++, &next);
+    }
+    if (rc) return tos_set_status(rc);
+    tos_set_status(TOS_OK);
+    return g;
+}

@@ -1,0 +1,120 @@
+/*
+ * tos_kernels.h - internal C-callable launchers for the sm_100a kernels.
+ *
+ * The C11 host runtime (csrc/host) calls only these functions; each
+ * enqueues work on the given stream and returns a cudaError_t value (0 = ok).
+ * Nothing here allocates device memory except tosk_qmat_alloc.
+ */
+#ifndef TOS_KERNELS_H
+#define TOS_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml_type_t values, runtime/nn/gguf.h:38-58 */
+#define TOSK_F32 0
+#define TOSK_F16 1
+#define TOSK_Q4_0 2
+#define TOSK_Q8_0 8
+
+/* Device-resident quantised matrix in "plane" layout: the per-block fp16
+ * scales and the packed quants of the GGUF blocks (llm.c:142-146) are split
+ * so that every row's quants are 16-byte aligned for bulk copies. */
+typedef struct {
+    int type;        /* TOSK_Q4_0 or TOSK_Q8_0 */
+    int rows, cols;  /* out_dim, in_dim (cols a multiple of 32) */
+    int nb;          /* blocks per row = cols/32 */
+    int nbp;         /* scale row stride in halves = nb rounded up to 8 */
+    int qb;          /* quant bytes per block: 16 (Q4_0) or 32 (Q8_0) */
+    uint8_t *qs;     /* [rows][nb][qb] */
+    uint16_t *sc;    /* [rows][nbp] fp16 bit patterns */
+    size_t bytes;    /* device bytes held by qs + sc */
+} tosk_qmat_t;
+
+/* ---- weight planes ---- */
+int tosk_qmat_alloc(tosk_qmat_t *m, int type, int rows, int cols);
+void tosk_qmat_free(tosk_qmat_t *m);
+/* Repack GGUF blocks already on the device into m (row-concatenation of
+ * n_src sources, or row interleave when interleave != 0: dst row
+ * n_src*i + s <- source s row i). */
+int tosk_qmat_repack(tosk_qmat_t *m, const void *const *src_dev, const int *src_rows,
+                     int n_src, int interleave, cudaStream_t st);
+
+/* ---- GEMV epilogues ---- */
+enum {
+    TOSK_EPI_STORE = 0,   /* out[r] = y */
+    TOSK_EPI_RESID = 1,   /* out[r] = resid[r] + y   (llm_vadd_f32) */
+    TOSK_EPI_QKV = 2,     /* RoPE q/k rows, q -> out, k/v -> KV cache at *pos */
+    TOSK_EPI_SWIGLU = 3   /* rows (2i, 2i+1) = (gate_i, up_i): out[i] = silu(g)*u */
+};
+
+typedef struct {
+    int kind;
+    const float *resid;        /* RESID */
+    /* QKV */
+    const float2 *rope_cs;     /* [max_seq][hd/2] (cos, sin) */
+    const int *pos;            /* device int: current position */
+    int hd;                    /* head dim */
+    int q_rows;                /* n_heads*hd */
+    int kv_rows;               /* n_kv*hd */
+    int kv_type;               /* TOSK_F32 or TOSK_F16 */
+    void *k_cache;             /* this layer's [max_seq][kv_rows] */
+    void *v_cache;
+} tosk_epi_t;
+
+typedef struct {
+    const float *norm_w;       /* non-NULL: fuse RMSNorm of x (F32 weights) */
+    float eps;
+} tosk_norm_t;
+
+/* y = W * x with the reference's exact per-block lane tree and serial
+ * block order (llm.c:148-237).  x (length cols) is device memory. */
+int tosk_gemv(const tosk_qmat_t *w, const float *x, const tosk_norm_t *norm,
+              float *out, const tosk_epi_t *epi, int *err, int pdl, cudaStream_t st);
+
+/* per-block exact partials: blocks in GGUF layout, n_blocks consecutive,
+ * x of length 32*n_blocks, out[n_blocks] (q4_0_dot32 / q8_0_dot32) */
+int tosk_block_dots(const void *blocks, int type, const float *x, int n_blocks, float *out,
+                    cudaStream_t st);
+/* fp32-scale 20-byte Q4 (quantize4.c:122-198) */
+int tosk_q4f_gemv(const void *blocks, const float *x, float *out, int rows, int cols,
+                  cudaStream_t st);
+/* F16/F32 weight rows (llm.c:239-284) */
+int tosk_gemv_float(const void *w, int type, const float *x, float *out, int rows, int cols,
+                    cudaStream_t st);
+
+/* ---- elementwise / small ops (exact) ---- */
+int tosk_rmsnorm(float *out, const float *x, const void *w, int wtype, int dim, float eps,
+                 int pdl, cudaStream_t st);
+int tosk_rope_table(float2 *cs, int max_seq, int hd, float base, cudaStream_t st);
+int tosk_rope(float *vec, int n_vec, const int *pos_dev, int pos, int hd, float base,
+              cudaStream_t st);
+int tosk_softmax(float *x, int n, cudaStream_t st);
+int tosk_silu(float *x, int n, cudaStream_t st);
+int tosk_vadd(float *dst, const float *src, int n, cudaStream_t st);
+int tosk_vmul(float *dst, const float *src, int n, cudaStream_t st);
+int tosk_axpy(float *dst, float s, const float *src, int n, cudaStream_t st);
+int tosk_dot(const float *a, const float *b, int n, float *out, cudaStream_t st);
+int tosk_embed(float *out, const void *embd, int type, int dim, const int *tok_dev, int tok,
+               int pdl, cudaStream_t st);
+int tosk_argmax(const float *x, int n, int *out_idx, float *out_val, int pdl, cudaStream_t st);
+
+/* ---- decode attention ---- */
+enum { TOSK_ATTN_EXACT = 0, TOSK_ATTN_FAST = 1 };
+size_t tosk_attention_ws_bytes(int n_heads, int max_ctx);
+int tosk_attention(float *out, const float *q, const void *k_cache, const void *v_cache,
+                   int kv_type, int n_heads, int n_kv, int hd, const int *pos_dev, int pos,
+                   int max_ctx, int mode, void *ws, size_t ws_bytes, int *err, int pdl,
+                   cudaStream_t st);
+
+int tosk_num_sms(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

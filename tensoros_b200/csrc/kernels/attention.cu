@@ -1,0 +1,400 @@
+// attention.cu - single-query decode attention over the KV cache
+// (runtime/nn/llm.c:683-714), fp32 or fp16 cache laid out [pos][n_kv*hd].
+//
+// Reference order, per query head h (kv head kvh = h / (n_heads/n_kv)):
+//   score[t] = llm_dot_f32(q_h, K[t][kvh]) * (1/sqrt(hd))      t = 0..pos
+//   llm_softmax(score, pos+1): max, e_t = llm_expf(s_t - max), serial sum,
+//     inv = 1/(sum + 1e-10), p_t = e_t * inv
+//   head[d] = 0; for t: head[d] = head[d] + p_t * V[t][kvh][d]   (serial in t)
+//
+// EXACT mode keeps every reference rounding:
+//   scores_kernel  - persistent CTAs over (kv head, 128-position tile); the K
+//                    tile is staged in shared memory (padded rows) and each
+//                    thread forms one exact 8-chain dot per query head of the
+//                    group.  Fully parallel, HBM-bound.
+//   softmax_pv_kernel - one warp per (head, 64-wide slice of d): max over the
+//                    scores, e_t in parallel, the serial sum in lane 0, p_t in
+//                    parallel, then the serial PV chain with each lane owning
+//                    two d (packed f32x2).  V rows stream through a cp.async
+//                    ring.  The chains are the bound: ~4-5 cycles per position.
+// FAST mode splits positions into chunks (flash-decoding style) and combines
+// the partial sums in a tree; e_t still uses the reference's llm_expf of
+// (s_t - global max), so only summation order differs (tolerance 1e-4).
+#include <cuda_runtime.h>
+
+#include "tos_dev.cuh"
+#include "tos_kernels.h"
+
+namespace tos {
+
+constexpr int kScoreTile = 128;
+constexpr int kPvRows = 64;     // rows per V stage
+constexpr int kPvStages = 4;
+constexpr int kFastChunk = 256; // positions per FAST partial
+
+template <int ESZ>
+__device__ __forceinline__ void load8(const uint8_t* p, float2 (&v)[4]) {
+  if constexpr (ESZ == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    v[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    v[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[2] = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+    v[3] = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 16);
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(b.x, b.y);
+    v[3] = make_float2(b.z, b.w);
+  }
+}
+
+template <int ESZ>
+__device__ __forceinline__ float load1(const uint8_t* p) {
+  if constexpr (ESZ == 2) return h2f(*reinterpret_cast<const uint16_t*>(p));
+  return *reinterpret_cast<const float*>(p);
+}
+
+// ---------------------------------------------------------------------------
+// scores
+// ---------------------------------------------------------------------------
+template <int ESZ>
+__global__ void __launch_bounds__(kScoreTile) scores_kernel(const float* __restrict__ q,
+                                                            const uint8_t* __restrict__ kc,
+                                                            int n_heads, int n_kv, int hd,
+                                                            const int* __restrict__ pos_dev,
+                                                            int pos_arg, float* __restrict__ S,
+                                                            int max_ctx) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  pdl_wait();
+  pdl_trigger();
+  const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
+  const int group = n_heads / n_kv;
+  const int kv_dim = n_kv * hd;
+  const int rowb = hd * ESZ;           // bytes of one K row slice
+  const int strideb = rowb + 16;       // padded to spread banks
+  float* qs = reinterpret_cast<float*>(sm);
+  uint8_t* ks = sm + ((group * hd * 4 + 15) & ~15);
+  const int ntile = (n + kScoreTile - 1) / kScoreTile;
+  const int items = n_kv * ntile;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const int hd8 = hd & ~7;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int kvh = item / ntile;
+    const int t0 = (item % ntile) * kScoreTile;
+    const int rows = min(kScoreTile, n - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qs[i] = q[(size_t)kvh * group * hd + i];
+    const int cpr = rowb / 16;  // 16-byte chunks per row (hd*ESZ is a multiple of 16)
+    for (int c = threadIdx.x; c < rows * cpr; c += blockDim.x) {
+      const int r = c / cpr, k = c % cpr;
+      const uint4 v =
+          *reinterpret_cast<const uint4*>(kc + ((size_t)(t0 + r) * kv_dim + (size_t)kvh * hd) * ESZ + k * 16);
+      *reinterpret_cast<uint4*>(ks + r * strideb + k * 16) = v;
+    }
+    __syncthreads();
+    const int r = threadIdx.x;
+    if (r < rows) {
+      const uint8_t* kr = ks + r * strideb;
+      for (int g = 0; g < group; ++g) {
+        const float* qh = qs + g * hd;
+        float2 acc[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[p] = make_float2(0.0f, 0.0f);
+        for (int m = 0; m < hd8; m += 8) {
+          float2 kv[4];
+          load8<ESZ>(kr + m * ESZ, kv);
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            acc[p] = __fadd2_rn(acc[p], __fmul2_rn(make_float2(qh[m + 2 * p], qh[m + 2 * p + 1]), kv[p]));
+        }
+        const float2 t01 = __fadd2_rn(acc[0], acc[2]);
+        const float2 t23 = __fadd2_rn(acc[1], acc[3]);
+        float sum = __fadd_rn(__fadd_rn(__fadd_rn(t01.x, t01.y), t23.x), t23.y);
+        for (int i = hd8; i < hd; ++i) sum = __fadd_rn(sum, __fmul_rn(qh[i], load1<ESZ>(kr + i * ESZ)));
+        S[(size_t)(kvh * group + g) * max_ctx + t0 + r] = __fmul_rn(sum, scale);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streams V rows [t_begin, t_end) of this warp's slice through the ring and
+// accumulates acc += p_t * v_t (serial in t).  P holds p indexed by t.
+template <int ESZ>
+__device__ __forceinline__ float2 pv_chain(const uint8_t* __restrict__ vbase, size_t row_stride_b,
+                                           int slice_b, const float* __restrict__ P, int p_off,
+                                           int t_begin, int t_end, uint8_t* ring, int lane, bool active,
+                                           float2 acc) {
+  const int cpr = slice_b / 16;
+  const int stage_b = kPvRows * slice_b;
+  const int nrows = t_end - t_begin;
+  const int nst = (nrows + kPvRows - 1) / kPvRows;
+  auto issue = [&](int s) {
+    if (s < nst) {
+      const int r0 = t_begin + s * kPvRows;
+      const int rows = min(kPvRows, t_end - r0);
+      uint8_t* dst = ring + (s % kPvStages) * stage_b;
+      for (int c = lane; c < rows * cpr; c += 32) {
+        const int r = c / cpr, k = c % cpr;
+        cp_async16(dst + r * slice_b + k * 16, vbase + (size_t)(r0 + r) * row_stride_b + k * 16);
+      }
+    }
+    cp_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < kPvStages - 1; ++s) issue(s);
+  for (int s = 0; s < nst; ++s) {
+    issue(s + kPvStages - 1);
+    cp_wait<kPvStages - 1>();
+    __syncwarp();
+    const uint8_t* buf = ring + (s % kPvStages) * stage_b;
+    const int r0 = t_begin + s * kPvRows;
+    const int rows = min(kPvRows, t_end - r0);
+    if (active) {
+      for (int r = 0; r < rows; ++r) {
+        const float p = P[r0 + r - p_off];
+        float2 v;
+        if constexpr (ESZ == 2)
+          v = __half22float2(*reinterpret_cast<const __half2*>(buf + r * slice_b + lane * 4));
+        else
+          v = *reinterpret_cast<const float2*>(buf + r * slice_b + lane * 8);
+        acc = __fadd2_rn(acc, __fmul2_rn(make_float2(p, p), v));   // llm.c:586-588
+      }
+    }
+    __syncwarp();
+  }
+  cp_wait<0>();
+  return acc;
+}
+
+template <int ESZ>
+__global__ void __launch_bounds__(32) softmax_pv_kernel(const float* __restrict__ S,
+                                                        const uint8_t* __restrict__ vc, int n_heads,
+                                                        int n_kv, int hd, const int* __restrict__ pos_dev,
+                                                        int pos_arg, int max_ctx, float* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  float* P = reinterpret_cast<float*>(sm);
+  uint8_t* ring = sm + (((size_t)max_ctx * 4 + 15) & ~(size_t)15);
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x;
+  const int ngr = (hd + 63) / 64;
+  const int h = blockIdx.x / ngr, g = blockIdx.x % ngr;
+  const int kvh = h / (n_heads / n_kv);
+  const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
+  const float* Sh = S + (size_t)h * max_ctx;
+  // llm.c:509-511: max
+  float m = -INFINITY;
+  for (int t = lane; t < n; t += 32) m = fmaxf(m, Sh[t]);
+  m = warp_max(m);
+  // llm.c:514-517: e_t (parallel), then the serial sum in lane 0
+  for (int t = lane; t < n; t += 32) P[t] = ref_expf(__fsub_rn(Sh[t], m));
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) {
+    float sum = 0.0f;
+    int t = 0;
+    for (; t + 4 <= n; t += 4) {
+      const float4 e = *reinterpret_cast<const float4*>(P + t);
+      sum = __fadd_rn(sum, e.x);
+      sum = __fadd_rn(sum, e.y);
+      sum = __fadd_rn(sum, e.z);
+      sum = __fadd_rn(sum, e.w);
+    }
+    for (; t < n; ++t) sum = __fadd_rn(sum, P[t]);
+    inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
+  }
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+  for (int t = lane; t < n; t += 32) P[t] = __fmul_rn(P[t], inv);
+  __syncwarp();
+  // llm.c:703-709: serial PV chain
+  const int d0 = 64 * g;
+  const int slice = min(64, hd - d0);
+  const bool active = 2 * lane < slice;
+  const int kv_dim = n_kv * hd;
+  const uint8_t* vbase = vc + ((size_t)kvh * hd + d0) * ESZ;
+  float2 acc = pv_chain<ESZ>(vbase, (size_t)kv_dim * ESZ, slice * ESZ, P, 0, 0, n, ring, lane, active,
+                             make_float2(0.0f, 0.0f));
+  if (active) {
+    out[(size_t)h * hd + d0 + 2 * lane] = acc.x;
+    out[(size_t)h * hd + d0 + 2 * lane + 1] = acc.y;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FAST mode: per (head, slice, chunk) partial sums, then a combine pass.
+// ws layout after the scores: Msum[n_heads] (max), then partial e-sums
+// [n_heads][nchunk], then partial PV [n_heads][nchunk][hd].
+// ---------------------------------------------------------------------------
+template <int ESZ>
+__global__ void __launch_bounds__(32) fast_partial_kernel(const float* __restrict__ S,
+                                                          const uint8_t* __restrict__ vc, int n_heads,
+                                                          int n_kv, int hd, const int* __restrict__ pos_dev,
+                                                          int pos_arg, int max_ctx, float* __restrict__ esum,
+                                                          float* __restrict__ pv, int max_chunks) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  float* P = reinterpret_cast<float*>(sm);
+  uint8_t* ring = sm + kFastChunk * 4;
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x;
+  const int ngr = (hd + 63) / 64;
+  const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
+  const int nchunk = (n + kFastChunk - 1) / kFastChunk;
+  const int items = n_heads * ngr * nchunk;
+  const int kv_dim = n_kv * hd;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int c = item % nchunk;
+    const int hg = item / nchunk;
+    const int h = hg / ngr, g = hg % ngr;
+    const int kvh = h / (n_heads / n_kv);
+    const float* Sh = S + (size_t)h * max_ctx;
+    float m = -INFINITY;
+    for (int t = lane; t < n; t += 32) m = fmaxf(m, Sh[t]);
+    m = warp_max(m);
+    const int t0 = c * kFastChunk, t1 = min(n, t0 + kFastChunk);
+    float part = 0.0f;
+    __syncwarp();
+    for (int t = t0 + lane; t < t1; t += 32) {
+      const float e = ref_expf(__fsub_rn(Sh[t], m));
+      P[t - t0] = e;
+      part = __fadd_rn(part, e);
+    }
+    for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+    __syncwarp();
+    const int d0 = 64 * g;
+    const int slice = min(64, hd - d0);
+    const bool active = 2 * lane < slice;
+    const uint8_t* vbase = vc + ((size_t)kvh * hd + d0) * ESZ;
+    float2 acc = pv_chain<ESZ>(vbase, (size_t)kv_dim * ESZ, slice * ESZ, P, t0, t0, t1, ring, lane,
+                               active, make_float2(0.0f, 0.0f));
+    if (g == 0 && lane == 0) esum[(size_t)h * max_chunks + c] = part;
+    if (active) {
+      float* o = pv + ((size_t)h * max_chunks + c) * hd + d0 + 2 * lane;
+      o[0] = acc.x;
+      o[1] = acc.y;
+    }
+  }
+}
+
+__global__ void fast_combine_kernel(const float* __restrict__ esum, const float* __restrict__ pv,
+                                    int n_heads, int hd, const int* __restrict__ pos_dev, int pos_arg,
+                                    int max_chunks, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
+  const int nchunk = (n + kFastChunk - 1) / kFastChunk;
+  const int h = blockIdx.x;
+  __shared__ float s_inv;
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int c = 0; c < nchunk; ++c) sum = __fadd_rn(sum, esum[(size_t)h * max_chunks + c]);
+    s_inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int c = 0; c < nchunk; ++c) acc = __fadd_rn(acc, pv[((size_t)h * max_chunks + c) * hd + d]);
+    out[(size_t)h * hd + d] = __fmul_rn(acc, s_inv);
+  }
+}
+
+}  // namespace tos
+
+using namespace tos;
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+extern "C" size_t tosk_attention_ws_bytes(int n_heads, int max_ctx) {
+  const size_t maxc = (size_t)(max_ctx + kFastChunk - 1) / kFastChunk;
+  return align256((size_t)n_heads * max_ctx * 4) + align256((size_t)n_heads * maxc * 4) +
+         align256((size_t)n_heads * maxc * 256 * 4);
+}
+
+template <typename K>
+static int launch_k(K kern, int grid, int threads, size_t smem, int pdl, cudaStream_t st, void** args) {
+  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem > 48 * 1024 ? (int)smem : 48 * 1024);
+  if (e != cudaSuccess) return (int)e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return (int)cudaLaunchKernelExC(&cfg, (const void*)kern, args);
+}
+
+extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, const void* v_cache,
+                              int kv_type, int n_heads, int n_kv, int hd, const int* pos_dev, int pos,
+                              int max_ctx, int mode, void* ws, size_t ws_bytes, int* err, int pdl,
+                              cudaStream_t st) {
+  (void)err;
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || hd <= 0 || max_ctx <= 0) return (int)cudaErrorInvalidValue;
+  if (kv_type != TOSK_F16 && kv_type != TOSK_F32) return (int)cudaErrorInvalidValue;
+  const int esz = kv_type == TOSK_F16 ? 2 : 4;
+  if ((hd * esz) % 16 != 0 || hd % 2 != 0) return (int)cudaErrorInvalidValue;
+  if (ws_bytes < tosk_attention_ws_bytes(n_heads, max_ctx)) return (int)cudaErrorInvalidValue;
+  if (!pos_dev && (pos < 0 || pos >= max_ctx)) return (int)cudaErrorInvalidValue;
+  float* S = (float*)ws;
+  const int group = n_heads / n_kv;
+  // scores
+  {
+    const size_t smem = ((size_t)group * hd * 4 + 15) / 16 * 16 + (size_t)kScoreTile * (hd * esz + 16);
+    if (smem > 227 * 1024) return (int)cudaErrorInvalidValue;
+    const int tiles = (max_ctx + kScoreTile - 1) / kScoreTile;
+    int grid = n_kv * tiles;
+    const int cap = tosk_num_sms() * 4;
+    if (grid > cap) grid = cap;
+    const uint8_t* kc = (const uint8_t*)k_cache;
+    void* args[] = {(void*)&q, (void*)&kc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &S, &max_ctx};
+    int e = esz == 2 ? launch_k(scores_kernel<2>, grid, kScoreTile, smem, pdl, st, args)
+                     : launch_k(scores_kernel<4>, grid, kScoreTile, smem, pdl, st, args);
+    if (e) return e;
+  }
+  const int ngr = (hd + 63) / 64;
+  const uint8_t* vc = (const uint8_t*)v_cache;
+  if (mode == TOSK_ATTN_EXACT) {
+    const size_t ring = (size_t)kPvStages * kPvRows * 64 * esz;
+    const size_t smem = (((size_t)max_ctx * 4 + 15) & ~(size_t)15) + ring;
+    if (smem > 227 * 1024) return (int)cudaErrorInvalidValue;
+    void* args[] = {&S, (void*)&vc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &max_ctx, &out};
+    return esz == 2 ? launch_k(softmax_pv_kernel<2>, n_heads * ngr, 32, smem, pdl, st, args)
+                    : launch_k(softmax_pv_kernel<4>, n_heads * ngr, 32, smem, pdl, st, args);
+  }
+  const int max_chunks = (max_ctx + kFastChunk - 1) / kFastChunk;
+  if (hd > 256) return (int)cudaErrorInvalidValue;
+  float* esum = (float*)((char*)ws + align256((size_t)n_heads * max_ctx * 4));
+  float* pv = (float*)((char*)esum + align256((size_t)n_heads * max_chunks * 4));
+  {
+    const size_t smem = (size_t)kFastChunk * 4 + (size_t)kPvStages * kPvRows * 64 * esz;
+    int grid = n_heads * ngr * max_chunks;
+    const int cap = tosk_num_sms() * 8;
+    if (grid > cap) grid = cap;
+    void* args[] = {&S, (void*)&vc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &max_ctx, &esum, &pv, (void*)&max_chunks};
+    int e = esz == 2 ? launch_k(fast_partial_kernel<2>, grid, 32, smem, pdl, st, args)
+                     : launch_k(fast_partial_kernel<4>, grid, 32, smem, pdl, st, args);
+    if (e) return e;
+  }
+  void* args[] = {&esum, &pv, &n_heads, &hd, (void*)&pos_dev, &pos, (void*)&max_chunks, &out};
+  return launch_k(fast_combine_kernel, n_heads, 128, 0, pdl, st, args);
+}

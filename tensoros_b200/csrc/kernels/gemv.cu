@@ -1,0 +1,562 @@
+// gemv.cu - exact Q4_0 / Q8_0 GEMV for sm_100a (TensorOS runtime/nn llm_gemv).
+//
+// Reference semantics (runtime/nn/llm.c):
+//   q4_0_dot32 / q8_0_dot32 (llm.c:148-209): per 32-weight block, eight lane
+//     chains c = 0..7 each summing the products (float)q[8k+c] * x[8k+c] over
+//     k = 0..3 from +0.0f; t_l = chain_l + chain_{l+4}; r = ((t0+t1)+t2)+t3;
+//     the block value is r * fp16_to_fp32(scale).
+//   llm_vec_dot (llm.c:221-237): row sum = 0.0f, then += block value in block
+//     order (a serial fp32 chain).
+//   llm_gemv (llm.c:329-349): one row sum per output element.
+//
+// Design (B200):
+//   * Weights are repacked once into two planes: quants [rows][nb][16|32 B]
+//     and fp16 scales [rows][nbp] (nbp = nb rounded up to 8).  Every 8-row
+//     tile of either plane is one contiguous, 16-byte aligned range, so it is
+//     fetched with a single cp.async.bulk into shared memory.  Algorithmic
+//     bytes are the GGUF bytes (18 or 34 per block).
+//   * One persistent CTA per SM owns a contiguous row range.  Warp 0 is the
+//     producer: it streams 8-row stages through an S-deep shared-memory ring
+//     (mbarrier complete_tx).  Weights do not depend on the previous kernel, so
+//     the ring fills before griddepcontrol.wait returns (PDL overlap).
+//   * Compute warps: thread (block b, row group g) keeps x[32b..32b+31] in
+//     registers for the whole kernel (optionally RMS-normalised in the
+//     prologue, llm.c:416-442) and computes the exact block values of its
+//     rows with packed f32x2 IEEE ops: nibble/byte -> float via the 2^23 magic
+//     (exact), products and lane chains in the reference order.  Values go to
+//     a shared "partials" tile P[8][nb].
+//   * Two chain warps take alternate stages; lane r of a chain warp adds the
+//     nb partials of row r serially (the reference's row chain), then runs the
+//     fused epilogue (plain store, residual add, RoPE + KV-cache store, or
+//     SiLU(gate)*up).
+//   Every mbarrier wait is bounded (tos::mbar_wait) and reports through *err.
+#include <cuda_runtime.h>
+
+#include "tos_dev.cuh"
+#include "tos_kernels.h"
+
+namespace tos {
+
+constexpr int kTR = 8;    // rows per stage
+constexpr int kNCH = 2;   // chain warps
+
+// Exact block dot, Q4_0.  q holds qs[0..15]; word k = bytes 4k..4k+3 covers
+// elements 8k..8k+7; byte j of the word gives element 8k+2j (low nibble) and
+// 8k+2j+1 (high nibble), i.e. lane chains 2j and 2j+1.  Pair p of the f32x2
+// accumulators is (chain 2p, chain 2p+1).
+// kZeroInit adds the reference's leading +0.0f; it only changes the sign of
+// an all-zero chain, which a row sum starting from +0.0f cannot observe, so
+// the GEMV skips it and the per-block entry point keeps it.
+template <bool kZeroInit>
+__device__ __forceinline__ float dot_q4_0(const uint4 q, const float d, const float (&x)[32]) {
+  const float kM = 8388616.0f;  // 2^23 + 8
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  float2 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = w[k] & 0x0F0F0F0Fu;
+    const uint32_t hi = (w[k] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t sel = 0x7540u | (uint32_t)p;
+      const float a = __uint_as_float(prmt(lo, 0x4B000000u, sel));
+      const float b = __uint_as_float(prmt(hi, 0x4B000000u, sel));
+      const float2 qv = __fadd2_rn(make_float2(a, b), make_float2(-kM, -kM));
+      const float2 pr = __fmul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
+      if (k == 0)
+        acc[p] = kZeroInit ? __fadd2_rn(make_float2(0.0f, 0.0f), pr) : pr;
+      else
+        acc[p] = __fadd2_rn(acc[p], pr);
+    }
+  }
+  const float2 t01 = __fadd2_rn(acc[0], acc[2]);
+  const float2 t23 = __fadd2_rn(acc[1], acc[3]);
+  const float r = __fadd_rn(__fadd_rn(__fadd_rn(t01.x, t01.y), t23.x), t23.y);
+  return __fmul_rn(r, d);
+}
+
+// Exact block dot, Q8_0.  Elements 8k..8k+3 are word 2k, 8k+4..8k+7 word 2k+1.
+template <bool kZeroInit>
+__device__ __forceinline__ float dot_q8_0(const uint4 qa, const uint4 qb, const float d,
+                                          const float (&x)[32]) {
+  const float kM = 8388736.0f;  // 2^23 + 128
+  const uint32_t w[8] = {qa.x ^ 0x80808080u, qa.y ^ 0x80808080u, qa.z ^ 0x80808080u,
+                         qa.w ^ 0x80808080u, qb.x ^ 0x80808080u, qb.y ^ 0x80808080u,
+                         qb.z ^ 0x80808080u, qb.w ^ 0x80808080u};
+  float2 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t word = w[2 * k + (p >> 1)];
+      const uint32_t s0 = 0x7540u | (uint32_t)((2 * p) & 3);
+      const uint32_t s1 = 0x7540u | (uint32_t)((2 * p + 1) & 3);
+      const float a = __uint_as_float(prmt(word, 0x4B000000u, s0));
+      const float b = __uint_as_float(prmt(word, 0x4B000000u, s1));
+      const float2 qv = __fadd2_rn(make_float2(a, b), make_float2(-kM, -kM));
+      const float2 pr = __fmul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
+      if (k == 0)
+        acc[p] = kZeroInit ? __fadd2_rn(make_float2(0.0f, 0.0f), pr) : pr;
+      else
+        acc[p] = __fadd2_rn(acc[p], pr);
+    }
+  }
+  const float2 t01 = __fadd2_rn(acc[0], acc[2]);
+  const float2 t23 = __fadd2_rn(acc[1], acc[3]);
+  const float r = __fadd_rn(__fadd_rn(__fadd_rn(t01.x, t01.y), t23.x), t23.y);
+  return __fmul_rn(r, d);
+}
+
+struct GemvArgs {
+  const uint8_t* qs;
+  const uint16_t* sc;
+  const float* x;
+  const float* norm_w;
+  float eps;
+  float* out;
+  int* err;
+  int R, nb, nbp, cols;
+  int unit;      // CTA row ranges are multiples of `unit` rows
+  int S;         // ring depth
+  int pstride;   // partials row stride (floats)
+  int nwb, rg;   // compute warps per row of blocks, row groups
+  uint32_t off_x, off_p, off_st, stage_bytes, stage_sc_off;
+  tosk_epi_t epi;
+};
+
+template <int QB>
+__device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t* sts, int r, int b,
+                                             int nb, int nbp, const float (&x)[32]) {
+  const float d = h2f(sts[r * nbp + b]);
+  if constexpr (QB == 16) {
+    const uint4 q = *reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 16);
+    return dot_q4_0<false>(q, d, x);
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 32);
+    return dot_q8_0<false>(p[0], p[1], d, x);
+  }
+}
+
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int QB, bool kNorm, int kEpi>
+__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = a.S;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  uint64_t* pfull = empty + S;
+  uint64_t* pempty = pfull + kNCH;
+  float* misc = reinterpret_cast<float*>(pempty + kNCH);
+  float* xs = reinterpret_cast<float*>(smem + a.off_x);
+  float* P = reinterpret_cast<float*>(smem + a.off_p);
+  uint8_t* stages = smem + a.off_st;
+
+  const int NU = (a.R + a.unit - 1) / a.unit;
+  const int u0 = (int)(((long long)blockIdx.x * NU) / gridDim.x);
+  const int u1 = (int)(((long long)(blockIdx.x + 1) * NU) / gridDim.x);
+  const int rb = u0 * a.unit;
+  const int re = min(u1 * a.unit, a.R);
+  const int nst = re > rb ? (re - rb + kTR - 1) / kTR : 0;
+  const int ncw = a.nwb * a.rg;
+  const int nb = a.nb, nbp = a.nbp;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncw);
+    }
+    for (int c = 0; c < kNCH; ++c) {
+      mbar_init(&pfull[c], ncw);
+      mbar_init(&pempty[c], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < nst; ++it) {
+        const int s = it % S;
+        if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.err, 1)) break;
+        const int r0 = rb + it * kTR;
+        const int n = min(kTR, re - r0);
+        const uint32_t bq = (uint32_t)(n * nb * QB);
+        const uint32_t bs = (uint32_t)(n * nbp * 2);
+        uint8_t* st = stages + (size_t)s * a.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], bq + bs);
+        bulk_g2s(st, a.qs + (size_t)r0 * nb * QB, bq, &full[s]);
+        bulk_g2s(st + a.stage_sc_off, a.sc + (size_t)r0 * nbp, bs, &full[s]);
+        issued = it + 1;
+      }
+      // Leave only when every copy issued into this CTA's ring has landed.
+      for (int it = max(0, issued - S); it < issued; ++it)
+        mbar_wait(&full[it % S], (it / S) & 1, a.err, 5);
+    }
+    return;
+  }
+
+  // ---------------- all non-producer warps ----------------
+  const int nthr = (int)blockDim.x - 32;
+  pdl_wait();  // x (and the residual / position) come from earlier kernels
+  float ss = 1.0f;
+  if constexpr (kNorm) {
+    for (int i = threadIdx.x - 32; i < a.cols; i += nthr) xs[i] = a.x[i];
+    named_sync(1, nthr);
+    if (warp == 1 && lane < 4) {
+      // llm.c:421-427: lane l sums x[4i+l]^2 serially
+      float acc = 0.0f;
+      for (int i0 = 0; i0 + 4 <= a.cols; i0 += 4)
+        acc = __fadd_rn(acc, __fmul_rn(xs[i0 + lane], xs[i0 + lane]));
+      misc[lane] = acc;
+    }
+    named_sync(1, nthr);
+    if (threadIdx.x == 32) {
+      float s2 = __fadd_rn(__fadd_rn(__fadd_rn(misc[0], misc[1]), misc[2]), misc[3]);
+      for (int i = a.cols & ~3; i < a.cols; ++i) s2 = __fadd_rn(s2, __fmul_rn(xs[i], xs[i]));
+      // llm.c:431: ss = 1 / sqrt(ss/dim + eps)
+      misc[4] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s2, (float)a.cols), a.eps)));
+    }
+    named_sync(1, nthr);
+    ss = misc[4];
+  }
+
+  if (warp >= 1 + kNCH) {
+    // ---------------- compute warps ----------------
+    const int ct = (warp - 1 - kNCH) * 32 + lane;
+    const int bw = a.nwb * 32;
+    const int b = ct % bw;
+    const int g = ct / bw;
+    const bool valid = b < nb;
+    float xr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) xr[i] = 0.0f;
+    if (valid) {
+      if constexpr (kNorm) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          xr[i] = __fmul_rn(__fmul_rn(xs[32 * b + i], ss), a.norm_w[32 * b + i]);
+      } else {
+        const float4* xv = reinterpret_cast<const float4*>(a.x + 32 * b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = xv[i];
+          xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
+        }
+      }
+    }
+    for (int it = 0; it < nst; ++it) {
+      const int s = it % S;
+      if (!mbar_wait(&full[s], (it / S) & 1, a.err, 2)) break;
+      const int c = it % kNCH;
+      if (it >= kNCH && !mbar_wait(&pempty[c], ((it / kNCH) & 1) ^ 1, a.err, 3)) break;
+      const int n = min(kTR, re - (rb + it * kTR));
+      const uint8_t* stq = stages + (size_t)s * a.stage_bytes;
+      const uint16_t* sts = reinterpret_cast<const uint16_t*>(stq + a.stage_sc_off);
+      float* Pc = P + c * kTR * a.pstride;
+      if (valid) {
+#pragma unroll 2
+        for (int r = g; r < n; r += a.rg) Pc[r * a.pstride + b] = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&pfull[c]);
+      }
+    }
+    return;
+  }
+
+  // ---------------- chain warps (warp 1 .. kNCH) ----------------
+  const int cw = warp - 1;
+  int pos = 0;
+  if constexpr (kEpi == TOSK_EPI_QKV) pos = *a.epi.pos;
+  for (int it = cw; it < nst; it += kNCH) {
+    if (!mbar_wait(&pfull[cw], (it / kNCH) & 1, a.err, 4)) break;
+    const int r0 = rb + it * kTR;
+    const int n = min(kTR, re - r0);
+    const float* Pr = P + (cw * kTR + min(lane, kTR - 1)) * a.pstride;
+    float y = 0.0f;  // llm.c:223: sum = 0.0f, then += block value, in block order
+    if (lane < n) {
+      int bb = 0;
+      for (; bb + 4 <= nb; bb += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(Pr + bb);
+        y = __fadd_rn(y, v.x);
+        y = __fadd_rn(y, v.y);
+        y = __fadd_rn(y, v.z);
+        y = __fadd_rn(y, v.w);
+      }
+      for (; bb < nb; ++bb) y = __fadd_rn(y, Pr[bb]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&pempty[cw]);
+    const int r = r0 + lane;
+    if constexpr (kEpi == TOSK_EPI_STORE) {
+      if (lane < n) a.out[r] = y;
+    } else if constexpr (kEpi == TOSK_EPI_RESID) {
+      if (lane < n) a.out[r] = __fadd_rn(a.epi.resid[r], y);  // llm.c:599-614
+    } else if constexpr (kEpi == TOSK_EPI_SWIGLU) {
+      // llm.c:726-729: g = silu(g); g *= u
+      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+      if (lane < n && (r & 1) == 0) a.out[r >> 1] = __fmul_rn(ref_silu(y), partner);
+    } else if constexpr (kEpi == TOSK_EPI_QKV) {
+      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+      const int qr = a.epi.q_rows, kr = a.epi.kv_rows, hd = a.epi.hd;
+      if (lane < n) {
+        float v = y;
+        if (r < qr + kr) {
+          // llm.c:488-492 (RoPE on q and k rows, adjacent pairs)
+          const int i = (r < qr ? r : r - qr) % hd;
+          const float2 cs = a.epi.rope_cs[(size_t)pos * (hd >> 1) + (i >> 1)];
+          if ((i & 1) == 0)
+            v = __fsub_rn(__fmul_rn(y, cs.x), __fmul_rn(partner, cs.y));
+          else
+            v = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(y, cs.x));
+        }
+        if (r < qr) {
+          a.out[r] = v;
+        } else {
+          // llm.c:673-681: store k, v at [pos][kv_dim]
+          const bool is_k = r < qr + kr;
+          const int e = is_k ? r - qr : r - qr - kr;
+          void* cache = is_k ? a.epi.k_cache : a.epi.v_cache;
+          const size_t idx = (size_t)pos * kr + e;
+          if (a.epi.kv_type == TOSK_F16)
+            reinterpret_cast<uint16_t*>(cache)[idx] = f2h(v);
+          else
+            reinterpret_cast<float*>(cache)[idx] = v;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight repack: GGUF blocks -> planes
+// ---------------------------------------------------------------------------
+__global__ void repack_kernel(const uint8_t* __restrict__ src, int src_rows, int nb, int qb,
+                              uint8_t* __restrict__ qs, uint16_t* __restrict__ sc, int nbp,
+                              int dst_row0, int dst_row_step) {
+  const size_t total = (size_t)src_rows * nb;
+  const int bsz = qb + 2;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / nb);
+    const int b = (int)(i % nb);
+    const uint8_t* s = src + i * bsz;
+    const size_t drow = (size_t)dst_row0 + (size_t)row * dst_row_step;
+    sc[drow * nbp + b] = (uint16_t)(s[0] | (s[1] << 8));
+    uint8_t* d = qs + (drow * nb + b) * qb;
+    for (int j = 0; j < qb; ++j) d[j] = s[2 + j];
+  }
+}
+
+// Per-block exact values (with the reference's leading +0.0f), GGUF layout.
+__global__ void block_dots_kernel(const uint8_t* __restrict__ blocks, int type,
+                                  const float* __restrict__ x, int n_blocks,
+                                  float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_blocks) return;
+  float xr[32];
+  const float4* xv = reinterpret_cast<const float4*>(x + 32 * (size_t)i);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float4 v = xv[k];
+    xr[4 * k] = v.x; xr[4 * k + 1] = v.y; xr[4 * k + 2] = v.z; xr[4 * k + 3] = v.w;
+  }
+  if (type == TOSK_Q4_0) {
+    const uint8_t* p = blocks + (size_t)i * 18;
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = p[2 + 4 * k] | (p[3 + 4 * k] << 8) | (p[4 + 4 * k] << 16) | ((uint32_t)p[5 + 4 * k] << 24);
+    out[i] = dot_q4_0<true>(make_uint4(w[0], w[1], w[2], w[3]), h2f((uint16_t)(p[0] | (p[1] << 8))), xr);
+  } else {
+    const uint8_t* p = blocks + (size_t)i * 34;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      w[k] = p[2 + 4 * k] | (p[3 + 4 * k] << 8) | (p[4 + 4 * k] << 16) | ((uint32_t)p[5 + 4 * k] << 24);
+    out[i] = dot_q8_0<true>(make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]),
+                            h2f((uint16_t)(p[0] | (p[1] << 8))), xr);
+  }
+}
+
+}  // namespace tos
+
+using namespace tos;
+
+static int g_num_sms = 0;
+
+extern "C" int tosk_num_sms(void) {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+extern "C" int tosk_qmat_alloc(tosk_qmat_t* m, int type, int rows, int cols) {
+  if (!m || rows <= 0 || cols <= 0 || (cols % 32) != 0) return (int)cudaErrorInvalidValue;
+  if (type != TOSK_Q4_0 && type != TOSK_Q8_0) return (int)cudaErrorInvalidValue;
+  m->type = type;
+  m->rows = rows;
+  m->cols = cols;
+  m->nb = cols / 32;
+  m->nbp = (m->nb + 7) & ~7;
+  m->qb = type == TOSK_Q4_0 ? 16 : 32;
+  const size_t qbytes = (size_t)rows * m->nb * m->qb;
+  const size_t sbytes = (size_t)rows * m->nbp * 2;
+  m->qs = nullptr;
+  m->sc = nullptr;
+  cudaError_t e = cudaMalloc((void**)&m->qs, qbytes);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMalloc((void**)&m->sc, sbytes);
+  if (e != cudaSuccess) {
+    cudaFree(m->qs);
+    m->qs = nullptr;
+    return (int)e;
+  }
+  m->bytes = qbytes + sbytes;
+  return (int)cudaMemset(m->sc, 0, sbytes);
+}
+
+extern "C" void tosk_qmat_free(tosk_qmat_t* m) {
+  if (!m) return;
+  if (m->qs) cudaFree(m->qs);
+  if (m->sc) cudaFree(m->sc);
+  m->qs = nullptr;
+  m->sc = nullptr;
+  m->bytes = 0;
+}
+
+extern "C" int tosk_qmat_repack(tosk_qmat_t* m, const void* const* src, const int* src_rows,
+                                int n_src, int interleave, cudaStream_t st) {
+  int row0 = 0;
+  for (int s = 0; s < n_src; ++s) {
+    const int dst_row0 = interleave ? s : row0;
+    const int step = interleave ? n_src : 1;
+    const size_t total = (size_t)src_rows[s] * m->nb;
+    const int threads = 256;
+    const int grid = (int)((total + threads - 1) / threads < 65535 ? (total + threads - 1) / threads : 65535);
+    repack_kernel<<<grid, threads, 0, st>>>((const uint8_t*)src[s], src_rows[s], m->nb, m->qb, m->qs,
+                                            m->sc, m->nbp, dst_row0, step);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    row0 += src_rows[s];
+  }
+  return 0;
+}
+
+template <int QB, bool kNorm, int kEpi>
+static int launch_gemv(const GemvArgs& a, int grid, int threads, size_t smem, int pdl,
+                       cudaStream_t st) {
+  static bool configured = false;
+  auto kern = gemv_kernel<QB, kNorm, kEpi>;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return (int)cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int QB>
+static int dispatch_gemv(const GemvArgs& a, bool norm, int epi, int grid, int threads, size_t smem,
+                         int pdl, cudaStream_t st) {
+  if (norm) {
+    switch (epi) {
+      case TOSK_EPI_STORE: return launch_gemv<QB, true, TOSK_EPI_STORE>(a, grid, threads, smem, pdl, st);
+      case TOSK_EPI_QKV: return launch_gemv<QB, true, TOSK_EPI_QKV>(a, grid, threads, smem, pdl, st);
+      case TOSK_EPI_SWIGLU: return launch_gemv<QB, true, TOSK_EPI_SWIGLU>(a, grid, threads, smem, pdl, st);
+      default: return (int)cudaErrorInvalidValue;
+    }
+  }
+  switch (epi) {
+    case TOSK_EPI_STORE: return launch_gemv<QB, false, TOSK_EPI_STORE>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_RESID: return launch_gemv<QB, false, TOSK_EPI_RESID>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_QKV: return launch_gemv<QB, false, TOSK_EPI_QKV>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_SWIGLU: return launch_gemv<QB, false, TOSK_EPI_SWIGLU>(a, grid, threads, smem, pdl, st);
+    default: return (int)cudaErrorInvalidValue;
+  }
+}
+
+static inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t* norm, float* out,
+                         const tosk_epi_t* epi, int* err, int pdl, cudaStream_t st) {
+  if (!w || !x || !out) return (int)cudaErrorInvalidValue;
+  GemvArgs a = {};
+  a.qs = w->qs;
+  a.sc = w->sc;
+  a.x = x;
+  const bool fuse_norm = norm && norm->norm_w;
+  a.norm_w = fuse_norm ? norm->norm_w : nullptr;
+  a.eps = norm ? norm->eps : 1e-6f;
+  a.out = out;
+  a.err = err;
+  a.R = w->rows;
+  a.nb = w->nb;
+  a.nbp = w->nbp;
+  a.cols = w->cols;
+  const int kind = epi ? epi->kind : TOSK_EPI_STORE;
+  a.unit = (kind == TOSK_EPI_QKV || kind == TOSK_EPI_SWIGLU) ? 2 : 1;
+  if (epi) a.epi = *epi;
+  a.epi.kind = kind;
+  a.nwb = (w->nb + 31) / 32;
+  if (a.nwb > 13) return (int)cudaErrorInvalidValue;  // cols > 13*1024: not supported
+  a.rg = a.nwb >= 8 ? 1 : (8 / a.nwb);
+  if (a.rg > kTR) a.rg = kTR;
+  const int threads = 32 * (1 + kNCH + a.nwb * a.rg);
+  a.pstride = (int)round_up((uint32_t)w->nb, 8) + 4;
+  const uint32_t qbytes = (uint32_t)(kTR * w->nb * w->qb);
+  a.stage_sc_off = round_up(qbytes, 16);
+  a.stage_bytes = round_up(a.stage_sc_off + (uint32_t)(kTR * w->nbp * 2), 128);
+  const uint32_t hdr = 128;
+  a.off_x = hdr;
+  const uint32_t xbytes = fuse_norm ? round_up((uint32_t)w->cols * 4, 128) : 0;
+  a.off_p = a.off_x + xbytes;
+  const uint32_t pbytes = round_up((uint32_t)(kNCH * kTR * a.pstride * 4), 128);
+  a.off_st = a.off_p + pbytes;
+  const uint32_t budget_lo = 100 * 1024, budget_hi = 227 * 1024;
+  int S = (int)((budget_lo > a.off_st ? budget_lo - a.off_st : 0) / a.stage_bytes);
+  if (S < 2) S = 2;
+  if (S > 8) S = 8;
+  if (a.off_st + (uint32_t)S * a.stage_bytes > budget_hi) return (int)cudaErrorInvalidValue;
+  // header holds 2*S + 2*kNCH barriers + 8 floats
+  if ((uint32_t)(8 * (2 * S + 2 * kNCH) + 32) > hdr) return (int)cudaErrorInvalidValue;
+  a.S = S;
+  const size_t smem = a.off_st + (size_t)S * a.stage_bytes;
+  const int NU = (a.R + a.unit - 1) / a.unit;
+  int grid = tosk_num_sms();
+  if (grid > NU) grid = NU;
+  if (w->qb == 16) return dispatch_gemv<16>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
+  return dispatch_gemv<32>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
+}
+
+extern "C" int tosk_block_dots(const void* blocks, int type, const float* x, int n_blocks, float* out,
+                               cudaStream_t st) {
+  if (type != TOSK_Q4_0 && type != TOSK_Q8_0) return (int)cudaErrorInvalidValue;
+  if (n_blocks <= 0) return 0;
+  block_dots_kernel<<<(n_blocks + 127) / 128, 128, 0, st>>>((const uint8_t*)blocks, type, x, n_blocks, out);
+  return (int)cudaGetLastError();
+}

@@ -1,0 +1,333 @@
+// ops.cu - exact device versions of runtime/nn/llm.c's small operators.
+//
+// Each kernel reproduces the fp32 operation order of the reference operator
+// named beside it, using IEEE round-to-nearest intrinsics only.  Serial
+// reference chains (the RMSNorm lane sums, the softmax sum) stay serial: they
+// are short (dim/4, n) and run in one thread while the other threads do the
+// element-parallel parts.
+#include <cuda_runtime.h>
+
+#include "tos_dev.cuh"
+#include "tos_kernels.h"
+
+namespace tos {
+
+// llm.c:352-362 llm_get_f: F32 / F16 read, any other type reads 0
+__device__ __forceinline__ float get_f(const void* w, int i, int type) {
+  if (type == TOSK_F32) return reinterpret_cast<const float*>(w)[i];
+  if (type == TOSK_F16) return h2f(reinterpret_cast<const uint16_t*>(w)[i]);
+  return 0.0f;
+}
+
+// llm.c:416-442 (single CTA).  Lane l of warp 0 (l < 4) sums x[4i+l]^2
+// serially; thread 0 combines ((s0+s1)+s2)+s3, adds the scalar tail, and
+// forms 1/sqrt(ss/dim + eps); every thread then writes (x*ss)*w.
+__global__ void rmsnorm_kernel(float* __restrict__ out, const float* __restrict__ x,
+                               const void* __restrict__ w, int wtype, int dim, float eps) {
+  __shared__ float lanes[4];
+  __shared__ float s_ss;
+  pdl_wait();
+  if (threadIdx.x < 4) {
+    float acc = 0.0f;
+    for (int i0 = 0; i0 + 4 <= dim; i0 += 4) {
+      const float v = x[i0 + threadIdx.x];
+      acc = __fadd_rn(acc, __fmul_rn(v, v));
+    }
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = __fadd_rn(__fadd_rn(__fadd_rn(lanes[0], lanes[1]), lanes[2]), lanes[3]);
+    for (int i = dim & ~3; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+    s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+  }
+  __syncthreads();
+  pdl_trigger();
+  const float ss = s_ss;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x)
+    out[i] = __fmul_rn(__fmul_rn(x[i], ss), get_f(w, i, wtype));
+}
+
+// llm.c:460-487: cos/sin for element pair i of a head at position pos.
+__device__ __forceinline__ float2 rope_cs(int pos, int i, int hd, float base) {
+  const float exponent = __fdiv_rn(-(float)i, (float)hd);
+  float b = base;
+  int k = 0;
+  while (b > 2.0f) {
+    b = __fmul_rn(b, 0.5f);
+    ++k;
+  }
+  const float m1 = __fsub_rn(b, 1.0f);
+  const float inner = __fsub_rn(1.0f, __fmul_rn(m1, __fsub_rn(0.5f, __fmul_rn(m1, 0.3333f))));
+  const float log_base = __fadd_rn(__fmul_rn((float)k, 0.6931472f), __fmul_rn(m1, inner));
+  const float freq = ref_expf(__fmul_rn(exponent, log_base));
+  float theta = __fmul_rn((float)pos, freq);
+  const float pi = 3.14159265f;
+  const float two_pi = 2.0f * pi;
+  while (theta > pi) theta = __fsub_rn(theta, two_pi);
+  while (theta < -pi) theta = __fadd_rn(theta, two_pi);
+  const float t2 = __fmul_rn(theta, theta);
+  const float c = __fsub_rn(
+      1.0f, __fmul_rn(t2, __fsub_rn(0.5f, __fmul_rn(t2, __fsub_rn(0.04166667f, __fmul_rn(t2, 0.001388889f))))));
+  const float s = __fmul_rn(
+      theta,
+      __fsub_rn(1.0f, __fmul_rn(t2, __fsub_rn(0.1666667f,
+                                              __fmul_rn(t2, __fsub_rn(0.008333333f, __fmul_rn(t2, 0.000198413f)))))));
+  return make_float2(c, s);
+}
+
+__global__ void rope_table_kernel(float2* __restrict__ cs, int max_seq, int hd, float base) {
+  const int half = hd >> 1;
+  const long long total = (long long)max_seq * half;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int pos = (int)(idx / half);
+    const int j = (int)(idx % half);
+    cs[idx] = rope_cs(pos, 2 * j, hd, base);
+  }
+}
+
+// llm.c:488-492 applied to n_vec consecutive heads of hd elements
+__global__ void rope_kernel(float* __restrict__ vec, int n_vec, const int* __restrict__ pos_dev,
+                            int pos_arg, int hd, float base) {
+  const int half = hd >> 1;
+  const int pos = pos_dev ? *pos_dev : pos_arg;
+  const int total = n_vec * half;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int h = idx / half, j = idx % half;
+    const float2 cs = rope_cs(pos, 2 * j, hd, base);
+    float* v = vec + (size_t)h * hd + 2 * j;
+    const float v0 = v[0], v1 = v[1];
+    v[0] = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+    v[1] = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+  }
+}
+
+// llm.c:506-532 (single CTA): max (first pass, strict >), e = exp(x-max) in
+// parallel, serial sum by thread 0, inv = 1/(sum+1e-10), x *= inv.
+__global__ void softmax_kernel(float* __restrict__ x, int n) {
+  __shared__ float s_max, s_inv;
+  if (threadIdx.x == 0) {
+    float m = x[0];
+    for (int i = 1; i < n; ++i)
+      if (x[i] > m) m = x[i];
+    s_max = m;
+  }
+  __syncthreads();
+  const float m = s_max;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = ref_expf(__fsub_rn(x[i], m));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) sum = __fadd_rn(sum, x[i]);
+    s_inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(x[i], inv);
+}
+
+enum { EW_SILU = 0, EW_VADD = 1, EW_VMUL = 2, EW_AXPY = 3 };
+
+__global__ void elementwise_kernel(int op, float* __restrict__ dst, const float* __restrict__ src,
+                                   float s, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    switch (op) {
+      case EW_SILU: dst[i] = ref_silu(dst[i]); break;                            // llm.c:538-544
+      case EW_VADD: dst[i] = __fadd_rn(dst[i], src[i]); break;                   // llm.c:599-614
+      case EW_VMUL: dst[i] = __fmul_rn(dst[i], src[i]); break;                   // llm.c:617-632
+      case EW_AXPY: dst[i] = __fadd_rn(dst[i], __fmul_rn(s, src[i])); break;     // llm.c:580-596
+    }
+  }
+}
+
+// llm.c:551-577: chain c (0..7) over elements 8m+c; t_l = c_l + c_{l+4};
+// ((t0+t1)+t2)+t3; scalar tail.  One warp.
+__global__ void dot_kernel(const float* __restrict__ a, const float* __restrict__ b, int n,
+                           float* __restrict__ out) {
+  const int lane = threadIdx.x;
+  const int n8 = n & ~7;
+  float acc = 0.0f;
+  if (lane < 8)
+    for (int i = 0; i < n8; i += 8) acc = __fadd_rn(acc, __fmul_rn(a[i + lane], b[i + lane]));
+  const float hi = __shfl_down_sync(0xffffffffu, acc, 4);
+  const float t = __fadd_rn(acc, hi);  // lanes 0..3: t_l
+  const float t1 = __shfl_sync(0xffffffffu, t, 1);
+  const float t2 = __shfl_sync(0xffffffffu, t, 2);
+  const float t3 = __shfl_sync(0xffffffffu, t, 3);
+  if (lane == 0) {
+    float sum = __fadd_rn(__fadd_rn(__fadd_rn(t, t1), t2), t3);
+    for (int i = n8; i < n; ++i) sum = __fadd_rn(sum, __fmul_rn(a[i], b[i]));
+    *out = sum;
+  }
+}
+
+// llm.c:365-410: dequantise the embedding row of one token
+__global__ void embed_kernel(float* __restrict__ out, const uint8_t* __restrict__ embd, int type,
+                             int dim, const int* __restrict__ tok_dev, int tok_arg) {
+  pdl_wait();
+  const int tok = tok_dev ? *tok_dev : tok_arg;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+    float v = 0.0f;
+    if (type == TOSK_Q4_0) {
+      const uint8_t* blk = embd + ((size_t)tok * (dim / 32) + i / 32) * 18;
+      const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+      const int j = i & 31;
+      const uint8_t byte = blk[2 + (j >> 1)];
+      const int nib = (j & 1) ? (byte >> 4) : (byte & 0x0F);
+      v = __fmul_rn((float)(nib - 8), d);
+    } else if (type == TOSK_Q8_0) {
+      const uint8_t* blk = embd + ((size_t)tok * (dim / 32) + i / 32) * 34;
+      const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+      v = __fmul_rn((float)(int8_t)blk[2 + (i & 31)], d);
+    } else if (type == TOSK_F16) {
+      v = h2f(reinterpret_cast<const uint16_t*>(embd)[(size_t)tok * dim + i]);
+    } else if (type == TOSK_F32) {
+      v = reinterpret_cast<const float*>(embd)[(size_t)tok * dim + i];
+    }
+    out[i] = v;
+  }
+  pdl_trigger();
+}
+
+// llm.c:1129-1140.  The serial scan returns the first strict maximum and
+// never lets a NaN win except x[0]; the parallel form reduces candidates by
+// (larger value, then lower index), skipping NaNs, and returns 0 when x[0]
+// is NaN.  One CTA of 1024 threads.
+__device__ __forceinline__ void arg_combine(float& v, int& i, float v2, int i2) {
+  if (i2 < 0) return;
+  if (i < 0 || v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n,
+                                                      int* __restrict__ out_idx,
+                                                      float* __restrict__ out_val) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait();
+  float v = 0.0f;
+  int idx = -1;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float xi = x[i];
+    if (!(xi != xi) && (idx < 0 || xi > v)) {
+      v = xi;
+      idx = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_down_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_down_sync(0xffffffffu, idx, o);
+    arg_combine(v, idx, v2, i2);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = idx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    v = lane < nw ? sv[lane] : 0.0f;
+    idx = lane < nw ? si[lane] : -1;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_down_sync(0xffffffffu, v, o);
+      const int i2 = __shfl_down_sync(0xffffffffu, idx, o);
+      arg_combine(v, idx, v2, i2);
+    }
+    if (lane == 0) {
+      const float x0 = x[0];
+      if (x0 != x0 || idx < 0) {
+        idx = 0;
+        v = x0;
+      }
+      *out_idx = idx;
+      if (out_val) *out_val = v;
+    }
+  }
+  pdl_trigger();
+}
+
+}  // namespace tos
+
+using namespace tos;
+
+static int launch_pdl(const void* func, dim3 grid, dim3 block, void** args, int pdl, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return (int)cudaLaunchKernelExC(&cfg, func, args);
+}
+
+extern "C" int tosk_rmsnorm(float* out, const float* x, const void* w, int wtype, int dim, float eps,
+                            int pdl, cudaStream_t st) {
+  if (dim <= 0) return 0;
+  void* args[] = {&out, &x, &w, &wtype, &dim, &eps};
+  return launch_pdl((const void*)rmsnorm_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_rope_table(float2* cs, int max_seq, int hd, float base, cudaStream_t st) {
+  const long long total = (long long)max_seq * (hd / 2);
+  int grid = (int)((total + 255) / 256);
+  if (grid > 4096) grid = 4096;
+  if (grid < 1) grid = 1;
+  rope_table_kernel<<<grid, 256, 0, st>>>(cs, max_seq, hd, base);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int tosk_rope(float* vec, int n_vec, const int* pos_dev, int pos, int hd, float base,
+                         cudaStream_t st) {
+  const int total = n_vec * (hd / 2);
+  if (total <= 0) return 0;
+  rope_kernel<<<(total + 255) / 256, 256, 0, st>>>(vec, n_vec, pos_dev, pos, hd, base);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int tosk_softmax(float* x, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  softmax_kernel<<<1, 1024, 0, st>>>(x, n);
+  return (int)cudaGetLastError();
+}
+
+static int ew(int op, float* dst, const float* src, float s, int n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  int grid = (n + 255) / 256;
+  if (grid > 1184) grid = 1184;
+  elementwise_kernel<<<grid, 256, 0, st>>>(op, dst, src, s, n);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int tosk_silu(float* x, int n, cudaStream_t st) { return ew(EW_SILU, x, nullptr, 0.0f, n, st); }
+extern "C" int tosk_vadd(float* d, const float* s, int n, cudaStream_t st) { return ew(EW_VADD, d, s, 0.0f, n, st); }
+extern "C" int tosk_vmul(float* d, const float* s, int n, cudaStream_t st) { return ew(EW_VMUL, d, s, 0.0f, n, st); }
+extern "C" int tosk_axpy(float* d, float sc, const float* s, int n, cudaStream_t st) {
+  return ew(EW_AXPY, d, s, sc, n, st);
+}
+
+extern "C" int tosk_dot(const float* a, const float* b, int n, float* out, cudaStream_t st) {
+  dot_kernel<<<1, 32, 0, st>>>(a, b, n, out);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int tosk_embed(float* out, const void* embd, int type, int dim, const int* tok_dev, int tok,
+                          int pdl, cudaStream_t st) {
+  if (dim <= 0) return 0;
+  int grid = (dim + 255) / 256;
+  void* args[] = {&out, &embd, &type, &dim, &tok_dev, &tok};
+  return launch_pdl((const void*)embed_kernel, dim3(grid), dim3(256), args, pdl, st);
+}
+
+extern "C" int tosk_argmax(const float* x, int n, int* out_idx, float* out_val, int pdl, cudaStream_t st) {
+  if (n <= 0) return (int)cudaErrorInvalidValue;
+  void* args[] = {&x, &n, &out_idx, &out_val};
+  return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
