@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200 TensorOS decode path.
+
+Workload: Llama-2-7B-shaped decoder (32 layers, d_model 4096, 32 heads, SwiGLU
+11008, vocab 32000), random-init Q4_0 weights (GGUF layout, seeded), fp16 KV
+cache of capacity 4096; a 128-token prompt is prefilled, then greedy decode at
+batch 1.  A step is one decoded token.
+
+  value      tokens/s with the model resident in HBM: K greedy steps chained on
+             the device (tos_model_decode), timed with CUDA events on the
+             model's stream.  Weights (3.7 GB per step) exceed L2 (126 MB), so
+             no flush is needed.
+  e2e        the same metric through tos_model_forward_argmax: every step
+             copies token+position host->device (8 B, pinned) and the next
+             token device->host (8 B).
+  roofline   the dominant kernel, the Q4_0 GEMV, timed in isolation on the
+             4096x4096 shape (one launch streams 9,469,952 algorithmic bytes),
+             rotating 32 weight copies (303 MB) so every launch is L2-cold.
+  cpu_baseline  the reference's own C implementation (runtime/nn/llm.c,
+             compiled hosted) on one host core, rank 0 at N=1.
+
+--impl reference times that reference CPU implementation alone.
+With --gpus N > 1 every rank runs an independent replica (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+GEMV_BYTES_4096 = 4096 * 128 * 18 + 4096 * 4 + 4096 * 4   # 9,469,952 B per launch
+METRIC = "decode tokens/sec (Llama-2-7B-shaped, Q4_0, batch 1)"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def ref_cpu_decode(synth, n_tokens: int, start_pos: int, warmup: int):
+    """Times the reference's llm_forward_token on this host (1 core)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle
+    if pyoracle.reference_available():
+        ops, kind = pyoracle.reference(), "reference"
+        model = ops.model(synth)
+    else:
+        ops, kind = pyoracle.oracle(), "port"
+        model = ops.model(synth, kv_type=0)
+    try:
+        os.sched_setaffinity(0, {sorted(os.sched_getaffinity(0))[0]})
+    except Exception:
+        pass
+    tok = 1
+    pos = start_pos
+    for _ in range(warmup):
+        model.forward(tok, pos)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        lg = model.forward(tok, pos)
+        tok = int(lg.argmax())
+        pos += 1
+    dt = time.perf_counter() - t0
+    model.close()
+    return n_tokens / dt, kind, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from tensoros_b200 import workloads as W
+    cfg = dict(W.LLAMA2_7B, kv_type=W.TYPE_F32)
+    synth = W.make_model(cfg, W.SEED)
+    n = max(1, min(args.steps, args.ref_tokens))
+    w = min(args.warmup, 1)
+    value, kind, dt = ref_cpu_decode(synth, n, args.prefill, w)
+    sample = (f"{n} decode tokens (after {w} warm-up) at positions {args.prefill + w}.. of the 7B Q4_0 model, "
+              f"fp32 KV cache (the reference's only cache type), prefix positions left zero instead of a "
+              f"{args.prefill}-token CPU prefill; reference runtime/nn/llm.c built hosted, 1 core")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, random-init weights)",
+        "config": {"workload": "llama2-7b-shape-q4_0 decode, batch 1", "global_batch": 1,
+                   "seq_len": args.prefill, "parallelism": "none (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def gemv_roofline(lib, torch, n_copies=32, reps=4):
+    """Isolated Q4_0 GEMV 4096x4096, L2-cold by rotating weight copies."""
+    import ctypes
+    from tensoros_b200 import workloads as W
+    hs = []
+    try:
+        for c in range(n_copies):
+            w = W.q4_0(4096, 4096, W.SEED, 9000 + c)
+            h = ctypes.c_void_p()
+            assert lib.tos_weight_create(ctypes.byref(h), w.ctypes.data, 4096, 4096, W.TYPE_Q4_0) == 0
+            hs.append(h)
+        x = torch.from_numpy(W.normal_f32(4096, W.SEED, 9999)).cuda()
+        y = torch.empty(4096, device="cuda")
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            sp = s.cuda_stream
+            for h in hs[:4]:
+                lib.tos_gemv_dev(h, x.data_ptr(), y.data_ptr(), sp)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(reps):
+                    for h in hs:
+                        lib.tos_gemv_dev(h, x.data_ptr(), y.data_ptr(), sp)
+            g.replay()
+            s.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * n_copies)
+        return ms
+    finally:
+        for h in hs:
+            lib.tos_weight_destroy(h)
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from tensoros_b200 import lib as _lib
+    from tensoros_b200 import ops
+    from tensoros_b200 import workloads as W
+    lib = _lib()
+    assert lib.tos_init(local) == 0, "tos_init failed"
+    cfg = dict(W.LLAMA2_7B)
+    t_gen = time.perf_counter()
+    synth = W.make_model(cfg, W.SEED)
+    model = ops.Model(synth, attn_mode=args.attn)
+    t_gen = time.perf_counter() - t_gen
+    prompt = W.tokens(args.prefill, cfg["vocab_size"], W.SEED)
+    nxt = 0
+    for i, t in enumerate(prompt):
+        nxt = model.forward_argmax(int(t), i)
+    pos = args.prefill
+    warm = max(3, args.warmup)
+    toks = model.decode(nxt, pos, warm)
+    nxt, pos = int(toks[-1]), pos + warm
+    stream = torch.cuda.ExternalStream(model.stream())
+    K = args.steps
+    if pos + 2 * K + 2 > cfg["max_seq"]:
+        raise SystemExit("steps too large for the 4096-position cache")
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: device-chained decode
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.cudart().cudaProfilerStart()
+        e0.record(stream)
+        toks = model.decode(nxt, pos, K)
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    nxt, pos = int(toks[-1]), pos + K
+    # ---- e2e: per step host round trip through tos_model_forward_argmax
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(K):
+        nxt = model.forward_argmax(nxt, pos)
+        pos += 1
+    e3.record(stream)
+    e3.synchronize()
+    barrier()
+    t_e2e = e2.elapsed_time(e3)
+    if world > 1:
+        tt = torch.tensor([t_ms, t_e2e], device="cuda")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_ms, t_e2e = float(tt[0]), float(tt[1])
+    value = world * K / (t_ms / 1000.0)
+    e2e = world * K / (t_e2e / 1000.0)
+
+    res = {}
+    if rank == 0:
+        gemv_ms = gemv_roofline(lib, torch)
+        peak, peak_kind = peaks()
+        achieved = GEMV_BYTES_4096 / (gemv_ms / 1000.0) / 1e9
+        L = cfg["n_layers"]
+        per_layer = 1 + (2 if args.attn == 0 else 3) + 3
+        launches = K * (1 + L * per_layer + 3)
+        weight_bytes = (L * (4096 * 128 * 18 * 4 + 3 * 11008 * 128 * 18) + 32000 * 128 * 18)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, kind, dt = ref_cpu_decode(synth, args.ref_tokens, args.prefill, 1)
+            cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
+                   "sample": f"{args.ref_tokens} decode tokens of the same 7B Q4_0 model (fp32 KV, the "
+                             f"reference's cache type) at positions {args.prefill + 1}.., one host core, {dt:.1f} s"}
+        res = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": warm, "ms_per_step": t_ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init Q4_0 weights; BASELINE distributions)",
+            "config": {"workload": "llama2-7b-shape-q4_0 greedy decode, batch 1, after a 128-token prefill",
+                       "model": cfg["name"], "global_batch": world, "seq_len": args.prefill,
+                       "kv_cache": "fp16, capacity 4096", "attention": "exact" if args.attn == 0 else "fast",
+                       "positions": [args.prefill + warm, args.prefill + warm + K - 1],
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_0> 4096x4096 (isolated, L2-cold)",
+                         "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
+            "decode_weight_gbs": weight_bytes * value / world / 1e9,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "setup_s": round(t_gen, 1),
+        }
+        print(json.dumps(res), flush=True)
+    model.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prefill", type=int, default=128)
+    ap.add_argument("--attn", type=int, default=0, help="0 exact, 1 fast")
+    ap.add_argument("--ref-tokens", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -175,6 +175,13 @@ int tos_model_forward_argmax(tos_model_t *m, int token, int pos, int *next);
  * prefill the prompt token by token, then n_gen greedy tokens into out.
  * Returns the number generated or a negative status. */
 int tos_model_generate_greedy(tos_model_t *m, const int *prompt, int n_prompt, int n_gen, int *out);
+/* Greedy decode of n_steps tokens kept on the device: step i consumes the
+ * previous token (token for i = 0) at position pos+i and its argmax becomes
+ * out_tokens[i] (host, copied once at the end).  Same tokens as n_steps
+ * calls of tos_model_forward_argmax, without a host round trip per step. */
+int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_tokens);
+/* the model's CUDA stream (cudaStream_t as void*) */
+void *tos_model_stream(const tos_model_t *m);
 /* device pointer of the last logits (vocab_size floats) */
 const float *tos_model_logits_dev(const tos_model_t *m);
 size_t tos_model_device_bytes(const tos_model_t *m);

@@ -148,6 +148,7 @@ class Oracle(_Ops):
         L.orc_embed.restype, L.orc_embed.argtypes = None, [vp, vp, i32, i32, i32]
         L.orc_rmsnorm.restype, L.orc_rmsnorm.argtypes = None, [vp, vp, vp, i32, i32, f32]
         L.orc_rope_cs.restype, L.orc_rope_cs.argtypes = None, [i32, i32, i32, f32, C.POINTER(f32), C.POINTER(f32)]
+        L.orc_rope_rows.restype, L.orc_rope_rows.argtypes = None, [vp, i32, i32, i32, vp, f32]
         L.orc_attention.restype, L.orc_attention.argtypes = None, [vp, vp, vp, vp, i32, i32, i32, i32, i32]
         L.orc_q4f_dot_block.restype, L.orc_q4f_dot_block.argtypes = f32, [vp, vp]
         L.orc_q4f_gemv.restype, L.orc_q4f_gemv.argtypes = None, [vp, vp, vp, i32, i32]
@@ -176,6 +177,12 @@ class Oracle(_Ops):
         c, s = f32(), f32()
         self.lib.orc_rope_cs(pos, i, hd, base, C.byref(c), C.byref(s))
         return np.float32(c.value), np.float32(s.value)
+
+    def rope_rows(self, rows, hd, positions, base):
+        r = _f32(rows).copy()
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        self.lib.orc_rope_rows(_p(r), r.shape[0], r.shape[1], hd, _p(pos), base)
+        return r
 
     def attention(self, q, kc, vc, kv_type, n_heads, n_kv, hd, pos):
         out = np.empty(n_heads * hd, dtype=np.float32)

@@ -15,6 +15,7 @@
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 static float bits_f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 static uint32_t f_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -301,6 +302,14 @@ void orc_rope(float *vec, int pos, int head_dim, float base)
     }
 }
 
+/* llm_rope applied to every head of n_rows rows of length row_len (heads of
+ * hd elements), row r at position pos[r] (llm.c:668-671 per position). */
+void orc_rope_rows(float *rows, int n_rows, int row_len, int hd, const int *pos, float base)
+{
+    for (int r = 0; r < n_rows; r++)
+        for (int h = 0; h + hd <= row_len; h += hd) orc_rope(rows + (size_t)r * row_len + h, pos[r], hd, base);
+}
+
 /* llm.c:506-532 */
 void orc_softmax(float *x, int n)
 {
@@ -485,7 +494,10 @@ void orc_forward_token(void *p, float *logits, int token, int pos)
     orc_model_t *m = (orc_model_t *)p;
     const orc_model_desc_t *d = &m->d;
     int dim = d->dim, hd = m->hd, kvd = m->kv_dim, ff = d->ff_dim;
-    int nt = 1;
+    /* rows of a GEMV are independent, so splitting them over threads gives
+     * the same bits as the single-threaded reference loop */
+    long ncpu = sysconf(_SC_NPROCESSORS_ONLN);
+    int nt = ncpu > 16 ? 16 : (ncpu < 1 ? 1 : (int)ncpu);
     orc_embed(m->x, d->token_embd, d->embd_type, dim, token);
     for (int L = 0; L < d->n_layers; L++) {
         orc_rmsnorm(m->xn, m->x, d->attn_norm[L], ORC_TYPE_F32, dim, d->norm_eps);

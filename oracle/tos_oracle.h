@@ -42,6 +42,7 @@ void orc_embed(float *out, const void *embd, int type, int dim, int token);
 void orc_rmsnorm(float *out, const float *x, const void *w, int wtype, int dim, float eps);
 void orc_rope_cs(int pos, int i, int head_dim, float base, float *cos_out, float *sin_out);
 void orc_rope(float *vec, int pos, int head_dim, float base);
+void orc_rope_rows(float *rows, int n_rows, int row_len, int hd, const int *pos, float base);
 void orc_softmax(float *x, int n);
 void orc_silu(float *x, int n);
 float orc_dot_f32(const float *a, const float *b, int n);

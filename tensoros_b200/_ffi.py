@@ -86,6 +86,8 @@ NN_FUNCS = {
     "tos_model_forward_token": (i32, [vp, vp, i32, i32]),
     "tos_model_forward_argmax": (i32, [vp, i32, i32, ip]),
     "tos_model_generate_greedy": (i32, [vp, vp, i32, i32, vp]),
+    "tos_model_decode": (i32, [vp, i32, i32, i32, vp]),
+    "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),
 }

@@ -32,4 +32,9 @@ void *tos_scratch(size_t bytes);
 int tos_check_device_error(void);
 cudaStream_t tos_pick_stream(void *s);
 
+/* RoPE arguments the reference's range reduction (llm.c:468-482) can finish
+ * on: a finite base and positions below 2^20. */
+#define TOS_MAX_POS (1 << 20)
+int tos_rope_args_ok(int pos, float base);
+
 #endif

@@ -36,11 +36,12 @@ struct tos_model {
     float2 *rope;             /* [max_seq][hd/2] */
     void *ws;
     size_t ws_bytes;
-    int *io;                  /* device: token, pos, next, err */
+    int *io;                  /* device: token, pos, next, err, ring count */
     int *io_host;             /* pinned mirror */
+    int *ring;                /* device: tokens produced by tos_model_decode */
     cudaStream_t st;
-    cudaGraphExec_t gexec;
-    int have_graph;
+    cudaGraphExec_t gexec, gexec_chain;
+    int have_graph, have_chain;
     size_t dev_bytes;
 };
 
@@ -95,6 +96,7 @@ void tos_model_destroy(tos_model_t *m)
     if (!m) return;
     if (m->st) cudaStreamSynchronize(m->st);
     if (m->have_graph) cudaGraphExecDestroy(m->gexec);
+    if (m->have_chain) cudaGraphExecDestroy(m->gexec_chain);
     for (int L = 0; m->wqkv && L < m->d.n_layers; L++) {
         tosk_qmat_free(&m->wqkv[L]);
         tosk_qmat_free(&m->wo[L]);
@@ -104,7 +106,7 @@ void tos_model_destroy(tos_model_t *m)
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
-                    m->rope, m->ws, m->io};
+                    m->rope, m->ws, m->io, m->ring};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
     if (m->io_host) cudaFreeHost(m->io_host);
@@ -118,6 +120,7 @@ static int validate(const tos_model_desc_t *d)
         d->ff_dim <= 0 || d->vocab_size <= 0 || d->max_seq <= 0)
         return TOS_EINVAL;
     if (d->dim % d->n_heads || d->n_heads % d->n_kv_heads) return TOS_EINVAL;
+    if (d->max_seq > TOS_MAX_POS || !tos_rope_args_ok(0, d->rope_base)) return TOS_EINVAL;
     int hd = d->dim / d->n_heads;
     if (hd & 1) return TOS_EINVAL;
     if (d->dim % 32 || d->ff_dim % 32) return TOS_ENOTSUP;
@@ -209,9 +212,10 @@ int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
     if (!e) e = tosk_rope_table(m->rope, d->max_seq, m->hd, d->rope_base, m->st);
     m->ws_bytes = tosk_attention_ws_bytes(d->n_heads, d->max_seq);
     if (!e) e = dmalloc(m, &m->ws, m->ws_bytes);
-    if (!e) e = dmalloc(m, (void **)&m->io, 4 * sizeof(int));
-    if (!e) e = cudaMemset(m->io, 0, 4 * sizeof(int));
-    if (!e) e = cudaMallocHost((void **)&m->io_host, 4 * sizeof(int));
+    if (!e) e = dmalloc(m, (void **)&m->io, 8 * sizeof(int));
+    if (!e) e = cudaMemset(m->io, 0, 8 * sizeof(int));
+    if (!e) e = dmalloc(m, (void **)&m->ring, (size_t)d->max_seq * sizeof(int));
+    if (!e) e = cudaMallocHost((void **)&m->io_host, 8 * sizeof(int));
     if (!e) e = cudaStreamSynchronize(m->st);
     if (e) {
         tos_model_destroy(m);
@@ -234,9 +238,10 @@ int tos_model_reset(tos_model_t *m)
     return tos_set_status(tos_from_cuda(e));
 }
 
-/* Enqueue one token step; reads token from io[0] and position from io[1],
- * leaves the greedy next token in io[2]. */
-static int enqueue_token(tos_model_t *m)
+/* Enqueue one token step; reads the token from io[0] (io[2] when chained:
+ * the previous step's argmax) and the position from io[1], leaves the greedy
+ * next token in io[2].  A chained step then records it and advances io[1]. */
+static int enqueue_token(tos_model_t *m, int chained)
 {
     const tos_model_desc_t *d = &m->d;
     cudaStream_t st = m->st;
@@ -244,7 +249,7 @@ static int enqueue_token(tos_model_t *m)
     const int pdl = 1;
     const int dim = d->dim;
     size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
-    int e = tosk_embed(m->x, m->embd, d->embd_type, dim, m->io, 0, pdl, st);
+    int e = tosk_embed(m->x, m->embd, d->embd_type, dim, chained ? m->io + 2 : m->io, 0, pdl, st);
     for (int l = 0; !e && l < d->n_layers; l++) {
         tosk_norm_t n1 = {m->norms + (size_t)(2 * l) * dim, d->norm_eps};
         tosk_epi_t qkv;
@@ -277,7 +282,23 @@ static int enqueue_token(tos_model_t *m)
     tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps};
     if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, err, pdl, st);
     if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
+    if (!e && chained) e = tosk_decode_advance(m->io, m->ring, pdl, st);
     return e;
+}
+
+/* Captures the (plain or chained) token step into a graph. */
+static int capture(tos_model_t *m, int chained, cudaGraphExec_t *out)
+{
+    cudaGraph_t g = NULL;
+    int ok = 0;
+    if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        int ce = enqueue_token(m, chained);
+        int ee = cudaStreamEndCapture(m->st, &g);
+        if (!ce && !ee && g && cudaGraphInstantiate(out, g, 0) == cudaSuccess) ok = 1;
+        if (g) cudaGraphDestroy(g);
+    }
+    cudaGetLastError();
+    return ok;
 }
 
 static int run_token(tos_model_t *m, int token, int pos)
@@ -289,17 +310,10 @@ static int run_token(tos_model_t *m, int token, int pos)
     if (e) return tos_from_cuda(e);
     if (!m->have_graph) {
         /* first step runs eagerly (sets kernel attributes), then capture */
-        e = enqueue_token(m);
+        e = enqueue_token(m, 0);
         if (!e) e = cudaStreamSynchronize(m->st);
         if (e) return tos_from_cuda(e);
-        cudaGraph_t g = NULL;
-        if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
-            int ce = enqueue_token(m);
-            int ee = cudaStreamEndCapture(m->st, &g);
-            if (!ce && !ee && g && cudaGraphInstantiate(&m->gexec, g, 0) == cudaSuccess) m->have_graph = 1;
-            if (g) cudaGraphDestroy(g);
-        }
-        cudaGetLastError();
+        m->have_graph = capture(m, 0, &m->gexec);
     } else {
         e = cudaGraphLaunch(m->gexec, m->st);
         if (e) return tos_from_cuda(e);
@@ -354,4 +368,40 @@ int tos_model_generate_greedy(tos_model_t *m, const int *prompt, int n_prompt, i
     if (rc) return tos_set_status(rc);
     tos_set_status(TOS_OK);
     return g;
+}
+
+void *tos_model_stream(const tos_model_t *m) { return m ? (void *)m->st : NULL; }
+
+int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_tokens)
+{
+    if (!m || n_steps < 0 || (n_steps && !out_tokens)) return tos_set_status(TOS_EINVAL);
+    if (token < 0 || token >= m->d.vocab_size || pos < 0 || pos + n_steps > m->d.max_seq)
+        return tos_set_status(TOS_EINVAL);
+    if (n_steps == 0) return tos_set_status(TOS_OK);
+    m->io_host[0] = token;
+    m->io_host[1] = pos;
+    m->io_host[2] = token;
+    m->io_host[3] = 0;
+    m->io_host[4] = 0;
+    int e = cudaMemcpyAsync(m->io, m->io_host, 5 * sizeof(int), cudaMemcpyHostToDevice, m->st);
+    int step = 0;
+    if (!e && !m->have_chain) {
+        /* one eager chained step (configures kernels), then capture */
+        e = enqueue_token(m, 1);
+        if (!e) e = cudaStreamSynchronize(m->st);
+        step = 1;
+        if (!e) m->have_chain = capture(m, 1, &m->gexec_chain);
+    }
+    for (; !e && step < n_steps; step++)
+        e = m->have_chain ? cudaGraphLaunch(m->gexec_chain, m->st) : enqueue_token(m, 1);
+    if (!e) e = cudaMemcpyAsync(out_tokens, m->ring, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, m->st);
+    if (!e) e = cudaMemcpyAsync(m->io_host + 3, m->io + 3, sizeof(int), cudaMemcpyDeviceToHost, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);
+    if (e) return tos_set_status(tos_from_cuda(e));
+    if (m->io_host[3] != 0) {
+        cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
+        cudaStreamSynchronize(m->st);
+        return tos_set_status(TOS_ETIMEOUT);
+    }
+    return tos_set_status(TOS_OK);
 }

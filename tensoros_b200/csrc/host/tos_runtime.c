@@ -115,6 +115,11 @@ void *tos_stream(void) { return tos_ensure_init() == TOS_OK ? (void *)tos_g.stre
 
 cudaStream_t tos_pick_stream(void *s) { return s ? (cudaStream_t)s : tos_g.stream; }
 
+int tos_rope_args_ok(int pos, float base)
+{
+    return pos >= 0 && pos < TOS_MAX_POS && base == base && base < 3.4e38f && base > -3.4e38f;
+}
+
 int tos_synchronize(void)
 {
     if (tos_ensure_init() != TOS_OK) return tos_set_status(TOS_ENODEV);
@@ -283,7 +288,7 @@ int tos_rmsnorm_dev(float *out, const float *x, const void *w, int wtype, int di
 int tos_rope_dev(float *vec, int n_vec, int pos, int head_dim, float base, void *stream)
 {
     DEV_PROLOGUE();
-    if (n_vec < 0 || head_dim <= 0 || (head_dim & 1) || pos < 0) return tos_set_status(TOS_EINVAL);
+    if (n_vec < 0 || head_dim <= 0 || (head_dim & 1) || !tos_rope_args_ok(pos, base)) return tos_set_status(TOS_EINVAL);
     return tos_set_status(tos_from_cuda(tosk_rope(vec, n_vec, NULL, pos, head_dim, base, tos_pick_stream(stream))));
 }
 
@@ -523,7 +528,7 @@ void tos_axpy_f32(float *dst, float s, const float *src, int n) { inplace1(dst, 
 void tos_rope(float *vec, int pos, int head_dim, float base)
 {
     if (head_dim <= 0) { tos_set_status(TOS_OK); return; }
-    if (!vec || (head_dim & 1) || pos < 0) { tos_set_status(TOS_EINVAL); return; }
+    if (!vec || (head_dim & 1) || !tos_rope_args_ok(pos, base)) { tos_set_status(TOS_EINVAL); return; }
     if (tos_ensure_init()) { tos_set_status(TOS_ENODEV); return; }
     if (!tos_scratch((size_t)head_dim * 4)) { tos_set_status(TOS_ENOMEM); return; }
     int e = h2d(0, vec, (size_t)head_dim * 4);

@@ -103,6 +103,8 @@ int tosk_dot(const float *a, const float *b, int n, float *out, cudaStream_t st)
 int tosk_embed(float *out, const void *embd, int type, int dim, const int *tok_dev, int tok,
                int pdl, cudaStream_t st);
 int tosk_argmax(const float *x, int n, int *out_idx, float *out_val, int pdl, cudaStream_t st);
+/* io[2] -> ring[io[4]]; io[4] += 1; io[1] += 1 (device-side greedy chaining) */
+int tosk_decode_advance(int *io, int *ring, int pdl, cudaStream_t st);
 
 /* ---- decode attention ---- */
 enum { TOSK_ATTN_EXACT = 0, TOSK_ATTN_FAST = 1 };

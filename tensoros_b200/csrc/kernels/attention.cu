@@ -326,11 +326,23 @@ extern "C" size_t tosk_attention_ws_bytes(int n_heads, int max_ctx) {
          align256((size_t)n_heads * maxc * 256 * 4);
 }
 
+// Raises a kernel's dynamic shared-memory limit to the sm_100 maximum once
+// (not inside stream capture: the first call of every launcher is eager).
+static int allow_max_smem(const void* kern) {
+  static const void* done[16];
+  static int n_done = 0;
+  for (int i = 0; i < n_done; ++i)
+    if (done[i] == kern) return 0;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return (int)e;
+  if (n_done < 16) done[n_done++] = kern;
+  return 0;
+}
+
 template <typename K>
 static int launch_k(K kern, int grid, int threads, size_t smem, int pdl, cudaStream_t st, void** args) {
-  cudaError_t e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem > 48 * 1024 ? (int)smem : 48 * 1024);
-  if (e != cudaSuccess) return (int)e;
+  int e0 = allow_max_smem((const void*)kern);
+  if (e0) return e0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);

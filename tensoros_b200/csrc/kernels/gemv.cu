@@ -120,6 +120,7 @@ struct GemvArgs {
   int S;         // ring depth
   int pstride;   // partials row stride (floats)
   int nwb, rg;   // compute warps per row of blocks, row groups
+  int tr;        // rows per stage (<= kTR)
   uint32_t off_x, off_p, off_st, stage_bytes, stage_sc_off;
   tosk_epi_t epi;
 };
@@ -161,11 +162,16 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   const int u1 = (int)(((long long)(blockIdx.x + 1) * NU) / gridDim.x);
   const int rb = u0 * a.unit;
   const int re = min(u1 * a.unit, a.R);
-  const int nst = re > rb ? (re - rb + kTR - 1) / kTR : 0;
+  const int tr = a.tr;
+  const int nst = re > rb ? (re - rb + tr - 1) / tr : 0;
   const int ncw = a.nwb * a.rg;
   const int nb = a.nb, nbp = a.nbp;
 
+  __shared__ int s_failed;
   if (threadIdx.x == 0) {
+    // An earlier kernel whose bounded wait ran out leaves *err set: skip the
+    // work so one failure cannot turn into a chain of timeouts.
+    s_failed = a.err ? *reinterpret_cast<volatile int*>(a.err) : 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], ncw);
@@ -178,6 +184,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   }
   __syncthreads();
   pdl_trigger();
+  if (s_failed) return;
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -186,8 +193,8 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
       for (int it = 0; it < nst; ++it) {
         const int s = it % S;
         if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.err, 1)) break;
-        const int r0 = rb + it * kTR;
-        const int n = min(kTR, re - r0);
+        const int r0 = rb + it * tr;
+        const int n = min(tr, re - r0);
         const uint32_t bq = (uint32_t)(n * nb * QB);
         const uint32_t bs = (uint32_t)(n * nbp * 2);
         uint8_t* st = stages + (size_t)s * a.stage_bytes;
@@ -257,7 +264,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
       if (!mbar_wait(&full[s], (it / S) & 1, a.err, 2)) break;
       const int c = it % kNCH;
       if (it >= kNCH && !mbar_wait(&pempty[c], ((it / kNCH) & 1) ^ 1, a.err, 3)) break;
-      const int n = min(kTR, re - (rb + it * kTR));
+      const int n = min(tr, re - (rb + it * tr));
       const uint8_t* stq = stages + (size_t)s * a.stage_bytes;
       const uint16_t* sts = reinterpret_cast<const uint16_t*>(stq + a.stage_sc_off);
       float* Pc = P + c * kTR * a.pstride;
@@ -280,8 +287,8 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   if constexpr (kEpi == TOSK_EPI_QKV) pos = *a.epi.pos;
   for (int it = cw; it < nst; it += kNCH) {
     if (!mbar_wait(&pfull[cw], (it / kNCH) & 1, a.err, 4)) break;
-    const int r0 = rb + it * kTR;
-    const int n = min(kTR, re - r0);
+    const int r0 = rb + it * tr;
+    const int n = min(tr, re - r0);
     const float* Pr = P + (cw * kTR + min(lane, kTR - 1)) * a.pstride;
     float y = 0.0f;  // llm.c:223: sum = 0.0f, then += block value, in block order
     if (lane < n) {
@@ -528,16 +535,23 @@ extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t
   if (a.rg > kTR) a.rg = kTR;
   const int threads = 32 * (1 + kNCH + a.nwb * a.rg);
   a.pstride = (int)round_up((uint32_t)w->nb, 8) + 4;
-  const uint32_t qbytes = (uint32_t)(kTR * w->nb * w->qb);
-  a.stage_sc_off = round_up(qbytes, 16);
-  a.stage_bytes = round_up(a.stage_sc_off + (uint32_t)(kTR * w->nbp * 2), 128);
-  const uint32_t hdr = 128;
+  const uint32_t hdr = 256;   // up to 2*8 + 2*kNCH mbarriers and 8 floats
   a.off_x = hdr;
   const uint32_t xbytes = fuse_norm ? round_up((uint32_t)w->cols * 4, 128) : 0;
   a.off_p = a.off_x + xbytes;
   const uint32_t pbytes = round_up((uint32_t)(kNCH * kTR * a.pstride * 4), 128);
   a.off_st = a.off_p + pbytes;
   const uint32_t budget_lo = 100 * 1024, budget_hi = 227 * 1024;
+  // Rows per stage: 8 unless two stages of very long rows would not fit.
+  // Paired epilogues (RoPE, SiLU*up) need an even count.
+  a.tr = kTR;
+  for (;;) {
+    const uint32_t qbytes = (uint32_t)(a.tr * w->nb * w->qb);
+    a.stage_sc_off = round_up(qbytes, 16);
+    a.stage_bytes = round_up(a.stage_sc_off + (uint32_t)(a.tr * w->nbp * 2), 128);
+    if (a.off_st + 2 * a.stage_bytes <= budget_hi || a.tr <= a.unit) break;
+    a.tr >>= 1;
+  }
   int S = (int)((budget_lo > a.off_st ? budget_lo - a.off_st : 0) / a.stage_bytes);
   if (S < 2) S = 2;
   if (S > 8) S = 8;

@@ -51,9 +51,12 @@ __global__ void rmsnorm_kernel(float* __restrict__ out, const float* __restrict_
 // llm.c:460-487: cos/sin for element pair i of a head at position pos.
 __device__ __forceinline__ float2 rope_cs(int pos, int i, int hd, float base) {
   const float exponent = __fdiv_rn(-(float)i, (float)hd);
+  // The host rejects a non-finite base and positions >= 2^20, where these
+  // reduction loops of the reference would not terminate; the iteration
+  // bounds below are a second guard.
   float b = base;
   int k = 0;
-  while (b > 2.0f) {
+  while (b > 2.0f && k < 256) {
     b = __fmul_rn(b, 0.5f);
     ++k;
   }
@@ -64,8 +67,8 @@ __device__ __forceinline__ float2 rope_cs(int pos, int i, int hd, float base) {
   float theta = __fmul_rn((float)pos, freq);
   const float pi = 3.14159265f;
   const float two_pi = 2.0f * pi;
-  while (theta > pi) theta = __fsub_rn(theta, two_pi);
-  while (theta < -pi) theta = __fadd_rn(theta, two_pi);
+  for (int it = 0; theta > pi && it < (1 << 20); ++it) theta = __fsub_rn(theta, two_pi);
+  for (int it = 0; theta < -pi && it < (1 << 20); ++it) theta = __fadd_rn(theta, two_pi);
   const float t2 = __fmul_rn(theta, theta);
   const float c = __fsub_rn(
       1.0f, __fmul_rn(t2, __fsub_rn(0.5f, __fmul_rn(t2, __fsub_rn(0.04166667f, __fmul_rn(t2, 0.001388889f))))));
@@ -250,6 +253,17 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   pdl_trigger();
 }
 
+// Greedy decode on the device: record the token the last argmax produced
+// (io[2]) in ring[io[4]], then advance the position io[1] and the counter.
+__global__ void decode_advance_kernel(int* __restrict__ io, int* __restrict__ ring) {
+  pdl_wait();
+  const int k = io[4];
+  ring[k] = io[2];
+  io[4] = k + 1;
+  io[1] = io[1] + 1;
+  pdl_trigger();
+}
+
 }  // namespace tos
 
 using namespace tos;
@@ -330,4 +344,9 @@ extern "C" int tosk_argmax(const float* x, int n, int* out_idx, float* out_val, 
   if (n <= 0) return (int)cudaErrorInvalidValue;
   void* args[] = {&x, &n, &out_idx, &out_val};
   return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_decode_advance(int* io, int* ring, int pdl, cudaStream_t st) {
+  void* args[] = {&io, &ring};
+  return launch_pdl((const void*)decode_advance_kernel, dim3(1), dim3(1), args, pdl, st);
 }

@@ -214,5 +214,13 @@ class Model:
             raise TosError(n, "tos_model_generate_greedy")
         return out[:n]
 
+    def decode(self, token: int, pos: int, n_steps: int) -> np.ndarray:
+        out = np.zeros(max(n_steps, 1), dtype=np.int32)
+        _check("tos_model_decode", _lib().tos_model_decode(self.h, token, pos, n_steps, _p(out)))
+        return out[:n_steps]
+
+    def stream(self) -> int:
+        return int(_lib().tos_model_stream(self.h) or 0)
+
     def device_bytes(self) -> int:
         return int(_lib().tos_model_device_bytes(self.h))
