@@ -32,6 +32,19 @@ __device__ __forceinline__ float ref_silu(float x) {
   return __fmul_rn(x, s);
 }
 
+// Packed fp32 product that is never fused with the add consuming it.
+// The compiler contracts __fmul2_rn followed by __fadd2_rn into a packed FMA
+// (one rounding instead of two) even without -fmad; passing the product
+// through an opaque register barrier keeps the reference's two roundings.
+// Bit-exactness of every user is covered by the GPU parity tests.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  const float2 m = __fmul2_rn(a, b);
+  unsigned long long u =
+      (unsigned long long)__float_as_uint(m.x) | ((unsigned long long)__float_as_uint(m.y) << 32);
+  asm volatile("" : "+l"(u));
+  return make_float2(__uint_as_float((unsigned)u), __uint_as_float((unsigned)(u >> 32)));
+}
+
 __device__ __forceinline__ float h2f(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }

@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(kScoreTile) scores_kernel(const float* __restr
           load8<ESZ>(kr + m * ESZ, kv);
 #pragma unroll
           for (int p = 0; p < 4; ++p)
-            acc[p] = __fadd2_rn(acc[p], __fmul2_rn(make_float2(qh[m + 2 * p], qh[m + 2 * p + 1]), kv[p]));
+            acc[p] = __fadd2_rn(acc[p], mul2_rn(make_float2(qh[m + 2 * p], qh[m + 2 * p + 1]), kv[p]));
         }
         const float2 t01 = __fadd2_rn(acc[0], acc[2]);
         const float2 t23 = __fadd2_rn(acc[1], acc[3]);
@@ -173,7 +173,7 @@ __device__ __forceinline__ float2 pv_chain(const uint8_t* __restrict__ vbase, si
           v = __half22float2(*reinterpret_cast<const __half2*>(buf + r * slice_b + lane * 4));
         else
           v = *reinterpret_cast<const float2*>(buf + r * slice_b + lane * 8);
-        acc = __fadd2_rn(acc, __fmul2_rn(make_float2(p, p), v));   // llm.c:586-588
+        acc = __fadd2_rn(acc, mul2_rn(make_float2(p, p), v));   // llm.c:586-588
       }
     }
     __syncwarp();
@@ -333,7 +333,11 @@ static int allow_max_smem(const void* kern) {
   static int n_done = 0;
   for (int i = 0; i < n_done; ++i)
     if (done[i] == kern) return 0;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           227 * 1024 - (int)fa.sharedSizeBytes);
   if (e != cudaSuccess) return (int)e;
   if (n_done < 16) done[n_done++] = kern;
   return 0;

@@ -62,7 +62,7 @@ __device__ __forceinline__ float dot_q4_0(const uint4 q, const float d, const fl
       const float a = __uint_as_float(prmt(lo, 0x4B000000u, sel));
       const float b = __uint_as_float(prmt(hi, 0x4B000000u, sel));
       const float2 qv = __fadd2_rn(make_float2(a, b), make_float2(-kM, -kM));
-      const float2 pr = __fmul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
+      const float2 pr = mul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
       if (k == 0)
         acc[p] = kZeroInit ? __fadd2_rn(make_float2(0.0f, 0.0f), pr) : pr;
       else
@@ -94,7 +94,7 @@ __device__ __forceinline__ float dot_q8_0(const uint4 qa, const uint4 qb, const 
       const float a = __uint_as_float(prmt(word, 0x4B000000u, s0));
       const float b = __uint_as_float(prmt(word, 0x4B000000u, s1));
       const float2 qv = __fadd2_rn(make_float2(a, b), make_float2(-kM, -kM));
-      const float2 pr = __fmul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
+      const float2 pr = mul2_rn(qv, make_float2(x[8 * k + 2 * p], x[8 * k + 2 * p + 1]));
       if (k == 0)
         acc[p] = kZeroInit ? __fadd2_rn(make_float2(0.0f, 0.0f), pr) : pr;
       else
@@ -167,11 +167,11 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   const int ncw = a.nwb * a.rg;
   const int nb = a.nb, nbp = a.nbp;
 
-  __shared__ int s_failed;
+  int* s_failed = reinterpret_cast<int*>(misc + 6);
   if (threadIdx.x == 0) {
     // An earlier kernel whose bounded wait ran out leaves *err set: skip the
     // work so one failure cannot turn into a chain of timeouts.
-    s_failed = a.err ? *reinterpret_cast<volatile int*>(a.err) : 0;
+    *s_failed = a.err ? *reinterpret_cast<volatile int*>(a.err) : 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], ncw);
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   }
   __syncthreads();
   pdl_trigger();
-  if (s_failed) return;
+  if (*s_failed) return;
 
   if (warp == 0) {
     // ---------------- producer ----------------
