@@ -258,7 +258,9 @@ int tos_gemv_dev(const tos_weight_t *w, const float *x, float *out, void *stream
 {
     DEV_PROLOGUE();
     if (!w || !x || !out) return tos_set_status(TOS_EINVAL);
-    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, NULL, out, NULL, tos_g.err_dev, 0, tos_pick_stream(stream))));
+    /* programmatic dependent launch: weight prefetch overlaps the previous
+     * kernel; x is read only after that kernel completes */
+    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, NULL, out, NULL, tos_g.err_dev, 1, tos_pick_stream(stream))));
 }
 
 int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
@@ -267,7 +269,7 @@ int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w
     DEV_PROLOGUE();
     if (!w || !x || !out || !norm_w) return tos_set_status(TOS_EINVAL);
     tosk_norm_t nrm = {norm_w, eps};
-    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, &nrm, out, NULL, tos_g.err_dev, 0, tos_pick_stream(stream))));
+    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, &nrm, out, NULL, tos_g.err_dev, 1, tos_pick_stream(stream))));
 }
 
 int tos_block_dots_dev(const void *blocks, int type, const float *x, int n_blocks, float *out, void *stream)

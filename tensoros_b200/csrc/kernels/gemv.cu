@@ -38,7 +38,9 @@
 namespace tos {
 
 constexpr int kTR = 8;    // rows per stage
-constexpr int kNCH = 2;   // chain warps
+constexpr int kNCH = 2;   // chain warps (each row chain is serial; two keep pace with the
+                          // compute warps and leave the CTA small enough (<= 12 warps,
+                          // ~85 registers) for the next kernel's CTA to co-reside)
 
 // Exact block dot, Q4_0.  q holds qs[0..15]; word k = bytes 4k..4k+3 covers
 // elements 8k..8k+7; byte j of the word gives element 8k+2j (low nibble) and
@@ -121,7 +123,7 @@ struct GemvArgs {
   int pstride;   // partials row stride (floats)
   int nwb, rg;   // compute warps per row of blocks, row groups
   int tr;        // rows per stage (<= kTR)
-  uint32_t off_x, off_p, off_st, stage_bytes, stage_sc_off;
+  uint32_t off_x, off_w, off_p, off_st, stage_bytes, stage_sc_off;
   tosk_epi_t epi;
 };
 
@@ -138,12 +140,16 @@ __device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t*
   }
 }
 
+// CTA named barrier over n threads.  The non-.aligned form: threads of one
+// warp may reach it from divergent paths (e.g. the lanes that ran a serial
+// chain and those that did not); callers still reconverge with __syncwarp.
 __device__ __forceinline__ void named_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+  __syncwarp();
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 template <int QB, bool kNorm, int kEpi>
-__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -152,9 +158,11 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   uint64_t* empty = full + S;
   uint64_t* pfull = empty + S;
   uint64_t* pempty = pfull + kNCH;
-  float* misc = reinterpret_cast<float*>(pempty + kNCH);
+  uint64_t* xbar = pempty + kNCH;
+  float* misc = reinterpret_cast<float*>(xbar + 1);
   float* xs = reinterpret_cast<float*>(smem + a.off_x);
   float* P = reinterpret_cast<float*>(smem + a.off_p);
+  float* ws = P;   // RMSNorm weights (kNorm): the partials area is idle until the x pass
   uint8_t* stages = smem + a.off_st;
 
   const int NU = (a.R + a.unit - 1) / a.unit;
@@ -180,18 +188,32 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
       mbar_init(&pfull[c], ncw);
       mbar_init(&pempty[c], 1);
     }
+    mbar_init(xbar, 1);   // one arrival (with the byte count of x and the norm weights)
+    *reinterpret_cast<volatile int*>(misc + 7) = 0;
     mbar_fence_init();
   }
   __syncthreads();
   pdl_trigger();
   if (*s_failed) return;
 
+  volatile int* xflag = reinterpret_cast<volatile int*>(misc + 7);
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- weight producer ----------------
     if (lane == 0) {
+      // Weights do not depend on earlier kernels, so the ring fills at once.
+      // After the first stage the producer gives the x copy (issued by the
+      // first chain warp once the previous kernel is complete) up to ~1.5 us
+      // to enter the copy queue first: x gates all compute, and copies
+      // complete roughly in issue order.
       int issued = 0;
       for (int it = 0; it < nst; ++it) {
         const int s = it % S;
+        if (it == 1) {
+          const long long t0 = clock64();
+          while (*xflag == 0 && clock64() - t0 < 3000) {
+          }
+          if constexpr (kNorm) bulk_g2s(ws, a.norm_w, (uint32_t)(a.cols * 4), xbar);
+        }
         if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.err, 1)) break;
         const int r0 = rb + it * tr;
         const int n = min(tr, re - r0);
@@ -203,25 +225,45 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
         bulk_g2s(st + a.stage_sc_off, a.sc + (size_t)r0 * nbp, bs, &full[s]);
         issued = it + 1;
       }
+      if (kNorm && nst <= 1) bulk_g2s(ws, a.norm_w, (uint32_t)(a.cols * 4), xbar);
       // Leave only when every copy issued into this CTA's ring has landed.
       for (int it = max(0, issued - S); it < issued; ++it)
         mbar_wait(&full[it % S], (it / S) & 1, a.err, 5);
+      mbar_wait(xbar, 0, a.err, 6);
     }
     return;
   }
 
   // ---------------- all non-producer warps ----------------
   const int nthr = (int)blockDim.x - 32;
-  pdl_wait();  // x (and the residual / position) come from earlier kernels
+  pdl_wait();  // x, the residual and the position come from earlier kernels
+  if (threadIdx.x == 32) {
+    // x (and the norm weights, issued by the producer) land on xbar
+    mbar_arrive_expect_tx(xbar, (uint32_t)(a.cols * 4) * (kNorm ? 2u : 1u));
+    bulk_g2s(xs, a.x, (uint32_t)(a.cols * 4), xbar);
+    *xflag = 1;
+  }
+  if (!mbar_wait(xbar, 0, a.err, 7)) return;   // x has landed in shared memory
   float ss = 1.0f;
   if constexpr (kNorm) {
-    for (int i = threadIdx.x - 32; i < a.cols; i += nthr) xs[i] = a.x[i];
-    named_sync(1, nthr);
+    // llm.c:421-427: lane l sums x[4i+l]^2 serially.  Each of four lanes
+    // reads x four elements at a time (a broadcast load), squares its own
+    // element and adds it; loads are batched ahead of the dependent adds.
     if (warp == 1 && lane < 4) {
-      // llm.c:421-427: lane l sums x[4i+l]^2 serially
+      const int q4 = a.cols >> 2;
       float acc = 0.0f;
-      for (int i0 = 0; i0 + 4 <= a.cols; i0 += 4)
-        acc = __fadd_rn(acc, __fmul_rn(xs[i0 + lane], xs[i0 + lane]));
+      int k = 0;
+      for (; k + 8 <= q4; k += 8) {
+        float e[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = xs[4 * (k + j) + lane];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+      }
+      for (; k < q4; ++k) {
+        const float v = xs[4 * k + lane];
+        acc = __fadd_rn(acc, __fmul_rn(v, v));
+      }
       misc[lane] = acc;
     }
     named_sync(1, nthr);
@@ -233,6 +275,35 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
     }
     named_sync(1, nthr);
     ss = misc[4];
+  }
+  // One in-place pass over x (normalised here when the norm is fused:
+  // (x*ss)*w, llm.c:437-440): the 16-byte chunk c of block b moves to slot
+  // c ^ (b & 7), so that below every lane reads its own block's chunks from
+  // distinct banks.  Eight consecutive threads own one block's eight chunks.
+  {
+    float4* x4 = reinterpret_cast<float4*>(xs);
+    const float4* w4 = reinterpret_cast<const float4*>(ws);
+    const int nchunk = a.cols >> 2;
+    for (int base = threadIdx.x - 32; base - (threadIdx.x - 32) < nchunk; base += nthr) {
+      const int t = base;   // chunk index owned by this thread in this round
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t < nchunk) {
+        v = x4[t];
+        if constexpr (kNorm) {
+          const float4 wv = w4[t];
+          v.x = __fmul_rn(__fmul_rn(v.x, ss), wv.x);
+          v.y = __fmul_rn(__fmul_rn(v.y, ss), wv.y);
+          v.z = __fmul_rn(__fmul_rn(v.z, ss), wv.z);
+          v.w = __fmul_rn(__fmul_rn(v.w, ss), wv.w);
+        }
+      }
+      __syncwarp();
+      if (t < nchunk) {
+        const int blk = t >> 3, c = t & 7;
+        x4[(blk << 3) | (c ^ (blk & 7))] = v;
+      }
+    }
+    named_sync(1, nthr);
   }
 
   if (warp >= 1 + kNCH) {
@@ -246,17 +317,11 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) xr[i] = 0.0f;
     if (valid) {
-      if constexpr (kNorm) {
+      const float4* xv = reinterpret_cast<const float4*>(xs) + 8 * b;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          xr[i] = __fmul_rn(__fmul_rn(xs[32 * b + i], ss), a.norm_w[32 * b + i]);
-      } else {
-        const float4* xv = reinterpret_cast<const float4*>(a.x + 32 * b);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 v = xv[i];
-          xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
-        }
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = xv[i ^ (b & 7)];
+        xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
       }
     }
     for (int it = 0; it < nst; ++it) {
@@ -269,8 +334,16 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
       const uint16_t* sts = reinterpret_cast<const uint16_t*>(stq + a.stage_sc_off);
       float* Pc = P + c * kTR * a.pstride;
       if (valid) {
-#pragma unroll 2
-        for (int r = g; r < n; r += a.rg) Pc[r * a.pstride + b] = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
+        // two rows per iteration: independent dot chains interleave
+        const int rg = a.rg;
+        int r = g;
+        for (; r + rg < n; r += 2 * rg) {
+          const float y0 = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
+          const float y1 = block_value<QB>(stq, sts, r + rg, b, nb, nbp, xr);
+          Pc[r * a.pstride + b] = y0;
+          Pc[(r + rg) * a.pstride + b] = y1;
+        }
+        if (r < n) Pc[r * a.pstride + b] = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
       }
       __syncwarp();
       if (lane == 0) {
@@ -292,7 +365,20 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
     const float* Pr = P + (cw * kTR + min(lane, kTR - 1)) * a.pstride;
     float y = 0.0f;  // llm.c:223: sum = 0.0f, then += block value, in block order
     if (lane < n) {
+      // loads batched ahead of the dependent adds (the chain itself is serial)
       int bb = 0;
+      for (; bb + 32 <= nb; bb += 32) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const float4*>(Pr + bb + 4 * j);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          y = __fadd_rn(y, v[j].x);
+          y = __fadd_rn(y, v[j].y);
+          y = __fadd_rn(y, v[j].z);
+          y = __fadd_rn(y, v[j].w);
+        }
+      }
       for (; bb + 4 <= nb; bb += 4) {
         const float4 v = *reinterpret_cast<const float4*>(Pr + bb);
         y = __fadd_rn(y, v.x);
@@ -512,6 +598,9 @@ static inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a
 extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t* norm, float* out,
                          const tosk_epi_t* epi, int* err, int pdl, cudaStream_t st) {
   if (!w || !x || !out) return (int)cudaErrorInvalidValue;
+  // x and the norm weights are fetched with bulk copies: 16-byte alignment
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (norm && (reinterpret_cast<uintptr_t>(norm->norm_w) & 15)))
+    return (int)cudaErrorInvalidValue;
   GemvArgs a = {};
   a.qs = w->qs;
   a.sc = w->sc;
@@ -530,18 +619,30 @@ extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t
   if (epi) a.epi = *epi;
   a.epi.kind = kind;
   a.nwb = (w->nb + 31) / 32;
-  if (a.nwb > 13) return (int)cudaErrorInvalidValue;  // cols > 13*1024: not supported
+  // cols > 16*1024 would need several blocks per thread: not supported
+  if (a.nwb > 16) return (int)cudaErrorInvalidValue;
+  // About 16 compute warps per CTA (one CTA per SM) for latency hiding:
+  // row groups split a stage's rows between warps holding the same blocks.
   a.rg = a.nwb >= 8 ? 1 : (8 / a.nwb);
   if (a.rg > kTR) a.rg = kTR;
   const int threads = 32 * (1 + kNCH + a.nwb * a.rg);
   a.pstride = (int)round_up((uint32_t)w->nb, 8) + 4;
-  const uint32_t hdr = 256;   // up to 2*8 + 2*kNCH mbarriers and 8 floats
+  const uint32_t hdr = 320;   // up to 2*8 + 2*kNCH + 1 mbarriers and 8 floats
   a.off_x = hdr;
-  const uint32_t xbytes = fuse_norm ? round_up((uint32_t)w->cols * 4, 128) : 0;
+  const uint32_t xbytes = round_up((uint32_t)w->cols * 4, 128);
+  a.off_w = 0;
   a.off_p = a.off_x + xbytes;
-  const uint32_t pbytes = round_up((uint32_t)(kNCH * kTR * a.pstride * 4), 128);
+  // the partials area also holds the RMSNorm weights until the x pass
+  uint32_t pbytes = (uint32_t)(kNCH * kTR * a.pstride * 4);
+  if (fuse_norm && pbytes < (uint32_t)w->cols * 4) pbytes = (uint32_t)w->cols * 4;
+  pbytes = round_up(pbytes, 128);
   a.off_st = a.off_p + pbytes;
-  const uint32_t budget_lo = 100 * 1024, budget_hi = 227 * 1024;
+  // ~110 KB lets the next kernel's CTA (programmatic dependent launch)
+  // co-reside and prefetch its own weights; a CTA of more than 11 warps
+  // (~88 registers each) cannot share an SM's register file anyway, so it
+  // takes a deeper ring instead.
+  const uint32_t budget_hi = 227 * 1024;
+  const uint32_t budget_lo = threads > 352 ? 200 * 1024 : 110 * 1024;
   // Rows per stage: 8 unless two stages of very long rows would not fit.
   // Paired epilogues (RoPE, SiLU*up) need an even count.
   a.tr = kTR;
@@ -557,9 +658,13 @@ extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t
   if (S > 8) S = 8;
   if (a.off_st + (uint32_t)S * a.stage_bytes > budget_hi) return (int)cudaErrorInvalidValue;
   // header holds 2*S + 2*kNCH barriers + 8 floats
-  if ((uint32_t)(8 * (2 * S + 2 * kNCH) + 32) > hdr) return (int)cudaErrorInvalidValue;
+  if ((uint32_t)(8 * (2 * S + 2 * kNCH + 1) + 32) > hdr) return (int)cudaErrorInvalidValue;
   a.S = S;
   const size_t smem = a.off_st + (size_t)S * a.stage_bytes;
+  // layout checks: every region inside its own range
+  if (a.off_x + (uint32_t)w->cols * 4 > a.off_p || a.off_p + pbytes > a.off_st ||
+      a.off_p + (uint32_t)(kNCH * kTR * a.pstride * 4) > a.off_st || smem > budget_hi)
+    return (int)cudaErrorInvalidValue;
   const int NU = (a.R + a.unit - 1) / a.unit;
   int grid = tosk_num_sms();
   if (grid > NU) grid = NU;

@@ -213,9 +213,33 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   pdl_wait();
   float v = 0.0f;
   int idx = -1;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  // each thread scans 4 consecutive elements per step (vector loads when x
+  // is 16-byte aligned), four steps in flight; in-thread order stays
+  // increasing so the first maximum wins
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  const int n4 = vec ? (n & ~3) : 0;
+  for (int base = 4 * threadIdx.x; base < n4; base += 16 * blockDim.x) {
+    float4 c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + 4 * u * blockDim.x;
+      c[u] = i < n4 ? *reinterpret_cast<const float4*>(x + i) : make_float4(NAN, NAN, NAN, NAN);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + 4 * u * blockDim.x;
+      const float e[4] = {c[u].x, c[u].y, c[u].z, c[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (!(e[j] != e[j]) && (idx < 0 || e[j] > v || (e[j] == v && i + j < idx))) {
+          v = e[j];
+          idx = i + j;
+        }
+    }
+  }
+  for (int i = n4 + threadIdx.x; i < n; i += blockDim.x) {
     const float xi = x[i];
-    if (!(xi != xi) && (idx < 0 || xi > v)) {
+    if (!(xi != xi) && (idx < 0 || xi > v || (xi == v && i < idx))) {
       v = xi;
       idx = i;
     }
