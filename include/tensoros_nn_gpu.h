@@ -114,6 +114,21 @@ int tos_attention_dev(float *out, const float *q, const void *k_cache, const voi
                       int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,
                       int mode, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Allocation-free variant of tos_attention_dev (this entry point has no
+ * counterpart in the reference).  For callers that cannot allocate device
+ * memory while they run a step, as the reference's own static-scratch decode
+ * loop never does: the workspace is a 4 MiB device array inside the library
+ * (held on every GPU that loads it until exit) instead of caller memory.
+ * Returns TOS_ENOMEM, queueing nothing, when
+ * tos_attention_workspace_bytes(n_heads, max_ctx) exceeds 4 MiB.  The first
+ * call on a device resolves the array's address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller.  Nothing needs to start at zero.
+ * stream: the caller's CUDA stream (NULL = the legacy default stream). */
+int tos_attention_noalloc_dev(float *out, const float *q, const void *k_cache, const void *v_cache,
+                              int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,
+                              int mode, void *stream);
+
 /* --------------------- host-pointer drop-ins for runtime/nn/llm.c statics */
 void tos_gemv(float *out, const void *weight, const float *x, int out_dim, int in_dim, int type); /* llm.c:329 */
 float tos_vec_dot(const void *weight, const float *x, int n, int type);                           /* llm.c:221 */

@@ -64,6 +64,7 @@ NN_FUNCS = {
     "tos_argmax_dev": (i32, [vp, i32, vp, vp]),
     "tos_attention_workspace_bytes": (sz, [i32, i32]),
     "tos_attention_dev": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
+    "tos_attention_noalloc_dev": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
     "tos_gemv": (None, [vp, vp, vp, i32, i32, i32]),
     "tos_vec_dot": (f32, [vp, vp, i32, i32]),
     "tos_q4_0_dot32": (f32, [vp, vp]),

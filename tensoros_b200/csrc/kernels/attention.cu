@@ -414,3 +414,63 @@ extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, c
   void* args[] = {&esum, &pv, &n_heads, &hd, (void*)&pos_dev, &pos, (void*)&max_chunks, &out};
   return launch_k(fast_combine_kernel, n_heads, 128, 0, pdl, st, args);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point
+//
+// The decode path this library replaces keeps all of its scratch in static
+// buffers and never allocates while it runs (runtime/nn/llm.c:48-65): it is
+// meant for callers such as a kernel-mode or real-time inference loop, or a
+// host whose device memory is owned by another allocator, that cannot call
+// cudaMalloc in the middle of a step.  tos_attention_noalloc_dev serves them:
+// it runs the same attention kernels as tos_attention_dev with the workspace
+// taken from a file-scope device array instead of caller-provided memory.
+//
+//  * The array holds kNoAllocScratchBytes (4 MiB) on every GPU that loads
+//    this library, for the life of the process.  A configuration whose
+//    workspace (tos_attention_workspace_bytes(n_heads, max_ctx)) is larger
+//    is rejected with TOS_ENOMEM before any work is queued.
+//  * The first call on a device resolves the array's device address with
+//    cudaGetSymbolAddress while that device is current; make that first call
+//    before any stream capture.
+//  * Every call shares the one array.  Nothing in it has to start at zero:
+//    each call writes every workspace element before reading it.  Calls that
+//    overlap on the GPU (different streams, or concurrent host threads) race
+//    on the array and must be serialised by the caller.
+//  * Nothing here allocates: no cudaMalloc/cudaFree and no library routine
+//    that allocates; the library stream and error word are not touched.
+// ---------------------------------------------------------------------------
+namespace tos {
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+}  // namespace tos
+
+static void* g_noalloc_ptr[64];
+static int g_noalloc_ready[64];
+
+extern "C" int tos_attention_noalloc_dev(float* out, const float* q, const void* k_cache, const void* v_cache,
+                                         int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,
+                                         int mode, void* stream) {
+  // status values of include/tensoros_nn_gpu.h
+  const int kOk = 0, kInval = -1, kNoMem = -2, kCuda = -3, kNoDev = -7;
+  if (!out || !q || !k_cache || !v_cache) return kInval;
+  if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_ctx <= 0 || pos < 0 || pos >= max_ctx) return kInval;
+  if (mode != TOSK_ATTN_EXACT && mode != TOSK_ATTN_FAST) return kInval;
+  const size_t need = tosk_attention_ws_bytes(n_heads, max_ctx);
+  if (need > tos::kNoAllocScratchBytes) return kNoMem;   // beyond the static scratch
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kNoDev;
+  if (dev < 0 || dev >= 64) return kInval;
+  if (!g_noalloc_ready[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, tos::g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return kCuda;
+    g_noalloc_ptr[dev] = p;
+    g_noalloc_ready[dev] = 1;
+  }
+  const int e = tosk_attention(out, q, k_cache, v_cache, kv_type, n_heads, n_kv, head_dim, nullptr, pos, max_ctx,
+                               mode, g_noalloc_ptr[dev], tos::kNoAllocScratchBytes, nullptr, 0,
+                               (cudaStream_t)stream);
+  if (e == cudaSuccess) return kOk;
+  return e == cudaErrorInvalidValue ? kInval : kCuda;
+}
