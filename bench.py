@@ -300,7 +300,10 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_0> 4096x4096 (isolated, L2-cold)",
                          "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch
+                         # of this kernel and shape (profiles/gemv_q4_0_4096x4096.md)
+                         "traffic": 9485568,
                          "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
             "decode_weight_gbs": weight_bytes * value / world / 1e9,
             "clocks": clk.summary(),
