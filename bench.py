@@ -8,7 +8,11 @@ batch 1.  A step is one decoded token.
 
   value      tokens/s with the model resident in HBM: K greedy steps chained on
              the device (tos_model_decode), timed with CUDA events on the
-             model's stream.  Weights (3.7 GB per step) exceed L2 (126 MB), so
+             model's stream.  --math fast (default): FAST GEMV and attention
+             arithmetic (normwise error <= 1e-4); --math exact: bit-identical
+             to the reference.  With fast, "exact" reports the bit-exact
+             arithmetic's tokens/s on the same prompt and whether its greedy
+             ids equal the fast run's.  Weights (3.7 GB per step) exceed L2 (126 MB), so
              no flush is needed.
   e2e        the same metric through tos_model_forward_argmax: every step
              copies token+position host->device (8 B, pinned) and the next
@@ -166,7 +170,7 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def gemv_roofline(lib, torch, n_copies=32, reps=4):
+def gemv_roofline(lib, torch, mode, n_copies=32, reps=4):
     """Isolated Q4_0 GEMV 4096x4096, L2-cold by rotating weight copies."""
     import ctypes
     from tensoros_b200 import workloads as W
@@ -183,13 +187,13 @@ def gemv_roofline(lib, torch, n_copies=32, reps=4):
         with torch.cuda.stream(s):
             sp = s.cuda_stream
             for h in hs[:4]:
-                lib.tos_gemv_dev(h, x.data_ptr(), y.data_ptr(), sp)
+                assert lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp) == 0
             s.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=s):
                 for _ in range(reps):
                     for h in hs:
-                        lib.tos_gemv_dev(h, x.data_ptr(), y.data_ptr(), sp)
+                        lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp)
             g.replay()
             s.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -202,6 +206,20 @@ def gemv_roofline(lib, torch, n_copies=32, reps=4):
     finally:
         for h in hs:
             lib.tos_weight_destroy(h)
+
+
+def run_gemv_only(args, local):
+    import torch
+    from tensoros_b200 import lib as _lib
+    torch.cuda.set_device(local)
+    lib = _lib()
+    assert lib.tos_init(local) == 0, "tos_init failed"
+    mode = int(args.math == "fast")
+    ms = gemv_roofline(lib, torch, mode, n_copies=args.gemv_copies)
+    peak, peak_kind = peaks()
+    gbs = GEMV_BYTES_4096 / (ms / 1000.0) / 1e9
+    print(json.dumps({"kernel": f"gemv Q4_0 4096x4096 {args.math}", "launch_us": ms * 1000.0, "GB/s": gbs,
+                      "frac": gbs / peak, "peak_source": peak_kind, "copies": args.gemv_copies}), flush=True)
 
 
 def run_ours(args, world, rank, local):
@@ -220,19 +238,12 @@ def run_ours(args, world, rank, local):
     cfg = dict(W.LLAMA2_7B)
     t_gen = time.perf_counter()
     synth = W.make_model(cfg, W.SEED)
-    model = ops.Model(synth, attn_mode=args.attn)
+    fast = args.math == "fast"
     t_gen = time.perf_counter() - t_gen
     prompt = W.tokens(args.prefill, cfg["vocab_size"], W.SEED)
-    nxt = 0
-    for i, t in enumerate(prompt):
-        nxt = model.forward_argmax(int(t), i)
-    pos = args.prefill
     warm = max(3, args.warmup)
-    toks = model.decode(nxt, pos, warm)
-    nxt, pos = int(toks[-1]), pos + warm
-    stream = torch.cuda.ExternalStream(model.stream())
     K = args.steps
-    if pos + 2 * K + 2 > cfg["max_seq"]:
+    if args.prefill + warm + 2 * K + 2 > cfg["max_seq"]:
         raise SystemExit("steps too large for the 4096-position cache")
 
     def barrier():
@@ -240,43 +251,69 @@ def run_ours(args, world, rank, local):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # ---- value: device-chained decode
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def timed_decode(model, clk=None):
+        """prefill, W warm-up steps, then K chained steps (value) and K host
+        round-trip steps (e2e); returns (ms, e2e ms, the 2K greedy ids)"""
+        nxt = 0
+        for i, t in enumerate(prompt):
+            nxt = model.forward_argmax(int(t), i)
+        pos = args.prefill
+        toks = model.decode(nxt, pos, warm)
+        nxt, pos = int(toks[-1]), pos + warm
+        stream = torch.cuda.ExternalStream(model.stream())
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if clk:
+            clk.__enter__()
         torch.cuda.cudart().cudaProfilerStart()
         e0.record(stream)
         toks = model.decode(nxt, pos, K)
         e1.record(stream)
         e1.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
-    barrier()
-    t_ms = e0.elapsed_time(e1)
-    nxt, pos = int(toks[-1]), pos + K
-    # ---- e2e: per step host round trip through tos_model_forward_argmax
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(K):
-        nxt = model.forward_argmax(nxt, pos)
-        pos += 1
-    e3.record(stream)
-    e3.synchronize()
-    barrier()
-    t_e2e = e2.elapsed_time(e3)
+        if clk:
+            clk.__exit__()
+        barrier()
+        ids = [int(t) for t in toks]
+        nxt, pos = ids[-1], pos + K
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(K):
+            nxt = model.forward_argmax(nxt, pos)
+            ids.append(int(nxt))
+            pos += 1
+        e3.record(stream)
+        e3.synchronize()
+        barrier()
+        return e0.elapsed_time(e1), e2.elapsed_time(e3), ids
+
+    # ---- value / e2e: the selected arithmetic
+    clk = ClockSampler(local)
+    model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast))
+    t_ms, t_e2e, ids = timed_decode(model, clk)
+    model.close()
+    # ---- the bit-exact path on the same prompt: its speed, and whether the
+    # greedy ids agree (EXACT equals the reference bit for bit)
+    exact_ms, exact_ids = None, None
+    if fast and not args.no_exact:
+        model = ops.Model(synth)
+        exact_ms, _, exact_ids = timed_decode(model)
+        model.close()
     if world > 1:
-        tt = torch.tensor([t_ms, t_e2e], device="cuda")
+        tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0], device="cuda")
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         t_ms, t_e2e = float(tt[0]), float(tt[1])
+        exact_ms = float(tt[2]) if exact_ms is not None else None
     value = world * K / (t_ms / 1000.0)
     e2e = world * K / (t_e2e / 1000.0)
 
     res = {}
     if rank == 0:
-        gemv_ms = gemv_roofline(lib, torch)
+        gemv_ms = gemv_roofline(lib, torch, int(fast))
         peak, peak_kind = peaks()
         achieved = GEMV_BYTES_4096 / (gemv_ms / 1000.0) / 1e9
         L = cfg["n_layers"]
-        per_layer = 1 + (2 if args.attn == 0 else 3) + 3
+        per_layer = 1 + 2 + 3   # QKV GEMV, attention (2 kernels), o / gate-up / down GEMVs
         launches = K * (1 + L * per_layer + 3)
         weight_bytes = (L * (4096 * 128 * 18 * 4 + 3 * 11008 * 128 * 18) + 32000 * 128 * 18)
         cpu = None
@@ -292,13 +329,13 @@ def run_ours(args, world, rank, local):
             "data": "synthetic (seeded random-init Q4_0 weights; BASELINE distributions)",
             "config": {"workload": "llama2-7b-shape-q4_0 greedy decode, batch 1, after a 128-token prefill",
                        "model": cfg["name"], "global_batch": world, "seq_len": args.prefill,
-                       "kv_cache": "fp16, capacity 4096", "attention": "exact" if args.attn == 0 else "fast",
+                       "kv_cache": "fp16, capacity 4096", "arithmetic": args.math,
                        "positions": [args.prefill + warm, args.prefill + warm + K - 1],
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_0> 4096x4096 (isolated, L2-cold)",
+            "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
                          "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak,
                          # dram__bytes_read.sum + dram__bytes_write.sum of one launch
@@ -307,11 +344,13 @@ def run_ours(args, world, rank, local):
                          "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
             "decode_weight_gbs": weight_bytes * value / world / 1e9,
             "clocks": clk.summary(),
+            "exact": None if exact_ms is None else {
+                "value": world * K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
+                "greedy_ids_identical": exact_ids == ids, "ids_compared": len(ids)},
             "cpu_baseline": cpu,
             "setup_s": round(t_gen, 1),
         }
         print(json.dumps(res), flush=True)
-    model.close()
     if world > 1:
         torch.distributed.destroy_process_group()
 
@@ -323,12 +362,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prefill", type=int, default=128)
-    ap.add_argument("--attn", type=int, default=0, help="0 exact, 1 fast")
+    ap.add_argument("--math", default="fast", choices=["exact", "fast"],
+                    help="exact: bit-identical to the reference; fast: FAST GEMV and attention "
+                         "(normwise error <= 1e-4, greedy ids identical)")
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-exact", action="store_true", help="skip the EXACT-arithmetic comparison run")
+    ap.add_argument("--gemv-only", action="store_true",
+                    help="time only the isolated Q4_0 4096x4096 GEMV (the roofline leg) and print it")
+    ap.add_argument("--gemv-copies", type=int, default=32)
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
-    if args.impl == "reference":
+    if args.gemv_only:
+        run_gemv_only(args, local)
+    elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
         run_ours(args, world, rank, local)

@@ -60,6 +60,13 @@ enum {
     TOS_ATTN_FAST = 1   /* split-position partial sums; max rel. error 1e-4 */
 };
 
+/* GEMV arithmetic (with the RMSNorm fused into it) */
+enum {
+    TOS_GEMV_EXACT = 0, /* reference lane tree and serial row chain, bit-identical */
+    TOS_GEMV_FAST = 1   /* integer dot products on 24-bit fixed-point x, tree sums;
+                           normwise error ~1e-7, bound 1e-4 */
+};
+
 const char *tos_status_string(int status);
 int tos_last_status(void);
 
@@ -89,6 +96,10 @@ int tos_gemv_dev(const tos_weight_t *w, const float *x, float *out, void *stream
 /* out = W rmsnorm(x, norm_w, eps): fused llm_rmsnorm + llm_gemv */
 int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
                       float *out, void *stream);
+/* either of the two above (norm_w NULL: no norm) in TOS_GEMV_EXACT or
+ * TOS_GEMV_FAST arithmetic; the EXACT form is tos_gemv_dev/tos_gemv_norm_dev */
+int tos_gemv_mode_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
+                      float *out, int mode, void *stream);
 /* per-block values q4_0_dot32 / q8_0_dot32 (llm.c:148-216) for n_blocks
  * consecutive GGUF blocks against x[32*n_blocks] */
 int tos_block_dots_dev(const void *blocks, int type, const float *x, int n_blocks, float *out,
@@ -173,6 +184,7 @@ typedef struct {
     const void *const *wgate;
     const void *const *wup;
     const void *const *wdown;
+    int gemv_mode;           /* TOS_GEMV_EXACT (default) or TOS_GEMV_FAST */
 } tos_model_desc_t;
 
 typedef struct tos_model tos_model_t;

@@ -39,7 +39,8 @@ CC_FLAGS = ["-std=c11", "-O2", "-fPIC", "-Wall", "-Wno-unused-function", "-D_GNU
 NN_CU = sorted((CSRC / "kernels").glob("*.cu"))
 NN_C = [CSRC / "host" / "tos_runtime.c", CSRC / "host" / "tos_model.c"]
 SYNTH_C = [CSRC / "host" / "tos_synth.c"]
-HEADERS = sorted((CSRC / "include").glob("*")) + sorted(INC.glob("*.h"))
+HEADERS = (sorted((CSRC / "include").glob("*")) + sorted((CSRC / "kernels").glob("*.cuh"))
+           + sorted(INC.glob("*.h")))
 
 LIB_NN = LIB / "libtensoros_nn.so"
 LIB_SYNTH = LIB / "libtos_synth.so"

@@ -32,6 +32,7 @@ class ModelDesc(C.Structure):
         ("attn_norm", C.POINTER(vp)), ("ffn_norm", C.POINTER(vp)),
         ("wq", C.POINTER(vp)), ("wk", C.POINTER(vp)), ("wv", C.POINTER(vp)), ("wo", C.POINTER(vp)),
         ("wgate", C.POINTER(vp)), ("wup", C.POINTER(vp)), ("wdown", C.POINTER(vp)),
+        ("gemv_mode", i32),
     ]
 
 
@@ -51,6 +52,7 @@ NN_FUNCS = {
     "tos_weight_cache_clear": (None, []),
     "tos_gemv_dev": (i32, [vp, vp, vp, vp]),
     "tos_gemv_norm_dev": (i32, [vp, vp, vp, f32, vp, vp]),
+    "tos_gemv_mode_dev": (i32, [vp, vp, vp, f32, vp, i32, vp]),
     "tos_block_dots_dev": (i32, [vp, i32, vp, i32, vp, vp]),
     "tos_rmsnorm_dev": (i32, [vp, vp, vp, i32, i32, f32, vp]),
     "tos_rope_dev": (i32, [vp, i32, i32, i32, f32, vp]),

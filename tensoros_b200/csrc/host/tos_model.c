@@ -127,6 +127,7 @@ static int validate(const tos_model_desc_t *d)
     if (d->wtype != TOS_TYPE_Q4_0 && d->wtype != TOS_TYPE_Q8_0) return TOS_ENOTSUP;
     if (d->kv_type != TOS_TYPE_F32 && d->kv_type != TOS_TYPE_F16) return TOS_ENOTSUP;
     if (d->attn_mode != TOS_ATTN_EXACT && d->attn_mode != TOS_ATTN_FAST) return TOS_EINVAL;
+    if (d->gemv_mode != TOS_GEMV_EXACT && d->gemv_mode != TOS_GEMV_FAST) return TOS_EINVAL;
     const void *head = d->output_weight ? d->output_weight : d->token_embd;
     int ht = d->output_weight ? d->out_type : d->embd_type;
     if (!head || (ht != TOS_TYPE_Q4_0 && ht != TOS_TYPE_Q8_0)) return TOS_ENOTSUP;
@@ -263,7 +264,7 @@ static int enqueue_token(tos_model_t *m, int chained)
         qkv.kv_type = d->kv_type;
         qkv.k_cache = (char *)m->kc + kv_layer * l;
         qkv.v_cache = (char *)m->vc + kv_layer * l;
-        e = tosk_gemv(&m->wqkv[l], m->x, &n1, m->q, &qkv, err, pdl, st);
+        e = tosk_gemv(&m->wqkv[l], m->x, &n1, m->q, &qkv, d->gemv_mode, err, pdl, st);
         if (!e) e = tosk_attention(m->att, m->q, qkv.k_cache, qkv.v_cache, d->kv_type, d->n_heads,
                                    d->n_kv_heads, m->hd, m->io + 1, 0, d->max_seq, d->attn_mode, m->ws,
                                    m->ws_bytes, err, pdl, st);
@@ -271,16 +272,16 @@ static int enqueue_token(tos_model_t *m, int chained)
         memset(&res, 0, sizeof(res));
         res.kind = TOSK_EPI_RESID;
         res.resid = m->x;
-        if (!e) e = tosk_gemv(&m->wo[l], m->att, NULL, m->x, &res, err, pdl, st);
+        if (!e) e = tosk_gemv(&m->wo[l], m->att, NULL, m->x, &res, d->gemv_mode, err, pdl, st);
         tosk_norm_t n2 = {m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps};
         tosk_epi_t sw;
         memset(&sw, 0, sizeof(sw));
         sw.kind = TOSK_EPI_SWIGLU;
-        if (!e) e = tosk_gemv(&m->wgu[l], m->x, &n2, m->h, &sw, err, pdl, st);
-        if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x, &res, err, pdl, st);
+        if (!e) e = tosk_gemv(&m->wgu[l], m->x, &n2, m->h, &sw, d->gemv_mode, err, pdl, st);
+        if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x, &res, d->gemv_mode, err, pdl, st);
     }
     tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps};
-    if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, err, pdl, st);
+    if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, d->gemv_mode, err, pdl, st);
     if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
     if (!e && chained) e = tosk_decode_advance(m->io, m->ring, pdl, st);
     return e;

@@ -260,7 +260,8 @@ int tos_gemv_dev(const tos_weight_t *w, const float *x, float *out, void *stream
     if (!w || !x || !out) return tos_set_status(TOS_EINVAL);
     /* programmatic dependent launch: weight prefetch overlaps the previous
      * kernel; x is read only after that kernel completes */
-    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, NULL, out, NULL, tos_g.err_dev, 1, tos_pick_stream(stream))));
+    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, NULL, out, NULL, TOSK_GEMV_EXACT, tos_g.err_dev, 1,
+                                                  tos_pick_stream(stream))));
 }
 
 int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
@@ -269,7 +270,19 @@ int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w
     DEV_PROLOGUE();
     if (!w || !x || !out || !norm_w) return tos_set_status(TOS_EINVAL);
     tosk_norm_t nrm = {norm_w, eps};
-    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, &nrm, out, NULL, tos_g.err_dev, 1, tos_pick_stream(stream))));
+    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, &nrm, out, NULL, TOSK_GEMV_EXACT, tos_g.err_dev, 1,
+                                                  tos_pick_stream(stream))));
+}
+
+int tos_gemv_mode_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
+                      float *out, int mode, void *stream)
+{
+    DEV_PROLOGUE();
+    if (!w || !x || !out) return tos_set_status(TOS_EINVAL);
+    if (mode != TOS_GEMV_EXACT && mode != TOS_GEMV_FAST) return tos_set_status(TOS_EINVAL);
+    tosk_norm_t nrm = {norm_w, eps};
+    return tos_set_status(tos_from_cuda(tosk_gemv(&w->m, x, norm_w ? &nrm : NULL, out, NULL, mode,
+                                                  tos_g.err_dev, 1, tos_pick_stream(stream))));
 }
 
 int tos_block_dots_dev(const void *blocks, int type, const float *x, int n_blocks, float *out, void *stream)
@@ -415,7 +428,8 @@ void tos_gemv(float *out, const void *weight, const float *x, int out_dim, int i
         if (!tos_scratch(oo + (size_t)out_dim * 4)) { tos_set_status(TOS_ENOMEM); return; }
         e = h2d(ox, x, (size_t)in_dim * 4);
         if (!e) e = tosk_gemv(&w->m, (const float *)((char *)tos_g.scratch + ox), NULL,
-                              (float *)((char *)tos_g.scratch + oo), NULL, tos_g.err_dev, 0, tos_g.stream);
+                              (float *)((char *)tos_g.scratch + oo), NULL, TOSK_GEMV_EXACT, tos_g.err_dev, 0,
+                              tos_g.stream);
         if (!e) e = finish_to_host(out, oo, (size_t)out_dim * 4);
     } else if (type == TOS_TYPE_F16 || type == TOS_TYPE_F32) {
         size_t wb = row_bytes(in_dim, type) * (size_t)out_dim;

@@ -72,10 +72,14 @@ typedef struct {
     float eps;
 } tosk_norm_t;
 
-/* y = W * x with the reference's exact per-block lane tree and serial
- * block order (llm.c:148-237).  x (length cols) is device memory. */
+/* y = W * x.  TOSK_GEMV_EXACT: the reference's per-block lane tree and
+ * serial block order (llm.c:148-237), bit for bit.  TOSK_GEMV_FAST: integer
+ * dot products on 24-bit fixed-point x and tree row sums (and a tree sum of
+ * squares for a fused RMSNorm); normwise error ~1e-7.  x (length cols) is
+ * device memory. */
+enum { TOSK_GEMV_EXACT = 0, TOSK_GEMV_FAST = 1 };
 int tosk_gemv(const tosk_qmat_t *w, const float *x, const tosk_norm_t *norm,
-              float *out, const tosk_epi_t *epi, int *err, int pdl, cudaStream_t st);
+              float *out, const tosk_epi_t *epi, int mode, int *err, int pdl, cudaStream_t st);
 
 /* per-block exact partials: blocks in GGUF layout, n_blocks consecutive,
  * x of length 32*n_blocks, out[n_blocks] (q4_0_dot32 / q8_0_dot32) */

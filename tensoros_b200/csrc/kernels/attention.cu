@@ -17,9 +17,14 @@
 //                    parallel, then the serial PV chain with each lane owning
 //                    two d (packed f32x2).  V rows stream through a cp.async
 //                    ring.  The chains are the bound: ~4-5 cycles per position.
-// FAST mode splits positions into chunks (flash-decoding style) and combines
-// the partial sums in a tree; e_t still uses the reference's llm_expf of
-// (s_t - global max), so only summation order differs (tolerance 1e-4).
+// FAST mode is a split-K flash-decoding pass in two kernels over 64-position
+// chunks: fast_scores_kernel (a warp per 16 positions with all 16 rows in
+// flight, lanes across d, one shuffle reduce-scatter per 16 dots) writes the
+// scores and per-chunk maxima; fast_pv_kernel forms e_t = llm_expf(s_t - global max) (the
+// reference's exponential of the same argument), the chunk's e-sum and
+// sum_t e_t v_t, and the last chunk of each head to finish (a counter per
+// head) adds the chunks in order and divides.  Only summation order and
+// the place of the 1/sum differ from the reference (tolerance 1e-4).
 #include <cuda_runtime.h>
 
 #include "tos_dev.cuh"
@@ -30,7 +35,9 @@ namespace tos {
 constexpr int kScoreTile = 128;
 constexpr int kPvRows = 64;     // rows per V stage
 constexpr int kPvStages = 4;
-constexpr int kFastChunk = 256; // positions per FAST partial
+constexpr int kFChunk = 64;     // positions per FAST chunk
+constexpr int kFThreads = 128;  // FAST CTAs: 4 warps x 16 positions
+constexpr int kFMaxHd = 256;
 
 template <int ESZ>
 __device__ __forceinline__ void load8(const uint8_t* p, float2 (&v)[4]) {
@@ -237,80 +244,192 @@ __global__ void __launch_bounds__(32) softmax_pv_kernel(const float* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// FAST mode: per (head, slice, chunk) partial sums, then a combine pass.
-// ws layout after the scores: Msum[n_heads] (max), then partial e-sums
-// [n_heads][nchunk], then partial PV [n_heads][nchunk][hd].
+// FAST mode.  Workspace: S[n_heads][max_ctx] | cmax[n_heads][maxc] |
+// lsum[n_heads][maxc] | opart[n_heads][maxc][kFMaxHd] | cnt[n_heads] (int).
 // ---------------------------------------------------------------------------
+// Four consecutive cache elements (8 bytes of fp16 or 16 of fp32) as floats.
 template <int ESZ>
-__global__ void __launch_bounds__(32) fast_partial_kernel(const float* __restrict__ S,
-                                                          const uint8_t* __restrict__ vc, int n_heads,
-                                                          int n_kv, int hd, const int* __restrict__ pos_dev,
-                                                          int pos_arg, int max_ctx, float* __restrict__ esum,
-                                                          float* __restrict__ pv, int max_chunks) {
-  extern __shared__ __align__(16) uint8_t sm[];
-  float* P = reinterpret_cast<float*>(sm);
-  uint8_t* ring = sm + kFastChunk * 4;
+__device__ __forceinline__ float4 load4(const uint8_t* p) {
+  if constexpr (ESZ == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    return *reinterpret_cast<const float4*>(p);
+  }
+}
+
+// Lane l covers d = 128 s + 4 l .. +3 for slabs s < ceil(hd / 128).
+constexpr int kFSlabs = kFMaxHd / 128;
+
+template <int ESZ>
+__global__ void __launch_bounds__(kFThreads) fast_scores_kernel(
+    const float* __restrict__ q, const uint8_t* __restrict__ kc, int n_heads, int n_kv, int hd,
+    const int* __restrict__ pos_dev, int pos_arg, float* __restrict__ S, float* __restrict__ cmax,
+    int* __restrict__ cnt, int max_ctx, int maxc) {
+  __shared__ float wmax[kFThreads / 32];
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x;
-  const int ngr = (hd + 63) / 64;
   const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
-  const int nchunk = (n + kFastChunk - 1) / kFastChunk;
-  const int items = n_heads * ngr * nchunk;
+  if (blockIdx.x == 0)
+    for (int h = threadIdx.x; h < n_heads; h += blockDim.x) cnt[h] = 0;   // fast_pv_kernel's counters
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = n_heads / n_kv;
   const int kv_dim = n_kv * hd;
+  const int nchunk = (n + kFChunk - 1) / kFChunk;
+  const int items = n_kv * nchunk;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    const int c = item % nchunk;
-    const int hg = item / nchunk;
-    const int h = hg / ngr, g = hg % ngr;
-    const int kvh = h / (n_heads / n_kv);
-    const float* Sh = S + (size_t)h * max_ctx;
-    float m = -INFINITY;
-    for (int t = lane; t < n; t += 32) m = fmaxf(m, Sh[t]);
-    m = warp_max(m);
-    const int t0 = c * kFastChunk, t1 = min(n, t0 + kFastChunk);
-    float part = 0.0f;
-    __syncwarp();
-    for (int t = t0 + lane; t < t1; t += 32) {
-      const float e = ref_expf(__fsub_rn(Sh[t], m));
-      P[t - t0] = e;
-      part = __fadd_rn(part, e);
-    }
-    for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
-    __syncwarp();
-    const int d0 = 64 * g;
-    const int slice = min(64, hd - d0);
-    const bool active = 2 * lane < slice;
-    const uint8_t* vbase = vc + ((size_t)kvh * hd + d0) * ESZ;
-    float2 acc = pv_chain<ESZ>(vbase, (size_t)kv_dim * ESZ, slice * ESZ, P, t0, t0, t1, ring, lane,
-                               active, make_float2(0.0f, 0.0f));
-    if (g == 0 && lane == 0) esum[(size_t)h * max_chunks + c] = part;
-    if (active) {
-      float* o = pv + ((size_t)h * max_chunks + c) * hd + d0 + 2 * lane;
-      o[0] = acc.x;
-      o[1] = acc.y;
+    const int kvh = item / nchunk, c = item % nchunk;
+    const int tw = c * kFChunk + warp * 16;   // this warp's first position
+    for (int g = 0; g < group; ++g) {
+      const int h = kvh * group + g;
+      float v[16];
+#pragma unroll
+      for (int p = 0; p < 16; ++p) v[p] = 0.0f;
+#pragma unroll
+      for (int sl = 0; sl < kFSlabs; ++sl) {
+        const int d = 128 * sl + 4 * lane;
+        if (d < hd) {
+          const float4 qv = *reinterpret_cast<const float4*>(q + (size_t)h * hd + d);
+          float4 kv[16];
+#pragma unroll
+          for (int p = 0; p < 16; ++p)   // all 16 rows in flight at once
+            kv[p] = tw + p < n ? load4<ESZ>(kc + ((size_t)(tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int p = 0; p < 16; ++p)
+            v[p] = fmaf(qv.x, kv[p].x, fmaf(qv.y, kv[p].y, fmaf(qv.z, kv[p].z, fmaf(qv.w, kv[p].w, v[p]))));
+        }
+      }
+      // reduce-scatter: after the steps over lane bits 4..1, lane l holds
+      // position l >> 1 summed over 16 lanes; bit 0 finishes the sum
+#pragma unroll
+      for (int half = 8, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? v[half + i] : v[i];
+          const float send = up ? v[i] : v[half + i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+      const int t = tw + (lane >> 1);
+      const float sc = dot * scale;
+      float m = -INFINITY;
+      if (t < n) {
+        m = sc;
+        if ((lane & 1) == 0) S[(size_t)h * max_ctx + t] = sc;
+      }
+      m = warp_max(m);
+      __syncthreads();
+      if (lane == 0) wmax[warp] = m;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float cm = wmax[0];
+        for (int w = 1; w < kFThreads / 32; ++w) cm = fmaxf(cm, wmax[w]);
+        cmax[(size_t)h * maxc + c] = cm;
+      }
     }
   }
 }
 
-__global__ void fast_combine_kernel(const float* __restrict__ esum, const float* __restrict__ pv,
-                                    int n_heads, int hd, const int* __restrict__ pos_dev, int pos_arg,
-                                    int max_chunks, float* __restrict__ out) {
+template <int ESZ>
+__global__ void __launch_bounds__(kFThreads) fast_pv_kernel(
+    const float* __restrict__ S, const float* __restrict__ cmax, const uint8_t* __restrict__ vc, int n_heads,
+    int n_kv, int hd, const int* __restrict__ pos_dev, int pos_arg, float* __restrict__ lsum,
+    float* __restrict__ opart, int* __restrict__ cnt, float* __restrict__ out, int max_ctx, int maxc) {
+  __shared__ float es[kFChunk];
+  __shared__ float red[kFThreads / 32];
+  __shared__ __align__(16) float wpart[kFThreads / 32][kFMaxHd];
+  __shared__ int s_last;
   pdl_wait();
   pdl_trigger();
   const int n = (pos_dev ? *pos_dev : pos_arg) + 1;
-  const int nchunk = (n + kFastChunk - 1) / kFastChunk;
-  const int h = blockIdx.x;
-  __shared__ float s_inv;
-  if (threadIdx.x == 0) {
-    float sum = 0.0f;
-    for (int c = 0; c < nchunk; ++c) sum = __fadd_rn(sum, esum[(size_t)h * max_chunks + c]);
-    s_inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
-  }
-  __syncthreads();
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int c = 0; c < nchunk; ++c) acc = __fadd_rn(acc, pv[((size_t)h * max_chunks + c) * hd + d]);
-    out[(size_t)h * hd + d] = __fmul_rn(acc, s_inv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = n_heads / n_kv;
+  const int kv_dim = n_kv * hd;
+  const int nchunk = (n + kFChunk - 1) / kFChunk;
+  const int items = n_heads * nchunk;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int h = item / nchunk, c = item % nchunk;
+    const int kvh = h / group;
+    const int t0 = c * kFChunk, cn = min(kFChunk, n - t0);
+    // global max of the head's scores (llm.c:509-511) from the chunk maxima
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < nchunk; i += blockDim.x) m = fmaxf(m, cmax[(size_t)h * maxc + i]);
+    m = warp_max(m);
+    __syncthreads();
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < kFThreads / 32; ++w) M = fmaxf(M, red[w]);
+    // e_t = llm_expf(s_t - max) (llm.c:514-517) and the chunk's e-sum
+    float e = 0.0f;
+    if (threadIdx.x < kFChunk) {
+      if (threadIdx.x < cn) e = ref_expf(__fsub_rn(S[(size_t)h * max_ctx + t0 + threadIdx.x], M));
+      es[threadIdx.x] = e;
+    }
+    float l = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = l;
+    // sum_t e_t v_t[d]: warp w takes 16 positions, lane l four consecutive d
+    const int tw = warp * 16;
+#pragma unroll
+    for (int sl = 0; sl < kFSlabs; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      if (d < hd) {
+        float4 vv[16];
+#pragma unroll
+        for (int p = 0; p < 16; ++p)   // all 16 rows in flight at once
+          vv[p] = tw + p < cn ? load4<ESZ>(vc + ((size_t)(t0 + tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const float ep = es[tw + p];
+          acc.x = fmaf(ep, vv[p].x, acc.x);
+          acc.y = fmaf(ep, vv[p].y, acc.y);
+          acc.z = fmaf(ep, vv[p].z, acc.z);
+          acc.w = fmaf(ep, vv[p].w, acc.w);
+        }
+        *reinterpret_cast<float4*>(&wpart[warp][d]) = acc;
+      }
+    }
+    __syncthreads();
+    float* op = opart + ((size_t)h * maxc + c) * kFMaxHd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      float o = wpart[0][d];
+      for (int w = 1; w < kFThreads / 32; ++w) o += wpart[w][d];
+      op[d] = o;
+    }
+    if (threadIdx.x == 0) {
+      float lc = red[0];
+      for (int w = 1; w < kFThreads / 32; ++w) lc += red[w];
+      lsum[(size_t)h * maxc + c] = lc;
+    }
+    // the last chunk of the head to finish combines (chunk order, so the
+    // result does not depend on which CTA that is)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&cnt[h], 1) == nchunk - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      float L = 0.0f;
+      for (int i = 0; i < nchunk; ++i) L += *reinterpret_cast<volatile const float*>(&lsum[(size_t)h * maxc + i]);
+      const float inv = 1.0f / (L + 1e-10f);   // llm.c:519
+      for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f;
+        for (int i = 0; i < nchunk; ++i)
+          o += *reinterpret_cast<volatile const float*>(&opart[((size_t)h * maxc + i) * kFMaxHd + d]);
+        out[(size_t)h * hd + d] = o * inv;
+      }
+    }
   }
 }
 
@@ -321,9 +440,9 @@ using namespace tos;
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 extern "C" size_t tosk_attention_ws_bytes(int n_heads, int max_ctx) {
-  const size_t maxc = (size_t)(max_ctx + kFastChunk - 1) / kFastChunk;
-  return align256((size_t)n_heads * max_ctx * 4) + align256((size_t)n_heads * maxc * 4) +
-         align256((size_t)n_heads * maxc * 256 * 4);
+  const size_t maxc = (size_t)(max_ctx + kFChunk - 1) / kFChunk;
+  return align256((size_t)n_heads * max_ctx * 4) + 2 * align256((size_t)n_heads * maxc * 4) +
+         align256((size_t)n_heads * maxc * kFMaxHd * 4) + align256((size_t)n_heads * 4);
 }
 
 // Raises a kernel's dynamic shared-memory limit to the sm_100 maximum once
@@ -360,6 +479,37 @@ static int launch_k(K kern, int grid, int threads, size_t smem, int pdl, cudaStr
   return (int)cudaLaunchKernelExC(&cfg, (const void*)kern, args);
 }
 
+// FAST mode (split-K flash decoding): scores + chunk maxima, then e_t, the
+// chunk partials and the per-head combine by the last chunk to finish.
+static int fast_attention(float* out, const float* q, const uint8_t* kc, const uint8_t* vc, int esz,
+                          int n_heads, int n_kv, int hd, const int* pos_dev, int pos, int max_ctx, void* ws,
+                          int pdl, cudaStream_t st) {
+  // four consecutive elements per lane: hd a multiple of 4, rows 16-byte aligned
+  if (hd > kFMaxHd || hd % 4 != 0 || (reinterpret_cast<uintptr_t>(kc) & 15) || (reinterpret_cast<uintptr_t>(vc) & 15) ||
+      (reinterpret_cast<uintptr_t>(q) & 15))
+    return (int)cudaErrorInvalidValue;
+  const int maxc = (max_ctx + kFChunk - 1) / kFChunk;
+  float* S = (float*)ws;
+  float* cmax = (float*)((char*)S + align256((size_t)n_heads * max_ctx * 4));
+  float* lsum = (float*)((char*)cmax + align256((size_t)n_heads * maxc * 4));
+  float* opart = (float*)((char*)lsum + align256((size_t)n_heads * maxc * 4));
+  int* cnt = (int*)((char*)opart + align256((size_t)n_heads * maxc * kFMaxHd * 4));
+  const int cap = tosk_num_sms() * 8;
+  {
+    int grid = n_kv * maxc;
+    if (grid > cap) grid = cap;
+    void* args[] = {(void*)&q, (void*)&kc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &S, &cmax, &cnt, &max_ctx, (void*)&maxc};
+    int e = esz == 2 ? launch_k(fast_scores_kernel<2>, grid, kFThreads, 0, pdl, st, args)
+                     : launch_k(fast_scores_kernel<4>, grid, kFThreads, 0, pdl, st, args);
+    if (e) return e;
+  }
+  int grid = n_heads * maxc;
+  if (grid > cap) grid = cap;
+  void* args[] = {&S, &cmax, (void*)&vc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &lsum, &opart, &cnt, &out, &max_ctx, (void*)&maxc};
+  return esz == 2 ? launch_k(fast_pv_kernel<2>, grid, kFThreads, 0, pdl, st, args)
+                  : launch_k(fast_pv_kernel<4>, grid, kFThreads, 0, pdl, st, args);
+}
+
 extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, const void* v_cache,
                               int kv_type, int n_heads, int n_kv, int hd, const int* pos_dev, int pos,
                               int max_ctx, int mode, void* ws, size_t ws_bytes, int* err, int pdl,
@@ -371,6 +521,10 @@ extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, c
   if ((hd * esz) % 16 != 0 || hd % 2 != 0) return (int)cudaErrorInvalidValue;
   if (ws_bytes < tosk_attention_ws_bytes(n_heads, max_ctx)) return (int)cudaErrorInvalidValue;
   if (!pos_dev && (pos < 0 || pos >= max_ctx)) return (int)cudaErrorInvalidValue;
+  if (mode == TOSK_ATTN_FAST)
+    return fast_attention(out, q, (const uint8_t*)k_cache, (const uint8_t*)v_cache, esz, n_heads, n_kv, hd,
+                          pos_dev, pos, max_ctx, ws, pdl, st);
+  if (mode != TOSK_ATTN_EXACT) return (int)cudaErrorInvalidValue;
   float* S = (float*)ws;
   const int group = n_heads / n_kv;
   // scores
@@ -397,23 +551,10 @@ extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, c
     return esz == 2 ? launch_k(softmax_pv_kernel<2>, n_heads * ngr, 32, smem, pdl, st, args)
                     : launch_k(softmax_pv_kernel<4>, n_heads * ngr, 32, smem, pdl, st, args);
   }
-  const int max_chunks = (max_ctx + kFastChunk - 1) / kFastChunk;
-  if (hd > 256) return (int)cudaErrorInvalidValue;
-  float* esum = (float*)((char*)ws + align256((size_t)n_heads * max_ctx * 4));
-  float* pv = (float*)((char*)esum + align256((size_t)n_heads * max_chunks * 4));
-  {
-    const size_t smem = (size_t)kFastChunk * 4 + (size_t)kPvStages * kPvRows * 64 * esz;
-    int grid = n_heads * ngr * max_chunks;
-    const int cap = tosk_num_sms() * 8;
-    if (grid > cap) grid = cap;
-    void* args[] = {&S, (void*)&vc, &n_heads, &n_kv, &hd, (void*)&pos_dev, &pos, &max_ctx, &esum, &pv, (void*)&max_chunks};
-    int e = esz == 2 ? launch_k(fast_partial_kernel<2>, grid, 32, smem, pdl, st, args)
-                     : launch_k(fast_partial_kernel<4>, grid, 32, smem, pdl, st, args);
-    if (e) return e;
-  }
-  void* args[] = {&esum, &pv, &n_heads, &hd, (void*)&pos_dev, &pos, (void*)&max_chunks, &out};
-  return launch_k(fast_combine_kernel, n_heads, 128, 0, pdl, st, args);
+  return 0;
 }
+
+
 
 // ---------------------------------------------------------------------------
 // Allocation-free entry point

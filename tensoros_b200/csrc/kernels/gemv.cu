@@ -1,4 +1,4 @@
-// gemv.cu - exact Q4_0 / Q8_0 GEMV for sm_100a (TensorOS runtime/nn llm_gemv).
+// gemv.cu - Q4_0 / Q8_0 GEMV for sm_100a (TensorOS runtime/nn llm_gemv), EXACT and FAST.
 //
 // Reference semantics (runtime/nn/llm.c):
 //   q4_0_dot32 / q8_0_dot32 (llm.c:148-209): per 32-weight block, eight lane
@@ -11,36 +11,42 @@
 //
 // Design (B200):
 //   * Weights are repacked once into two planes: quants [rows][nb][16|32 B]
-//     and fp16 scales [rows][nbp] (nbp = nb rounded up to 8).  Every 8-row
-//     tile of either plane is one contiguous, 16-byte aligned range, so it is
-//     fetched with a single cp.async.bulk into shared memory.  Algorithmic
-//     bytes are the GGUF bytes (18 or 34 per block).
-//   * One persistent CTA per SM owns a contiguous row range.  Warp 0 is the
-//     producer: it streams 8-row stages through an S-deep shared-memory ring
-//     (mbarrier complete_tx).  Weights do not depend on the previous kernel, so
-//     the ring fills before griddepcontrol.wait returns (PDL overlap).
-//   * Compute warps: thread (block b, row group g) keeps x[32b..32b+31] in
-//     registers for the whole kernel (optionally RMS-normalised in the
-//     prologue, llm.c:416-442) and computes the exact block values of its
-//     rows with packed f32x2 IEEE ops: nibble/byte -> float via the 2^23 magic
-//     (exact), products and lane chains in the reference order.  Values go to
-//     a shared "partials" tile P[8][nb].
-//   * Two chain warps take alternate stages; lane r of a chain warp adds the
-//     nb partials of row r serially (the reference's row chain), then runs the
-//     fused epilogue (plain store, residual add, RoPE + KV-cache store, or
-//     SiLU(gate)*up).
+//     and fp16 scales [rows][nbp] (nbp = nb rounded up to 8).  Every run of
+//     rows of either plane is one contiguous, 16-byte aligned range, so a
+//     stage of up to 16 rows is fetched with two cp.async.bulk copies.
+//     Algorithmic bytes are the GGUF bytes (18 or 34 per block).
+//   * One persistent CTA per SM owns a contiguous row range.  Warp 0 fills an
+//     S-deep shared-memory ring of stages (mbarrier complete_tx); weights do
+//     not depend on the previous kernel, so the ring fills before
+//     griddepcontrol.wait returns (programmatic dependent launch).  The
+//     compute warp that releases a slot last refills it.
+//   * x arrives by one bulk copy (after the first stage, ahead of the rest of
+//     the ring), is RMS-normalised in place when the norm is fused
+//     (llm.c:416-442), and is swizzled so that every lane reads its block
+//     from distinct banks.
+//   * Compute warps: thread (block b, row group g) keeps its block of x in
+//     registers for the whole kernel and writes one value per (row, block)
+//     of every stage to a shared "partials" tile P[tr][nb].
+//       EXACT: the reference block value with packed f32x2 IEEE ops
+//         (nibble/byte -> float via the 2^23 magic, lane chains in order).
+//       FAST: integer dot products on 24-bit fixed-point x
+//         (gemv_fastmath.cuh); the swizzle pass turns each block of x into
+//         its fixed-point record cooperatively.
+//   * Four chain warps take stages in turn.  EXACT: lane r adds the nb
+//     partials of row r serially (the reference's row chain).  FAST: lanes
+//     split a stage's rows and blocks, four running sums each, then a
+//     butterfly (fixed order: results are deterministic).  Then the fused
+//     epilogue: plain store, residual add, RoPE + KV-cache store, or
+//     SiLU(gate)*up.
 //   Every mbarrier wait is bounded (tos::mbar_wait) and reports through *err.
-#include <cuda_runtime.h>
-
-#include "tos_dev.cuh"
-#include "tos_kernels.h"
+#include "gemv_common.cuh"
+#include "gemv_fastmath.cuh"
 
 namespace tos {
 
-constexpr int kTR = 8;    // rows per stage
-constexpr int kNCH = 2;   // chain warps (each row chain is serial; two keep pace with the
-                          // compute warps and leave the CTA small enough (<= 12 warps,
-                          // ~85 registers) for the next kernel's CTA to co-reside)
+constexpr int kTR = 16;   // most rows per stage
+constexpr int kNCH = 4;   // chain warps: an EXACT row chain is serial (~1 us per stage of 128
+                          // blocks), so four partial buffers keep the compute warps fed
 
 // Exact block dot, Q4_0.  q holds qs[0..15]; word k = bytes 4k..4k+3 covers
 // elements 8k..8k+7; byte j of the word gives element 8k+2j (low nibble) and
@@ -109,24 +115,6 @@ __device__ __forceinline__ float dot_q8_0(const uint4 qa, const uint4 qb, const 
   return __fmul_rn(r, d);
 }
 
-struct GemvArgs {
-  const uint8_t* qs;
-  const uint16_t* sc;
-  const float* x;
-  const float* norm_w;
-  float eps;
-  float* out;
-  int* err;
-  int R, nb, nbp, cols;
-  int unit;      // CTA row ranges are multiples of `unit` rows
-  int S;         // ring depth
-  int pstride;   // partials row stride (floats)
-  int nwb, rg;   // compute warps per row of blocks, row groups
-  int tr;        // rows per stage (<= kTR)
-  uint32_t off_x, off_w, off_p, off_st, stage_bytes, stage_sc_off;
-  tosk_epi_t epi;
-};
-
 template <int QB>
 __device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t* sts, int r, int b,
                                              int nb, int nbp, const float (&x)[32]) {
@@ -140,23 +128,30 @@ __device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t*
   }
 }
 
-// CTA named barrier over n threads.  The non-.aligned form: threads of one
-// warp may reach it from divergent paths (e.g. the lanes that ran a serial
-// chain and those that did not); callers still reconverge with __syncwarp.
-__device__ __forceinline__ void named_sync(int id, int n) {
-  __syncwarp();
-  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+// (Capping registers at 72 so that two CTAs share an SM made every stage ~25%
+// slower than the overlap it buys; one CTA per SM keeps ~85 registers.)
+template <int QB>
+__device__ __forceinline__ float block_value_fast(const uint8_t* stq, const uint16_t* sts, int r, int b,
+                                                  int nb, int nbp, const XFix& f) {
+  const float d = h2f(sts[r * nbp + b]);
+  if constexpr (QB == 16) {
+    const uint4 q = *reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 16);
+    return fast_q4_0(q, d, f);
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 32);
+    return fast_q8_0(p[0], p[1], d, f);
+  }
 }
 
-template <int QB, bool kNorm, int kEpi>
-__global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
+template <int QB, bool kNorm, int kEpi, bool kFast>
+__global__ void __launch_bounds__(704, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = a.S;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + S;
-  uint64_t* pfull = empty + S;
+  int* slot_cnt = reinterpret_cast<int*>(full + S);   // S ints (room for S mbarriers)
+  uint64_t* pfull = full + 2 * S;
   uint64_t* pempty = pfull + kNCH;
   uint64_t* xbar = pempty + kNCH;
   float* misc = reinterpret_cast<float*>(xbar + 1);
@@ -177,12 +172,9 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
 
   int* s_failed = reinterpret_cast<int*>(misc + 6);
   if (threadIdx.x == 0) {
-    // An earlier kernel whose bounded wait ran out leaves *err set: skip the
-    // work so one failure cannot turn into a chain of timeouts.
-    *s_failed = a.err ? *reinterpret_cast<volatile int*>(a.err) : 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ncw);
+      slot_cnt[s] = 0;
     }
     for (int c = 0; c < kNCH; ++c) {
       mbar_init(&pfull[c], ncw);
@@ -194,41 +186,29 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
   }
   __syncthreads();
   pdl_trigger();
-  if (*s_failed) return;
 
   volatile int* xflag = reinterpret_cast<volatile int*>(misc + 7);
   if (warp == 0) {
-    // ---------------- weight producer ----------------
+    // ---------------- initial ring fill ----------------
     if (lane == 0) {
       // Weights do not depend on earlier kernels, so the ring fills at once.
-      // After the first stage the producer gives the x copy (issued by the
-      // first chain warp once the previous kernel is complete) up to ~1.5 us
-      // to enter the copy queue first: x gates all compute, and copies
-      // complete roughly in issue order.
-      int issued = 0;
-      for (int it = 0; it < nst; ++it) {
-        const int s = it % S;
+      // After the first stage the x copy (issued by the first chain warp once
+      // the previous kernel is complete) gets up to ~1.5 us to enter the copy
+      // queue first: x gates all compute, and copies complete roughly in
+      // issue order.  Later refills are issued by the compute warp that
+      // releases a slot last, so no thread has to win issue slots from the
+      // compute warps to keep the ring moving.
+      const int first = min(S, nst);
+      for (int it = 0; it < first; ++it) {
         if (it == 1) {
           const long long t0 = clock64();
           while (*xflag == 0 && clock64() - t0 < 3000) {
           }
           if constexpr (kNorm) bulk_g2s(ws, a.norm_w, (uint32_t)(a.cols * 4), xbar);
         }
-        if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.err, 1)) break;
-        const int r0 = rb + it * tr;
-        const int n = min(tr, re - r0);
-        const uint32_t bq = (uint32_t)(n * nb * QB);
-        const uint32_t bs = (uint32_t)(n * nbp * 2);
-        uint8_t* st = stages + (size_t)s * a.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], bq + bs);
-        bulk_g2s(st, a.qs + (size_t)r0 * nb * QB, bq, &full[s]);
-        bulk_g2s(st + a.stage_sc_off, a.sc + (size_t)r0 * nbp, bs, &full[s]);
-        issued = it + 1;
+        issue_stage<QB>(a, stages, full, it, it, rb, re);
       }
-      if (kNorm && nst <= 1) bulk_g2s(ws, a.norm_w, (uint32_t)(a.cols * 4), xbar);
-      // Leave only when every copy issued into this CTA's ring has landed.
-      for (int it = max(0, issued - S); it < issued; ++it)
-        mbar_wait(&full[it % S], (it / S) & 1, a.err, 5);
+      if (kNorm && first <= 1) bulk_g2s(ws, a.norm_w, (uint32_t)(a.cols * 4), xbar);
       mbar_wait(xbar, 0, a.err, 6);
     }
     return;
@@ -242,10 +222,29 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
     mbar_arrive_expect_tx(xbar, (uint32_t)(a.cols * 4) * (kNorm ? 2u : 1u));
     bulk_g2s(xs, a.x, (uint32_t)(a.cols * 4), xbar);
     *xflag = 1;
+    // An earlier kernel whose bounded wait ran out leaves *err set: this
+    // one then skips its work, so one failure cannot turn into a chain of
+    // timeouts.  Read once the earlier kernels are complete, while x is in
+    // flight (checked after the next CTA barrier).
+    *s_failed = a.err ? *reinterpret_cast<volatile int*>(a.err) : 0;
   }
   if (!mbar_wait(xbar, 0, a.err, 7)) return;   // x has landed in shared memory
   float ss = 1.0f;
-  if constexpr (kNorm) {
+  if constexpr (kFast && kNorm) {
+    // RMSNorm (llm.c:416-442) scale from a tree sum of squares: per-thread
+    // strided sums, warp sums, then the warp partials in warp order
+    float* wpart = misc + 8;
+    float q = 0.0f;
+    for (int i = threadIdx.x - 32; i < a.cols; i += nthr) q = fmaf(xs[i], xs[i], q);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) wpart[warp - 1] = q;
+    named_sync(1, nthr);
+    float s2 = 0.0f;
+    for (int i = 0; i < nthr / 32; ++i) s2 += wpart[i];
+    ss = 1.0f / sqrtf(s2 / (float)a.cols + a.eps);
+  }
+  if constexpr (kNorm && !kFast) {
     // llm.c:421-427: lane l sums x[4i+l]^2 serially.  Each of four lanes
     // reads x four elements at a time (a broadcast load), squares its own
     // element and adds it; loads are batched ahead of the dependent adds.
@@ -297,13 +296,42 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
           v.w = __fmul_rn(__fmul_rn(v.w, ss), wv.w);
         }
       }
-      __syncwarp();
-      if (t < nchunk) {
-        const int blk = t >> 3, c = t & 7;
-        x4[(blk << 3) | (c ^ (blk & 7))] = v;
+      if constexpr (kFast) {
+        // FAST: the block becomes its fixed-point record in place (128 B:
+        // limb words 0..23, c, s), 16-byte chunk j at slot j ^ (b & 7)
+        uint32_t w0, w1, w2;
+        int wi, csum;
+        float sc;
+        xfix_group<QB>(v, t & 7, w0, w1, w2, wi, csum, sc);
+        __syncwarp();
+        if (t < nchunk) {
+          const int blk = t >> 3;
+          uint32_t* rec = reinterpret_cast<uint32_t*>(xs) + 32 * blk;
+          const int sw = blk & 7;
+          auto put = [&](int word, uint32_t val) { rec[(((word >> 2) ^ sw) << 2) | (word & 3)] = val; };
+          put(wi, w0);
+          put(8 + wi, w1);
+          put(16 + wi, w2);
+          if ((t & 7) == 0) {
+            put(24, (uint32_t)csum);
+            put(25, __float_as_uint(sc));
+          }
+        }
+      } else {
+        __syncwarp();
+        if (t < nchunk) {
+          const int blk = t >> 3, c = t & 7;
+          x4[(blk << 3) | (c ^ (blk & 7))] = v;
+        }
       }
     }
     named_sync(1, nthr);
+  }
+  if (*s_failed) {
+    // skip the work, but let the stages already in flight land first
+    const int first = min(S, nst);
+    for (int s = 0; s < first; ++s) mbar_wait(&full[s], 0, nullptr, 0);
+    return;
   }
 
   if (warp >= 1 + kNCH) {
@@ -314,14 +342,31 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
     const int g = ct / bw;
     const bool valid = b < nb;
     float xr[32];
+    XFix xf;
 #pragma unroll
     for (int i = 0; i < 32; ++i) xr[i] = 0.0f;
     if (valid) {
-      const float4* xv = reinterpret_cast<const float4*>(xs) + 8 * b;
+      const uint4* xv = reinterpret_cast<const uint4*>(xs) + 8 * b;
+      if constexpr (kFast) {
+        // the block's fixed-point record (chunks 0..6 of 8)
+        uint32_t wds[28];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = xv[i ^ (b & 7)];
-        xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
+        for (int j = 0; j < 7; ++j) {
+          const uint4 u = xv[j ^ (b & 7)];
+          wds[4 * j] = u.x; wds[4 * j + 1] = u.y; wds[4 * j + 2] = u.z; wds[4 * j + 3] = u.w;
+        }
+#pragma unroll
+        for (int l = 0; l < 3; ++l)
+#pragma unroll
+          for (int w = 0; w < 8; ++w) xf.l[l][w] = wds[8 * l + w];
+        xf.c = (int)wds[24];
+        xf.s = __uint_as_float(wds[25]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = *reinterpret_cast<const float4*>(&xv[i ^ (b & 7)]);
+          xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
+        }
       }
     }
     for (int it = 0; it < nst; ++it) {
@@ -332,23 +377,40 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
       const int n = min(tr, re - (rb + it * tr));
       const uint8_t* stq = stages + (size_t)s * a.stage_bytes;
       const uint16_t* sts = reinterpret_cast<const uint16_t*>(stq + a.stage_sc_off);
-      float* Pc = P + c * kTR * a.pstride;
+      float* Pc = P + c * tr * a.pstride;
       if (valid) {
         // two rows per iteration: independent dot chains interleave
         const int rg = a.rg;
         int r = g;
-        for (; r + rg < n; r += 2 * rg) {
-          const float y0 = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
-          const float y1 = block_value<QB>(stq, sts, r + rg, b, nb, nbp, xr);
-          Pc[r * a.pstride + b] = y0;
-          Pc[(r + rg) * a.pstride + b] = y1;
+        if constexpr (kFast) {
+          for (; r + rg < n; r += 2 * rg) {
+            const float y0 = block_value_fast<QB>(stq, sts, r, b, nb, nbp, xf);
+            const float y1 = block_value_fast<QB>(stq, sts, r + rg, b, nb, nbp, xf);
+            Pc[r * a.pstride + b] = y0;
+            Pc[(r + rg) * a.pstride + b] = y1;
+          }
+          if (r < n) Pc[r * a.pstride + b] = block_value_fast<QB>(stq, sts, r, b, nb, nbp, xf);
+        } else {
+          for (; r + rg < n; r += 2 * rg) {
+            const float y0 = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
+            const float y1 = block_value<QB>(stq, sts, r + rg, b, nb, nbp, xr);
+            Pc[r * a.pstride + b] = y0;
+            Pc[(r + rg) * a.pstride + b] = y1;
+          }
+          if (r < n) Pc[r * a.pstride + b] = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
         }
-        if (r < n) Pc[r * a.pstride + b] = block_value<QB>(stq, sts, r, b, nb, nbp, xr);
       }
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&empty[s]);
         mbar_arrive(&pfull[c]);
+        // release slot s; the last of the compute warps refills it
+        if (atomicAdd(&slot_cnt[s], 1) == ncw - 1) {
+          slot_cnt[s] = 0;
+          if (it + S < nst) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_stage<QB>(a, stages, full, it + S, s, rb, re);
+          }
+        }
       }
     }
     return;
@@ -362,9 +424,27 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
     if (!mbar_wait(&pfull[cw], (it / kNCH) & 1, a.err, 4)) break;
     const int r0 = rb + it * tr;
     const int n = min(tr, re - r0);
-    const float* Pr = P + (cw * kTR + min(lane, kTR - 1)) * a.pstride;
+    const float* Pr = P + (cw * tr + min(lane, tr - 1)) * a.pstride;
     float y = 0.0f;  // llm.c:223: sum = 0.0f, then += block value, in block order
-    if (lane < n) {
+    if constexpr (kFast) {
+      // tree sum: lane = (row lane % tr, segment lane / tr); four running sums
+      // per lane over its segment, then a butterfly across the segments
+      const int nseg = 32 / tr;
+      const int seg = lane / tr;
+      const int L = (((nb + nseg - 1) / nseg) + 3) & ~3;
+      const int j0 = min(nb, seg * L), j1 = min(nb, seg * L + L);
+      const float* Prow = P + (cw * tr + lane % tr) * a.pstride;
+      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+      int j = j0;
+      for (; j + 4 <= j1; j += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(Prow + j);
+        s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
+      }
+      for (; j < j1; ++j) s0 += Prow[j];
+      float t = (s0 + s1) + (s2 + s3);
+      for (int o = tr; o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      y = t;
+    } else if (lane < n) {
       // loads batched ahead of the dependent adds (the chain itself is serial)
       int bb = 0;
       for (; bb + 32 <= nb; bb += 32) {
@@ -390,44 +470,7 @@ __global__ void __launch_bounds__(640, 1) gemv_kernel(const GemvArgs a) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&pempty[cw]);
-    const int r = r0 + lane;
-    if constexpr (kEpi == TOSK_EPI_STORE) {
-      if (lane < n) a.out[r] = y;
-    } else if constexpr (kEpi == TOSK_EPI_RESID) {
-      if (lane < n) a.out[r] = __fadd_rn(a.epi.resid[r], y);  // llm.c:599-614
-    } else if constexpr (kEpi == TOSK_EPI_SWIGLU) {
-      // llm.c:726-729: g = silu(g); g *= u
-      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
-      if (lane < n && (r & 1) == 0) a.out[r >> 1] = __fmul_rn(ref_silu(y), partner);
-    } else if constexpr (kEpi == TOSK_EPI_QKV) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
-      const int qr = a.epi.q_rows, kr = a.epi.kv_rows, hd = a.epi.hd;
-      if (lane < n) {
-        float v = y;
-        if (r < qr + kr) {
-          // llm.c:488-492 (RoPE on q and k rows, adjacent pairs)
-          const int i = (r < qr ? r : r - qr) % hd;
-          const float2 cs = a.epi.rope_cs[(size_t)pos * (hd >> 1) + (i >> 1)];
-          if ((i & 1) == 0)
-            v = __fsub_rn(__fmul_rn(y, cs.x), __fmul_rn(partner, cs.y));
-          else
-            v = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(y, cs.x));
-        }
-        if (r < qr) {
-          a.out[r] = v;
-        } else {
-          // llm.c:673-681: store k, v at [pos][kv_dim]
-          const bool is_k = r < qr + kr;
-          const int e = is_k ? r - qr : r - qr - kr;
-          void* cache = is_k ? a.epi.k_cache : a.epi.v_cache;
-          const size_t idx = (size_t)pos * kr + e;
-          if (a.epi.kv_type == TOSK_F16)
-            reinterpret_cast<uint16_t*>(cache)[idx] = f2h(v);
-          else
-            reinterpret_cast<float*>(cache)[idx] = v;
-        }
-      }
-    }
+    gemv_epilogue<kEpi>(a, y, r0, n, lane, pos);
   }
 }
 
@@ -550,15 +593,15 @@ extern "C" int tosk_qmat_repack(tosk_qmat_t* m, const void* const* src, const in
   return 0;
 }
 
-template <int QB, bool kNorm, int kEpi>
+template <int QB, bool kNorm, int kEpi, bool kFast>
 static int launch_gemv(const GemvArgs& a, int grid, int threads, size_t smem, int pdl,
                        cudaStream_t st) {
-  static bool configured = false;
-  auto kern = gemv_kernel<QB, kNorm, kEpi>;
-  if (!configured) {
+  static bool done = false;
+  auto kern = gemv_kernel<QB, kNorm, kEpi, kFast>;
+  if (!done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return (int)e;
-    configured = true;
+    done = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -573,22 +616,22 @@ static int launch_gemv(const GemvArgs& a, int grid, int threads, size_t smem, in
   return (int)cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int QB>
+template <int QB, bool kFast>
 static int dispatch_gemv(const GemvArgs& a, bool norm, int epi, int grid, int threads, size_t smem,
                          int pdl, cudaStream_t st) {
   if (norm) {
     switch (epi) {
-      case TOSK_EPI_STORE: return launch_gemv<QB, true, TOSK_EPI_STORE>(a, grid, threads, smem, pdl, st);
-      case TOSK_EPI_QKV: return launch_gemv<QB, true, TOSK_EPI_QKV>(a, grid, threads, smem, pdl, st);
-      case TOSK_EPI_SWIGLU: return launch_gemv<QB, true, TOSK_EPI_SWIGLU>(a, grid, threads, smem, pdl, st);
+      case TOSK_EPI_STORE: return launch_gemv<QB, true, TOSK_EPI_STORE, kFast>(a, grid, threads, smem, pdl, st);
+      case TOSK_EPI_QKV: return launch_gemv<QB, true, TOSK_EPI_QKV, kFast>(a, grid, threads, smem, pdl, st);
+      case TOSK_EPI_SWIGLU: return launch_gemv<QB, true, TOSK_EPI_SWIGLU, kFast>(a, grid, threads, smem, pdl, st);
       default: return (int)cudaErrorInvalidValue;
     }
   }
   switch (epi) {
-    case TOSK_EPI_STORE: return launch_gemv<QB, false, TOSK_EPI_STORE>(a, grid, threads, smem, pdl, st);
-    case TOSK_EPI_RESID: return launch_gemv<QB, false, TOSK_EPI_RESID>(a, grid, threads, smem, pdl, st);
-    case TOSK_EPI_QKV: return launch_gemv<QB, false, TOSK_EPI_QKV>(a, grid, threads, smem, pdl, st);
-    case TOSK_EPI_SWIGLU: return launch_gemv<QB, false, TOSK_EPI_SWIGLU>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_STORE: return launch_gemv<QB, false, TOSK_EPI_STORE, kFast>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_RESID: return launch_gemv<QB, false, TOSK_EPI_RESID, kFast>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_QKV: return launch_gemv<QB, false, TOSK_EPI_QKV, kFast>(a, grid, threads, smem, pdl, st);
+    case TOSK_EPI_SWIGLU: return launch_gemv<QB, false, TOSK_EPI_SWIGLU, kFast>(a, grid, threads, smem, pdl, st);
     default: return (int)cudaErrorInvalidValue;
   }
 }
@@ -596,8 +639,9 @@ static int dispatch_gemv(const GemvArgs& a, bool norm, int epi, int grid, int th
 static inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t* norm, float* out,
-                         const tosk_epi_t* epi, int* err, int pdl, cudaStream_t st) {
+                         const tosk_epi_t* epi, int mode, int* err, int pdl, cudaStream_t st) {
   if (!w || !x || !out) return (int)cudaErrorInvalidValue;
+  if (mode != TOSK_GEMV_EXACT && mode != TOSK_GEMV_FAST) return (int)cudaErrorInvalidValue;
   // x and the norm weights are fetched with bulk copies: 16-byte alignment
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (norm && (reinterpret_cast<uintptr_t>(norm->norm_w) & 15)))
     return (int)cudaErrorInvalidValue;
@@ -621,32 +665,32 @@ extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t
   a.nwb = (w->nb + 31) / 32;
   // cols > 16*1024 would need several blocks per thread: not supported
   if (a.nwb > 16) return (int)cudaErrorInvalidValue;
-  // About 16 compute warps per CTA (one CTA per SM) for latency hiding:
-  // row groups split a stage's rows between warps holding the same blocks.
-  a.rg = a.nwb >= 8 ? 1 : (8 / a.nwb);
+  // Row groups split a stage's rows between warps holding the same blocks,
+  // each thread taking tr/rg rows of every stage.  EXACT: ~8 compute warps
+  // per CTA (one CTA per SM); FAST (cheaper block values): ~16.
+  const int want = mode == TOSK_GEMV_FAST ? 16 : 8;
+  a.rg = a.nwb >= want ? 1 : (want / a.nwb);
   if (a.rg > kTR) a.rg = kTR;
   const int threads = 32 * (1 + kNCH + a.nwb * a.rg);
   a.pstride = (int)round_up((uint32_t)w->nb, 8) + 4;
-  const uint32_t hdr = 320;   // up to 2*8 + 2*kNCH + 1 mbarriers and 8 floats
+  const uint32_t hdr = 384;   // up to 2*8 + 2*kNCH + 1 mbarriers, 8 floats, 24 warp partials
   a.off_x = hdr;
   const uint32_t xbytes = round_up((uint32_t)w->cols * 4, 128);
   a.off_w = 0;
   a.off_p = a.off_x + xbytes;
-  // the partials area also holds the RMSNorm weights until the x pass
-  uint32_t pbytes = (uint32_t)(kNCH * kTR * a.pstride * 4);
-  if (fuse_norm && pbytes < (uint32_t)w->cols * 4) pbytes = (uint32_t)w->cols * 4;
-  pbytes = round_up(pbytes, 128);
-  a.off_st = a.off_p + pbytes;
-  // ~110 KB lets the next kernel's CTA (programmatic dependent launch)
-  // co-reside and prefetch its own weights; a CTA of more than 11 warps
-  // (~88 registers each) cannot share an SM's register file anyway, so it
-  // takes a deeper ring instead.
+  // ~200 KB of shared memory (one CTA per SM).  Rows per stage: 16 unless two
+  // stages of long rows and their partials would not fit; paired epilogues
+  // (RoPE, SiLU*up) need an even count.
   const uint32_t budget_hi = 227 * 1024;
-  const uint32_t budget_lo = threads > 352 ? 200 * 1024 : 110 * 1024;
-  // Rows per stage: 8 unless two stages of very long rows would not fit.
-  // Paired epilogues (RoPE, SiLU*up) need an even count.
+  const uint32_t budget_lo = 200 * 1024;
+  uint32_t pbytes = 0;
   a.tr = kTR;
   for (;;) {
+    pbytes = (uint32_t)(kNCH * a.tr * a.pstride * 4);
+    // the partials area also holds the RMSNorm weights until the x pass
+    if (fuse_norm && pbytes < (uint32_t)w->cols * 4) pbytes = (uint32_t)w->cols * 4;
+    pbytes = round_up(pbytes, 128);
+    a.off_st = a.off_p + pbytes;
     const uint32_t qbytes = (uint32_t)(a.tr * w->nb * w->qb);
     a.stage_sc_off = round_up(qbytes, 16);
     a.stage_bytes = round_up(a.stage_sc_off + (uint32_t)(a.tr * w->nbp * 2), 128);
@@ -657,19 +701,24 @@ extern "C" int tosk_gemv(const tosk_qmat_t* w, const float* x, const tosk_norm_t
   if (S < 2) S = 2;
   if (S > 8) S = 8;
   if (a.off_st + (uint32_t)S * a.stage_bytes > budget_hi) return (int)cudaErrorInvalidValue;
-  // header holds 2*S + 2*kNCH barriers + 8 floats
-  if ((uint32_t)(8 * (2 * S + 2 * kNCH + 1) + 32) > hdr) return (int)cudaErrorInvalidValue;
+  // header holds 2*S + 2*kNCH barriers, 8 floats and 24 warp partials
+  if ((uint32_t)(8 * (2 * S + 2 * kNCH + 1) + 32 + 96) > hdr || threads / 32 - 1 > 24)
+    return (int)cudaErrorInvalidValue;
   a.S = S;
   const size_t smem = a.off_st + (size_t)S * a.stage_bytes;
   // layout checks: every region inside its own range
   if (a.off_x + (uint32_t)w->cols * 4 > a.off_p || a.off_p + pbytes > a.off_st ||
-      a.off_p + (uint32_t)(kNCH * kTR * a.pstride * 4) > a.off_st || smem > budget_hi)
+      a.off_p + (uint32_t)(kNCH * a.tr * a.pstride * 4) > a.off_st || smem > budget_hi)
     return (int)cudaErrorInvalidValue;
   const int NU = (a.R + a.unit - 1) / a.unit;
   int grid = tosk_num_sms();
   if (grid > NU) grid = NU;
-  if (w->qb == 16) return dispatch_gemv<16>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
-  return dispatch_gemv<32>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
+  const bool fast = mode == TOSK_GEMV_FAST;
+  if (w->qb == 16)
+    return fast ? dispatch_gemv<16, true>(a, fuse_norm, kind, grid, threads, smem, pdl, st)
+                : dispatch_gemv<16, false>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
+  return fast ? dispatch_gemv<32, true>(a, fuse_norm, kind, grid, threads, smem, pdl, st)
+              : dispatch_gemv<32, false>(a, fuse_norm, kind, grid, threads, smem, pdl, st);
 }
 
 extern "C" int tosk_block_dots(const void* blocks, int type, const float* x, int n_blocks, float* out,

@@ -171,10 +171,10 @@ class Model:
     """tos_model_t built from a workloads.SynthModel (or any arrays with the
     same fields); mirrors llm_forward_token / greedy llm_generate."""
 
-    def __init__(self, synth, attn_mode: int = 0, kv_type: int | None = None):
+    def __init__(self, synth, attn_mode: int = 0, kv_type: int | None = None, gemv_mode: int = 0):
         self.synth = synth
         self.desc = _ffi.ModelDesc()
-        synth.fill_desc(self.desc, attn_mode=attn_mode, kv_type=kv_type)
+        synth.fill_desc(self.desc, attn_mode=attn_mode, kv_type=kv_type, gemv_mode=gemv_mode)
         h = C.c_void_p()
         st = _lib().tos_model_create(C.byref(h), C.byref(self.desc))
         _check("tos_model_create", st)

@@ -128,7 +128,7 @@ class SynthModel:
         self._keep.append(arr)
         return arr
 
-    def fill_desc(self, desc, attn_mode: int = 0, kv_type: int | None = None):
+    def fill_desc(self, desc, attn_mode: int = 0, kv_type: int | None = None, gemv_mode: int = 0):
         """Fill a ctypes struct with tos_model_desc_t / orc_model_desc_t fields."""
         c = self.cfg
         desc.dim = c["dim"]; desc.n_layers = c["n_layers"]; desc.n_heads = c["n_heads"]
@@ -137,6 +137,8 @@ class SynthModel:
         desc.kv_type = c["kv_type"] if kv_type is None else kv_type
         if hasattr(desc, "attn_mode"):
             desc.attn_mode = attn_mode
+        if hasattr(desc, "gemv_mode"):
+            desc.gemv_mode = gemv_mode
         desc.wtype = c["wtype"]; desc.embd_type = c["embd_type"]; desc.out_type = c["out_type"]
         desc.token_embd = _ptr(self.token_embd)
         desc.output_weight = _ptr(self.output) if self.output is not None else None
