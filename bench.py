@@ -24,7 +24,9 @@ batch 1.  A step is one decoded token.
              compiled hosted) on one host core, rank 0 at N=1.
 
 --impl reference times that reference CPU implementation alone.
-With --gpus N > 1 every rank runs an independent replica (weak scaling).
+With --gpus N > 1 the model is row-sharded over the N GPUs (one process per
+GPU, NCCL all-gathers) and decodes one sequence: value is that sequence's
+tokens/s (strong scaling).
 """
 from __future__ import annotations
 
@@ -160,7 +162,7 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, random-init weights)",
         "config": {"workload": "llama2-7b-shape-q4_0 decode, batch 1", "global_batch": 1,
                    "seq_len": args.prefill, "parallelism": "none (CPU)"},
@@ -229,7 +231,10 @@ def run_ours(args, world, rank, local):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        # no NVLink multicast (NVLS) objects: a rank that dies while bound to
+        # one can fault its peers
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     from tensoros_b200 import lib as _lib
     from tensoros_b200 import ops
     from tensoros_b200 import workloads as W
@@ -287,16 +292,25 @@ def run_ours(args, world, rank, local):
         barrier()
         return e0.elapsed_time(e1), e2.elapsed_time(e3), ids
 
+    def shard():
+        """row-sharding over the ranks (one sequence, NCCL all-gathers); a
+        fresh communicator id for every model"""
+        if world == 1:
+            return None
+        obj = [ops.nccl_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(obj, src=0)
+        return (rank, world, obj[0])
+
     # ---- value / e2e: the selected arithmetic
     clk = ClockSampler(local)
-    model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast))
+    model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard())
     t_ms, t_e2e, ids = timed_decode(model, clk)
     model.close()
     # ---- the bit-exact path on the same prompt: its speed, and whether the
     # greedy ids agree (EXACT equals the reference bit for bit)
     exact_ms, exact_ids = None, None
     if fast and not args.no_exact:
-        model = ops.Model(synth)
+        model = ops.Model(synth, shard=shard())
         exact_ms, _, exact_ids = timed_decode(model)
         model.close()
     if world > 1:
@@ -304,8 +318,9 @@ def run_ours(args, world, rank, local):
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         t_ms, t_e2e = float(tt[0]), float(tt[1])
         exact_ms = float(tt[2]) if exact_ms is not None else None
-    value = world * K / (t_ms / 1000.0)
-    e2e = world * K / (t_e2e / 1000.0)
+    # one sequence whatever the GPU count (row-sharded): tokens of the job
+    value = K / (t_ms / 1000.0)
+    e2e = K / (t_e2e / 1000.0)
 
     res = {}
     if rank == 0:
@@ -325,13 +340,14 @@ def run_ours(args, world, rank, local):
         res = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": warm, "ms_per_step": t_ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init Q4_0 weights; BASELINE distributions)",
             "config": {"workload": "llama2-7b-shape-q4_0 greedy decode, batch 1, after a 128-token prefill",
-                       "model": cfg["name"], "global_batch": world, "seq_len": args.prefill,
+                       "model": cfg["name"], "global_batch": 1, "seq_len": args.prefill,
                        "kv_cache": "fp16, capacity 4096", "arithmetic": args.math,
                        "positions": [args.prefill + warm, args.prefill + warm + K - 1],
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"row-sharded x{world} (heads, rows, vocabulary; NCCL all-gather)"
+                                       if world > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches,
@@ -342,10 +358,10 @@ def run_ours(args, world, rank, local):
                          # of this kernel and shape (profiles/gemv_q4_0_4096x4096.md)
                          "traffic": 9485568,
                          "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
-            "decode_weight_gbs": weight_bytes * value / world / 1e9,
+            "decode_weight_gbs": weight_bytes * value / 1e9,   # all GPUs together
             "clocks": clk.summary(),
             "exact": None if exact_ms is None else {
-                "value": world * K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
+                "value": K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
                 "greedy_ids_identical": exact_ids == ids, "ids_compared": len(ids)},
             "cpu_baseline": cpu,
             "setup_s": round(t_gen, 1),

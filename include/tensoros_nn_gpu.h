@@ -115,6 +115,11 @@ int tos_axpy_dev(float *dst, float s, const float *src, int n, void *stream);
 int tos_dot_dev(const float *a, const float *b, int n, float *out, void *stream);
 int tos_embed_dev(float *out, const void *embd, int type, int dim, int token, void *stream);
 int tos_argmax_dev(const float *x, int n, int *out_index, void *stream);
+/* The distributed argmax of a row-sharded model, on one device: x is cut into
+ * `world` equal slices, each slice gives a (value, index) pair and the pairs
+ * reduce with llm_argmax's rule (llm.c:1129-1140); same kernels as a sharded
+ * model's last step.  No counterpart in the reference. */
+int tos_argmax_sharded_dev(const float *x, int n, int world, int *out_index, void *stream);
 
 /* Single-query attention over a KV cache [ctx][n_kv*head_dim] (kv_type F32 or
  * F16) for query heads q[n_heads*head_dim] at position pos (attends t<=pos),
@@ -212,6 +217,42 @@ void *tos_model_stream(const tos_model_t *m);
 /* device pointer of the last logits (vocab_size floats) */
 const float *tos_model_logits_dev(const tos_model_t *m);
 size_t tos_model_device_bytes(const tos_model_t *m);
+
+/* ------------------------------------------ multi-GPU (one node, NCCL)
+ * No counterpart in the reference (a single-CPU decoder).  A model is
+ * row-sharded over `world` ranks, one process and one GPU per rank: rank r
+ * keeps heads, residual rows, FFN rows and vocabulary rows
+ * [r*n/world, (r+1)*n/world) of each projection and its heads' KV cache;
+ * the slices produced by each GEMV are all-gathered, and the greedy token is
+ * a distributed argmax.  Rows are computed exactly as on one GPU, so every
+ * rank's logits and tokens equal the one-GPU model's (bit-identical in EXACT
+ * mode).  Every rank passes the full host weights (the GGUF tensors of the
+ * one-GPU descriptor) and uploads only its rows. */
+typedef struct {
+    int world, rank;
+    int head0, n_heads;            /* query heads */
+    int kv_head0, n_kv_heads;      /* key/value heads (and KV cache) */
+    int q_row0, n_q_rows;          /* rows of wq = heads * head_dim */
+    int kv_row0, n_kv_rows;        /* rows of wk / wv */
+    int row0, n_rows;              /* rows of wo and wdown (residual stream) */
+    int ff0, n_ff;                 /* rows of wgate / wup */
+    int vocab0, n_vocab;           /* LM-head rows */
+} tos_shard_plan_t;
+
+/* [begin, begin+count) of `total` for `rank`: equal slices of whole `unit`s;
+ * TOS_ENOTSUP when total is not a multiple of unit*world */
+int tos_shard_range(int total, int unit, int world, int rank, int *begin, int *count);
+/* the rows rank `rank` of `world` keeps (heads whole, other slices in
+ * multiples of 32 rows) */
+int tos_shard_plan(const tos_model_desc_t *desc, int world, int rank, tos_shard_plan_t *plan);
+/* NCCL unique id (NCCL_UNIQUE_ID_BYTES = 128) for tos_model_create_sharded:
+ * made by one rank and handed to all (NCCL is loaded at run time) */
+int tos_nccl_unique_id(void *id, size_t bytes);
+/* Collective: every rank calls it with the same descriptor and id, on its
+ * own current device (tos_init(local_gpu) first).  world == 1 is
+ * tos_model_create. */
+int tos_model_create_sharded(tos_model_t **m, const tos_model_desc_t *desc, int rank, int world,
+                             const void *nccl_id);
 
 #ifdef __cplusplus
 }

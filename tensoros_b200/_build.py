@@ -37,7 +37,7 @@ CC_FLAGS = ["-std=c11", "-O2", "-fPIC", "-Wall", "-Wno-unused-function", "-D_GNU
             "-I" + str(CSRC / "include"), "-I" + str(INC), "-I" + str(Path(CUDA_HOME) / "include")]
 
 NN_CU = sorted((CSRC / "kernels").glob("*.cu"))
-NN_C = [CSRC / "host" / "tos_runtime.c", CSRC / "host" / "tos_model.c"]
+NN_C = [CSRC / "host" / "tos_runtime.c", CSRC / "host" / "tos_model.c", CSRC / "host" / "tos_shard.c"]
 SYNTH_C = [CSRC / "host" / "tos_synth.c"]
 HEADERS = (sorted((CSRC / "include").glob("*")) + sorted((CSRC / "kernels").glob("*.cuh"))
            + sorted(INC.glob("*.h")))
@@ -110,7 +110,7 @@ def build_nn(verbose=False, jobs=None) -> Path:
         if p.wait() != 0:
             raise RuntimeError("compile failed")
     tmp = LIB_NN.with_suffix(".so.tmp")
-    _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", tmp] + objs + ["-lpthread"], verbose)
+    _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", tmp] + objs + ["-lpthread", "-ldl"], verbose)
     os.replace(tmp, LIB_NN)
     _stamp(LIB_NN, digest)
     return LIB_NN

@@ -36,6 +36,13 @@ class ModelDesc(C.Structure):
     ]
 
 
+class ShardPlan(C.Structure):
+    """tos_shard_plan_t"""
+    _fields_ = [(n, i32) for n in ("world", "rank", "head0", "n_heads", "kv_head0", "n_kv_heads", "q_row0",
+                                   "n_q_rows", "kv_row0", "n_kv_rows", "row0", "n_rows", "ff0", "n_ff",
+                                   "vocab0", "n_vocab")]
+
+
 # name -> (restype, argtypes)
 NN_FUNCS = {
     "tos_status_string": (C.c_char_p, [i32]),
@@ -93,6 +100,11 @@ NN_FUNCS = {
     "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),
+    "tos_shard_range": (i32, [i32, i32, i32, i32, ip, ip]),
+    "tos_shard_plan": (i32, [C.POINTER(ModelDesc), i32, i32, C.POINTER(ShardPlan)]),
+    "tos_nccl_unique_id": (i32, [vp, sz]),
+    "tos_model_create_sharded": (i32, [C.POINTER(vp), C.POINTER(ModelDesc), i32, i32, vp]),
+    "tos_argmax_sharded_dev": (i32, [vp, i32, i32, vp, vp]),
 }
 
 SYNTH_FUNCS = {

@@ -37,4 +37,9 @@ cudaStream_t tos_pick_stream(void *s);
 #define TOS_MAX_POS (1 << 20)
 int tos_rope_args_ok(int pos, float base);
 
+/* NCCL plumbing (tos_shard.c) */
+int tos_nccl_comm_init(void **comm, int world, int rank, const void *id);
+void tos_nccl_comm_destroy(void *comm);
+int tos_nccl_all_gather(const void *send, void *recv, size_t count, int is_int, void *comm, cudaStream_t st);
+
 #endif

@@ -18,6 +18,13 @@
  * Weights are uploaded from the caller's GGUF buffers and repacked into the
  * GEMV plane layout: q|k|v rows concatenated, gate/up rows interleaved
  * (row 2i = gate i, row 2i+1 = up i) so the SiLU*up epilogue sees both.
+ *
+ * Sharded over G GPUs (tos_model_create_sharded; plan in tos_shard.c) each
+ * rank keeps its slice of rows of every projection and its heads' KV cache,
+ * and the stream adds four in-place all-gathers per layer (attention output,
+ * residual after o, SwiGLU output, residual after down) and, after the LM
+ * head, an all-gather of the ranks' (value, index) argmax pairs; the plain
+ * (non-chained) step also gathers the logits for tos_model_forward_token.
  */
 #include <stdlib.h>
 #include <string.h>
@@ -26,13 +33,17 @@
 
 struct tos_model {
     tos_model_desc_t d;
-    int hd, kv_dim, q_dim, esz;
+    tos_shard_plan_t sp;      /* this rank's rows (everything when world == 1) */
+    void *comm;               /* NCCL communicator when world > 1 */
+    int hd, kv_dim, q_dim, esz;   /* kv_dim, q_dim: this rank's rows */
     tosk_qmat_t *wqkv, *wo, *wgu, *wdown;
     tosk_qmat_t lm;
     void *embd;
     float *norms;             /* [n_layers][2][dim], then output norm [dim] */
     void *kc, *vc;            /* [n_layers][max_seq][kv_dim] */
-    float *x, *q, *att, *h, *logits;
+    float *x, *q, *att, *h, *logits;   /* x, att, h: full vectors; q, logits: local rows */
+    float *logits_full;       /* sharded: gathered logits */
+    int *pairs;               /* sharded: [world][2] argmax (value bits, index) */
     float2 *rope;             /* [max_seq][hd/2] */
     void *ws;
     size_t ws_bytes;
@@ -95,8 +106,10 @@ void tos_model_destroy(tos_model_t *m)
 {
     if (!m) return;
     if (m->st) cudaStreamSynchronize(m->st);
+    /* graphs holding collectives go before the communicator */
     if (m->have_graph) cudaGraphExecDestroy(m->gexec);
     if (m->have_chain) cudaGraphExecDestroy(m->gexec_chain);
+    if (m->comm) tos_nccl_comm_destroy(m->comm);
     for (int L = 0; m->wqkv && L < m->d.n_layers; L++) {
         tosk_qmat_free(&m->wqkv[L]);
         tosk_qmat_free(&m->wo[L]);
@@ -106,7 +119,7 @@ void tos_model_destroy(tos_model_t *m)
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
-                    m->rope, m->ws, m->io, m->ring};
+                    m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
     if (m->io_host) cudaFreeHost(m->io_host);
@@ -137,23 +150,33 @@ static int validate(const tos_model_desc_t *d)
     return TOS_OK;
 }
 
-int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
+static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, int rank, const void *nccl_id)
 {
     if (!out) return tos_set_status(TOS_EINVAL);
     *out = NULL;
     int rc = validate(d);
     if (rc) return tos_set_status(rc);
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) return tos_set_status(TOS_EINVAL);
     rc = tos_ensure_init();
+    if (rc) return tos_set_status(rc);
+    tos_shard_plan_t sp;
+    rc = tos_shard_plan(d, world, rank, &sp);
     if (rc) return tos_set_status(rc);
     tos_model_t *m = (tos_model_t *)calloc(1, sizeof(*m));
     if (!m) return tos_set_status(TOS_ENOMEM);
     m->d = *d;
+    m->sp = sp;
     const int L = d->n_layers, dim = d->dim, ff = d->ff_dim;
     m->hd = dim / d->n_heads;
-    m->q_dim = d->n_heads * m->hd;
-    m->kv_dim = d->n_kv_heads * m->hd;
+    m->q_dim = sp.n_q_rows;
+    m->kv_dim = sp.n_kv_rows;
     m->esz = d->kv_type == TOS_TYPE_F16 ? 2 : 4;
+    const int full_q = d->n_heads * m->hd;
     int e = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking);
+    if (!e && world > 1) {
+        rc = tos_nccl_comm_init(&m->comm, world, rank, nccl_id);
+        if (rc) { tos_model_destroy(m); return tos_set_status(rc); }
+    }
     m->wqkv = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
     m->wo = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
     m->wgu = (tosk_qmat_t *)calloc((size_t)L, sizeof(tosk_qmat_t));
@@ -170,21 +193,26 @@ int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
     if (t > stage_b) stage_b = t;
     t = 2 * AL256(qrow_bytes(dim, wt) * (size_t)ff); if (t > stage_b) stage_b = t;
     t = AL256(qrow_bytes(ff, wt) * (size_t)dim); if (t > stage_b) stage_b = t;
-    t = AL256(qrow_bytes(m->q_dim, wt) * (size_t)dim); if (t > stage_b) stage_b = t;
+    t = AL256(qrow_bytes(full_q, wt) * (size_t)dim); if (t > stage_b) stage_b = t;
     t = AL256(qrow_bytes(dim, ht) * (size_t)d->vocab_size); if (t > stage_b) stage_b = t;
 #undef AL256
     void *stage = NULL;
     if (!e) e = cudaMalloc(&stage, stage_b);
 
+    /* this rank's rows of each GGUF matrix (row-major: a row range is one
+     * contiguous byte range) */
+#define ROWS(p, r0, cols, type) ((const char *)(p) + (size_t)(r0) * qrow_bytes((cols), (type)))
     for (int l = 0; !e && l < L; l++) {
-        const void *qkv[3] = {d->wq[l], d->wk[l], d->wv[l]};
+        const void *qkv[3] = {ROWS(d->wq[l], sp.q_row0, dim, wt), ROWS(d->wk[l], sp.kv_row0, dim, wt),
+                              ROWS(d->wv[l], sp.kv_row0, dim, wt)};
         int rq[3] = {m->q_dim, m->kv_dim, m->kv_dim};
         e = upload_qmat(m, &m->wqkv[l], qkv, rq, 3, 0, wt, dim, stage);
-        if (!e) { const void *s1[1] = {d->wo[l]}; int r1[1] = {dim}; e = upload_qmat(m, &m->wo[l], s1, r1, 1, 0, wt, m->q_dim, stage); }
-        if (!e) { const void *gu[2] = {d->wgate[l], d->wup[l]}; int r2[2] = {ff, ff}; e = upload_qmat(m, &m->wgu[l], gu, r2, 2, 1, wt, dim, stage); }
-        if (!e) { const void *s1[1] = {d->wdown[l]}; int r1[1] = {dim}; e = upload_qmat(m, &m->wdown[l], s1, r1, 1, 0, wt, ff, stage); }
+        if (!e) { const void *s1[1] = {ROWS(d->wo[l], sp.row0, full_q, wt)}; int r1[1] = {sp.n_rows}; e = upload_qmat(m, &m->wo[l], s1, r1, 1, 0, wt, full_q, stage); }
+        if (!e) { const void *gu[2] = {ROWS(d->wgate[l], sp.ff0, dim, wt), ROWS(d->wup[l], sp.ff0, dim, wt)}; int r2[2] = {sp.n_ff, sp.n_ff}; e = upload_qmat(m, &m->wgu[l], gu, r2, 2, 1, wt, dim, stage); }
+        if (!e) { const void *s1[1] = {ROWS(d->wdown[l], sp.row0, ff, wt)}; int r1[1] = {sp.n_rows}; e = upload_qmat(m, &m->wdown[l], s1, r1, 1, 0, wt, ff, stage); }
     }
-    if (!e) { const void *s1[1] = {head}; int r1[1] = {d->vocab_size}; e = upload_qmat(m, &m->lm, s1, r1, 1, 0, ht, dim, stage); }
+    if (!e) { const void *s1[1] = {ROWS(head, sp.vocab0, dim, ht)}; int r1[1] = {sp.n_vocab}; e = upload_qmat(m, &m->lm, s1, r1, 1, 0, ht, dim, stage); }
+#undef ROWS
     if (stage) cudaFree(stage);
 
     size_t eb = embd_row_bytes(dim, d->embd_type) * (size_t)d->vocab_size;
@@ -208,10 +236,12 @@ int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
     if (!e) e = dmalloc(m, (void **)&m->q, (size_t)mx * 4);
     if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
     if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
-    if (!e) e = dmalloc(m, (void **)&m->logits, (size_t)d->vocab_size * 4);
+    if (!e) e = dmalloc(m, (void **)&m->logits, (size_t)sp.n_vocab * 4);
+    if (!e && world > 1) e = dmalloc(m, (void **)&m->logits_full, (size_t)d->vocab_size * 4);
+    if (!e && world > 1) e = dmalloc(m, (void **)&m->pairs, (size_t)world * 2 * sizeof(int));
     if (!e) e = dmalloc(m, (void **)&m->rope, (size_t)d->max_seq * (m->hd / 2) * sizeof(float2));
     if (!e) e = tosk_rope_table(m->rope, d->max_seq, m->hd, d->rope_base, m->st);
-    m->ws_bytes = tosk_attention_ws_bytes(d->n_heads, d->max_seq);
+    m->ws_bytes = tosk_attention_ws_bytes(sp.n_heads, d->max_seq);
     if (!e) e = dmalloc(m, &m->ws, m->ws_bytes);
     if (!e) e = dmalloc(m, (void **)&m->io, 8 * sizeof(int));
     if (!e) e = cudaMemset(m->io, 0, 8 * sizeof(int));
@@ -226,8 +256,22 @@ int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
     return tos_set_status(TOS_OK);
 }
 
+int tos_model_create(tos_model_t **out, const tos_model_desc_t *d)
+{
+    return create_impl(out, d, 1, 0, NULL);
+}
+
+int tos_model_create_sharded(tos_model_t **out, const tos_model_desc_t *d, int rank, int world,
+                             const void *nccl_id)
+{
+    return create_impl(out, d, world, rank, nccl_id);
+}
+
 size_t tos_model_device_bytes(const tos_model_t *m) { return m ? m->dev_bytes : 0; }
-const float *tos_model_logits_dev(const tos_model_t *m) { return m ? m->logits : NULL; }
+const float *tos_model_logits_dev(const tos_model_t *m)
+{
+    return m ? (m->sp.world > 1 ? m->logits_full : m->logits) : NULL;
+}
 
 int tos_model_reset(tos_model_t *m)
 {
@@ -237,6 +281,17 @@ int tos_model_reset(tos_model_t *m)
     if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
     if (!e) e = cudaStreamSynchronize(m->st);
     return tos_set_status(tos_from_cuda(e));
+}
+
+/* In-place all-gather: this rank's count floats sit at full + rank*count. */
+static int gather(tos_model_t *m, float *full, int count)
+{
+    return tos_nccl_all_gather(full + (size_t)m->sp.rank * count, full, (size_t)count, 0, m->comm, m->st);
+}
+
+static int gather_to(tos_model_t *m, const float *mine, float *full, int count)
+{
+    return tos_nccl_all_gather(mine, full, (size_t)count, 0, m->comm, m->st);
 }
 
 /* Enqueue one token step; reads the token from io[0] (io[2] when chained:
@@ -249,6 +304,8 @@ static int enqueue_token(tos_model_t *m, int chained)
     int *err = m->io + 3;
     const int pdl = 1;
     const int dim = d->dim;
+    const tos_shard_plan_t *sp = &m->sp;
+    const int G = sp->world;
     size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
     int e = tosk_embed(m->x, m->embd, d->embd_type, dim, chained ? m->io + 2 : m->io, 0, pdl, st);
     for (int l = 0; !e && l < d->n_layers; l++) {
@@ -265,24 +322,37 @@ static int enqueue_token(tos_model_t *m, int chained)
         qkv.k_cache = (char *)m->kc + kv_layer * l;
         qkv.v_cache = (char *)m->vc + kv_layer * l;
         e = tosk_gemv(&m->wqkv[l], m->x, &n1, m->q, &qkv, d->gemv_mode, err, pdl, st);
-        if (!e) e = tosk_attention(m->att, m->q, qkv.k_cache, qkv.v_cache, d->kv_type, d->n_heads,
-                                   d->n_kv_heads, m->hd, m->io + 1, 0, d->max_seq, d->attn_mode, m->ws,
+        float *att = m->att + sp->q_row0;   /* this rank's heads of the full output */
+        if (!e) e = tosk_attention(att, m->q, qkv.k_cache, qkv.v_cache, d->kv_type, sp->n_heads,
+                                   sp->n_kv_heads, m->hd, m->io + 1, 0, d->max_seq, d->attn_mode, m->ws,
                                    m->ws_bytes, err, pdl, st);
+        if (!e && G > 1) e = gather(m, m->att, sp->n_q_rows);
         tosk_epi_t res;
         memset(&res, 0, sizeof(res));
         res.kind = TOSK_EPI_RESID;
-        res.resid = m->x;
-        if (!e) e = tosk_gemv(&m->wo[l], m->att, NULL, m->x, &res, d->gemv_mode, err, pdl, st);
+        res.resid = m->x + sp->row0;
+        if (!e) e = tosk_gemv(&m->wo[l], m->att, NULL, m->x + sp->row0, &res, d->gemv_mode, err, pdl, st);
+        if (!e && G > 1) e = gather(m, m->x, sp->n_rows);
         tosk_norm_t n2 = {m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps};
         tosk_epi_t sw;
         memset(&sw, 0, sizeof(sw));
         sw.kind = TOSK_EPI_SWIGLU;
-        if (!e) e = tosk_gemv(&m->wgu[l], m->x, &n2, m->h, &sw, d->gemv_mode, err, pdl, st);
-        if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x, &res, d->gemv_mode, err, pdl, st);
+        if (!e) e = tosk_gemv(&m->wgu[l], m->x, &n2, m->h + sp->ff0, &sw, d->gemv_mode, err, pdl, st);
+        if (!e && G > 1) e = gather(m, m->h, sp->n_ff);
+        if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x + sp->row0, &res, d->gemv_mode, err, pdl, st);
+        if (!e && G > 1) e = gather(m, m->x, sp->n_rows);
     }
     tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps};
     if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, d->gemv_mode, err, pdl, st);
-    if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
+    if (G == 1) {
+        if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
+    } else {
+        int *mine = m->pairs + 2 * sp->rank;
+        if (!e) e = tosk_argmax_slice(m->logits, sp->n_vocab, sp->vocab0, sp->rank == 0, mine, pdl, st);
+        if (!e) e = tos_nccl_all_gather(mine, m->pairs, 2, 1, m->comm, st);
+        if (!e) e = tosk_argmax_pairs(m->pairs, G, m->io + 2, pdl, st);
+        if (!e && !chained) e = gather_to(m, m->logits, m->logits_full, sp->n_vocab);
+    }
     if (!e && chained) e = tosk_decode_advance(m->io, m->ring, pdl, st);
     return e;
 }
@@ -326,7 +396,8 @@ static int finish(tos_model_t *m, float *logits, int *next)
 {
     int e = cudaMemcpyAsync(m->io_host + 2, m->io + 2, 2 * sizeof(int), cudaMemcpyDeviceToHost, m->st);
     if (!e && logits)
-        e = cudaMemcpyAsync(logits, m->logits, (size_t)m->d.vocab_size * 4, cudaMemcpyDeviceToHost, m->st);
+        e = cudaMemcpyAsync(logits, m->sp.world > 1 ? m->logits_full : m->logits, (size_t)m->d.vocab_size * 4,
+                            cudaMemcpyDeviceToHost, m->st);
     if (!e) e = cudaStreamSynchronize(m->st);
     if (e) return tos_from_cuda(e);
     if (m->io_host[3] != 0) {

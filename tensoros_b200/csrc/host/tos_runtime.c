@@ -44,6 +44,7 @@ const char *tos_status_string(int st)
 int tos_from_cuda(int e)
 {
     if (e == cudaSuccess) return TOS_OK;
+    if (e < 0) return e;   /* already a tos_status_t (e.g. TOS_ENCCL from a collective) */
     if (e == cudaErrorMemoryAllocation) return TOS_ENOMEM;
     if (e == cudaErrorInvalidValue) return TOS_EINVAL;
     if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return TOS_ENODEV;
@@ -357,6 +358,24 @@ int tos_argmax_dev(const float *x, int n, int *out_index, void *stream)
     DEV_PROLOGUE();
     if (!x || n <= 0 || !out_index) return tos_set_status(TOS_EINVAL);
     return tos_set_status(tos_from_cuda(tosk_argmax(x, n, out_index, NULL, 0, tos_pick_stream(stream))));
+}
+
+int tos_argmax_sharded_dev(const float *x, int n, int world, int *out_index, void *stream)
+{
+    DEV_PROLOGUE();
+    if (!x || n <= 0 || world <= 0 || n % world || !out_index) return tos_set_status(TOS_EINVAL);
+    cudaStream_t st = tos_pick_stream(stream);
+    /* the pairs live in the library scratch: order after the caller's stream */
+    if (st != tos_g.stream && cudaStreamSynchronize(st) != cudaSuccess) return tos_set_status(TOS_ECUDA);
+    int *pairs = (int *)tos_scratch((size_t)world * 2 * sizeof(int));
+    if (!pairs) return tos_set_status(TOS_ENOMEM);
+    const int per = n / world;
+    int e = 0;
+    for (int r = 0; !e && r < world; r++)
+        e = tosk_argmax_slice(x + (size_t)r * per, per, r * per, r == 0, pairs + 2 * r, 0, st);
+    if (!e) e = tosk_argmax_pairs(pairs, world, out_index, 0, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    return tos_set_status(tos_from_cuda(e));
 }
 
 size_t tos_attention_workspace_bytes(int n_heads, int max_ctx)

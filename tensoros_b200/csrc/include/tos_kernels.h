@@ -107,6 +107,11 @@ int tosk_dot(const float *a, const float *b, int n, float *out, cudaStream_t st)
 int tosk_embed(float *out, const void *embd, int type, int dim, const int *tok_dev, int tok,
                int pdl, cudaStream_t st);
 int tosk_argmax(const float *x, int n, int *out_idx, float *out_val, int pdl, cudaStream_t st);
+/* one rank's slice of a row-sharded vector: pair = {value bits, index+offset
+ * or -1}; first_rule for the slice that starts the vector (rank 0) */
+int tosk_argmax_slice(const float *x, int n, int offset, int first_rule, int *pair, int pdl, cudaStream_t st);
+/* reduce world pairs (rank order) to the reference's argmax */
+int tosk_argmax_pairs(const int *pairs, int world, int *out_idx, int pdl, cudaStream_t st);
 /* io[2] -> ring[io[4]]; io[4] += 1; io[1] += 1 (device-side greedy chaining) */
 int tosk_decode_advance(int *io, int *ring, int pdl, cudaStream_t st);
 

@@ -205,9 +205,14 @@ __device__ __forceinline__ void arg_combine(float& v, int& i, float v2, int i2) 
   }
 }
 
+// first_rule: the reference's rule for a whole vector (x[0] wins when it is
+// NaN or nothing beats it).  Without it (a later slice of a row-sharded
+// vector) the result is the first non-NaN maximum, or index -1.  Indices are
+// reported plus `offset`.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int n,
                                                       int* __restrict__ out_idx,
-                                                      float* __restrict__ out_val) {
+                                                      float* __restrict__ out_val, int first_rule,
+                                                      int offset) {
   __shared__ float sv[32];
   __shared__ int si[32];
   pdl_wait();
@@ -265,14 +270,37 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
       arg_combine(v, idx, v2, i2);
     }
     if (lane == 0) {
-      const float x0 = x[0];
-      if (x0 != x0 || idx < 0) {
-        idx = 0;
-        v = x0;
+      if (first_rule) {
+        const float x0 = x[0];
+        if (x0 != x0 || idx < 0) {
+          idx = 0;
+          v = x0;
+        }
       }
-      *out_idx = idx;
+      *out_idx = idx < 0 ? -1 : idx + offset;
       if (out_val) *out_val = v;
     }
+  }
+  pdl_trigger();
+}
+
+// Distributed argmax: (value bits, index) pairs of the ranks' vocabulary
+// slices in rank order (rank 0 applied the whole-vector rule); a later slice
+// wins only with a strictly larger value, as in llm.c:1129-1140.
+__global__ void argmax_pairs_kernel(const int* __restrict__ pairs, int world, int* __restrict__ out_idx) {
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    float bv = __int_as_float(pairs[0]);
+    int bi = pairs[1];
+    for (int r = 1; r < world; ++r) {
+      const float v = __int_as_float(pairs[2 * r]);
+      const int i = pairs[2 * r + 1];
+      if (i >= 0 && v > bv) {
+        bv = v;
+        bi = i;
+      }
+    }
+    *out_idx = bi;
   }
   pdl_trigger();
 }
@@ -366,8 +394,24 @@ extern "C" int tosk_embed(float* out, const void* embd, int type, int dim, const
 
 extern "C" int tosk_argmax(const float* x, int n, int* out_idx, float* out_val, int pdl, cudaStream_t st) {
   if (n <= 0) return (int)cudaErrorInvalidValue;
-  void* args[] = {&x, &n, &out_idx, &out_val};
+  int first_rule = 1, offset = 0;
+  void* args[] = {&x, &n, &out_idx, &out_val, &first_rule, &offset};
   return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_argmax_slice(const float* x, int n, int offset, int first_rule, int* pair, int pdl,
+                                 cudaStream_t st) {
+  if (n <= 0 || !pair) return (int)cudaErrorInvalidValue;
+  int* out_idx = pair + 1;
+  float* out_val = reinterpret_cast<float*>(pair);
+  void* args[] = {&x, &n, &out_idx, &out_val, &first_rule, &offset};
+  return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_argmax_pairs(const int* pairs, int world, int* out_idx, int pdl, cudaStream_t st) {
+  if (world <= 0) return (int)cudaErrorInvalidValue;
+  void* args[] = {&pairs, &world, &out_idx};
+  return launch_pdl((const void*)argmax_pairs_kernel, dim3(1), dim3(32), args, pdl, st);
 }
 
 extern "C" int tosk_decode_advance(int* io, int* ring, int pdl, cudaStream_t st) {

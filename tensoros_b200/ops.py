@@ -171,13 +171,22 @@ class Model:
     """tos_model_t built from a workloads.SynthModel (or any arrays with the
     same fields); mirrors llm_forward_token / greedy llm_generate."""
 
-    def __init__(self, synth, attn_mode: int = 0, kv_type: int | None = None, gemv_mode: int = 0):
+    def __init__(self, synth, attn_mode: int = 0, kv_type: int | None = None, gemv_mode: int = 0,
+                 shard: tuple | None = None):
+        """shard = (rank, world, nccl_id bytes): this process's rows of a model
+        row-sharded over `world` GPUs (tos_model_create_sharded)."""
         self.synth = synth
         self.desc = _ffi.ModelDesc()
         synth.fill_desc(self.desc, attn_mode=attn_mode, kv_type=kv_type, gemv_mode=gemv_mode)
         h = C.c_void_p()
-        st = _lib().tos_model_create(C.byref(h), C.byref(self.desc))
-        _check("tos_model_create", st)
+        if shard is None:
+            st = _lib().tos_model_create(C.byref(h), C.byref(self.desc))
+            _check("tos_model_create", st)
+        else:
+            rank, world, nid = shard
+            buf = C.create_string_buffer(bytes(nid), 128)
+            st = _lib().tos_model_create_sharded(C.byref(h), C.byref(self.desc), rank, world, buf)
+            _check("tos_model_create_sharded", st)
         self.h = h
         self.vocab = synth.cfg["vocab_size"]
 
@@ -224,3 +233,21 @@ class Model:
 
     def device_bytes(self) -> int:
         return int(_lib().tos_model_device_bytes(self.h))
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for tos_model_create_sharded."""
+    buf = C.create_string_buffer(128)
+    _check("tos_nccl_unique_id", _lib().tos_nccl_unique_id(buf, 128))
+    return buf.raw
+
+
+def shard_plan(synth_or_cfg, world: int, rank: int) -> dict:
+    """The rows rank `rank` of `world` keeps (tos_shard_plan)."""
+    d = _ffi.ModelDesc()
+    cfg = synth_or_cfg.cfg if hasattr(synth_or_cfg, "cfg") else synth_or_cfg
+    d.dim, d.n_layers, d.n_heads, d.n_kv_heads = cfg["dim"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"]
+    d.ff_dim, d.vocab_size, d.max_seq = cfg["ff_dim"], cfg["vocab_size"], cfg["max_seq"]
+    p = _ffi.ShardPlan()
+    _check("tos_shard_plan", _lib().tos_shard_plan(C.byref(d), world, rank, C.byref(p)))
+    return {name: getattr(p, name) for name, _ in _ffi.ShardPlan._fields_}

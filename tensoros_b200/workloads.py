@@ -101,6 +101,13 @@ LLAMA2_7B = dict(name="llama2-7b-shape-q4_0", dim=4096, n_layers=32, n_heads=32,
                  out_type=TYPE_Q4_0, kv_type=TYPE_F16, max_seq=4096, rope_base=10000.0,
                  norm_eps=1e-6, n_prompt=128, n_gen=256)
 
+# A small grouped-query decoder whose every dimension splits over 1/2/4 ranks
+# in 32-row units (8 heads of 32, 4 kv heads): the multi-GPU parity case.
+SHARD_SMALL = dict(name="shard-small-2L-256d-gqa-q8_0", dim=256, n_layers=2, n_heads=8, n_kv_heads=4,
+                   ff_dim=512, vocab_size=1024, wtype=TYPE_Q8_0, embd_type=TYPE_Q8_0,
+                   out_type=TYPE_Q8_0, kv_type=TYPE_F32, max_seq=64, rope_base=10000.0,
+                   norm_eps=1e-6, n_prompt=8, n_gen=16)
+
 
 def stream_id(layer: int, what: str) -> int:
     names = ["wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "attn_norm", "ffn_norm"]
