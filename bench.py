@@ -224,6 +224,57 @@ def run_gemv_only(args, local):
                       "frac": gbs / peak, "peak_source": peak_kind, "copies": args.gemv_copies}), flush=True)
 
 
+def time_prefill(model, prompt, prompt_next, torch):
+    """The prompt as one batched pass (tos_model_prefill: tensor-core GEMMs),
+    against the token-by-token pass the decode measurement ran."""
+    stream = torch.cuda.ExternalStream(model.stream())
+    times = []
+    nxt = None
+    for rep in range(3):
+        model.reset()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        nxt = model.prefill(prompt, 0)
+        e1.record(stream)
+        e1.synchronize()
+        if rep:
+            times.append(e0.elapsed_time(e1))
+    ms = min(times)
+    return {"tokens": len(prompt), "ms": ms, "tokens_per_s": len(prompt) / (ms / 1000.0),
+            "stepwise_ms": prompt_next["stepwise_s"] * 1000.0,
+            "next_token_identical_to_stepwise": nxt == prompt_next["token"]}
+
+
+def gemm_roofline(lib, torch, m=128, n=22016, k=4096, reps=10):
+    """Isolated tensor-core GEMM of the prefill (gate|up shape)."""
+    import ctypes
+    from tensoros_b200 import workloads as W
+    w = W.q4_0(n, k, W.SEED, 9500)
+    h = ctypes.c_void_p()
+    assert lib.tos_weight_create(ctypes.byref(h), w.ctypes.data, n, k, W.TYPE_Q4_0) == 0
+    try:
+        x = torch.randn(m, k, device="cuda")
+        y = torch.empty(m, n, device="cuda")
+        wsb = lib.tos_gemm_workspace_bytes(m, n, k)
+        ws = torch.empty(wsb + 256, dtype=torch.uint8, device="cuda")
+        wp = (ws.data_ptr() + 255) & ~255
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                assert lib.tos_gemm_dev(h, x.data_ptr(), m, y.data_ptr(), wp, wsb, s.cuda_stream) == 0
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                lib.tos_gemm_dev(h, x.data_ptr(), m, y.data_ptr(), wp, wsb, s.cuda_stream)
+            e1.record(s)
+            e1.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / reps
+    finally:
+        lib.tos_weight_destroy(h)
+    return us, 2.0 * m * n * k
+
+
 def run_ours(args, world, rank, local):
     import numpy as np
     import torch
@@ -256,12 +307,18 @@ def run_ours(args, world, rank, local):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    prompt_next = {}
+
     def timed_decode(model, clk=None):
-        """prefill, W warm-up steps, then K chained steps (value) and K host
-        round-trip steps (e2e); returns (ms, e2e ms, the 2K greedy ids)"""
+        """prompt token by token, W warm-up steps, then K chained steps
+        (value) and K host round-trip steps (e2e); returns (ms, e2e ms, the
+        2K greedy ids)"""
         nxt = 0
+        t0 = time.perf_counter()
         for i, t in enumerate(prompt):
             nxt = model.forward_argmax(int(t), i)
+        prompt_next["stepwise_s"] = time.perf_counter() - t0
+        prompt_next["token"] = nxt
         pos = args.prefill
         toks = model.decode(nxt, pos, warm)
         nxt, pos = int(toks[-1]), pos + warm
@@ -305,6 +362,9 @@ def run_ours(args, world, rank, local):
     clk = ClockSampler(local)
     model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard())
     t_ms, t_e2e, ids = timed_decode(model, clk)
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = time_prefill(model, prompt, prompt_next, torch)
     model.close()
     # ---- the bit-exact path on the same prompt: its speed, and whether the
     # greedy ids agree (EXACT equals the reference bit for bit)
@@ -325,6 +385,15 @@ def run_ours(args, world, rank, local):
     res = {}
     if rank == 0:
         gemv_ms = gemv_roofline(lib, torch, int(fast))
+        if prefill is not None:
+            g_us, g_flops = gemm_roofline(lib, torch)
+            tpeak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+                if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+            prefill["gemm_roofline"] = {
+                "bound": "tensor", "kernel": "gemm_tc_kernel<Q4_0> 128x22016x4096", "launch_us": g_us,
+                "achieved": g_flops / (g_us * 1e-6) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
+                "frac": g_flops / (g_us * 1e-6) / 1e12 / tpeak,
+                "note": "algorithmic 2MNK; the exact fp16 hi/lo split issues 3 MMAs per product"}
         peak, peak_kind = peaks()
         achieved = GEMV_BYTES_4096 / (gemv_ms / 1000.0) / 1e9
         L = cfg["n_layers"]
@@ -359,6 +428,7 @@ def run_ours(args, world, rank, local):
                          "traffic": 9485568,
                          "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
             "decode_weight_gbs": weight_bytes * value / 1e9,   # all GPUs together
+            "prefill": prefill,
             "clocks": clk.summary(),
             "exact": None if exact_ms is None else {
                 "value": K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
@@ -384,6 +454,7 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-exact", action="store_true", help="skip the EXACT-arithmetic comparison run")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill measurement")
     ap.add_argument("--gemv-only", action="store_true",
                     help="time only the isolated Q4_0 4096x4096 GEMV (the roofline leg) and print it")
     ap.add_argument("--gemv-copies", type=int, default=32)

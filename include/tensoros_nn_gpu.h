@@ -100,6 +100,17 @@ int tos_gemv_norm_dev(const tos_weight_t *w, const float *x, const float *norm_w
  * TOS_GEMV_FAST arithmetic; the EXACT form is tos_gemv_dev/tos_gemv_norm_dev */
 int tos_gemv_mode_dev(const tos_weight_t *w, const float *x, const float *norm_w, float eps,
                       float *out, int mode, void *stream);
+/* Batched GEMM for prefill and batched decode: y[m][out_dim] = x[m][in_dim]
+ * W^T for m rows of activations (row-major, device memory), i.e. m calls of
+ * llm_gemv (llm.c:329-349) at once.  No counterpart in the reference (which
+ * runs tokens one by one).  Runs on the tcgen05 tensor cores with an exact
+ * fp16 hi/lo split of the dequantised weights and a 22-bit split of the
+ * activations, fp32 accumulation: normwise error ~1e-6 against the fp32
+ * GEMV.  in_dim a multiple of 64; ws: tos_gemm_workspace_bytes bytes,
+ * 256-byte aligned. */
+size_t tos_gemm_workspace_bytes(int m, int out_dim, int in_dim);
+int tos_gemm_dev(const tos_weight_t *w, const float *x, int m, float *y, void *ws, size_t ws_bytes,
+                 void *stream);
 /* per-block values q4_0_dot32 / q8_0_dot32 (llm.c:148-216) for n_blocks
  * consecutive GGUF blocks against x[32*n_blocks] */
 int tos_block_dots_dev(const void *blocks, int type, const float *x, int n_blocks, float *out,
@@ -212,6 +223,14 @@ int tos_model_generate_greedy(tos_model_t *m, const int *prompt, int n_prompt, i
  * out_tokens[i] (host, copied once at the end).  Same tokens as n_steps
  * calls of tos_model_forward_argmax, without a host round trip per step. */
 int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_tokens);
+/* Batched prompt pass (no counterpart in the reference, which runs the
+ * prompt token by token, llm.c:1279-1281): tokens[0..n) at positions
+ * pos0.. go through every layer together, the projections as tensor-core
+ * GEMMs (tos_gemm_dev numerics) and attention causal per token; the KV cache
+ * is filled for those positions.  logits (may be NULL) and *next (may be
+ * NULL) get the last token's logits and greedy next token.  Needs dim and
+ * ff_dim multiples of 64; not for sharded models (TOS_ENOTSUP). */
+int tos_model_prefill(tos_model_t *m, const int *tokens, int n, int pos0, float *logits, int *next);
 /* the model's CUDA stream (cudaStream_t as void*) */
 void *tos_model_stream(const tos_model_t *m);
 /* device pointer of the last logits (vocab_size floats) */

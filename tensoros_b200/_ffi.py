@@ -97,6 +97,7 @@ NN_FUNCS = {
     "tos_model_forward_argmax": (i32, [vp, i32, i32, ip]),
     "tos_model_generate_greedy": (i32, [vp, vp, i32, i32, vp]),
     "tos_model_decode": (i32, [vp, i32, i32, i32, vp]),
+    "tos_model_prefill": (i32, [vp, vp, i32, i32, vp, ip]),
     "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),
@@ -105,6 +106,8 @@ NN_FUNCS = {
     "tos_nccl_unique_id": (i32, [vp, sz]),
     "tos_model_create_sharded": (i32, [C.POINTER(vp), C.POINTER(ModelDesc), i32, i32, vp]),
     "tos_argmax_sharded_dev": (i32, [vp, i32, i32, vp, vp]),
+    "tos_gemm_workspace_bytes": (sz, [i32, i32, i32]),
+    "tos_gemm_dev": (i32, [vp, vp, i32, vp, vp, sz, vp]),
 }
 
 SYNTH_FUNCS = {

@@ -54,6 +54,12 @@ struct tos_model {
     cudaGraphExec_t gexec, gexec_chain;
     int have_graph, have_chain;
     size_t dev_bytes;
+    /* batched prompt pass (allocated on first use): up to pf_cap tokens */
+    int pf_cap;
+    int *pf_toks;
+    float *pf_x, *pf_xn, *pf_qkv, *pf_q, *pf_att, *pf_gu, *pf_h, *pf_tmp;
+    void *pf_ws;
+    size_t pf_ws_bytes;
 };
 
 static size_t qrow_bytes(int cols, int type)
@@ -119,7 +125,9 @@ void tos_model_destroy(tos_model_t *m)
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
-                    m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring};
+                    m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
+                    m->pf_toks, m->pf_x, m->pf_xn, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
+                    m->pf_tmp, m->pf_ws};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
     if (m->io_host) cudaFreeHost(m->io_host);
@@ -283,6 +291,8 @@ int tos_model_reset(tos_model_t *m)
     return tos_set_status(tos_from_cuda(e));
 }
 
+static int enqueue_head(tos_model_t *m, int chained);
+
 /* In-place all-gather: this rank's count floats sit at full + rank*count. */
 static int gather(tos_model_t *m, float *full, int count)
 {
@@ -342,7 +352,20 @@ static int enqueue_token(tos_model_t *m, int chained)
         if (!e) e = tosk_gemv(&m->wdown[l], m->h, NULL, m->x + sp->row0, &res, d->gemv_mode, err, pdl, st);
         if (!e && G > 1) e = gather(m, m->x, sp->n_rows);
     }
-    tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps};
+    if (!e) e = enqueue_head(m, chained);
+    return e;
+}
+
+/* Final norm, LM head and greedy token (llm.c:737-742, 1129) from m->x. */
+static int enqueue_head(tos_model_t *m, int chained)
+{
+    const tos_model_desc_t *d = &m->d;
+    const tos_shard_plan_t *sp = &m->sp;
+    const int G = sp->world, pdl = 1;
+    cudaStream_t st = m->st;
+    int *err = m->io + 3;
+    int e = 0;
+    tosk_norm_t no = {m->norms + (size_t)2 * d->n_layers * d->dim, d->norm_eps};
     if (!e) e = tosk_gemv(&m->lm, m->x, &no, m->logits, NULL, d->gemv_mode, err, pdl, st);
     if (G == 1) {
         if (!e) e = tosk_argmax(m->logits, d->vocab_size, m->io + 2, NULL, pdl, st);
@@ -476,4 +499,89 @@ int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_t
         return tos_set_status(TOS_ETIMEOUT);
     }
     return tos_set_status(TOS_OK);
+}
+
+/* ---------------------------------------------------------------- prefill */
+
+#define TOS_PF_CAP 128
+
+static int pf_alloc(tos_model_t *m)
+{
+    if (m->pf_cap) return 0;
+    const tos_model_desc_t *d = &m->d;
+    const int C = TOS_PF_CAP, dim = d->dim, ff = d->ff_dim;
+    const int nqkv = m->q_dim + 2 * m->kv_dim;
+    int e = dmalloc(m, (void **)&m->pf_toks, (size_t)C * sizeof(int));
+    if (!e) e = dmalloc(m, (void **)&m->pf_x, (size_t)C * dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_xn, (size_t)C * dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_qkv, (size_t)C * nqkv * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_q, (size_t)C * m->q_dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_att, (size_t)C * m->q_dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_gu, (size_t)C * 2 * ff * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_h, (size_t)C * ff * 4);
+    if (!e) e = dmalloc(m, (void **)&m->pf_tmp, (size_t)C * dim * 4);
+    size_t ws = 0, t;
+    t = tosk_gemm_ws_bytes(C, nqkv, dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, dim, m->q_dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, 2 * ff, dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, dim, ff); if (t > ws) ws = t;
+    if (!e) e = dmalloc(m, &m->pf_ws, ws);
+    if (e) return e;
+    m->pf_ws_bytes = ws;
+    m->pf_cap = C;
+    return 0;
+}
+
+/* n <= TOS_PF_CAP tokens at positions pos0.. through every layer with the
+ * projections as batched tensor-core GEMMs; leaves the last token's row in
+ * m->x. */
+static int pf_chunk(tos_model_t *m, const int *tokens, int n, int pos0)
+{
+    const tos_model_desc_t *d = &m->d;
+    cudaStream_t st = m->st;
+    int *err = m->io + 3;
+    const int dim = d->dim, ff = d->ff_dim, hd = m->hd;
+    const int nqkv = m->q_dim + 2 * m->kv_dim;
+    size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
+    int e = cudaMemcpyAsync(m->pf_toks, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (!e) e = tosk_pf_embed(m->pf_x, m->embd, d->embd_type, dim, m->pf_toks, n, st);
+    for (int l = 0; !e && l < d->n_layers; l++) {
+        void *kc = (char *)m->kc + kv_layer * l, *vc = (char *)m->vc + kv_layer * l;
+        e = tosk_pf_rmsnorm(m->pf_xn, m->pf_x, m->norms + (size_t)(2 * l) * dim, dim, d->norm_eps, n, st);
+        if (!e) e = tosk_gemm_q(&m->wqkv[l], m->pf_xn, n, m->pf_qkv, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_rope_store(m->pf_qkv, m->q_dim, m->kv_dim, hd, m->rope, pos0, m->pf_q, kc, vc,
+                                       d->kv_type, n, st);
+        if (!e) e = tosk_pf_attention(m->pf_q, kc, vc, d->kv_type, d->n_heads, d->n_kv_heads, hd, pos0, n,
+                                      m->pf_att, st);
+        if (!e) e = tosk_gemm_q(&m->wo[l], m->pf_att, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
+        if (!e) e = tosk_pf_rmsnorm(m->pf_xn, m->pf_x, m->norms + (size_t)(2 * l + 1) * dim, dim, d->norm_eps, n, st);
+        if (!e) e = tosk_gemm_q(&m->wgu[l], m->pf_xn, n, m->pf_gu, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_swiglu(m->pf_h, m->pf_gu, (size_t)n * ff, st);
+        if (!e) e = tosk_gemm_q(&m->wdown[l], m->pf_h, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
+    }
+    (void)nqkv;
+    if (!e) e = cudaMemcpyAsync(m->x, m->pf_x + (size_t)(n - 1) * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice, st);
+    return e;
+}
+
+int tos_model_prefill(tos_model_t *m, const int *tokens, int n, int pos0, float *logits, int *next)
+{
+    if (!m || !tokens || n <= 0 || pos0 < 0 || pos0 + n > m->d.max_seq) return tos_set_status(TOS_EINVAL);
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= m->d.vocab_size) return tos_set_status(TOS_EINVAL);
+    /* batched GEMMs take K in 64-column chunks; one rank's model only */
+    if (m->sp.world > 1 || m->d.dim % 64 || m->d.ff_dim % 64 || m->q_dim % 64) return tos_set_status(TOS_ENOTSUP);
+    int e = pf_alloc(m);
+    for (int c0 = 0; !e && c0 < n; c0 += TOS_PF_CAP) {
+        const int nc = n - c0 < TOS_PF_CAP ? n - c0 : TOS_PF_CAP;
+        e = pf_chunk(m, tokens + c0, nc, pos0 + c0);
+        /* the host token buffer is read by the copy above: finish it before
+         * the next chunk reuses the device token array */
+        if (!e) e = cudaStreamSynchronize(m->st);
+    }
+    if (!e) e = enqueue_head(m, 0);
+    if (e) return tos_set_status(tos_from_cuda(e));
+    return tos_set_status(finish(m, logits, next));
 }

@@ -360,6 +360,21 @@ int tos_argmax_dev(const float *x, int n, int *out_index, void *stream)
     return tos_set_status(tos_from_cuda(tosk_argmax(x, n, out_index, NULL, 0, tos_pick_stream(stream))));
 }
 
+size_t tos_gemm_workspace_bytes(int m, int out_dim, int in_dim)
+{
+    return tosk_gemm_ws_bytes(m, out_dim, in_dim);
+}
+
+int tos_gemm_dev(const tos_weight_t *w, const float *x, int m, float *y, void *ws, size_t ws_bytes,
+                 void *stream)
+{
+    DEV_PROLOGUE();
+    if (!w || !x || !y || !ws || m <= 0) return tos_set_status(TOS_EINVAL);
+    if (ws_bytes < tosk_gemm_ws_bytes(m, w->m.rows, w->m.cols)) return tos_set_status(TOS_EINVAL);
+    return tos_set_status(tos_from_cuda(tosk_gemm_q(&w->m, x, m, y, ws, ws_bytes, tos_g.err_dev, 1,
+                                                    tos_pick_stream(stream))));
+}
+
 int tos_argmax_sharded_dev(const float *x, int n, int world, int *out_index, void *stream)
 {
     DEV_PROLOGUE();

@@ -33,7 +33,8 @@ typedef struct {
     int qb;          /* quant bytes per block: 16 (Q4_0) or 32 (Q8_0) */
     uint8_t *qs;     /* [rows][nb][qb] */
     uint16_t *sc;    /* [rows][nbp] fp16 bit patterns */
-    size_t bytes;    /* device bytes held by qs + sc */
+    float *rws;      /* [rows] power-of-two row scales of the tensor-core path */
+    size_t bytes;    /* device bytes held by qs + sc + rws */
 } tosk_qmat_t;
 
 /* ---- weight planes ---- */
@@ -80,6 +81,25 @@ typedef struct {
 enum { TOSK_GEMV_EXACT = 0, TOSK_GEMV_FAST = 1 };
 int tosk_gemv(const tosk_qmat_t *w, const float *x, const tosk_norm_t *norm,
               float *out, const tosk_epi_t *epi, int mode, int *err, int pdl, cudaStream_t st);
+
+/* Y[M][N] = X[M][K] W^T on the tcgen05 tensor cores (fp16 hi/lo split of
+ * dequantised weights and scaled activations, fp32 accumulation; ~1e-6
+ * normwise vs the fp32 GEMV).  X, Y row-major fp32 device memory; ws of
+ * tosk_gemm_ws_bytes(M, N, K) bytes, 256-byte aligned. */
+size_t tosk_gemm_ws_bytes(int M, int N, int K);
+/* batched prompt pass (prefill.cu): n tokens, row-major [n][...] */
+int tosk_pf_embed(float *x, const void *embd, int type, int dim, const int *toks, int n, cudaStream_t st);
+int tosk_pf_rmsnorm(float *y, const float *x, const float *w, int dim, float eps, int n, cudaStream_t st);
+int tosk_pf_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const float2 *cs, int pos0,
+                       float *q_out, void *kc, void *vc, int kv_type, int n, cudaStream_t st);
+int tosk_pf_attention(const float *q, const void *kc, const void *vc, int kv_type, int n_heads, int n_kv,
+                      int hd, int pos0, int n, float *out, cudaStream_t st);
+int tosk_pf_add(float *x, const float *y, size_t n, cudaStream_t st);
+int tosk_pf_swiglu(float *h, const float *gu, size_t n, cudaStream_t st);
+/* m->rws from m->sc (run after the planes are filled) */
+int tosk_qmat_row_scales(tosk_qmat_t *m, cudaStream_t st);
+int tosk_gemm_q(const tosk_qmat_t *w, const float *x, int M, float *y, void *ws, size_t ws_bytes,
+                int *err, int pdl, cudaStream_t st);
 
 /* per-block exact partials: blocks in GGUF layout, n_blocks consecutive,
  * x of length 32*n_blocks, out[n_blocks] (q4_0_dot32 / q8_0_dot32) */

@@ -554,15 +554,19 @@ extern "C" int tosk_qmat_alloc(tosk_qmat_t* m, int type, int rows, int cols) {
   const size_t sbytes = (size_t)rows * m->nbp * 2;
   m->qs = nullptr;
   m->sc = nullptr;
+  m->rws = nullptr;
   cudaError_t e = cudaMalloc((void**)&m->qs, qbytes);
   if (e != cudaSuccess) return (int)e;
   e = cudaMalloc((void**)&m->sc, sbytes);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&m->rws, (size_t)rows * 4);
   if (e != cudaSuccess) {
     cudaFree(m->qs);
+    if (m->sc) cudaFree(m->sc);
     m->qs = nullptr;
+    m->sc = nullptr;
     return (int)e;
   }
-  m->bytes = qbytes + sbytes;
+  m->bytes = qbytes + sbytes + (size_t)rows * 4;
   return (int)cudaMemset(m->sc, 0, sbytes);
 }
 
@@ -570,8 +574,10 @@ extern "C" void tosk_qmat_free(tosk_qmat_t* m) {
   if (!m) return;
   if (m->qs) cudaFree(m->qs);
   if (m->sc) cudaFree(m->sc);
+  if (m->rws) cudaFree(m->rws);
   m->qs = nullptr;
   m->sc = nullptr;
+  m->rws = nullptr;
   m->bytes = 0;
 }
 
@@ -590,7 +596,7 @@ extern "C" int tosk_qmat_repack(tosk_qmat_t* m, const void* const* src, const in
     if (e != cudaSuccess) return (int)e;
     row0 += src_rows[s];
   }
-  return 0;
+  return tosk_qmat_row_scales(m, st);
 }
 
 template <int QB, bool kNorm, int kEpi, bool kFast>

@@ -1,0 +1,246 @@
+// prefill.cu - per-token kernels of the batched prompt pass (prefill): the
+// projections run as tensor-core GEMMs (gemm_tc.cu); these kernels do the
+// row-wise work between them for n tokens at positions pos0 .. pos0+n-1.
+// Reference: llm_forward_token per token (runtime/nn/llm.c:641-743).
+//   pf_embed_kernel      llm_embed (llm.c:365-410), one CTA per token
+//   pf_rmsnorm_kernel    llm_rmsnorm (llm.c:416-452) in the reference's order
+//   pf_rope_store_kernel RoPE of q and k (llm.c:460-500, table of the decode
+//                        path) and the K/V cache store (llm.c:673-681)
+//   pf_attention_kernel  causal single-query attention of every token over
+//                        the cache (llm.c:683-714) with llm_expf weights,
+//                        tree sums (FAST numerics)
+//   pf_add_kernel, pf_swiglu_kernel  residual (llm.c:718, 733) and
+//                        SiLU(gate)*up (llm.c:726-729) with the decode order
+#include <cuda_runtime.h>
+
+#include "tos_dev.cuh"
+#include "tos_kernels.h"
+
+namespace tos {
+
+__device__ __forceinline__ float embed_elem(const uint8_t* embd, int type, int dim, int tok, int i) {
+  if (type == TOSK_Q4_0) {
+    const uint8_t* blk = embd + ((size_t)tok * (dim / 32) + i / 32) * 18;
+    const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+    const int j = i & 31;
+    const uint8_t byte = blk[2 + (j >> 1)];
+    return __fmul_rn((float)(((j & 1) ? (byte >> 4) : (byte & 0x0F)) - 8), d);
+  }
+  if (type == TOSK_Q8_0) {
+    const uint8_t* blk = embd + ((size_t)tok * (dim / 32) + i / 32) * 34;
+    return __fmul_rn((float)(int8_t)blk[2 + (i & 31)], h2f((uint16_t)(blk[0] | (blk[1] << 8))));
+  }
+  if (type == TOSK_F16) return h2f(reinterpret_cast<const uint16_t*>(embd)[(size_t)tok * dim + i]);
+  return reinterpret_cast<const float*>(embd)[(size_t)tok * dim + i];
+}
+
+__global__ void pf_embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ embd, int type, int dim,
+                                const int* __restrict__ toks) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int tok = toks[t];
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)t * dim + i] = embed_elem(embd, type, dim, tok, i);
+}
+
+// The reference's order: four serial lane sums over i = 0, 4, 8, ..., then
+// ((f0+f1)+f2)+f3 and the scalar tail; ss = 1/sqrt(ss/dim + eps); (x*ss)*w.
+__global__ void pf_rmsnorm_kernel(float* __restrict__ y, const float* __restrict__ x, const float* __restrict__ w,
+                                  int dim, float eps) {
+  __shared__ float lanes[4];
+  __shared__ float s_ss;
+  pdl_wait();
+  pdl_trigger();
+  const float* xr = x + (size_t)blockIdx.x * dim;
+  float* yr = y + (size_t)blockIdx.x * dim;
+  if (threadIdx.x < 4) {
+    float acc = 0.0f;
+    for (int i0 = 0; i0 + 4 <= dim; i0 += 4) {
+      const float v = xr[i0 + threadIdx.x];
+      acc = __fadd_rn(acc, __fmul_rn(v, v));
+    }
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = __fadd_rn(__fadd_rn(__fadd_rn(lanes[0], lanes[1]), lanes[2]), lanes[3]);
+    for (int i = dim & ~3; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+  }
+  __syncthreads();
+  const float ss = s_ss;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], ss), w[i]);
+}
+
+// qkv rows [q_rows | kv_rows | kv_rows] per token; q (roped) -> q_out,
+// k (roped) and v -> the caches at position pos0 + t.
+__global__ void pf_rope_store_kernel(const float* __restrict__ qkv, int q_rows, int kv_rows, int hd,
+                                     const float2* __restrict__ cs, int pos0, float* __restrict__ q_out,
+                                     void* __restrict__ kc, void* __restrict__ vc, int kv_type) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int pos = pos0 + t;
+  const int nrow = q_rows + 2 * kv_rows;
+  const float* row = qkv + (size_t)t * nrow;
+  for (int r = threadIdx.x; r < nrow; r += blockDim.x) {
+    const float y = row[r];
+    float v = y;
+    if (r < q_rows + kv_rows) {
+      const float partner = row[r ^ 1];
+      const int i = (r < q_rows ? r : r - q_rows) % hd;
+      const float2 c = cs[(size_t)pos * (hd >> 1) + (i >> 1)];
+      v = (i & 1) == 0 ? __fsub_rn(__fmul_rn(y, c.x), __fmul_rn(partner, c.y))
+                       : __fadd_rn(__fmul_rn(partner, c.y), __fmul_rn(y, c.x));
+    }
+    if (r < q_rows) {
+      q_out[(size_t)t * q_rows + r] = v;
+    } else {
+      const bool is_k = r < q_rows + kv_rows;
+      const int e = is_k ? r - q_rows : r - q_rows - kv_rows;
+      void* cache = is_k ? kc : vc;
+      const size_t idx = (size_t)pos * kv_rows + e;
+      if (kv_type == TOSK_F16)
+        reinterpret_cast<uint16_t*>(cache)[idx] = f2h(v);
+      else
+        reinterpret_cast<float*>(cache)[idx] = v;
+    }
+  }
+}
+
+__device__ __forceinline__ float kv_load(const void* c, int kv_type, size_t idx) {
+  return kv_type == TOSK_F16 ? h2f(reinterpret_cast<const uint16_t*>(c)[idx])
+                             : reinterpret_cast<const float*>(c)[idx];
+}
+
+// One CTA per (head, token): scores over positions 0..pos0+t, llm_expf
+// weights of (s - max), tree sums, sum_j e_j v_j / (sum_j e_j + 1e-10).
+__global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restrict__ q, const void* __restrict__ kc,
+                                                           const void* __restrict__ vc, int kv_type, int n_heads,
+                                                           int n_kv, int hd, int pos0, float* __restrict__ out) {
+  extern __shared__ float sc[];   // [pos0 + n] scores, then weights
+  __shared__ float red[4];
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, t = blockIdx.y;
+  const int n = pos0 + t + 1;
+  const int kvh = h / (n_heads / n_kv);
+  const int kv_dim = n_kv * hd;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* qh = q + ((size_t)t * n_heads + h) * hd;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  for (int j = warp; j < n; j += 4) {
+    float acc = 0.0f;
+    for (int d = lane; d < hd; d += 32) acc = fmaf(qh[d], kv_load(kc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), acc);
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) sc[j] = acc * scale;
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float l = 0.0f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float e = ref_expf(__fsub_rn(sc[j], M));   // llm.c:514-517
+    sc[j] = e;
+    l += e;
+  }
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  const float inv = 1.0f / ((red[0] + red[1]) + (red[2] + red[3]) + 1e-10f);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float a0 = 0.0f, a1 = 0.0f;
+    int j = 0;
+    for (; j + 2 <= n; j += 2) {
+      a0 = fmaf(sc[j], kv_load(vc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), a0);
+      a1 = fmaf(sc[j + 1], kv_load(vc, kv_type, (size_t)(j + 1) * kv_dim + (size_t)kvh * hd + d), a1);
+    }
+    if (j < n) a0 = fmaf(sc[j], kv_load(vc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), a0);
+    out[((size_t)t * n_heads + h) * hd + d] = (a0 + a1) * inv;
+  }
+}
+
+__global__ void pf_add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = __fadd_rn(x[i], y[i]);
+}
+
+// gu rows interleaved (2j = gate j, 2j+1 = up j) -> h[j] = silu(g) * u
+__global__ void pf_swiglu_kernel(float* __restrict__ h, const float* __restrict__ gu, size_t n) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    h[i] = __fmul_rn(ref_silu(gu[2 * i]), gu[2 * i + 1]);
+}
+
+}  // namespace tos
+
+using namespace tos;
+
+namespace {
+int launch_pf(const void* func, dim3 grid, dim3 block, size_t smem, void** args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelExC(&cfg, func, args);
+}
+int ew_grid(size_t n) {
+  size_t g = (n + 255) / 256;
+  return (int)(g > 4096 ? 4096 : (g < 1 ? 1 : g));
+}
+}  // namespace
+
+extern "C" int tosk_pf_embed(float* x, const void* embd, int type, int dim, const int* toks, int n, cudaStream_t st) {
+  void* args[] = {&x, (void*)&embd, &type, &dim, (void*)&toks};
+  return launch_pf((const void*)pf_embed_kernel, dim3(n), dim3(256), 0, args, st);
+}
+
+extern "C" int tosk_pf_rmsnorm(float* y, const float* x, const float* w, int dim, float eps, int n, cudaStream_t st) {
+  void* args[] = {&y, (void*)&x, (void*)&w, &dim, &eps};
+  return launch_pf((const void*)pf_rmsnorm_kernel, dim3(n), dim3(256), 0, args, st);
+}
+
+extern "C" int tosk_pf_rope_store(const float* qkv, int q_rows, int kv_rows, int hd, const float2* cs, int pos0,
+                                  float* q_out, void* kc, void* vc, int kv_type, int n, cudaStream_t st) {
+  void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type};
+  return launch_pf((const void*)pf_rope_store_kernel, dim3(n), dim3(256), 0, args, st);
+}
+
+extern "C" int tosk_pf_attention(const float* q, const void* kc, const void* vc, int kv_type, int n_heads, int n_kv,
+                                 int hd, int pos0, int n, float* out, cudaStream_t st) {
+  const size_t smem = (size_t)(pos0 + n) * 4;
+  if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr && smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               200 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out};
+  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
+}
+
+extern "C" int tosk_pf_add(float* x, const float* y, size_t n, cudaStream_t st) {
+  void* args[] = {&x, (void*)&y, &n};
+  return launch_pf((const void*)pf_add_kernel, dim3(ew_grid(n)), dim3(256), 0, args, st);
+}
+
+extern "C" int tosk_pf_swiglu(float* h, const float* gu, size_t n, cudaStream_t st) {
+  void* args[] = {&h, (void*)&gu, &n};
+  return launch_pf((const void*)pf_swiglu_kernel, dim3(ew_grid(n)), dim3(256), 0, args, st);
+}

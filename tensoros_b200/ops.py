@@ -223,6 +223,16 @@ class Model:
             raise TosError(n, "tos_model_generate_greedy")
         return out[:n]
 
+    def prefill(self, tokens, pos0: int = 0, logits: bool = False):
+        """Batched prompt pass (tos_model_prefill): the greedy next token,
+        and the last token's logits when asked."""
+        p = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.vocab, dtype=np.float32) if logits else None
+        nxt = C.c_int()
+        _check("tos_model_prefill", _lib().tos_model_prefill(self.h, _p(p), len(p), pos0,
+                                                             _p(out) if logits else None, C.byref(nxt)))
+        return (nxt.value, out) if logits else nxt.value
+
     def decode(self, token: int, pos: int, n_steps: int) -> np.ndarray:
         out = np.zeros(max(n_steps, 1), dtype=np.int32)
         _check("tos_model_decode", _lib().tos_model_decode(self.h, token, pos, n_steps, _p(out)))
