@@ -424,8 +424,9 @@ def run_ours(args, world, rank, local):
                          "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak,
                          # dram__bytes_read.sum + dram__bytes_write.sum of one launch
-                         # of this kernel and shape (profiles/gemv_q4_0_4096x4096.md)
-                         "traffic": 9485568,
+                         # of this kernel and shape (profiles/gemv_q4_0_fast_4096x4096.md,
+                         # profiles/gemv_q4_0_4096x4096.md for the exact arithmetic)
+                         "traffic": 9482496 if args.math == "fast" else 9485568,
                          "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
             "decode_weight_gbs": weight_bytes * value / 1e9,   # all GPUs together
             "prefill": prefill,
@@ -458,10 +459,21 @@ def main():
     ap.add_argument("--gemv-only", action="store_true",
                     help="time only the isolated Q4_0 4096x4096 GEMV (the roofline leg) and print it")
     ap.add_argument("--gemv-copies", type=int, default=32)
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time only the prefill tensor-core GEMM (128x22016x4096 Q4_0) and print it")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.gemv_only:
         run_gemv_only(args, local)
+    elif args.gemm_only:
+        import torch
+        from tensoros_b200 import lib as _lib
+        torch.cuda.set_device(local)
+        lib = _lib()
+        assert lib.tos_init(local) == 0, "tos_init failed"
+        us, flops = gemm_roofline(lib, torch)
+        print(json.dumps({"kernel": "gemm_tc Q4_0 128x22016x4096", "launch_us": us,
+                          "TFLOP/s": flops / (us * 1e-6) / 1e12}), flush=True)
     elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
