@@ -360,7 +360,9 @@ def run_ours(args, world, rank, local):
 
     # ---- value / e2e: the selected arithmetic
     clk = ClockSampler(local)
-    model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard())
+    model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(),
+                      fused_step=int(args.fused and fast))
+    fused = model.fused
     t_ms, t_e2e, ids = timed_decode(model, clk)
     prefill = None
     if world == 1 and not args.no_prefill:
@@ -398,8 +400,13 @@ def run_ours(args, world, rank, local):
         achieved = GEMV_BYTES_4096 / (gemv_ms / 1000.0) / 1e9
         L = cfg["n_layers"]
         per_layer = 1 + 2 + 3   # QKV GEMV, attention (2 kernels), o / gate-up / down GEMVs
-        launches = K * (1 + L * per_layer + 3)
+        launches = K if fused else K * (1 + L * per_layer + 3)
         weight_bytes = (L * (4096 * 128 * 18 * 4 + 3 * 11008 * 128 * 18) + 32000 * 128 * 18)
+        # fused step: its own roofline, algorithmic bytes of one token = every
+        # weight plane + the KV rows read and written (fp16) + the embedding
+        # row, norms and the small vectors (<1 MB, ignored)
+        ctx = args.prefill + warm + K // 2
+        step_bytes = weight_bytes + L * 2 * (ctx + 1) * 4096 * 2
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, kind, dt = ref_cpu_decode(synth, args.ref_tokens, args.prefill, 1)
@@ -414,12 +421,18 @@ def run_ours(args, world, rank, local):
             "config": {"workload": "llama2-7b-shape-q4_0 greedy decode, batch 1, after a 128-token prefill",
                        "model": cfg["name"], "global_batch": 1, "seq_len": args.prefill,
                        "kv_cache": "fp16, capacity 4096", "arithmetic": args.math,
+                       "step": "one fused kernel per token" if fused else "a kernel per operator (CUDA graph)",
                        "positions": [args.prefill + warm, args.prefill + warm + K - 1],
                        "parallelism": (f"row-sharded x{world} (heads, rows, vocabulary; NCCL all-gather)"
                                        if world > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches,
+            "step_roofline": None if not fused else {
+                "bound": "hbm", "kernel": "decode_step_kernel (one launch per token)",
+                "achieved": step_bytes / (t_ms / K / 1000.0) / 1e9, "peak": peak, "peak_source": peak_kind,
+                "unit": "GB/s", "frac": step_bytes / (t_ms / K / 1000.0) / 1e9 / peak,
+                "algorithmic_bytes_per_launch": step_bytes, "launch_us": t_ms / K * 1000.0},
             "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
                          "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -454,6 +467,8 @@ def main():
                          "(normwise error <= 1e-4, greedy ids identical)")
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fused", action="store_true",
+                    help="run each token as the one fused persistent kernel (fast arithmetic, one GPU)")
     ap.add_argument("--no-exact", action="store_true", help="skip the EXACT-arithmetic comparison run")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill measurement")
     ap.add_argument("--gemv-only", action="store_true",

@@ -201,6 +201,8 @@ typedef struct {
     const void *const *wup;
     const void *const *wdown;
     int gemv_mode;           /* TOS_GEMV_EXACT (default) or TOS_GEMV_FAST */
+    int fused_step;          /* 1: with FAST arithmetic on one GPU each token runs as one fused
+                                persistent kernel; 0 (default): one kernel per operator */
 } tos_model_desc_t;
 
 typedef struct tos_model tos_model_t;
@@ -236,6 +238,8 @@ void *tos_model_stream(const tos_model_t *m);
 /* device pointer of the last logits (vocab_size floats) */
 const float *tos_model_logits_dev(const tos_model_t *m);
 size_t tos_model_device_bytes(const tos_model_t *m);
+/* 1 when each token runs as the one fused kernel (see fused_step) */
+int tos_model_fused(const tos_model_t *m);
 
 /* ------------------------------------------ multi-GPU (one node, NCCL)
  * No counterpart in the reference (a single-CPU decoder).  A model is

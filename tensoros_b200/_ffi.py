@@ -32,7 +32,7 @@ class ModelDesc(C.Structure):
         ("attn_norm", C.POINTER(vp)), ("ffn_norm", C.POINTER(vp)),
         ("wq", C.POINTER(vp)), ("wk", C.POINTER(vp)), ("wv", C.POINTER(vp)), ("wo", C.POINTER(vp)),
         ("wgate", C.POINTER(vp)), ("wup", C.POINTER(vp)), ("wdown", C.POINTER(vp)),
-        ("gemv_mode", i32),
+        ("gemv_mode", i32), ("fused_step", i32),
     ]
 
 
@@ -101,6 +101,7 @@ NN_FUNCS = {
     "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),
+    "tos_model_fused": (i32, [vp]),
     "tos_shard_range": (i32, [i32, i32, i32, i32, ip, ip]),
     "tos_shard_plan": (i32, [C.POINTER(ModelDesc), i32, i32, C.POINTER(ShardPlan)]),
     "tos_nccl_unique_id": (i32, [vp, sz]),

@@ -52,7 +52,12 @@ struct tos_model {
     int *ring;                /* device: tokens produced by tos_model_decode */
     cudaStream_t st;
     cudaGraphExec_t gexec, gexec_chain;
-    int have_graph, have_chain;
+    int have_graph, have_chain;   /* 1: captured, -1: capture unavailable (eager launches) */
+    /* one fused kernel per token (decode_step.cu) when FAST on one GPU */
+    int fused;
+    tosk_step_t step;
+    tosk_step_layer_t *step_layers;   /* device [n_layers] */
+    unsigned *step_sync;
     size_t dev_bytes;
     /* batched prompt pass (allocated on first use): up to pf_cap tokens */
     int pf_cap;
@@ -113,8 +118,8 @@ void tos_model_destroy(tos_model_t *m)
     if (!m) return;
     if (m->st) cudaStreamSynchronize(m->st);
     /* graphs holding collectives go before the communicator */
-    if (m->have_graph) cudaGraphExecDestroy(m->gexec);
-    if (m->have_chain) cudaGraphExecDestroy(m->gexec_chain);
+    if (m->have_graph > 0) cudaGraphExecDestroy(m->gexec);
+    if (m->have_chain > 0) cudaGraphExecDestroy(m->gexec_chain);
     if (m->comm) tos_nccl_comm_destroy(m->comm);
     for (int L = 0; m->wqkv && L < m->d.n_layers; L++) {
         tosk_qmat_free(&m->wqkv[L]);
@@ -125,6 +130,7 @@ void tos_model_destroy(tos_model_t *m)
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
+                    m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
                     m->pf_toks, m->pf_x, m->pf_xn, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
                     m->pf_tmp, m->pf_ws};
@@ -156,6 +162,71 @@ static int validate(const tos_model_desc_t *d)
         !d->wv || !d->wo || !d->wgate || !d->wup || !d->wdown)
         return TOS_EINVAL;
     return TOS_OK;
+}
+
+/* The fused per-token kernel (decode_step.cu) runs the step when the
+ * descriptor asks for it (fused_step), the model uses FAST arithmetic on one
+ * GPU and the device and shapes allow it. */
+static int setup_step(tos_model_t *m)
+{
+    const tos_model_desc_t *d = &m->d;
+    if (m->sp.world != 1 || d->gemv_mode != TOS_GEMV_FAST || d->attn_mode != TOS_ATTN_FAST || !d->fused_step)
+        return 0;
+    const int L = d->n_layers;
+    tosk_step_layer_t *hl = (tosk_step_layer_t *)calloc((size_t)L, sizeof(*hl));
+    if (!hl) return cudaErrorMemoryAllocation;
+    size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
+    for (int l = 0; l < L; l++) {
+        const tosk_qmat_t *w[4] = {&m->wqkv[l], &m->wo[l], &m->wgu[l], &m->wdown[l]};
+        for (int k = 0; k < 4; k++) {
+            hl[l].qs[k] = w[k]->qs;
+            hl[l].sc[k] = w[k]->sc;
+        }
+        hl[l].norm_att = m->norms + (size_t)(2 * l) * d->dim;
+        hl[l].norm_ffn = m->norms + (size_t)(2 * l + 1) * d->dim;
+        hl[l].k_cache = (char *)m->kc + kv_layer * l;
+        hl[l].v_cache = (char *)m->vc + kv_layer * l;
+    }
+    int e = dmalloc(m, (void **)&m->step_layers, (size_t)L * sizeof(*hl));
+    if (!e) e = cudaMemcpy(m->step_layers, hl, (size_t)L * sizeof(*hl), cudaMemcpyHostToDevice);
+    free(hl);
+    if (!e) e = dmalloc(m, (void **)&m->step_sync, tosk_step_sync_bytes());
+    if (!e) e = cudaMemset(m->step_sync, 0, tosk_step_sync_bytes());
+    if (e) return e;
+    tosk_step_t *s = &m->step;
+    memset(s, 0, sizeof(*s));
+    s->layers = m->step_layers;
+    s->n_layers = L;
+    s->wtype = d->wtype;
+    s->lm_type = m->lm.type;
+    s->lm_qs = m->lm.qs;
+    s->lm_sc = m->lm.sc;
+    s->norm_out = m->norms + (size_t)2 * L * d->dim;
+    s->embd = m->embd;
+    s->embd_type = d->embd_type;
+    s->x = m->x;
+    s->q = m->q;
+    s->att = m->att;
+    s->h = m->h;
+    s->logits = m->logits;
+    s->attn_ws = m->ws;
+    s->rope = m->rope;
+    s->io = m->io;
+    s->ring = m->ring;
+    s->sync = m->step_sync;
+    s->dim = d->dim;
+    s->ff = d->ff_dim;
+    s->n_heads = d->n_heads;
+    s->n_kv = d->n_kv_heads;
+    s->hd = m->hd;
+    s->vocab = d->vocab_size;
+    s->max_seq = d->max_seq;
+    s->kv_type = d->kv_type;
+    s->eps = d->norm_eps;
+    /* shapes or devices the fused kernel does not cover keep the per-operator path */
+    m->fused = tosk_step_check(s) == 0;
+    cudaGetLastError();
+    return 0;
 }
 
 static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, int rank, const void *nccl_id)
@@ -255,6 +326,7 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
     if (!e) e = cudaMemset(m->io, 0, 8 * sizeof(int));
     if (!e) e = dmalloc(m, (void **)&m->ring, (size_t)d->max_seq * sizeof(int));
     if (!e) e = cudaMallocHost((void **)&m->io_host, 8 * sizeof(int));
+    if (!e) e = setup_step(m);
     if (!e) e = cudaStreamSynchronize(m->st);
     if (e) {
         tos_model_destroy(m);
@@ -276,6 +348,7 @@ int tos_model_create_sharded(tos_model_t **out, const tos_model_desc_t *d, int r
 }
 
 size_t tos_model_device_bytes(const tos_model_t *m) { return m ? m->dev_bytes : 0; }
+int tos_model_fused(const tos_model_t *m) { return m ? m->fused : 0; }
 const float *tos_model_logits_dev(const tos_model_t *m)
 {
     return m ? (m->sp.world > 1 ? m->logits_full : m->logits) : NULL;
@@ -309,6 +382,10 @@ static int gather_to(tos_model_t *m, const float *mine, float *full, int count)
  * next token in io[2].  A chained step then records it and advances io[1]. */
 static int enqueue_token(tos_model_t *m, int chained)
 {
+    if (m->fused) {
+        m->step.chained = chained;
+        return tosk_step_launch(&m->step, m->st);
+    }
     const tos_model_desc_t *d = &m->d;
     cudaStream_t st = m->st;
     int *err = m->io + 3;
@@ -402,17 +479,29 @@ static int run_token(tos_model_t *m, int token, int pos)
     m->io_host[1] = pos;
     int e = cudaMemcpyAsync(m->io, m->io_host, 2 * sizeof(int), cudaMemcpyHostToDevice, m->st);
     if (e) return tos_from_cuda(e);
-    if (!m->have_graph) {
-        /* first step runs eagerly (sets kernel attributes), then capture */
+    if (m->have_graph <= 0) {
+        /* first step runs eagerly (sets kernel attributes), then capture;
+         * without a graph every step stays eager */
         e = enqueue_token(m, 0);
-        if (!e) e = cudaStreamSynchronize(m->st);
+        if (!e && m->have_graph == 0) {
+            e = cudaStreamSynchronize(m->st);
+            if (!e) m->have_graph = capture(m, 0, &m->gexec) ? 1 : -1;
+        }
         if (e) return tos_from_cuda(e);
-        m->have_graph = capture(m, 0, &m->gexec);
     } else {
         e = cudaGraphLaunch(m->gexec, m->st);
         if (e) return tos_from_cuda(e);
     }
     return TOS_OK;
+}
+
+/* After a bounded wait ran out: clear the error word and the fused step's
+ * barrier counters (a step that stopped early leaves them mid-count). */
+static void clear_error(tos_model_t *m)
+{
+    cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
+    if (m->step_sync) cudaMemsetAsync(m->step_sync, 0, tosk_step_sync_bytes(), m->st);
+    cudaStreamSynchronize(m->st);
 }
 
 static int finish(tos_model_t *m, float *logits, int *next)
@@ -424,8 +513,7 @@ static int finish(tos_model_t *m, float *logits, int *next)
     if (!e) e = cudaStreamSynchronize(m->st);
     if (e) return tos_from_cuda(e);
     if (m->io_host[3] != 0) {
-        cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
-        cudaStreamSynchronize(m->st);
+        clear_error(m);
         return TOS_ETIMEOUT;
     }
     if (next) *next = m->io_host[2];
@@ -480,22 +568,21 @@ int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_t
     m->io_host[4] = 0;
     int e = cudaMemcpyAsync(m->io, m->io_host, 5 * sizeof(int), cudaMemcpyHostToDevice, m->st);
     int step = 0;
-    if (!e && !m->have_chain) {
+    if (!e && m->have_chain == 0) {
         /* one eager chained step (configures kernels), then capture */
         e = enqueue_token(m, 1);
         if (!e) e = cudaStreamSynchronize(m->st);
         step = 1;
-        if (!e) m->have_chain = capture(m, 1, &m->gexec_chain);
+        if (!e) m->have_chain = capture(m, 1, &m->gexec_chain) ? 1 : -1;
     }
     for (; !e && step < n_steps; step++)
-        e = m->have_chain ? cudaGraphLaunch(m->gexec_chain, m->st) : enqueue_token(m, 1);
+        e = m->have_chain > 0 ? cudaGraphLaunch(m->gexec_chain, m->st) : enqueue_token(m, 1);
     if (!e) e = cudaMemcpyAsync(out_tokens, m->ring, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, m->st);
     if (!e) e = cudaMemcpyAsync(m->io_host + 3, m->io + 3, sizeof(int), cudaMemcpyDeviceToHost, m->st);
     if (!e) e = cudaStreamSynchronize(m->st);
     if (e) return tos_set_status(tos_from_cuda(e));
     if (m->io_host[3] != 0) {
-        cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
-        cudaStreamSynchronize(m->st);
+        clear_error(m);
         return tos_set_status(TOS_ETIMEOUT);
     }
     return tos_set_status(TOS_OK);

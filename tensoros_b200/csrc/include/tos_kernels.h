@@ -145,6 +145,42 @@ int tosk_attention(float *out, const float *q, const void *k_cache, const void *
 
 int tosk_num_sms(void);
 
+/* ---- fused decode step (decode_step.cu): one cooperative kernel per token
+ * runs every layer, the LM head and the greedy argmax with FAST arithmetic
+ * (tosk_gemv FAST block values, FAST attention) ---- */
+typedef struct {
+    const uint8_t *qs[4];      /* planes of q|k|v, o, gate|up (interleaved), down */
+    const uint16_t *sc[4];
+    const float *norm_att, *norm_ffn;
+    void *k_cache, *v_cache;   /* this layer's [max_seq][kv_dim] */
+} tosk_step_layer_t;
+
+typedef struct {
+    const tosk_step_layer_t *layers;  /* device array [n_layers] */
+    int n_layers;
+    int wtype;                        /* TOSK_Q4_0 / TOSK_Q8_0: every projection */
+    int lm_type;                      /* LM head */
+    const uint8_t *lm_qs;
+    const uint16_t *lm_sc;
+    const float *norm_out;
+    const void *embd;
+    int embd_type;                    /* TOSK_Q4_0 / TOSK_Q8_0 / TOSK_F16 / TOSK_F32 */
+    float *x, *q, *att, *h, *logits;  /* residual [dim], q [q_dim], attention out [q_dim], [ff], [vocab] */
+    void *attn_ws;                    /* tosk_attention_ws_bytes(n_heads, max_seq) bytes */
+    const float2 *rope;               /* [max_seq][hd/2] */
+    int *io;                          /* token, pos, next, err, ring count */
+    int *ring;
+    int chained;                      /* token from io[2]; then ring[io[4]++] = next, io[1] += 1 */
+    unsigned *sync;                   /* tosk_step_sync_bytes(), zero before the first launch */
+    int dim, ff, n_heads, n_kv, hd, vocab, max_seq, kv_type;
+    float eps;
+} tosk_step_t;
+
+size_t tosk_step_sync_bytes(void);
+/* 0 when the fused step supports this configuration on this device */
+int tosk_step_check(const tosk_step_t *s);
+int tosk_step_launch(const tosk_step_t *s, cudaStream_t st);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,1133 @@
+// decode_step.cu - the whole greedy decode step of one token in one
+// persistent kernel (TensorOS runtime/nn llm_forward_token, llm.c:641-743,
+// and llm_argmax, llm.c:1129-1140), FAST arithmetic.
+//
+// Why one kernel: a batch-1 decode step is ~160 dependent GEMVs and attention
+// passes, each a few microseconds long.  As separate launches every one pays
+// its CTA start-up and the DRAM latency of its first weight stage, and the
+// next launch cannot prefetch (its CTAs need the shared memory the previous
+// kernel still holds).  Here one CTA per SM stays resident for the token:
+//
+//   * warp 0 (the producer) streams the weight planes of EVERY projection of
+//     the step, in execution order, through a 5-slot shared-memory ring
+//     (cp.async.bulk, mbarrier complete_tx).  Weights depend on nothing, so
+//     the producer only waits for free slots: while the other warps wait at
+//     a grid barrier or run attention, the next projection's rows are
+//     already landing.
+//   * warps 4..19 (compute) evaluate block values of the ring's stages
+//     exactly as the FAST GEMV does (integer dp4a dot products on 24-bit
+//     fixed-point x, gemv_fastmath.cuh) into a partials tile;
+//   * warps 1..3 (chain) add each row's partials in a fixed tree order and
+//     run the fused epilogue (RoPE + KV store, residual add, SiLU*up, logits
+//     with a running argmax);
+//   * between dependent phases all 148 CTAs meet at a grid barrier (an
+//     atomic counter in global memory, release/acquire at GPU scope, every
+//     wait bounded); attention runs on 16 worker warps as four groups of
+//     four (the split-K scores / softmax*V passes of attention.cu's FAST
+//     mode).
+//
+// Each CTA owns the same contiguous row range of a given projection in every
+// layer, so the residual rows it adds to are the rows it wrote (no extra
+// barrier for the residual), and every vector another CTA wrote is read
+// through L2 (ld.global.cg).
+//
+// Numerics: FAST (tolerance 1e-4 normwise to the reference, greedy ids equal
+// to the exact path on every tested configuration).  Block values and the
+// fixed-point conversion are those of the FAST GEMV; row sums, the RMSNorm
+// sum of squares and the attention passes use fixed tree orders, so results
+// are deterministic run to run.
+//
+// Launch: cooperative (all CTAs co-resident), one per SM.  Every wait is
+// bounded (tos::kWaitCycles); a wait that runs out records a code in the
+// step's error word and the CTAs leave together at the next grid barrier.
+#include <cuda_runtime.h>
+
+#include "gemv_common.cuh"
+#include "gemv_fastmath.cuh"
+
+namespace tos {
+namespace step {
+
+// 20 warps: five per SM sub-partition leave 96 registers a thread
+constexpr int kThreads = 640;            // warp 0 producer, 1..3 chain, 4..19 compute
+constexpr int kChain = 3;
+constexpr int kCompute = 16;
+constexpr int kWorkers = kThreads - 32;  // chain + compute threads
+constexpr int kSlot = 36864;             // ring slot: 16 rows of a 4096-column Q4_0 matrix
+constexpr int kSlots = 3;
+constexpr int kHdr = 2048;
+constexpr int kPreRows = 128;           // residual rows a CTA can stage for its epilogue
+constexpr int kXBytes = 58368;           // fixed-point records of x: 128 B a block, up to 456 blocks
+constexpr int kPBytes = 25344;           // partials tile (also attention scratch)
+constexpr int kSmem = kHdr + kXBytes + kPBytes + kSlots * kSlot;
+static_assert(kSmem <= 227 * 1024, "shared memory");
+constexpr int kGroups = 4;               // attention groups of four worker warps (warps 1..16)
+constexpr int kChunk = 64;               // attention positions per chunk
+constexpr int kMaxHd = 256;
+constexpr int kMaxGrid = 1024;
+enum { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4, K_N = 5 };
+// named barriers (0 is __syncthreads)
+enum { B_COMPUTE = 1, B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4 };
+
+// Geometry of one projection (the same in every layer).
+struct Geo {
+  int R, nb, nbp, qb, unit, tr, pstride, sc_off;
+};
+
+struct Params {
+  tosk_step_t s;
+  Geo g[K_N];
+  float* S;        // attention workspace (the FAST attention layout)
+  float* cmax;
+  float* lsum;
+  float* opart;
+  int* cnt;
+  int maxc;
+};
+
+struct Hdr {
+  uint64_t full[kSlots];
+  uint64_t empty[kSlots];
+  uint64_t pfull[kChain];
+  uint64_t pempty[kChain];
+  int abort;
+  int tok, pos, skip;
+  float wpart[kCompute];
+  float av[kChain];
+  int ai[kChain];
+  // epilogue operands the chain warps stage while the compute warps build
+  // the input records: this CTA's residual rows, RoPE (cos, sin) of pos
+  float res[kPreRows];
+  float2 cs[kMaxHd / 2];
+};
+static_assert(sizeof(Hdr) <= kHdr, "header");
+
+// Attention scratch of one group inside the partials area (floats).
+constexpr int kGroupFloats = kChunk + 8 + 4 * kMaxHd + 8;
+static_assert(kGroups * kGroupFloats * 4 <= kPBytes, "attention scratch");
+static_assert((1024 + (kWorkers / 32) * kMaxHd + 32) * 4 <= kXBytes, "per-head attention scratch");
+
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or ~the hint passes) instead of spinning, so the producer and
+// the chain warps, which wait most of the time, leave the issue slots to the
+// compute warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool wait_mb(uint64_t* bar, uint32_t parity, int* err, int code,
+                                        volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (int i = 0;; ++i) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        atomicCAS(err, 0, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier for the worker threads of every CTA: the k-th call waits for
+// the counter to reach k * gridDim.x.  Returns false, in every worker thread
+// of the CTA alike, when the step must stop (an error here or elsewhere).
+__device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target, int* err) {
+  named_sync(B_WORKERS, kWorkers);
+  if (threadIdx.x == 32 && !*reinterpret_cast<volatile int*>(&h->abort)) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    const long long t0 = clock64();
+    for (int i = 0;; ++i) {
+      if (ld_acquire(bar) >= target) break;
+      __nanosleep(32);
+      if ((i & 7) == 7) {
+        if (*reinterpret_cast<volatile int*>(err)) {
+          h->abort = 1;
+          break;
+        }
+        if (clock64() - t0 > kWaitCycles) {
+          atomicCAS(err, 0, 20);
+          h->abort = 1;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  named_sync(B_WORKERS, kWorkers);
+  return !*reinterpret_cast<volatile int*>(&h->abort);
+}
+
+__device__ __forceinline__ void row_range(const Geo& G, int& rb, int& re, int& nst) {
+  const int NU = (G.R + G.unit - 1) / G.unit;
+  const int u0 = (int)(((long long)blockIdx.x * NU) / gridDim.x);
+  const int u1 = (int)(((long long)(blockIdx.x + 1) * NU) / gridDim.x);
+  rb = u0 * G.unit;
+  re = min(u1 * G.unit, G.R);
+  nst = re > rb ? (re - rb + G.tr - 1) / G.tr : 0;
+}
+
+__device__ __forceinline__ void planes(const Params& p, int kind, int layer, const uint8_t*& qs,
+                                       const uint16_t*& sc) {
+  if (kind == K_LM) {
+    qs = p.s.lm_qs;
+    sc = p.s.lm_sc;
+  } else {
+    const tosk_step_layer_t& L = p.s.layers[layer];
+    qs = L.qs[kind];
+    sc = L.sc[kind];
+  }
+}
+
+// The phases of one token in order: per layer q|k|v, scores, softmax*V, o,
+// gate|up, down; then the LM head.  Weight-streaming phases only.
+__device__ __forceinline__ int gemv_kind_of(int i, int n_layers, int& layer) {
+  if (i >= 4 * n_layers) {
+    layer = n_layers;
+    return K_LM;
+  }
+  layer = i >> 2;
+  return i & 3;
+}
+
+// (value, index) order of llm_argmax (llm.c:1129-1140) for partial results:
+// a larger value wins, equal values go to the lower index, NaNs never win
+// (index -1 marks "no candidate").  Associative and commutative, so the
+// result does not depend on the order partial results are combined in.
+__device__ __forceinline__ void arg_better(float& v, int& i, float v2, int i2) {
+  if (i2 < 0) return;
+  if (i < 0 || v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// producer: every weight stage of the step, in order
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void producer(const Params& p, Hdr* h, uint8_t* ring) {
+  int* err = p.s.io + 3;
+  int gs = 0;
+  bool ok = true;
+  const int nphase = 4 * p.s.n_layers + 1;
+  for (int i = 0; i < nphase && ok; ++i) {
+    int layer;
+    const int kind = gemv_kind_of(i, p.s.n_layers, layer);
+    const Geo& G = p.g[kind];
+    const uint8_t* qs;
+    const uint16_t* sc;
+    planes(p, kind, layer, qs, sc);
+    int rb, re, nst;
+    row_range(G, rb, re, nst);
+    for (int it = 0; it < nst; ++it) {
+      const int s = gs % kSlots;
+      if (gs >= kSlots && !wait_mb(&h->empty[s], ((gs / kSlots) - 1) & 1, err, 1, &h->abort)) {
+        ok = false;
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(&h->abort)) {
+        ok = false;
+        break;
+      }
+      const int r0 = rb + it * G.tr;
+      const int n = min(G.tr, re - r0);
+      const uint32_t bq = (uint32_t)(n * G.nb * G.qb);
+      const uint32_t bs = (uint32_t)(n * G.nbp * 2);
+      uint8_t* dst = ring + (size_t)s * kSlot;
+      mbar_arrive_expect_tx(&h->full[s], bq + bs);
+      bulk_g2s(dst, qs + (size_t)r0 * G.nb * G.qb, bq, &h->full[s]);
+      bulk_g2s(dst + G.sc_off, sc + (size_t)r0 * G.nbp, bs, &h->full[s]);
+      ++gs;
+    }
+  }
+  // the copies of the last stages land before the CTA may exit
+  for (int j = max(0, gs - kSlots); j < gs; ++j) mbar_wait(&h->full[j % kSlots], (j / kSlots) & 1, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------
+// compute warps: the phase's input block in fixed point, then block values
+// ---------------------------------------------------------------------------
+// Chunk q (elements 4q .. 4q+3) of token tok's embedding row (llm.c:365-410;
+// the arithmetic of embed_kernel: (n - 8) * d, q * d, fp16 widening, a copy).
+__device__ __forceinline__ float4 embed_chunk(const void* embd, int type, int dim, int tok, int q) {
+  const int nb = dim / 32, blk = q >> 3, c = q & 7;
+  float4 v;
+  if (type == TOSK_Q4_0) {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(embd) + ((size_t)tok * nb + blk) * 18;
+    const float d = h2f((uint16_t)(b[0] | (b[1] << 8)));
+    const int b0 = b[2 + 2 * c], b1 = b[3 + 2 * c];
+    v.x = __fmul_rn((float)((b0 & 0x0F) - 8), d);
+    v.y = __fmul_rn((float)((b0 >> 4) - 8), d);
+    v.z = __fmul_rn((float)((b1 & 0x0F) - 8), d);
+    v.w = __fmul_rn((float)((b1 >> 4) - 8), d);
+  } else if (type == TOSK_Q8_0) {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(embd) + ((size_t)tok * nb + blk) * 34 + 2 + 4 * c;
+    const float d = h2f((uint16_t)(b[-2 - 4 * c] | (b[-1 - 4 * c] << 8)));
+    v.x = __fmul_rn((float)(int8_t)b[0], d);
+    v.y = __fmul_rn((float)(int8_t)b[1], d);
+    v.z = __fmul_rn((float)(int8_t)b[2], d);
+    v.w = __fmul_rn((float)(int8_t)b[3], d);
+  } else if (type == TOSK_F16) {
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(embd) + (size_t)tok * dim + 4 * q;
+    v = make_float4(h2f(e[0]), h2f(e[1]), h2f(e[2]), h2f(e[3]));
+  } else {
+    const float* e = reinterpret_cast<const float*>(embd) + (size_t)tok * dim + 4 * q;
+    v = make_float4(e[0], e[1], e[2], e[3]);
+  }
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// compute warps: the phase's input vector in fixed point, then block values
+// ---------------------------------------------------------------------------
+// The input vector becomes per-block fixed-point records in shared memory
+// (128 B a block: limb words 0..23, c, s; 16-byte chunk j at slot j ^ (b & 7)),
+// eight lanes a block (xfix_group); with a fused RMSNorm the raw vector is
+// staged there first for the sum of squares.  Each compute thread then keeps
+// its block's record in registers for the whole phase.
+template <int QB>
+__device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
+                                             int kind, int layer, int& gs) {
+  const Geo& G = p.g[kind];
+  int* err = p.s.io + 3;
+  const int ct = (int)threadIdx.x - 32 * (1 + kChain);   // 0 .. 511
+  const int lane = threadIdx.x & 31;
+  const int nwb = (G.nb + 31) >> 5;
+  int rg = kCompute / nwb;
+  if (rg < 1) rg = 1;
+  if (rg > G.tr) rg = G.tr;
+  const int bw = nwb * 32;
+  const int b = ct % bw, g = ct / bw;
+  const bool active = b < G.nb && g < rg;
+  int rb, re, nst;
+  row_range(G, rb, re, nst);
+
+  {
+    const bool emb = kind == K_QKV && layer == 0;
+    const float* src = (kind == K_O) ? p.s.att : (kind == K_D) ? p.s.h : p.s.x;
+    const float* nw = kind == K_QKV ? p.s.layers[layer].norm_att
+                    : kind == K_GU  ? p.s.layers[layer].norm_ffn
+                    : kind == K_LM  ? p.s.norm_out : nullptr;
+    const int nq = G.nb * 8;   // 16-byte chunks
+    float4* X4 = reinterpret_cast<float4*>(X);
+    int orb = 0, ore = 0;
+    if (emb) {
+      int ons;
+      row_range(p.g[K_O], orb, ore, ons);
+    }
+    auto fetch = [&](int q) -> float4 {
+      if (emb) {
+        const float4 v = embed_chunk(p.s.embd, p.s.embd_type, p.s.dim, h->tok, q);
+        // the residual stream starts as the embedding: this CTA writes the
+        // rows it owns in the o / down phases (their residual adds are its own)
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (4 * q + i >= orb && 4 * q + i < ore) p.s.x[4 * q + i] = e[i];
+        return v;
+      }
+      return __ldcg(reinterpret_cast<const float4*>(src) + q);
+    };
+    float ss = 1.0f;
+    // a fused RMSNorm stages the raw chunks in the record area and its
+    // weights in the (idle) partials area, every load of a thread in flight
+    const bool stage_w = nw && nq * 16 <= kPBytes;
+    float4* W4 = reinterpret_cast<float4*>(P);
+    if (nw) {
+      // RMSNorm (llm.c:416-442): tree sum of squares (serial per thread,
+      // butterfly per warp, warps in order)
+      float acc = 0.0f;
+#pragma unroll 2
+      for (int q = ct; q < nq; q += 32 * kCompute) {
+        const float4 v = fetch(q);
+        if (stage_w) W4[q] = __ldg(reinterpret_cast<const float4*>(nw) + q);
+        X4[q] = v;
+        acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) h->wpart[ct >> 5] = acc;
+      named_sync(B_COMPUTE, 32 * kCompute);
+      float s2 = 0.0f;
+      for (int w = 0; w < kCompute; ++w) s2 += h->wpart[w];
+      ss = 1.0f / sqrtf(s2 / (float)p.s.dim + p.s.eps);
+    }
+    // every lane runs the same number of rounds (xfix_group shuffles within
+    // eight-lane groups; a round's eight lanes share a block)
+    for (int base = 0; base < nq; base += 32 * kCompute) {
+      const int q = base + ct;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q < nq) {
+        if (nw) {
+          v = X4[q];
+          const float4 wv = stage_w ? W4[q] : __ldg(reinterpret_cast<const float4*>(nw) + q);
+          v.x = __fmul_rn(__fmul_rn(v.x, ss), wv.x);
+          v.y = __fmul_rn(__fmul_rn(v.y, ss), wv.y);
+          v.z = __fmul_rn(__fmul_rn(v.z, ss), wv.z);
+          v.w = __fmul_rn(__fmul_rn(v.w, ss), wv.w);
+        } else {
+          v = fetch(q);
+        }
+      }
+      uint32_t w0, w1, w2;
+      int wi, csum;
+      float sc;
+      xfix_group<QB>(v, q & 7, w0, w1, w2, wi, csum, sc);
+      __syncwarp();   // the raw chunks of this block are read before its record overwrites them
+      if (q < nq) {
+        const int blk = q >> 3;
+        uint32_t* rec = X + 32 * blk;
+        const int sw = blk & 7;
+        auto put = [&](int word, uint32_t val) { rec[(((word >> 2) ^ sw) << 2) | (word & 3)] = val; };
+        put(wi, w0);
+        put(8 + wi, w1);
+        put(16 + wi, w2);
+        if ((q & 7) == 0) {
+          put(24, (uint32_t)csum);
+          put(25, __float_as_uint(sc));
+        }
+      }
+    }
+    named_sync(B_COMPUTE, 32 * kCompute);
+  }
+  XFix xf;
+  if (active) {
+    const uint4* xv = reinterpret_cast<const uint4*>(X) + 8 * b;
+    uint32_t wds[28];
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      const uint4 u = xv[j ^ (b & 7)];
+      wds[4 * j] = u.x; wds[4 * j + 1] = u.y; wds[4 * j + 2] = u.z; wds[4 * j + 3] = u.w;
+    }
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+#pragma unroll
+      for (int w = 0; w < 8; ++w) xf.l[l][w] = wds[8 * l + w];
+    xf.c = (int)wds[24];
+    xf.s = __uint_as_float(wds[25]);
+  }
+
+  for (int it = 0; it < nst; ++it, ++gs) {
+    const int s = gs % kSlots;
+    if (!wait_mb(&h->full[s], (gs / kSlots) & 1, err, 2, &h->abort)) return;
+    const int c = gs % kChain;
+    if (gs >= kChain && !wait_mb(&h->pempty[c], ((gs / kChain) & 1) ^ 1, err, 3, &h->abort)) return;
+    const int n = min(G.tr, re - (rb + it * G.tr));
+    const uint8_t* stq = ring + (size_t)s * kSlot;
+    const uint16_t* sts = reinterpret_cast<const uint16_t*>(stq + G.sc_off);
+    float* Pc = P + c * G.tr * G.pstride;
+    if (active) {
+      int r = g;
+      for (; r + rg < n; r += 2 * rg) {   // two rows in flight
+        const float y0 = block_value_fast<QB>(stq, sts, r, b, G.nb, G.nbp, xf);
+        const float y1 = block_value_fast<QB>(stq, sts, r + rg, b, G.nb, G.nbp, xf);
+        Pc[r * G.pstride + b] = y0;
+        Pc[(r + rg) * G.pstride + b] = y1;
+      }
+      if (r < n) Pc[r * G.pstride + b] = block_value_fast<QB>(stq, sts, r, b, G.nb, G.nbp, xf);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&h->pfull[c]);
+      mbar_arrive(&h->empty[s]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// chain warps: row sums and the fused epilogues
+// ---------------------------------------------------------------------------
+// Lane i (< n) holds the sum of row r0 + i.  Paired epilogues see both rows
+// of a pair in lanes i, i ^ 1 (stages and row ranges start at even rows).
+template <int ESZ>
+__device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind, int layer, float y, int r0, int n,
+                                         int lane, int pos, int rb, bool pre_res, float& bv, int& bi) {
+  const int r = r0 + lane;
+  const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+  if (lane >= n) return;
+  if (kind == K_QKV) {
+    const int qr = p.s.n_heads * p.s.hd, kr = p.s.n_kv * p.s.hd, hd = p.s.hd;
+    float v = y;
+    if (r < qr + kr) {
+      // llm.c:488-492: RoPE on q and k rows (adjacent pairs)
+      const int i = (r < qr ? r : r - qr) % hd;
+      const float2 cs = h->cs[i >> 1];
+      if ((i & 1) == 0)
+        v = __fsub_rn(__fmul_rn(y, cs.x), __fmul_rn(partner, cs.y));
+      else
+        v = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(y, cs.x));
+    }
+    if (r < qr) {
+      p.s.q[r] = v;
+    } else {
+      // llm.c:673-681: k, v of this position into the cache
+      const bool is_k = r < qr + kr;
+      const int e = is_k ? r - qr : r - qr - kr;
+      const tosk_step_layer_t& L = p.s.layers[layer];
+      const size_t idx = (size_t)pos * kr + e;
+      if constexpr (ESZ == 2)
+        reinterpret_cast<uint16_t*>(is_k ? L.k_cache : L.v_cache)[idx] = f2h(v);
+      else
+        reinterpret_cast<float*>(is_k ? L.k_cache : L.v_cache)[idx] = v;
+    }
+  } else if (kind == K_O || kind == K_D) {
+    p.s.x[r] = __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + r), y);   // llm.c:717-718, 732-733
+  } else if (kind == K_GU) {
+    if ((r & 1) == 0) p.s.h[r >> 1] = __fmul_rn(ref_silu(y), partner);   // llm.c:726-729
+  } else {
+    p.s.logits[r] = y;
+    if (!(y != y)) arg_better(bv, bi, y, r);
+  }
+}
+
+// Chain warps after the LM head: the CTA's (value, index), then the last CTA
+// to finish reduces all of them and writes the greedy token.
+__device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv, int bi) {
+  const int cw = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_down_sync(0xffffffffu, bv, o);
+    const int i2 = __shfl_down_sync(0xffffffffu, bi, o);
+    arg_better(bv, bi, v2, i2);
+  }
+  if (lane == 0) {
+    h->av[cw] = bv;
+    h->ai[cw] = bi;
+  }
+  named_sync(B_CHAIN, 32 * kChain);
+  if (threadIdx.x != 32) return;
+  float v = h->av[0];
+  int i = h->ai[0];
+  for (int c = 1; c < kChain; ++c) arg_better(v, i, h->av[c], h->ai[c]);
+  int* pairs = reinterpret_cast<int*>(p.s.sync + 64);
+  pairs[2 * blockIdx.x] = __float_as_int(v);
+  pairs[2 * blockIdx.x + 1] = i;
+  __threadfence();
+  if (atomicAdd(p.s.sync + 1, 1u) != gridDim.x - 1) return;
+  __threadfence();
+  float best = 0.0f;
+  int idx = -1;
+  for (unsigned k = 0; k < gridDim.x; ++k)
+    arg_better(best, idx, __int_as_float(__ldcg(pairs + 2 * k)), __ldcg(pairs + 2 * k + 1));
+  // llm.c:1130: x[0] is the starting candidate; it stays when NaN or unbeaten
+  const float x0 = __ldcg(p.s.logits);
+  if (x0 != x0 || idx < 0) idx = 0;
+  int* io = p.s.io;
+  io[2] = idx;
+  if (p.s.chained) {
+    const int k = io[4];
+    p.s.ring[k] = idx;
+    io[4] = k + 1;
+    io[1] = io[1] + 1;
+  }
+  // every CTA is past its last grid barrier: reset the counters for the next step
+  atomicExch(p.s.sync, 0u);
+  atomicExch(p.s.sync + 1, 0u);
+}
+
+template <int ESZ>
+__device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float* P, int kind, int layer, int& gs) {
+  float bv = 0.0f;   // LM head: this lane's running (value, index) of llm_argmax
+  int bi = -1;
+  const Geo& G = p.g[kind];
+  int* err = p.s.io + 3;
+  const int cw = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  int rb, re, nst;
+  row_range(G, rb, re, nst);
+  const int gs0 = gs;
+  gs += nst;
+  // lane = row * nseg + segment; each lane sums its segment of the row's
+  // partials with four running sums, then a butterfly over the segments
+  const int tr = G.tr;
+  int nseg = 1;
+  while (nseg * 2 * tr <= 32) nseg <<= 1;
+  const int row = min(lane / nseg, tr - 1), seg = lane % nseg;
+  const int L = ((G.nb + nseg - 1) / nseg + 3) & ~3;
+  const int j0 = min(G.nb, seg * L), j1 = min(G.nb, seg * L + L);
+  const int pos = h->pos;
+  const bool pre_res = (kind == K_O || kind == K_D) && re - rb <= kPreRows;
+  {
+    const int ct = (int)threadIdx.x - 32;   // 0 .. 32 * kChain - 1
+    if (pre_res)
+      for (int i = ct; i < re - rb; i += 32 * kChain) h->res[i] = __ldcg(p.s.x + rb + i);
+    if (kind == K_QKV)
+      for (int i = ct; i < (p.s.hd >> 1); i += 32 * kChain) h->cs[i] = p.s.rope[(size_t)pos * (p.s.hd >> 1) + i];
+    named_sync(B_CHAIN, 32 * kChain);
+  }
+  for (int it = ((cw - gs0) % kChain + kChain) % kChain; it < nst; it += kChain) {
+    const int gsi = gs0 + it;
+    if (!wait_mb(&h->pfull[cw], (gsi / kChain) & 1, err, 4, &h->abort)) break;
+    const int r0 = rb + it * tr;
+    const int n = min(tr, re - r0);
+    const float* Prow = P + (cw * tr + row) * G.pstride;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int j = j0;
+    for (; j + 4 <= j1; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(Prow + j);
+      s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
+    }
+    for (; j < j1; ++j) s0 += Prow[j];
+    float t = (s0 + s1) + (s2 + s3);
+    for (int o = 1; o < nseg; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    const float y = __shfl_sync(0xffffffffu, t, min(lane, tr - 1) * nseg);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&h->pempty[cw]);
+    epilogue<ESZ>(p, h, kind, layer, y, r0, n, lane, pos, rb, pre_res, bv, bi);
+  }
+  if (kind == K_LM) argmax_finish(p, h, bv, bi);
+}
+
+// ---------------------------------------------------------------------------
+// attention (llm.c:683-714), FAST: split-K over 64-position chunks
+// ---------------------------------------------------------------------------
+template <int ESZ>
+__device__ __forceinline__ float4 ldcg4(const uint8_t* p) {
+  if constexpr (ESZ == 2) {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+  }
+}
+
+// Four consecutive elements of a cache row, loaded now and widened later
+// (so a prefetch holds 8 bytes a lane for fp16 caches).
+template <int ESZ>
+struct Raw4 {
+  uint2 u;
+};
+template <>
+struct Raw4<4> {
+  float4 f;
+};
+template <int ESZ>
+__device__ __forceinline__ Raw4<ESZ> ldcg_raw(const uint8_t* p) {
+  Raw4<ESZ> r;
+  if constexpr (ESZ == 2)
+    r.u = __ldcg(reinterpret_cast<const uint2*>(p));
+  else
+    r.f = __ldcg(reinterpret_cast<const float4*>(p));
+  return r;
+}
+template <int ESZ>
+__device__ __forceinline__ float4 widen(const Raw4<ESZ>& r) {
+  if constexpr (ESZ == 2) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    return r.f;
+  }
+}
+template <int ESZ>
+__device__ __forceinline__ Raw4<ESZ> raw_zero() {
+  Raw4<ESZ> r;
+  if constexpr (ESZ == 2)
+    r.u = make_uint2(0u, 0u);
+  else
+    r.f = make_float4(0.f, 0.f, 0.f, 0.f);
+  return r;
+}
+
+__device__ __forceinline__ float warp_max_f(float m) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
+// Scores of one (kv head, chunk) item per group of four warps: a warp per 16
+// positions, lane l covering d = 128 s + 4 l .. +3, all 16 rows in flight,
+// then a shuffle reduce-scatter; per-chunk maxima for the softmax pass.
+template <int ESZ>
+__device__ __noinline__ void attn_scores(const Params& p, Hdr* h, float* P, int layer) {
+  const int w = (int)(threadIdx.x >> 5) - 1;
+  const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
+  float* wmax = P + grp * kGroupFloats + kChunk + 4;
+  const int n = h->pos + 1;
+  const int n_heads = p.s.n_heads, n_kv = p.s.n_kv, hd = p.s.hd;
+  if (blockIdx.x == 0)
+    for (int i = (int)threadIdx.x - 32; i < n_heads; i += kWorkers) p.cnt[i] = 0;   // the pv pass's counters
+  if (grp >= kGroups) return;
+  const int group = n_heads / n_kv, kv_dim = n_kv * hd;
+  const int nchunk = (n + kChunk - 1) / kChunk;
+  const int items = n_kv * nchunk;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const uint8_t* kc = reinterpret_cast<const uint8_t*>(p.s.layers[layer].k_cache);
+  for (int item = blockIdx.x * kGroups + grp; item < items; item += gridDim.x * kGroups) {
+    const int kvh = item / nchunk, c = item % nchunk;
+    const int tw = c * kChunk + gw * 16;
+    for (int gi = 0; gi < group; ++gi) {
+      const int hh = kvh * group + gi;
+      float v[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = 0.0f;
+#pragma unroll
+      for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+        const int d = 128 * sl + 4 * lane;
+        if (d < hd) {
+          const float4 qv = __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d));
+#pragma unroll
+          for (int hf = 0; hf < 16; hf += 8) {   // eight rows in flight at a time
+            float4 kv[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              kv[q] = tw + hf + q < n
+                          ? ldcg4<ESZ>(kc + ((size_t)(tw + hf + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              v[hf + q] = fmaf(qv.x, kv[q].x, fmaf(qv.y, kv[q].y, fmaf(qv.z, kv[q].z, fmaf(qv.w, kv[q].w, v[hf + q]))));
+          }
+        }
+      }
+#pragma unroll
+      for (int half = 8, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? v[half + i] : v[i];
+          const float send = up ? v[i] : v[half + i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+      const int t = tw + (lane >> 1);
+      float m = -INFINITY;
+      if (t < n) {
+        m = dot * scale;
+        if ((lane & 1) == 0) p.S[(size_t)hh * p.s.max_seq + t] = m;
+      }
+      m = warp_max_f(m);
+      named_sync(B_GROUP0 + grp, 128);
+      if (lane == 0) wmax[gw] = m;
+      named_sync(B_GROUP0 + grp, 128);
+      if (gw == 0 && lane == 0)
+        p.cmax[(size_t)hh * p.maxc + c] = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    }
+  }
+}
+
+// e_t = llm_expf(s_t - max) with the head's global max (llm.c:509-517), the
+// chunk's e-sum and sum_t e_t v_t; the last chunk of a head to finish adds
+// the chunks in order and divides by the sum (llm.c:519-521, 703-712).
+template <int ESZ>
+__device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int layer) {
+  const int w = (int)(threadIdx.x >> 5) - 1;
+  const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
+  const int gt = gw * 32 + lane;
+  float* es = P + grp * kGroupFloats;
+  float* red = es + kChunk;
+  float* wpart = es + kChunk + 8;
+  int* s_last = reinterpret_cast<int*>(wpart + 4 * kMaxHd);
+  if (grp >= kGroups) return;
+  const int n = h->pos + 1;
+  const int n_heads = p.s.n_heads, n_kv = p.s.n_kv, hd = p.s.hd;
+  const int group = n_heads / n_kv, kv_dim = n_kv * hd;
+  const int nchunk = (n + kChunk - 1) / kChunk;
+  const int items = n_heads * nchunk;
+  const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.s.layers[layer].v_cache);
+  for (int item = blockIdx.x * kGroups + grp; item < items; item += gridDim.x * kGroups) {
+    const int hh = item / nchunk, c = item % nchunk;
+    const int kvh = hh / group;
+    const int t0 = c * kChunk, cn = min(kChunk, n - t0);
+    float m = -INFINITY;
+    for (int i = gt; i < nchunk; i += 128) m = fmaxf(m, __ldcg(p.cmax + (size_t)hh * p.maxc + i));
+    m = warp_max_f(m);
+    named_sync(B_GROUP0 + grp, 128);
+    if (lane == 0) red[gw] = m;
+    named_sync(B_GROUP0 + grp, 128);
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float e = 0.0f;
+    if (gt < kChunk) {
+      if (gt < cn) e = ref_expf(__fsub_rn(__ldcg(p.S + (size_t)hh * p.s.max_seq + t0 + gt), M));
+      es[gt] = e;
+    }
+    float l = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    named_sync(B_GROUP0 + grp, 128);
+    if (lane == 0) red[4 + gw] = l;
+    const int tw = gw * 16;
+#pragma unroll
+    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      if (d < hd) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int hf = 0; hf < 16; hf += 8) {   // eight rows in flight at a time
+          float4 vv[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            vv[q] = tw + hf + q < cn
+                        ? ldcg4<ESZ>(vc + ((size_t)(t0 + tw + hf + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float ep = es[tw + hf + q];
+            acc.x = fmaf(ep, vv[q].x, acc.x);
+            acc.y = fmaf(ep, vv[q].y, acc.y);
+            acc.z = fmaf(ep, vv[q].z, acc.z);
+            acc.w = fmaf(ep, vv[q].w, acc.w);
+          }
+        }
+        *reinterpret_cast<float4*>(&wpart[gw * kMaxHd + d]) = acc;
+      }
+    }
+    named_sync(B_GROUP0 + grp, 128);
+    float* op = p.opart + ((size_t)hh * p.maxc + c) * kMaxHd;
+    for (int d = gt; d < hd; d += 128)
+      op[d] = ((wpart[d] + wpart[kMaxHd + d]) + wpart[2 * kMaxHd + d]) + wpart[3 * kMaxHd + d];
+    if (gt == 0) p.lsum[(size_t)hh * p.maxc + c] = ((red[4] + red[5]) + red[6]) + red[7];
+    __threadfence();
+    named_sync(B_GROUP0 + grp, 128);
+    if (gt == 0) *s_last = atomicAdd(p.cnt + hh, 1) == nchunk - 1;
+    named_sync(B_GROUP0 + grp, 128);
+    if (*s_last) {
+      __threadfence();
+      float Ls = 0.0f;
+      for (int i = 0; i < nchunk; ++i) Ls += __ldcg(p.lsum + (size_t)hh * p.maxc + i);
+      const float inv = 1.0f / (Ls + 1e-10f);
+      for (int d = gt; d < hd; d += 128) {
+        float o = 0.0f;
+        for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
+        p.s.att[(size_t)hh * hd + d] = o * inv;
+      }
+    }
+    named_sync(B_GROUP0 + grp, 128);   // es / red / wpart / s_last are reused by the next item
+  }
+}
+
+// Short contexts (n <= kHeadMaxN positions): one CTA per head does the whole
+// attention of that head in one phase, scores and e_t in shared memory, so
+// no grid barrier separates the max from the exponentials.  Worker warp w
+// takes positions w, w + 19, ... eight at a time (all eight K or V rows in
+// flight); the eight dot products of a warp meet in one reduce-scatter.
+constexpr int kHeadMaxN = 1024;
+constexpr int kNW = kWorkers / 32;   // 19 worker warps
+
+template <int ESZ>
+__device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, int layer) {
+  const int w = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int wt = (int)threadIdx.x - 32;
+  const int n = h->pos + 1;
+  const int hd = p.s.hd, n_heads = p.s.n_heads, group = n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
+  float* sc = smf;                              // [n]: scores, then e_t
+  float* part = smf + kHeadMaxN;                // [kNW][kMaxHd] PV partials
+  float* red = part + kNW * kMaxHd;             // [32]
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].k_cache);
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].v_cache);
+  for (int hh = blockIdx.x; hh < n_heads; hh += gridDim.x) {
+    const int kvh = hh / group;
+    const uint8_t* kc = kbase + (size_t)kvh * hd * ESZ;
+    const uint8_t* vc = vbase + (size_t)kvh * hd * ESZ;
+    float4 qv[kMaxHd / 128];
+#pragma unroll
+    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      qv[sl] = d < hd ? __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // scores (llm.c:686-692), eight positions per warp per pass
+    for (int t0 = w; t0 < n; t0 += 8 * kNW) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+#pragma unroll
+      for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+        const int d = 128 * sl + 4 * lane;
+        if (d < hd) {
+          float4 kv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int t = t0 + u * kNW;
+            kv[u] = t < n ? ldcg4<ESZ>(kc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            v[u] = fmaf(qv[sl].x, kv[u].x, fmaf(qv[sl].y, kv[u].y, fmaf(qv[sl].z, kv[u].z, fmaf(qv[sl].w, kv[u].w, v[u]))));
+        }
+      }
+      // reduce-scatter over lane bits 4, 3, 2: lane l ends with position
+      // (l >> 2) & 7 summed over those bits; bits 1, 0 finish the sum
+#pragma unroll
+      for (int half = 4, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? v[half + i] : v[i];
+          const float send = up ? v[i] : v[half + i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      const int t = t0 + ((lane >> 2) & 7) * kNW;
+      if ((lane & 3) == 0 && t < n) sc[t] = dot * scale;
+    }
+    // the V rows of this warp's first PV pass (slab 0) start loading now, so
+    // their latency overlaps the softmax
+    Raw4<ESZ> vpre[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int t = w + u * kNW;
+      vpre[u] = (t < n && 4 * lane < hd) ? ldcg_raw<ESZ>(vc + ((size_t)t * kv_dim + 4 * lane) * ESZ) : raw_zero<ESZ>();
+    }
+    named_sync(B_WORKERS, kWorkers);
+    // llm.c:509-521: max, e_t = llm_expf(s_t - max), sum (tree), 1/(sum + 1e-10)
+    float m = -INFINITY;
+    for (int t = wt; t < n; t += kWorkers) m = fmaxf(m, sc[t]);
+    m = warp_max_f(m);
+    if (lane == 0) red[w] = m;
+    named_sync(B_WORKERS, kWorkers);
+    float M = red[0];
+    for (int i = 1; i < kNW; ++i) M = fmaxf(M, red[i]);
+    float l = 0.0f;
+    for (int t = wt; t < n; t += kWorkers) {
+      const float e = ref_expf(__fsub_rn(sc[t], M));
+      sc[t] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    named_sync(B_WORKERS, kWorkers);   // every thread has read red (the max) and written its e_t
+    if (lane == 0) red[w] = l;
+    // sum_t e_t v_t[d] (llm.c:703-712): warp w over its positions, lane l four d
+#pragma unroll
+    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      if (d < hd) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t0 = w; t0 < n; t0 += 8 * kNW) {
+          float4 vv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int t = t0 + u * kNW;
+            if (sl == 0 && t0 == w)
+              vv[u] = widen<ESZ>(vpre[u]);
+            else
+              vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int t = t0 + u * kNW;
+            const float e = t < n ? sc[t] : 0.0f;
+            acc.x = fmaf(e, vv[u].x, acc.x);
+            acc.y = fmaf(e, vv[u].y, acc.y);
+            acc.z = fmaf(e, vv[u].z, acc.z);
+            acc.w = fmaf(e, vv[u].w, acc.w);
+          }
+        }
+        *reinterpret_cast<float4*>(part + w * kMaxHd + d) = acc;
+      }
+    }
+    named_sync(B_WORKERS, kWorkers);
+    float L = red[0];
+    for (int i = 1; i < kNW; ++i) L += red[i];
+    const float inv = 1.0f / (L + 1e-10f);
+    for (int d = wt; d < hd; d += kWorkers) {
+      float o = part[d];
+      for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
+      p.s.att[(size_t)hh * hd + d] = o * inv;
+    }
+    named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the step
+// ---------------------------------------------------------------------------
+template <int ESZ>
+__device__ __forceinline__ void gemv_phase(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
+                                           int kind, int layer, int& gs) {
+  if ((threadIdx.x >> 5) <= kChain)
+    chain_gemv<ESZ>(p, h, P, kind, layer, gs);
+  else if (p.g[kind].qb == 16)
+    compute_gemv<16>(p, h, X, P, ring, kind, layer, gs);
+  else
+    compute_gemv<32>(p, h, X, P, ring, kind, layer, gs);
+}
+
+template <int ESZ>
+__global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  Hdr* h = reinterpret_cast<Hdr*>(smem);
+  uint32_t* X = reinterpret_cast<uint32_t*>(smem + kHdr);
+  float* P = reinterpret_cast<float*>(smem + kHdr + kXBytes);
+  uint8_t* ring = smem + kHdr + kXBytes + kPBytes;
+  int* err = p.s.io + 3;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&h->full[s], 1);
+      mbar_init(&h->empty[s], kCompute);
+    }
+    for (int c = 0; c < kChain; ++c) {
+      mbar_init(&h->pfull[c], kCompute);
+      mbar_init(&h->pempty[c], 1);
+    }
+    h->abort = 0;
+    // an earlier step whose bounded wait ran out leaves the error word set:
+    // then nothing runs (the host reports it and resets the step)
+    h->skip = *reinterpret_cast<volatile int*>(err) != 0;
+    h->pos = p.s.io[1];
+    h->tok = p.s.chained ? p.s.io[2] : p.s.io[0];
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (h->skip) return;
+  if (threadIdx.x < 32) {
+    if (threadIdx.x == 0) producer(p, h, ring);
+    return;
+  }
+  int gs = 0;
+  // per layer: q|k|v, attention (one phase per head for short contexts,
+  // else split-K scores then softmax*V), o, gate|up, down; then the LM head.
+  // One call site per role keeps every role inlined once.
+  const bool short_ctx = h->pos + 1 <= kHeadMaxN;
+  unsigned nsync = 0;
+  const int nph = 6 * p.s.n_layers + 1;
+  for (int ph = 0; ph < nph; ++ph) {
+    const int l = ph / 6, r = ph - 6 * l;
+    if (l == p.s.n_layers || r == 0 || r >= 3) {
+      const int kind = l == p.s.n_layers ? K_LM : r == 0 ? K_QKV : r == 3 ? K_O : r == 4 ? K_GU : K_D;
+      gemv_phase<ESZ>(p, h, X, P, ring, kind, l, gs);
+      if (kind == K_LM) break;
+    } else if (short_ctx) {
+      if (r == 2) continue;
+      attn_head<ESZ>(p, h, reinterpret_cast<float*>(X), l);
+    } else if (r == 1) {
+      attn_scores<ESZ>(p, h, P, l);
+    } else {
+      attn_pv<ESZ>(p, h, P, l);
+    }
+    if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) return;
+  }
+}
+
+}  // namespace step
+}  // namespace tos
+
+using namespace tos;
+using namespace tos::step;
+
+extern "C" size_t tosk_step_sync_bytes(void) { return 256 + (size_t)kMaxGrid * 8; }
+
+static inline int round_up_i(int v, int a) { return (v + a - 1) / a * a; }
+static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static int make_geo(int R, int cols, int qtype, int unit, Geo& G) {
+  if (R <= 0 || cols <= 0 || cols % 32 != 0 || R % unit != 0) return (int)cudaErrorInvalidValue;
+  if (qtype != TOSK_Q4_0 && qtype != TOSK_Q8_0) return (int)cudaErrorNotSupported;
+  G.R = R;
+  G.nb = cols / 32;
+  // a block per compute thread; its fixed-point record in shared memory
+  if (G.nb > 32 * kCompute || G.nb * 128 > kXBytes) return (int)cudaErrorNotSupported;
+  G.nbp = round_up_i(G.nb, 8);
+  G.qb = qtype == TOSK_Q4_0 ? 16 : 32;
+  G.unit = unit;
+  G.pstride = round_up_i(G.nb, 8) + 4;
+  int tr = 32;
+  while (tr > 0 && (round_up_i(tr * G.nb * G.qb, 16) + tr * G.nbp * 2 > kSlot ||
+                    kChain * tr * G.pstride * 4 > kPBytes))
+    --tr;
+  if (unit == 2) tr &= ~1;
+  if (tr < unit) return (int)cudaErrorNotSupported;
+  G.tr = tr;
+  G.sc_off = round_up_i(tr * G.nb * G.qb, 16);
+  return 0;
+}
+
+template <int ESZ>
+static int prepare_kernel(int* occ) {
+  static int done = 0, occ_v = 0;
+  if (!done) {
+    cudaError_t e = cudaFuncSetAttribute(decode_step_kernel<ESZ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_v, decode_step_kernel<ESZ>, kThreads, kSmem);
+    if (e != cudaSuccess) return (int)e;
+    done = 1;
+  }
+  *occ = occ_v;
+  return 0;
+}
+
+static int plan(const tosk_step_t* s, Params* p) {
+  if (!s || !s->layers || !s->io || !s->sync || !s->attn_ws || s->n_layers <= 0) return (int)cudaErrorInvalidValue;
+  if (s->n_heads <= 0 || s->n_kv <= 0 || s->n_heads % s->n_kv != 0 || s->hd <= 0 || s->max_seq <= 0)
+    return (int)cudaErrorInvalidValue;
+  if (s->kv_type != TOSK_F16 && s->kv_type != TOSK_F32) return (int)cudaErrorNotSupported;
+  const int esz = s->kv_type == TOSK_F16 ? 2 : 4;
+  if (s->hd > kMaxHd || s->hd % 4 != 0 || (s->hd * esz) % 16 != 0) return (int)cudaErrorNotSupported;
+  if (s->dim % 32 != 0 || s->ff % 32 != 0) return (int)cudaErrorNotSupported;
+  const int q_dim = s->n_heads * s->hd, kv_dim = s->n_kv * s->hd;
+  if (q_dim % 32 != 0) return (int)cudaErrorNotSupported;
+  // 16-byte aligned vectors (float4 block loads)
+  const void* vecs[] = {s->x, s->q, s->att, s->h, s->logits};
+  for (const void* v : vecs)
+    if (!v || (reinterpret_cast<uintptr_t>(v) & 15)) return (int)cudaErrorInvalidValue;
+  memset(p, 0, sizeof(*p));
+  p->s = *s;
+  int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
+  if (!e) e = make_geo(s->dim, q_dim, s->wtype, 1, p->g[K_O]);
+  if (!e) e = make_geo(2 * s->ff, s->dim, s->wtype, 2, p->g[K_GU]);
+  if (!e) e = make_geo(s->dim, s->ff, s->wtype, 1, p->g[K_D]);
+  if (!e) e = make_geo(s->vocab, s->dim, s->lm_type, 1, p->g[K_LM]);
+  if (e) return e;
+  p->maxc = (s->max_seq + kChunk - 1) / kChunk;
+  char* ws = reinterpret_cast<char*>(s->attn_ws);
+  p->S = reinterpret_cast<float*>(ws);
+  p->cmax = reinterpret_cast<float*>(ws + al256((size_t)s->n_heads * s->max_seq * 4));
+  p->lsum = reinterpret_cast<float*>(reinterpret_cast<char*>(p->cmax) + al256((size_t)s->n_heads * p->maxc * 4));
+  p->opart = reinterpret_cast<float*>(reinterpret_cast<char*>(p->lsum) + al256((size_t)s->n_heads * p->maxc * 4));
+  p->cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(p->opart) +
+                                  al256((size_t)s->n_heads * p->maxc * kMaxHd * 4));
+  int occ = 0;
+  e = esz == 2 ? prepare_kernel<2>(&occ) : prepare_kernel<4>(&occ);
+  if (e) return e;
+  // every CTA must be resident at once (grid barriers): one per SM
+  if (occ < 1 || tosk_num_sms() > kMaxGrid) return (int)cudaErrorNotSupported;
+  return 0;
+}
+
+extern "C" int tosk_step_check(const tosk_step_t* s) {
+  Params p;
+  return plan(s, &p);
+}
+
+extern "C" int tosk_step_launch(const tosk_step_t* s, cudaStream_t st) {
+  Params p;
+  int e = plan(s, &p);
+  if (e) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tosk_num_sms());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (s->kv_type == TOSK_F16) return (int)cudaLaunchKernelEx(&cfg, decode_step_kernel<2>, p);
+  return (int)cudaLaunchKernelEx(&cfg, decode_step_kernel<4>, p);
+}

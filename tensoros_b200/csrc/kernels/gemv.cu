@@ -130,18 +130,6 @@ __device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t*
 
 // (Capping registers at 72 so that two CTAs share an SM made every stage ~25%
 // slower than the overlap it buys; one CTA per SM keeps ~85 registers.)
-template <int QB>
-__device__ __forceinline__ float block_value_fast(const uint8_t* stq, const uint16_t* sts, int r, int b,
-                                                  int nb, int nbp, const XFix& f) {
-  const float d = h2f(sts[r * nbp + b]);
-  if constexpr (QB == 16) {
-    const uint4 q = *reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 16);
-    return fast_q4_0(q, d, f);
-  } else {
-    const uint4* p = reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 32);
-    return fast_q8_0(p[0], p[1], d, f);
-  }
-}
 
 template <int QB, bool kNorm, int kEpi, bool kFast>
 __global__ void __launch_bounds__(704, 1) gemv_kernel(const GemvArgs a) {

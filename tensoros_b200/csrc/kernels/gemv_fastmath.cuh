@@ -48,9 +48,12 @@ __device__ __forceinline__ uint32_t dp4a_ss(uint32_t a, uint32_t b, uint32_t c) 
   return d;
 }
 
+// Six dot-product chains per block (each limb split over the low- and
+// high-nibble words, or even and odd words) keep the dependent dp4a runs
+// short; the integer total is the same in any order (mod 2^32).
 __device__ __forceinline__ float fast_q4_0(const uint4 q, const float d, const XFix& f) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-  uint32_t a0 = (uint32_t)f.c, a1 = 0, a2 = 0;
+  uint32_t a0 = (uint32_t)f.c, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t lo = w[k] & 0x0F0F0F0Fu;
@@ -58,26 +61,29 @@ __device__ __forceinline__ float fast_q4_0(const uint4 q, const float d, const X
     a0 = dp4a_uu(lo, f.l[0][2 * k], a0);
     a1 = dp4a_uu(lo, f.l[1][2 * k], a1);
     a2 = dp4a_us(lo, f.l[2][2 * k], a2);
-    a0 = dp4a_uu(hi, f.l[0][2 * k + 1], a0);
-    a1 = dp4a_uu(hi, f.l[1][2 * k + 1], a1);
-    a2 = dp4a_us(hi, f.l[2][2 * k + 1], a2);
+    b0 = dp4a_uu(hi, f.l[0][2 * k + 1], b0);
+    b1 = dp4a_uu(hi, f.l[1][2 * k + 1], b1);
+    b2 = dp4a_us(hi, f.l[2][2 * k + 1], b2);
   }
-  const int y = (int)(a0 + (a1 << 8) + (a2 << 16));
+  const int y = (int)((a0 + b0) + ((a1 + b1) << 8) + ((a2 + b2) << 16));
   return (float)y * (d * f.s);
 }
 
 __device__ __forceinline__ float fast_q8_0(const uint4 qa, const uint4 qb, const float d,
                                            const XFix& f) {
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  uint32_t a0 = 0, a1 = 0, a2 = 0;
+  uint32_t a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < 8; j += 2) {
     a0 = dp4a_su(w[j], f.l[0][j], a0);
     a1 = dp4a_su(w[j], f.l[1][j], a1);
     a2 = dp4a_ss(w[j], f.l[2][j], a2);
+    b0 = dp4a_su(w[j + 1], f.l[0][j + 1], b0);
+    b1 = dp4a_su(w[j + 1], f.l[1][j + 1], b1);
+    b2 = dp4a_ss(w[j + 1], f.l[2][j + 1], b2);
   }
-  const int lo = (int)(a0 + (a1 << 8));
-  return fmaf((float)(int)a2, 65536.0f, (float)lo) * (d * f.s);
+  const int lo = (int)((a0 + b0) + ((a1 + b1) << 8));
+  return fmaf((float)(int)(a2 + b2), 65536.0f, (float)lo) * (d * f.s);
 }
 
 // Byte limbs 0, 1, 2 of four integers, each packed low to high.
@@ -100,38 +106,30 @@ __device__ __forceinline__ void make_xfix(const float (&x)[32], XFix& f) {
   const int eb = (int)((__float_as_uint(m) >> 23) & 0xFF);   // biased exponent of the max
   const int e = max(eb - 127 - 21, -126);                      // max / 2^e < 2^22
   const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
-  int X[32];
+  const bool finite = eb != 255;
+  f.s = finite ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x7FC00000u);
   int sum = 0;
-  if (eb == 255) {
-    f.s = __uint_as_float(0x7FC00000u);
+  // eight elements at a time (quant word k): rint(x / 2^e) - x * 2^-e is
+  // exact and adding 1.5 * 2^23 rounds it to an integer held in the low
+  // mantissa bits (|X| <= 2^22); a block with a non-finite value gets X = 0
 #pragma unroll
-    for (int i = 0; i < 32; ++i) X[i] = 0;
-  } else {
-    f.s = __uint_as_float((uint32_t)(e + 127) << 23);
-    // rint(x / 2^e): x * 2^-e is exact and adding 1.5 * 2^23 rounds it to
-    // an integer held in the low mantissa bits (|X| <= 2^22)
+  for (int k = 0; k < 4; ++k) {
+    int X[8];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      X[i] = __float_as_int(fmaf(x[i], inv, 12582912.0f)) - 0x4B400000;
-      sum += X[i];
+    for (int j = 0; j < 8; ++j) {
+      X[j] = finite ? __float_as_int(fmaf(x[8 * k + j], inv, 12582912.0f)) - 0x4B400000 : 0;
+      sum += X[j];
+    }
+    if constexpr (QB == 16) {
+      // quant word k byte p holds elements 8k+2p (low nibble) and 8k+2p+1
+      pack_limbs(X[0], X[2], X[4], X[6], f.l[0][2 * k], f.l[1][2 * k], f.l[2][2 * k]);
+      pack_limbs(X[1], X[3], X[5], X[7], f.l[0][2 * k + 1], f.l[1][2 * k + 1], f.l[2][2 * k + 1]);
+    } else {
+      pack_limbs(X[0], X[1], X[2], X[3], f.l[0][2 * k], f.l[1][2 * k], f.l[2][2 * k]);
+      pack_limbs(X[4], X[5], X[6], X[7], f.l[0][2 * k + 1], f.l[1][2 * k + 1], f.l[2][2 * k + 1]);
     }
   }
   f.c = -8 * sum;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    if constexpr (QB == 16) {
-      // quant word k byte p holds elements 8k+2p (low nibble) and 8k+2p+1
-      pack_limbs(X[8 * k], X[8 * k + 2], X[8 * k + 4], X[8 * k + 6], f.l[0][2 * k], f.l[1][2 * k],
-                 f.l[2][2 * k]);
-      pack_limbs(X[8 * k + 1], X[8 * k + 3], X[8 * k + 5], X[8 * k + 7], f.l[0][2 * k + 1],
-                 f.l[1][2 * k + 1], f.l[2][2 * k + 1]);
-    } else {
-      pack_limbs(X[8 * k], X[8 * k + 1], X[8 * k + 2], X[8 * k + 3], f.l[0][2 * k], f.l[1][2 * k],
-                 f.l[2][2 * k]);
-      pack_limbs(X[8 * k + 4], X[8 * k + 5], X[8 * k + 6], X[8 * k + 7], f.l[0][2 * k + 1],
-                 f.l[1][2 * k + 1], f.l[2][2 * k + 1]);
-    }
-  }
 }
 
 // Cooperative form of make_xfix: eight consecutive lanes (chunk c = lane & 7)
@@ -179,6 +177,21 @@ __device__ __forceinline__ void xfix_group(float4 v, int c, uint32_t& w0, uint32
   } else {
     pack_limbs(X0, X1, X2, X3, w0, w1, w2);   // quant word c = elements 4c..4c+3
     wi = c;
+  }
+}
+
+// FAST value of block b of row r of a shared-memory stage (quants
+// [rows][nb][QB], fp16 scales [rows][nbp]).
+template <int QB>
+__device__ __forceinline__ float block_value_fast(const uint8_t* stq, const uint16_t* sts, int r, int b,
+                                                  int nb, int nbp, const XFix& f) {
+  const float d = h2f(sts[r * nbp + b]);
+  if constexpr (QB == 16) {
+    const uint4 q = *reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 16);
+    return fast_q4_0(q, d, f);
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(stq + ((size_t)r * nb + b) * 32);
+    return fast_q8_0(p[0], p[1], d, f);
   }
 }
 

@@ -172,12 +172,15 @@ class Model:
     same fields); mirrors llm_forward_token / greedy llm_generate."""
 
     def __init__(self, synth, attn_mode: int = 0, kv_type: int | None = None, gemv_mode: int = 0,
-                 shard: tuple | None = None):
+                 shard: tuple | None = None, fused_step: int = 0):
         """shard = (rank, world, nccl_id bytes): this process's rows of a model
-        row-sharded over `world` GPUs (tos_model_create_sharded)."""
+        row-sharded over `world` GPUs (tos_model_create_sharded).
+        fused_step = 1 runs each token as one fused persistent kernel where the
+        model allows it (FAST arithmetic on one GPU)."""
         self.synth = synth
         self.desc = _ffi.ModelDesc()
         synth.fill_desc(self.desc, attn_mode=attn_mode, kv_type=kv_type, gemv_mode=gemv_mode)
+        self.desc.fused_step = fused_step
         h = C.c_void_p()
         if shard is None:
             st = _lib().tos_model_create(C.byref(h), C.byref(self.desc))
@@ -243,6 +246,11 @@ class Model:
 
     def device_bytes(self) -> int:
         return int(_lib().tos_model_device_bytes(self.h))
+
+    @property
+    def fused(self) -> bool:
+        """True when each token runs as the one fused kernel (decode_step.cu)."""
+        return bool(_lib().tos_model_fused(self.h))
 
 
 def nccl_unique_id() -> bytes:

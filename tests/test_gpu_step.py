@@ -1,0 +1,149 @@
+"""The fused per-token decode kernel (decode_step.cu: every layer, the LM head
+and the greedy argmax of llm_forward_token, runtime/nn/llm.c:641-743 and
+1129-1140, in one cooperative kernel with FAST arithmetic) against the
+oracle (the C restatement pinned to the reference) and against the
+per-operator FAST kernels of the same model:
+  * logits within the FAST bound, normwise 1e-4, of the oracle's;
+  * logits no further from the oracle's than the per-operator FAST path's
+    (both differ from the exact values only by summation order: ~1e-7 per
+    projection, up to ~1e-5 after a few layers), and within 5e-5 of them
+    where no oracle run is affordable;
+  * greedy ids identical to the oracle's;
+  * bitwise-identical results when a step is repeated;
+  * device-chained decode equal to step-by-step calls."""
+import numpy as np
+import pytest
+
+from tensoros_b200 import ops
+from tensoros_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4     # FAST bound against the reference
+CLOSE = 5e-5   # fused kernel against the per-operator FAST kernels (model level)
+FAST = 1
+
+
+def normwise(got, ref):
+    s = float(np.max(np.abs(ref)))
+    return float(np.max(np.abs(got.astype(np.float64) - ref))) / (s if s > 0 else 1.0)
+
+
+def fast_model(synth, per_op=False, kv_type=None):
+    return ops.Model(synth, attn_mode=1, gemv_mode=FAST, kv_type=kv_type, fused_step=0 if per_op else 1)
+
+
+def compare_with_oracle(oracle, cfg, seed, n_steps, n_gen, layers=None):
+    synth = W.make_model(cfg, seed, n_layers=layers)
+    prompt = W.tokens(n_steps, cfg["vocab_size"], seed)
+    ref = oracle.model(synth)
+    fused, per_op = fast_model(synth), fast_model(synth, per_op=True)
+    try:
+        assert fused.fused and not per_op.fused
+        for i, t in enumerate(prompt):
+            lr = ref.forward(int(t), i)
+            lf = fused.forward(int(t), i)
+            lp = per_op.forward(int(t), i)
+            ef, ep = normwise(lf, lr), normwise(lp, lr)
+            assert ef <= TOL, (i, ef)
+            assert ef <= 4 * ep + 2e-6, (i, ef, ep)
+        ref.close()
+        ref = oracle.model(synth)
+        fused.reset()
+        ids_ref = ref.generate_greedy(prompt, n_gen)
+        ids = fused.generate_greedy(prompt, n_gen)
+        assert np.array_equal(ids, ids_ref), np.nonzero(ids != ids_ref)[0][:5]
+    finally:
+        ref.close()
+        fused.close()
+        per_op.close()
+
+
+def test_step_tiny_llama(gpu, oracle):
+    """dim 288 (9 blocks a row), 6 heads of 48, Q8_0 everywhere, fp32 KV"""
+    compare_with_oracle(oracle, W.TINY_LLAMA, 11, 12, 48)
+
+
+def test_step_gqa(gpu, oracle):
+    """grouped-query attention (8 heads over 4 KV heads), Q8_0, fp32 KV"""
+    compare_with_oracle(oracle, W.SHARD_SMALL, 5, 8, 32)
+
+
+def test_step_mixed_types(gpu, oracle):
+    """Q4_0 projections with a Q8_0 LM head and Q8_0 embeddings"""
+    cfg = dict(W.SHARD_SMALL, wtype=W.TYPE_Q4_0, embd_type=W.TYPE_Q8_0, out_type=W.TYPE_Q8_0)
+    compare_with_oracle(oracle, cfg, 6, 6, 24)
+
+
+def test_step_7b_layers_deterministic_and_chained(gpu):
+    """Llama-2-7B-shaped rows (4096 / 11008 / 32000 wide, fp16 KV), two
+    layers: fused vs per-operator logits, repeat-bitwise, and the chained
+    decode equal to step-by-step greedy calls."""
+    synth = W.make_model(W.LLAMA2_7B, 7, n_layers=2)
+    prompt = W.tokens(6, W.LLAMA2_7B["vocab_size"], 7)
+    fused, per_op = fast_model(synth), fast_model(synth, per_op=True)
+    try:
+        assert fused.fused
+        first = None
+        for i, t in enumerate(prompt):
+            lf = fused.forward(int(t), i)
+            lp = per_op.forward(int(t), i)
+            assert normwise(lf, lp) <= CLOSE, (i, normwise(lf, lp))
+            if first is None:
+                first = lf.copy()
+        fused.reset()
+        again = fused.forward(int(prompt[0]), 0)
+        assert np.array_equal(first.view(np.uint32), again.view(np.uint32)), "repeat must be bitwise equal"
+        # chained decode vs host-driven greedy steps from the same cache
+        fused.reset()
+        nxt = 0
+        for i, t in enumerate(prompt):
+            nxt = fused.forward_argmax(int(t), i)
+        chained = fused.decode(nxt, len(prompt), 12)
+        fused.reset()
+        for i, t in enumerate(prompt):
+            nxt = fused.forward_argmax(int(t), i)
+        steps = []
+        pos = len(prompt)
+        for _ in range(12):
+            steps.append(nxt)
+            nxt = fused.forward_argmax(nxt, pos)
+            pos += 1
+        # step k of the chained decode consumes steps[k] and yields steps[k + 1]
+        assert list(chained) == steps[1:] + [nxt]
+    finally:
+        fused.close()
+        per_op.close()
+
+
+def test_step_long_context(gpu):
+    """positions past several 64-position attention chunks: the prompt goes
+    through the batched prefill, then fused decode steps at positions
+    520.. agree with the per-operator kernels"""
+    synth = W.make_model(W.LLAMA2_7B, 9, n_layers=1)
+    prompt = W.tokens(520, W.LLAMA2_7B["vocab_size"], 9)
+    fused, per_op = fast_model(synth), fast_model(synth, per_op=True)
+    try:
+        a = fused.prefill(prompt[:512], 0)
+        b = per_op.prefill(prompt[:512], 0)
+        assert a == b
+        for i in range(512, 520):
+            lf = fused.forward(int(prompt[i]), i)
+            lp = per_op.forward(int(prompt[i]), i)
+            assert normwise(lf, lp) <= CLOSE, (i, normwise(lf, lp))
+    finally:
+        fused.close()
+        per_op.close()
+
+
+def test_step_off_for_exact_and_opt_out(gpu):
+    synth = W.make_model(W.SHARD_SMALL, 3)
+    for kw, want in [(dict(), False), (dict(fused_step=1), False),
+                     (dict(attn_mode=1, gemv_mode=FAST), False),
+                     (dict(attn_mode=1, gemv_mode=FAST, fused_step=1), True),
+                     (dict(attn_mode=0, gemv_mode=FAST, fused_step=1), False)]:
+        m = ops.Model(synth, **kw)
+        try:
+            assert m.fused == want, kw
+        finally:
+            m.close()
