@@ -9,17 +9,22 @@ batch 1.  A step is one decoded token.
   value      tokens/s with the model resident in HBM: K greedy steps chained on
              the device (tos_model_decode), timed with CUDA events on the
              model's stream.  --math fast (default): FAST GEMV and attention
-             arithmetic (normwise error <= 1e-4); --math exact: bit-identical
-             to the reference.  With fast, "exact" reports the bit-exact
+             arithmetic (normwise error <= 1e-4), each token one fused
+             persistent kernel (decode_step_kernel; --per-op: a kernel per
+             operator); --math exact: bit-identical to the reference, a
+             kernel per operator.  With fast, "exact" reports the bit-exact
              arithmetic's tokens/s on the same prompt and whether its greedy
              ids equal the fast run's.  Weights (3.7 GB per step) exceed L2 (126 MB), so
              no flush is needed.
   e2e        the same metric through tos_model_forward_argmax: every step
              copies token+position host->device (8 B, pinned) and the next
              token device->host (8 B).
-  roofline   the dominant kernel, the Q4_0 GEMV, timed in isolation on the
-             4096x4096 shape (one launch streams 9,469,952 algorithmic bytes),
-             rotating 32 weight copies (303 MB) so every launch is L2-cold.
+  roofline   the dominant kernel: the fused step (one launch per token: all
+             weight planes + the KV rows of the context per launch), or with
+             a kernel per operator the Q4_0 GEMV.  gemv_roofline: that GEMV
+             timed in isolation on the 4096x4096 shape (one launch streams
+             9,469,952 algorithmic bytes), rotating 32 weight copies (303 MB)
+             so every launch is L2-cold.
   cpu_baseline  the reference's own C implementation (runtime/nn/llm.c,
              compiled hosted) on one host core, rank 0 at N=1.
 
@@ -45,6 +50,7 @@ sys.path.insert(0, str(ROOT))
 
 GEMV_BYTES_4096 = 4096 * 128 * 18 + 4096 * 4 + 4096 * 4   # 9,469,952 B per launch
 METRIC = "decode tokens/sec (Llama-2-7B-shaped, Q4_0, batch 1)"
+STEP_TRAFFIC = None   # filled in from the committed ncu capture of the fused step
 
 
 def peaks():
@@ -361,7 +367,7 @@ def run_ours(args, world, rank, local):
     # ---- value / e2e: the selected arithmetic
     clk = ClockSampler(local)
     model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(),
-                      fused_step=int(args.fused and fast))
+                      fused_step=int(fast and not args.per_op))
     fused = model.fused
     t_ms, t_e2e, ids = timed_decode(model, clk)
     prefill = None
@@ -407,6 +413,21 @@ def run_ours(args, world, rank, local):
         # row, norms and the small vectors (<1 MB, ignored)
         ctx = args.prefill + warm + K // 2
         step_bytes = weight_bytes + L * 2 * (ctx + 1) * 4096 * 2
+        gemv_rl = {"bound": "hbm", "kernel": f"gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
+                   "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                   "frac": achieved / peak,
+                   # dram__bytes_read.sum + dram__bytes_write.sum of one launch
+                   # of this kernel and shape (profiles/gemv_q4_0_fast_4096x4096.md,
+                   # profiles/gemv_q4_0_4096x4096.md for the exact arithmetic)
+                   "traffic": 9482496 if args.math == "fast" else 9485568,
+                   "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0}
+        step_us = t_ms / K * 1000.0
+        step_rl = {"bound": "hbm", "kernel": "decode_step_kernel (one launch per token, all layers)",
+                   "achieved": step_bytes / (step_us * 1e-6) / 1e9, "peak": peak, "peak_source": peak_kind,
+                   "unit": "GB/s", "frac": step_bytes / (step_us * 1e-6) / 1e9 / peak,
+                   # dram bytes of one launch (profiles/decode_step_llama2_7b_q4_0.md)
+                   "traffic": STEP_TRAFFIC,
+                   "algorithmic_bytes_per_launch": step_bytes, "launch_us": step_us}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, kind, dt = ref_cpu_decode(synth, args.ref_tokens, args.prefill, 1)
@@ -428,19 +449,9 @@ def run_ours(args, world, rank, local):
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
             "gpu_launches": launches,
-            "step_roofline": None if not fused else {
-                "bound": "hbm", "kernel": "decode_step_kernel (one launch per token)",
-                "achieved": step_bytes / (t_ms / K / 1000.0) / 1e9, "peak": peak, "peak_source": peak_kind,
-                "unit": "GB/s", "frac": step_bytes / (t_ms / K / 1000.0) / 1e9 / peak,
-                "algorithmic_bytes_per_launch": step_bytes, "launch_us": t_ms / K * 1000.0},
-            "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
-                         "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch
-                         # of this kernel and shape (profiles/gemv_q4_0_fast_4096x4096.md,
-                         # profiles/gemv_q4_0_4096x4096.md for the exact arithmetic)
-                         "traffic": 9482496 if args.math == "fast" else 9485568,
-                         "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0},
+            # the dominant kernel: the fused step when it runs, else the GEMV
+            "roofline": step_rl if fused else gemv_rl,
+            "gemv_roofline": gemv_rl,
             "decode_weight_gbs": weight_bytes * value / 1e9,   # all GPUs together
             "prefill": prefill,
             "clocks": clk.summary(),
@@ -467,8 +478,8 @@ def main():
                          "(normwise error <= 1e-4, greedy ids identical)")
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--fused", action="store_true",
-                    help="run each token as the one fused persistent kernel (fast arithmetic, one GPU)")
+    ap.add_argument("--per-op", action="store_true",
+                    help="fast arithmetic with a kernel per operator instead of the one fused kernel per token")
     ap.add_argument("--no-exact", action="store_true", help="skip the EXACT-arithmetic comparison run")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill measurement")
     ap.add_argument("--gemv-only", action="store_true",

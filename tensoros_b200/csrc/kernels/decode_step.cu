@@ -14,7 +14,7 @@
 //     the producer only waits for free slots: while the other warps wait at
 //     a grid barrier or run attention, the next projection's rows are
 //     already landing.
-//   * warps 4..19 (compute) evaluate block values of the ring's stages
+//   * warps 4..15 (compute) evaluate block values of the ring's stages
 //     exactly as the FAST GEMV does (integer dp4a dot products on 24-bit
 //     fixed-point x, gemv_fastmath.cuh) into a partials tile;
 //   * warps 1..3 (chain) add each row's partials in a fixed tree order and
@@ -22,8 +22,7 @@
 //     with a running argmax);
 //   * between dependent phases all 148 CTAs meet at a grid barrier (an
 //     atomic counter in global memory, release/acquire at GPU scope, every
-//     wait bounded); attention runs on 16 worker warps as four groups of
-//     four (the split-K scores / softmax*V passes of attention.cu's FAST
+//     wait bounded); attention runs on the 15 worker warps (the split-K scores / softmax*V passes of attention.cu's FAST
 //     mode).
 //
 // Each CTA owns the same contiguous row range of a given projection in every
@@ -48,23 +47,26 @@
 namespace tos {
 namespace step {
 
-// 20 warps: five per SM sub-partition leave 96 registers a thread
-constexpr int kThreads = 640;            // warp 0 producer, 1..3 chain, 4..19 compute
+// 16 warps (four per SM sub-partition) leave 128 registers a thread: room
+// for four rows of block values in flight per compute thread
+constexpr int kThreads = 512;            // warp 0 producer, 1..3 chain, 4..15 compute
 constexpr int kChain = 3;
-constexpr int kCompute = 16;
+constexpr int kCompute = 12;
 constexpr int kWorkers = kThreads - 32;  // chain + compute threads
-constexpr int kSlot = 36864;             // ring slot: 16 rows of a 4096-column Q4_0 matrix
+constexpr int kSlot = 41472;             // ring slot: 18 rows of a 4096-column Q4_0 matrix
 constexpr int kSlots = 3;
 constexpr int kHdr = 2048;
 constexpr int kPreRows = 128;           // residual rows a CTA can stage for its epilogue
 constexpr int kXBytes = 58368;           // fixed-point records of x: 128 B a block, up to 456 blocks
-constexpr int kPBytes = 25344;           // partials tile (also attention scratch)
+constexpr int kPBytes = 28512;           // partials tile (also attention scratch)
 constexpr int kSmem = kHdr + kXBytes + kPBytes + kSlots * kSlot;
 static_assert(kSmem <= 227 * 1024, "shared memory");
-constexpr int kGroups = 4;               // attention groups of four worker warps (warps 1..16)
+constexpr int kGroups = kWorkers / 32 / 4;   // attention groups of four worker warps
 constexpr int kChunk = 64;               // attention positions per chunk
 constexpr int kMaxHd = 256;
 constexpr int kMaxGrid = 1024;
+constexpr int kHeadMaxN = 1024;          // longest context of the one-phase-per-head attention
+constexpr int kNW = kWorkers / 32;       // worker warps
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4, K_N = 5 };
 // named barriers (0 is __syncthreads)
 enum { B_COMPUTE = 1, B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4 };
@@ -140,6 +142,39 @@ __device__ __forceinline__ bool wait_mb(uint64_t* bar, uint32_t parity, int* err
   }
 }
 
+// L2 policies: weights are read once per token (evict first, so they do
+// not push out the KV rows and vectors the step reuses); KV rows prefetched
+// for the coming attention stay (evict last).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// bulk copy global -> shared with an L2 policy (no multicast)
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+// prefetch [src, src + bytes) into L2 (bytes a multiple of 16, 16-byte aligned)
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol)
+               : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared through L2 (cp.async.cg)
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -174,6 +209,17 @@ __device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target
   }
   named_sync(B_WORKERS, kWorkers);
   return !*reinterpret_cast<volatile int*>(&h->abort);
+}
+
+// A projection's geometry in registers: read once from the kernel
+// parameters and kept opaque to the compiler, which would otherwise reload
+// it inside the stage loops (a constant load with a computed index issues
+// on the narrow ADU pipe).
+__device__ __forceinline__ Geo geo_regs(const Params& p, int kind) {
+  Geo g = p.g[kind];
+  asm volatile("" : "+r"(g.R), "+r"(g.nb), "+r"(g.nbp), "+r"(g.qb), "+r"(g.unit), "+r"(g.tr), "+r"(g.pstride),
+               "+r"(g.sc_off));
+  return g;
 }
 
 __device__ __forceinline__ void row_range(const Geo& G, int& rb, int& re, int& nst) {
@@ -227,11 +273,12 @@ __device__ __forceinline__ void producer(const Params& p, Hdr* h, uint8_t* ring)
   int* err = p.s.io + 3;
   int gs = 0;
   bool ok = true;
+  const uint64_t pol = policy_evict_first();
   const int nphase = 4 * p.s.n_layers + 1;
   for (int i = 0; i < nphase && ok; ++i) {
     int layer;
     const int kind = gemv_kind_of(i, p.s.n_layers, layer);
-    const Geo& G = p.g[kind];
+    const Geo G = geo_regs(p, kind);
     const uint8_t* qs;
     const uint16_t* sc;
     planes(p, kind, layer, qs, sc);
@@ -253,8 +300,8 @@ __device__ __forceinline__ void producer(const Params& p, Hdr* h, uint8_t* ring)
       const uint32_t bs = (uint32_t)(n * G.nbp * 2);
       uint8_t* dst = ring + (size_t)s * kSlot;
       mbar_arrive_expect_tx(&h->full[s], bq + bs);
-      bulk_g2s(dst, qs + (size_t)r0 * G.nb * G.qb, bq, &h->full[s]);
-      bulk_g2s(dst + G.sc_off, sc + (size_t)r0 * G.nbp, bs, &h->full[s]);
+      bulk_g2s_hint(dst, qs + (size_t)r0 * G.nb * G.qb, bq, &h->full[s], pol);
+      bulk_g2s_hint(dst + G.sc_off, sc + (size_t)r0 * G.nbp, bs, &h->full[s], pol);
       ++gs;
     }
   }
@@ -306,7 +353,7 @@ __device__ __forceinline__ float4 embed_chunk(const void* embd, int type, int di
 template <int QB>
 __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
                                              int kind, int layer, int& gs) {
-  const Geo& G = p.g[kind];
+  const Geo G = geo_regs(p, kind);
   int* err = p.s.io + 3;
   const int ct = (int)threadIdx.x - 32 * (1 + kChain);   // 0 .. 511
   const int lane = threadIdx.x & 31;
@@ -333,8 +380,13 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
       int ons;
       row_range(p.g[K_O], orb, ore, ons);
     }
-    auto fetch = [&](int q) -> float4 {
-      if (emb) {
+    // every chunk of x (and of the norm weights) is fetched at once with
+    // asynchronous copies into the record area (and the idle partials area)
+    const bool stage_w = nw && nq * 16 <= kPBytes;
+    float4* W4 = reinterpret_cast<float4*>(P);
+    const int nr = (nq + 32 * kCompute - 1) / (32 * kCompute);   // rounds
+    if (emb) {
+      for (int q = ct; q < nq; q += 32 * kCompute) {
         const float4 v = embed_chunk(p.s.embd, p.s.embd_type, p.s.dim, h->tok, q);
         // the residual stream starts as the embedding: this CTA writes the
         // rows it owns in the o / down phases (their residual adds are its own)
@@ -342,24 +394,21 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if (4 * q + i >= orb && 4 * q + i < ore) p.s.x[4 * q + i] = e[i];
-        return v;
+        X4[q] = v;
       }
-      return __ldcg(reinterpret_cast<const float4*>(src) + q);
-    };
+    } else {
+      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(X4 + q, reinterpret_cast<const float4*>(src) + q);
+    }
+    if (stage_w)
+      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(W4 + q, reinterpret_cast<const float4*>(nw) + q);
+    cp_async_wait_all();   // a thread converts only the chunks it copied
     float ss = 1.0f;
-    // a fused RMSNorm stages the raw chunks in the record area and its
-    // weights in the (idle) partials area, every load of a thread in flight
-    const bool stage_w = nw && nq * 16 <= kPBytes;
-    float4* W4 = reinterpret_cast<float4*>(P);
     if (nw) {
       // RMSNorm (llm.c:416-442): tree sum of squares (serial per thread,
       // butterfly per warp, warps in order)
       float acc = 0.0f;
-#pragma unroll 2
       for (int q = ct; q < nq; q += 32 * kCompute) {
-        const float4 v = fetch(q);
-        if (stage_w) W4[q] = __ldg(reinterpret_cast<const float4*>(nw) + q);
-        X4[q] = v;
+        const float4 v = X4[q];
         acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
       }
 #pragma unroll
@@ -372,19 +421,17 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
     }
     // every lane runs the same number of rounds (xfix_group shuffles within
     // eight-lane groups; a round's eight lanes share a block)
-    for (int base = 0; base < nq; base += 32 * kCompute) {
-      const int q = base + ct;
+    for (int k = 0; k < nr; ++k) {
+      const int q = k * 32 * kCompute + ct;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (q < nq) {
+        v = X4[q];
         if (nw) {
-          v = X4[q];
           const float4 wv = stage_w ? W4[q] : __ldg(reinterpret_cast<const float4*>(nw) + q);
           v.x = __fmul_rn(__fmul_rn(v.x, ss), wv.x);
           v.y = __fmul_rn(__fmul_rn(v.y, ss), wv.y);
           v.z = __fmul_rn(__fmul_rn(v.z, ss), wv.z);
           v.w = __fmul_rn(__fmul_rn(v.w, ss), wv.w);
-        } else {
-          v = fetch(q);
         }
       }
       uint32_t w0, w1, w2;
@@ -436,7 +483,17 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
     float* Pc = P + c * G.tr * G.pstride;
     if (active) {
       int r = g;
-      for (; r + rg < n; r += 2 * rg) {   // two rows in flight
+      for (; r + 3 * rg < n; r += 4 * rg) {   // four rows in flight
+        const float y0 = block_value_fast<QB>(stq, sts, r, b, G.nb, G.nbp, xf);
+        const float y1 = block_value_fast<QB>(stq, sts, r + rg, b, G.nb, G.nbp, xf);
+        const float y2 = block_value_fast<QB>(stq, sts, r + 2 * rg, b, G.nb, G.nbp, xf);
+        const float y3 = block_value_fast<QB>(stq, sts, r + 3 * rg, b, G.nb, G.nbp, xf);
+        Pc[r * G.pstride + b] = y0;
+        Pc[(r + rg) * G.pstride + b] = y1;
+        Pc[(r + 2 * rg) * G.pstride + b] = y2;
+        Pc[(r + 3 * rg) * G.pstride + b] = y3;
+      }
+      for (; r + rg < n; r += 2 * rg) {
         const float y0 = block_value_fast<QB>(stq, sts, r, b, G.nb, G.nbp, xf);
         const float y1 = block_value_fast<QB>(stq, sts, r + rg, b, G.nb, G.nbp, xf);
         Pc[r * G.pstride + b] = y0;
@@ -547,7 +604,7 @@ template <int ESZ>
 __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float* P, int kind, int layer, int& gs) {
   float bv = 0.0f;   // LM head: this lane's running (value, index) of llm_argmax
   int bi = -1;
-  const Geo& G = p.g[kind];
+  const Geo G = geo_regs(p, kind);
   int* err = p.s.io + 3;
   const int cw = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
   int rb, re, nst;
@@ -568,8 +625,24 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
     const int ct = (int)threadIdx.x - 32;   // 0 .. 32 * kChain - 1
     if (pre_res)
       for (int i = ct; i < re - rb; i += 32 * kChain) h->res[i] = __ldcg(p.s.x + rb + i);
-    if (kind == K_QKV)
+    if (kind == K_QKV) {
       for (int i = ct; i < (p.s.hd >> 1); i += 32 * kChain) h->cs[i] = p.s.rope[(size_t)pos * (p.s.hd >> 1) + i];
+      if (pos + 1 <= kHeadMaxN) {
+        // the heads this CTA attends to next: their K and V rows of the
+        // earlier positions go to L2 while the projection runs
+        const tosk_step_layer_t& Ly = p.s.layers[layer];
+        const int hd = p.s.hd, group = p.s.n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
+        const uint32_t rowb = (uint32_t)(hd * ESZ);
+        const uint64_t keep = policy_evict_last();
+        for (int hh = blockIdx.x; hh < p.s.n_heads; hh += gridDim.x) {
+          const size_t off = (size_t)(hh / group) * hd * ESZ;
+          for (int t = ct; t < 2 * pos; t += 32 * kChain) {
+            const uint8_t* base = reinterpret_cast<const uint8_t*>(t < pos ? Ly.k_cache : Ly.v_cache);
+            prefetch_l2(base + (size_t)(t < pos ? t : t - pos) * kv_dim * ESZ + off, rowb, keep);
+          }
+        }
+      }
+    }
     named_sync(B_CHAIN, 32 * kChain);
   }
   for (int it = ((cw - gs0) % kChain + kChain) % kChain; it < nst; it += kChain) {
@@ -820,10 +893,8 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
 // Short contexts (n <= kHeadMaxN positions): one CTA per head does the whole
 // attention of that head in one phase, scores and e_t in shared memory, so
 // no grid barrier separates the max from the exponentials.  Worker warp w
-// takes positions w, w + 19, ... eight at a time (all eight K or V rows in
+// takes positions w, w + kNW, ... eight at a time (all eight K or V rows in
 // flight); the eight dot products of a warp meet in one reduce-scatter.
-constexpr int kHeadMaxN = 1024;
-constexpr int kNW = kWorkers / 32;   // 19 worker warps
 
 template <int ESZ>
 __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, int layer) {
@@ -853,7 +924,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       float v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) v[u] = 0.0f;
-#pragma unroll
+#pragma unroll 1
       for (int sl = 0; sl < kMaxHd / 128; ++sl) {
         const int d = 128 * sl + 4 * lane;
         if (d < hd) {
@@ -885,14 +956,6 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       const int t = t0 + ((lane >> 2) & 7) * kNW;
       if ((lane & 3) == 0 && t < n) sc[t] = dot * scale;
     }
-    // the V rows of this warp's first PV pass (slab 0) start loading now, so
-    // their latency overlaps the softmax
-    Raw4<ESZ> vpre[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int t = w + u * kNW;
-      vpre[u] = (t < n && 4 * lane < hd) ? ldcg_raw<ESZ>(vc + ((size_t)t * kv_dim + 4 * lane) * ESZ) : raw_zero<ESZ>();
-    }
     named_sync(B_WORKERS, kWorkers);
     // llm.c:509-521: max, e_t = llm_expf(s_t - max), sum (tree), 1/(sum + 1e-10)
     float m = -INFINITY;
@@ -913,7 +976,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
     named_sync(B_WORKERS, kWorkers);   // every thread has read red (the max) and written its e_t
     if (lane == 0) red[w] = l;
     // sum_t e_t v_t[d] (llm.c:703-712): warp w over its positions, lane l four d
-#pragma unroll
+#pragma unroll 1
     for (int sl = 0; sl < kMaxHd / 128; ++sl) {
       const int d = 128 * sl + 4 * lane;
       if (d < hd) {
@@ -923,10 +986,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int t = t0 + u * kNW;
-            if (sl == 0 && t0 == w)
-              vv[u] = widen<ESZ>(vpre[u]);
-            else
-              vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
