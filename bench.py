@@ -50,7 +50,10 @@ sys.path.insert(0, str(ROOT))
 
 GEMV_BYTES_4096 = 4096 * 128 * 18 + 4096 * 4 + 4096 * 4   # 9,469,952 B per launch
 METRIC = "decode tokens/sec (Llama-2-7B-shaped, Q4_0, batch 1)"
-STEP_TRAFFIC = None   # filled in from the committed ncu capture of the fused step
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_step_kernel launch
+# of the 32-layer model (profiles/decode_step_llama2_7b_q4_0.md; context 8: the
+# KV rows of a longer context add 16 KB per position and layer)
+STEP_TRAFFIC = 3721760768 + 13937152
 
 
 def peaks():
@@ -298,6 +301,8 @@ def run_ours(args, world, rank, local):
     lib = _lib()
     assert lib.tos_init(local) == 0, "tos_init failed"
     cfg = dict(W.LLAMA2_7B)
+    if args.layers:
+        cfg["n_layers"] = args.layers   # profiling of a small case only; the metric is the 32-layer model
     t_gen = time.perf_counter()
     synth = W.make_model(cfg, W.SEED)
     fast = args.math == "fast"
@@ -425,8 +430,8 @@ def run_ours(args, world, rank, local):
         step_rl = {"bound": "hbm", "kernel": "decode_step_kernel (one launch per token, all layers)",
                    "achieved": step_bytes / (step_us * 1e-6) / 1e9, "peak": peak, "peak_source": peak_kind,
                    "unit": "GB/s", "frac": step_bytes / (step_us * 1e-6) / 1e9 / peak,
-                   # dram bytes of one launch (profiles/decode_step_llama2_7b_q4_0.md)
-                   "traffic": STEP_TRAFFIC,
+                   # dram bytes of one launch at context 8, plus the KV rows of this context
+                   "traffic": STEP_TRAFFIC + L * 2 * (ctx - 8) * 4096 * 2,
                    "algorithmic_bytes_per_launch": step_bytes, "launch_us": step_us}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -478,6 +483,8 @@ def main():
                          "(normwise error <= 1e-4, greedy ids identical)")
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers (default: the 32 of the workload; fewer only to profile a small case)")
     ap.add_argument("--per-op", action="store_true",
                     help="fast arithmetic with a kernel per operator instead of the one fused kernel per token")
     ap.add_argument("--no-exact", action="store_true", help="skip the EXACT-arithmetic comparison run")
