@@ -29,9 +29,12 @@ batch 1.  A step is one decoded token.
              compiled hosted) on one host core, rank 0 at N=1.
 
 --impl reference times that reference CPU implementation alone.
-With --gpus N > 1 the model is row-sharded over the N GPUs (one process per
-GPU, NCCL all-gathers) and decodes one sequence: value is that sequence's
-tokens/s (strong scaling).
+With --gpus N > 1 (one process per GPU) every GPU holds the whole model and
+decodes its own sequence (data-parallel replicas, weak scaling): value is
+the tokens/s of all N sequences, timed as the slowest rank; "sharded" adds
+the same decode with one sequence row-sharded over the N GPUs (NCCL
+all-gathers, strong scaling), and --shard makes that the value.
+batch_decode: 16 sequences per step through the tensor-core GEMMs.
 """
 from __future__ import annotations
 
@@ -233,6 +236,33 @@ def run_gemv_only(args, local):
                       "frac": gbs / peak, "peak_source": peak_kind, "copies": args.gemv_copies}), flush=True)
 
 
+def time_batch(model, B, start, K, vocab, torch):
+    """Batched decode (tos_model_decode_batch): B independent sequences, one
+    token each per step, at positions start.. (the earlier cache rows of the
+    batch caches are zeros); host-driven steps, CUDA events on the model's
+    stream around K steps after 3 warm-up steps."""
+    import numpy as np
+    stream = torch.cuda.ExternalStream(model.stream())
+    toks = [(17 * i + 5) % vocab for i in range(B)]
+    pos = start
+    for _ in range(3):
+        toks = list(model.decode_batch(toks, [pos] * B))
+        pos += 1
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        toks = list(model.decode_batch(toks, [pos] * B))
+        pos += 1
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"sequences": B, "steps": K, "ms_per_step": ms / K, "tokens_per_s": B * K / (ms / 1000.0),
+            "positions": [start + 3, pos - 1],
+            "note": "B greedy sequences per step, projections as tcgen05 GEMMs over the B tokens; "
+                    "host-driven steps (8*B bytes in, 4*B out per step)"}
+
+
 def time_prefill(model, prompt, prompt_next, torch):
     """The prompt as one batched pass (tos_model_prefill: tensor-core GEMMs),
     against the token-by-token pass the decode measurement ran."""
@@ -307,7 +337,10 @@ def run_ours(args, world, rank, local):
     synth = W.make_model(cfg, W.SEED)
     fast = args.math == "fast"
     t_gen = time.perf_counter() - t_gen
-    prompt = W.tokens(args.prefill, cfg["vocab_size"], W.SEED)
+    # several GPUs: independent replicas, each decoding its own sequence
+    # (weak scaling), unless --shard row-shards one sequence over them
+    replicas = world > 1 and not args.shard
+    prompt = W.tokens(args.prefill, cfg["vocab_size"], W.SEED + (rank if replicas else 0))
     warm = max(3, args.warmup)
     K = args.steps
     if args.prefill + warm + 2 * K + 2 > cfg["max_seq"]:
@@ -360,10 +393,10 @@ def run_ours(args, world, rank, local):
         barrier()
         return e0.elapsed_time(e1), e2.elapsed_time(e3), ids
 
-    def shard():
+    def shard(force=False):
         """row-sharding over the ranks (one sequence, NCCL all-gathers); a
         fresh communicator id for every model"""
-        if world == 1:
+        if world == 1 or (replicas and not force):
             return None
         obj = [ops.nccl_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
@@ -379,6 +412,11 @@ def run_ours(args, world, rank, local):
     if world == 1 and not args.no_prefill:
         prefill = time_prefill(model, prompt, prompt_next, torch)
     model.close()
+    batch = None
+    if world == 1 and args.batch > 1:
+        bmodel = ops.Model(synth)
+        batch = time_batch(bmodel, args.batch, args.prefill, 16, cfg["vocab_size"], torch)
+        bmodel.close()
     # ---- the bit-exact path on the same prompt: its speed, and whether the
     # greedy ids agree (EXACT equals the reference bit for bit)
     exact_ms, exact_ids = None, None
@@ -386,14 +424,24 @@ def run_ours(args, world, rank, local):
         model = ops.Model(synth, shard=shard())
         exact_ms, _, exact_ids = timed_decode(model)
         model.close()
+    # replicas: the same sequence row-sharded over all the GPUs, for the
+    # latency of one sequence (strong scaling)
+    sharded_ms = None
+    if replicas:
+        model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(force=True))
+        sharded_ms, _, _ = timed_decode(model)
+        model.close()
     if world > 1:
-        tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0], device="cuda")
+        tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0, sharded_ms or 0.0], device="cuda")
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         t_ms, t_e2e = float(tt[0]), float(tt[1])
         exact_ms = float(tt[2]) if exact_ms is not None else None
-    # one sequence whatever the GPU count (row-sharded): tokens of the job
-    value = K / (t_ms / 1000.0)
-    e2e = K / (t_e2e / 1000.0)
+        sharded_ms = float(tt[3]) if sharded_ms is not None else None
+    # tokens of the whole job: one sequence per replica, or one sequence
+    # row-sharded over all GPUs
+    seqs = world if replicas else 1
+    value = seqs * K / (t_ms / 1000.0)
+    e2e = seqs * K / (t_e2e / 1000.0)
 
     res = {}
     if rank == 0:
@@ -442,14 +490,15 @@ def run_ours(args, world, rank, local):
         res = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": warm, "ms_per_step": t_ms / K, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if replicas else "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init Q4_0 weights; BASELINE distributions)",
             "config": {"workload": "llama2-7b-shape-q4_0 greedy decode, batch 1, after a 128-token prefill",
                        "model": cfg["name"], "global_batch": 1, "seq_len": args.prefill,
                        "kv_cache": "fp16, capacity 4096", "arithmetic": args.math,
                        "step": "one fused kernel per token" if fused else "a kernel per operator (CUDA graph)",
                        "positions": [args.prefill + warm, args.prefill + warm + K - 1],
-                       "parallelism": (f"row-sharded x{world} (heads, rows, vocabulary; NCCL all-gather)"
+                       "parallelism": (f"{world} data-parallel replicas, one sequence each" if replicas else
+                                       f"row-sharded x{world} (heads, rows, vocabulary; NCCL all-gather)"
                                        if world > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
@@ -459,7 +508,12 @@ def run_ours(args, world, rank, local):
             "gemv_roofline": gemv_rl,
             "decode_weight_gbs": weight_bytes * value / 1e9,   # all GPUs together
             "prefill": prefill,
+            "batch_decode": batch,
             "clocks": clk.summary(),
+            "sharded": None if sharded_ms is None else {
+                "value": K / (sharded_ms / 1000.0), "unit": "tokens/s", "ms_per_step": sharded_ms / K,
+                "scaling": "strong", "note": f"one sequence row-sharded over {world} GPUs, a kernel per "
+                                             "operator with NCCL all-gathers"},
             "exact": None if exact_ms is None else {
                 "value": K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
                 "greedy_ids_identical": exact_ids == ids, "ids_compared": len(ids)},
@@ -483,6 +537,10 @@ def main():
                          "(normwise error <= 1e-4, greedy ids identical)")
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", action="store_true",
+                    help="with several GPUs, row-shard one sequence over them instead of one replica per GPU")
+    ap.add_argument("--batch", type=int, default=16,
+                    help="also time batched decode of this many sequences (0/1: skip)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (default: the 32 of the workload; fewer only to profile a small case)")
     ap.add_argument("--per-op", action="store_true",

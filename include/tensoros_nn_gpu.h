@@ -233,6 +233,16 @@ int tos_model_decode(tos_model_t *m, int token, int pos, int n_steps, int *out_t
  * NULL) get the last token's logits and greedy next token.  Needs dim and
  * ff_dim multiples of 64; not for sharded models (TOS_ENOTSUP). */
 int tos_model_prefill(tos_model_t *m, const int *tokens, int n, int pos0, float *logits, int *next);
+/* Batched decode (no counterpart in the reference, which decodes one
+ * sequence): one greedy step of n <= 16 independent sequences: token[i] at
+ * position pos[i] of the sequence held in KV-cache slot slot[i] (distinct
+ * slots in [0, 16); the caches are allocated on first use and zeroed by
+ * tos_model_reset).  The projections run as tensor-core GEMMs over the n
+ * tokens (tos_gemm_dev numerics, FAST attention).  logits (n x vocab_size,
+ * may be NULL) and next[n] are host buffers.  Needs dim and ff_dim
+ * multiples of 64; one GPU (TOS_ENOTSUP). */
+int tos_model_decode_batch(tos_model_t *m, const int *slot, const int *tokens, const int *pos, int n,
+                           float *logits, int *next);
 /* the model's CUDA stream (cudaStream_t as void*) */
 void *tos_model_stream(const tos_model_t *m);
 /* device pointer of the last logits (vocab_size floats) */

@@ -98,6 +98,7 @@ NN_FUNCS = {
     "tos_model_generate_greedy": (i32, [vp, vp, i32, i32, vp]),
     "tos_model_decode": (i32, [vp, i32, i32, i32, vp]),
     "tos_model_prefill": (i32, [vp, vp, i32, i32, vp, ip]),
+    "tos_model_decode_batch": (i32, [vp, vp, vp, vp, i32, vp, vp]),
     "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),

@@ -65,6 +65,15 @@ struct tos_model {
     float *pf_x, *pf_xn, *pf_qkv, *pf_q, *pf_att, *pf_gu, *pf_h, *pf_tmp;
     void *pf_ws;
     size_t pf_ws_bytes;
+    /* batched decode (allocated on first use): up to bd_cap sequences, each
+     * with its own KV cache [n_layers][bd_cap][max_seq][kv_dim] */
+    int bd_cap;
+    void *bd_kc, *bd_vc;
+    int *bd_io;               /* device: tokens[cap], positions[cap], next[cap], slots[cap] */
+    int *bd_host;             /* pinned mirror */
+    float *bd_x, *bd_xn, *bd_qkv, *bd_q, *bd_att, *bd_gu, *bd_h, *bd_tmp, *bd_logits;
+    void *bd_ws;
+    size_t bd_ws_bytes;
 };
 
 static size_t qrow_bytes(int cols, int type)
@@ -133,10 +142,12 @@ void tos_model_destroy(tos_model_t *m)
                     m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
                     m->pf_toks, m->pf_x, m->pf_xn, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
-                    m->pf_tmp, m->pf_ws};
+                    m->pf_tmp, m->pf_ws, m->bd_kc, m->bd_vc, m->bd_io, m->bd_x, m->bd_xn, m->bd_qkv,
+                    m->bd_q, m->bd_att, m->bd_gu, m->bd_h, m->bd_tmp, m->bd_logits, m->bd_ws};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
     if (m->io_host) cudaFreeHost(m->io_host);
+    if (m->bd_host) cudaFreeHost(m->bd_host);
     if (m->st) cudaStreamDestroy(m->st);
     free(m);
 }
@@ -360,6 +371,8 @@ int tos_model_reset(tos_model_t *m)
     size_t kvb = (size_t)m->d.n_layers * m->d.max_seq * m->kv_dim * m->esz;
     int e = cudaMemsetAsync(m->kc, 0, kvb, m->st);
     if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
+    if (!e && m->bd_cap) e = cudaMemsetAsync(m->bd_kc, 0, kvb * m->bd_cap, m->st);
+    if (!e && m->bd_cap) e = cudaMemsetAsync(m->bd_vc, 0, kvb * m->bd_cap, m->st);
     if (!e) e = cudaStreamSynchronize(m->st);
     return tos_set_status(tos_from_cuda(e));
 }
@@ -671,4 +684,106 @@ int tos_model_prefill(tos_model_t *m, const int *tokens, int n, int pos0, float 
     if (!e) e = enqueue_head(m, 0);
     if (e) return tos_set_status(tos_from_cuda(e));
     return tos_set_status(finish(m, logits, next));
+}
+
+/* --------------------------------------------------------- batched decode */
+
+#define TOS_BATCH_CAP 16
+
+static int bd_alloc(tos_model_t *m)
+{
+    if (m->bd_cap) return 0;
+    const tos_model_desc_t *d = &m->d;
+    const int C = TOS_BATCH_CAP, dim = d->dim, ff = d->ff_dim;
+    const int nqkv = m->q_dim + 2 * m->kv_dim;
+    const size_t kvb = (size_t)d->n_layers * C * d->max_seq * m->kv_dim * m->esz;
+    int e = dmalloc(m, &m->bd_kc, kvb);
+    if (!e) e = dmalloc(m, &m->bd_vc, kvb);
+    if (!e) e = cudaMemset(m->bd_kc, 0, kvb);
+    if (!e) e = cudaMemset(m->bd_vc, 0, kvb);
+    if (!e) e = dmalloc(m, (void **)&m->bd_io, (size_t)4 * C * sizeof(int));
+    if (!e) e = cudaMallocHost((void **)&m->bd_host, (size_t)4 * C * sizeof(int));
+    if (!e) e = dmalloc(m, (void **)&m->bd_x, (size_t)C * dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_xn, (size_t)C * dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_qkv, (size_t)C * nqkv * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_q, (size_t)C * m->q_dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_att, (size_t)C * m->q_dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_gu, (size_t)C * 2 * ff * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_h, (size_t)C * ff * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_tmp, (size_t)C * dim * 4);
+    if (!e) e = dmalloc(m, (void **)&m->bd_logits, (size_t)C * d->vocab_size * 4);
+    size_t ws = 0, t;
+    t = tosk_gemm_ws_bytes(C, nqkv, dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, dim, m->q_dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, 2 * ff, dim); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, dim, ff); if (t > ws) ws = t;
+    t = tosk_gemm_ws_bytes(C, d->vocab_size, dim); if (t > ws) ws = t;
+    if (!e) e = dmalloc(m, &m->bd_ws, ws);
+    if (e) return e;
+    m->bd_ws_bytes = ws;
+    m->bd_cap = C;
+    return 0;
+}
+
+/* One greedy step of n independent sequences: token[i] at position pos[i]
+ * of the sequence in cache slot slot[i] (distinct slots).  The projections
+ * are tensor-core GEMMs over the n tokens (tos_gemm_dev numerics), attention
+ * is per sequence. */
+int tos_model_decode_batch(tos_model_t *m, const int *slot, const int *tokens, const int *pos, int n,
+                           float *logits, int *next)
+{
+    if (!m || !slot || !tokens || !pos || n <= 0 || n > TOS_BATCH_CAP) return tos_set_status(TOS_EINVAL);
+    const tos_model_desc_t *d = &m->d;
+    unsigned used = 0;
+    for (int i = 0; i < n; i++) {
+        if (tokens[i] < 0 || tokens[i] >= d->vocab_size || pos[i] < 0 || pos[i] >= d->max_seq ||
+            slot[i] < 0 || slot[i] >= TOS_BATCH_CAP || (used >> slot[i] & 1u))
+            return tos_set_status(TOS_EINVAL);
+        used |= 1u << slot[i];
+    }
+    if (m->sp.world > 1 || d->dim % 64 || d->ff_dim % 64 || m->q_dim % 64) return tos_set_status(TOS_ENOTSUP);
+    int e = bd_alloc(m);
+    if (e) return tos_set_status(tos_from_cuda(e));
+    cudaStream_t st = m->st;
+    int *err = m->io + 3;
+    const int C = m->bd_cap, dim = d->dim, ff = d->ff_dim, hd = m->hd;
+    const size_t cstride = (size_t)d->max_seq * m->kv_dim;           /* elements per sequence */
+    const size_t kv_layer = cstride * C * m->esz;                    /* bytes per layer */
+    memcpy(m->bd_host, tokens, (size_t)n * sizeof(int));
+    memcpy(m->bd_host + C, pos, (size_t)n * sizeof(int));
+    memcpy(m->bd_host + 3 * C, slot, (size_t)n * sizeof(int));
+    e = cudaMemcpyAsync(m->bd_io, m->bd_host, (size_t)4 * C * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (!e) e = tosk_pf_embed(m->bd_x, m->embd, d->embd_type, dim, m->bd_io, n, st);
+    for (int l = 0; !e && l < d->n_layers; l++) {
+        void *kc = (char *)m->bd_kc + kv_layer * l, *vc = (char *)m->bd_vc + kv_layer * l;
+        e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)(2 * l) * dim, dim, d->norm_eps, n, st);
+        if (!e) e = tosk_gemm_q(&m->wqkv[l], m->bd_xn, n, m->bd_qkv, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_bd_rope_store(m->bd_qkv, m->q_dim, m->kv_dim, hd, m->rope, m->bd_io + C, m->bd_io + 3 * C,
+                                       m->bd_q, kc, vc, cstride, d->kv_type, n, st);
+        if (!e) e = tosk_bd_attention(m->bd_q, kc, vc, cstride, d->kv_type, d->n_heads, d->n_kv_heads, hd,
+                                      m->bd_io + C, m->bd_io + 3 * C, d->max_seq, n, m->bd_att, st);
+        if (!e) e = tosk_gemm_q(&m->wo[l], m->bd_att, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
+        if (!e) e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)(2 * l + 1) * dim, dim, d->norm_eps, n, st);
+        if (!e) e = tosk_gemm_q(&m->wgu[l], m->bd_xn, n, m->bd_gu, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_swiglu(m->bd_h, m->bd_gu, (size_t)n * ff, st);
+        if (!e) e = tosk_gemm_q(&m->wdown[l], m->bd_h, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
+    }
+    if (!e) e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)2 * d->n_layers * dim, dim, d->norm_eps, n, st);
+    if (!e) e = tosk_gemm_q(&m->lm, m->bd_xn, n, m->bd_logits, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+    if (!e) e = tosk_argmax_rows(m->bd_logits, d->vocab_size, n, m->bd_io + 2 * C, st);
+    if (!e) e = cudaMemcpyAsync(m->bd_host + 2 * C, m->bd_io + 2 * C, (size_t)n * sizeof(int),
+                                cudaMemcpyDeviceToHost, st);
+    if (!e && logits)
+        e = cudaMemcpyAsync(logits, m->bd_logits, (size_t)n * d->vocab_size * 4, cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaMemcpyAsync(m->io_host + 3, m->io + 3, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    if (e) return tos_set_status(tos_from_cuda(e));
+    if (m->io_host[3] != 0) {
+        clear_error(m);
+        return tos_set_status(TOS_ETIMEOUT);
+    }
+    if (next) memcpy(next, m->bd_host + 2 * C, (size_t)n * sizeof(int));
+    return tos_set_status(TOS_OK);
 }

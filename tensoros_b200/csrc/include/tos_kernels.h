@@ -95,6 +95,14 @@ int tosk_pf_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const 
 int tosk_pf_attention(const float *q, const void *kc, const void *vc, int kv_type, int n_heads, int n_kv,
                       int hd, int pos0, int n, float *out, cudaStream_t st);
 int tosk_pf_add(float *x, const float *y, size_t n, cudaStream_t st);
+/* batched decode: n tokens of n sequences, token t of sequence slot[t] at
+ * position pos[t] (device arrays); slot s's cache at kc/vc + s*cstride elements */
+int tosk_bd_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const float2 *cs, const int *pos,
+                       const int *slot, float *q_out, void *kc, void *vc, size_t cstride, int kv_type, int n,
+                       cudaStream_t st);
+int tosk_bd_attention(const float *q, const void *kc, const void *vc, size_t cstride, int kv_type, int n_heads,
+                      int n_kv, int hd, const int *pos, const int *slot, int max_ctx, int n, float *out,
+                      cudaStream_t st);
 int tosk_pf_swiglu(float *h, const float *gu, size_t n, cudaStream_t st);
 /* m->rws from m->sc (run after the planes are filled) */
 int tosk_qmat_row_scales(tosk_qmat_t *m, cudaStream_t st);
@@ -130,6 +138,8 @@ int tosk_argmax(const float *x, int n, int *out_idx, float *out_val, int pdl, cu
 /* one rank's slice of a row-sharded vector: pair = {value bits, index+offset
  * or -1}; first_rule for the slice that starts the vector (rank 0) */
 int tosk_argmax_slice(const float *x, int n, int offset, int first_rule, int *pair, int pdl, cudaStream_t st);
+/* llm_argmax of each of `rows` consecutive rows of n (batched decode) */
+int tosk_argmax_rows(const float *x, int n, int rows, int *out_idx, cudaStream_t st);
 /* reduce world pairs (rank order) to the reference's argmax */
 int tosk_argmax_pairs(const int *pairs, int world, int *out_idx, int pdl, cudaStream_t st);
 /* io[2] -> ring[io[4]]; io[4] += 1; io[1] += 1 (device-side greedy chaining) */

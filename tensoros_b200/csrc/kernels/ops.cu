@@ -216,6 +216,10 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   __shared__ float sv[32];
   __shared__ int si[32];
   pdl_wait();
+  // one row per CTA (a grid of several CTAs reduces consecutive rows of n)
+  x += (size_t)blockIdx.x * n;
+  out_idx += blockIdx.x;
+  if (out_val) out_val += blockIdx.x;
   float v = 0.0f;
   int idx = -1;
   // each thread scans 4 consecutive elements per step (vector loads when x
@@ -397,6 +401,14 @@ extern "C" int tosk_argmax(const float* x, int n, int* out_idx, float* out_val, 
   int first_rule = 1, offset = 0;
   void* args[] = {&x, &n, &out_idx, &out_val, &first_rule, &offset};
   return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_argmax_rows(const float* x, int n, int rows, int* out_idx, cudaStream_t st) {
+  if (n <= 0 || rows <= 0) return (int)cudaErrorInvalidValue;
+  int first_rule = 1, offset = 0;
+  float* out_val = nullptr;
+  void* args[] = {&x, &n, &out_idx, &out_val, &first_rule, &offset};
+  return launch_pdl((const void*)argmax_kernel, dim3(rows), dim3(1024), args, 1, st);
 }
 
 extern "C" int tosk_argmax_slice(const float* x, int n, int offset, int first_rule, int* pair, int pdl,

@@ -11,6 +11,8 @@
 //                        tree sums (FAST numerics)
 //   pf_add_kernel, pf_swiglu_kernel  residual (llm.c:718, 733) and
 //                        SiLU(gate)*up (llm.c:726-729) with the decode order
+// The rope/store and attention kernels also serve batched decode: n tokens
+// of n different sequences, each at its own position with its own cache.
 #include <cuda_runtime.h>
 
 #include "tos_dev.cuh"
@@ -74,13 +76,22 @@ __global__ void pf_rmsnorm_kernel(float* __restrict__ y, const float* __restrict
 
 // qkv rows [q_rows | kv_rows | kv_rows] per token; q (roped) -> q_out,
 // k (roped) and v -> the caches at position pos0 + t.
+// Batched decode (pos_arr non-null): row t is a token of sequence slot[t]
+// at position pos_arr[t]; slot s's cache starts s*cstride elements in.
 __global__ void pf_rope_store_kernel(const float* __restrict__ qkv, int q_rows, int kv_rows, int hd,
                                      const float2* __restrict__ cs, int pos0, float* __restrict__ q_out,
-                                     void* __restrict__ kc, void* __restrict__ vc, int kv_type) {
+                                     void* __restrict__ kc, void* __restrict__ vc, int kv_type,
+                                     const int* __restrict__ pos_arr, const int* __restrict__ slot,
+                                     size_t cstride) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
-  const int pos = pos0 + t;
+  const int pos = pos_arr ? pos_arr[t] : pos0 + t;
+  const size_t esz = kv_type == TOSK_F16 ? 2 : 4;
+  if (pos_arr) {
+    kc = reinterpret_cast<char*>(kc) + (size_t)slot[t] * cstride * esz;
+    vc = reinterpret_cast<char*>(vc) + (size_t)slot[t] * cstride * esz;
+  }
   const int nrow = q_rows + 2 * kv_rows;
   const float* row = qkv + (size_t)t * nrow;
   for (int r = threadIdx.x; r < nrow; r += blockDim.x) {
@@ -117,13 +128,20 @@ __device__ __forceinline__ float kv_load(const void* c, int kv_type, size_t idx)
 // weights of (s - max), tree sums, sum_j e_j v_j / (sum_j e_j + 1e-10).
 __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restrict__ q, const void* __restrict__ kc,
                                                            const void* __restrict__ vc, int kv_type, int n_heads,
-                                                           int n_kv, int hd, int pos0, float* __restrict__ out) {
+                                                           int n_kv, int hd, int pos0, float* __restrict__ out,
+                                                           const int* __restrict__ pos_arr,
+                                                           const int* __restrict__ slot, size_t cstride) {
   extern __shared__ float sc[];   // [pos0 + n] scores, then weights
   __shared__ float red[4];
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x, t = blockIdx.y;
-  const int n = pos0 + t + 1;
+  const int n = (pos_arr ? pos_arr[t] : pos0 + t) + 1;
+  if (pos_arr) {
+    const size_t esz = kv_type == TOSK_F16 ? 2 : 4;
+    kc = reinterpret_cast<const char*>(kc) + (size_t)slot[t] * cstride * esz;
+    vc = reinterpret_cast<const char*>(vc) + (size_t)slot[t] * cstride * esz;
+  }
   const int kvh = h / (n_heads / n_kv);
   const int kv_dim = n_kv * hd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -216,7 +234,21 @@ extern "C" int tosk_pf_rmsnorm(float* y, const float* x, const float* w, int dim
 
 extern "C" int tosk_pf_rope_store(const float* qkv, int q_rows, int kv_rows, int hd, const float2* cs, int pos0,
                                   float* q_out, void* kc, void* vc, int kv_type, int n, cudaStream_t st) {
-  void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type};
+  const int* pos_arr = nullptr;
+  const int* slot = nullptr;
+  size_t cstride = 0;
+  void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type,
+                  (void*)&pos_arr, (void*)&slot, &cstride};
+  return launch_pf((const void*)pf_rope_store_kernel, dim3(n), dim3(256), 0, args, st);
+}
+
+extern "C" int tosk_bd_rope_store(const float* qkv, int q_rows, int kv_rows, int hd, const float2* cs,
+                                  const int* pos, const int* slot, float* q_out, void* kc, void* vc, size_t cstride,
+                                  int kv_type, int n, cudaStream_t st) {
+  if (!pos || !slot) return (int)cudaErrorInvalidValue;
+  int pos0 = 0;
+  void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type,
+                  (void*)&pos, (void*)&slot, &cstride};
   return launch_pf((const void*)pf_rope_store_kernel, dim3(n), dim3(256), 0, args, st);
 }
 
@@ -231,7 +263,29 @@ extern "C" int tosk_pf_attention(const float* q, const void* kc, const void* vc,
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
-  void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out};
+  const int* pos_arr = nullptr;
+  const int* slot = nullptr;
+  size_t cstride = 0;
+  void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out,
+                  (void*)&pos_arr, (void*)&slot, &cstride};
+  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
+}
+
+extern "C" int tosk_bd_attention(const float* q, const void* kc, const void* vc, size_t cstride, int kv_type,
+                                 int n_heads, int n_kv, int hd, const int* pos, const int* slot, int max_ctx, int n,
+                                 float* out, cudaStream_t st) {
+  const size_t smem = (size_t)max_ctx * 4;
+  if (!pos || !slot || smem > 200 * 1024) return (int)cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr && smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               200 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  int pos0 = 0;
+  void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out,
+                  (void*)&pos, (void*)&slot, &cstride};
   return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
 }
 

@@ -236,6 +236,20 @@ class Model:
                                                              _p(out) if logits else None, C.byref(nxt)))
         return (nxt.value, out) if logits else nxt.value
 
+    def decode_batch(self, tokens, positions, slots=None, logits: bool = False):
+        """One greedy step of len(tokens) independent sequences
+        (tos_model_decode_batch); slots[i] is the KV-cache slot of sequence i
+        (default 0..n-1).  The next token of each, and the logits when asked."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        n = len(t)
+        s = np.ascontiguousarray(range(n) if slots is None else slots, dtype=np.int32)
+        out = np.empty((n, self.vocab), dtype=np.float32) if logits else None
+        nxt = np.zeros(n, dtype=np.int32)
+        _check("tos_model_decode_batch", _lib().tos_model_decode_batch(self.h, _p(s), _p(t), _p(p), n,
+                                                                       _p(out) if logits else None, _p(nxt)))
+        return (nxt, out) if logits else nxt
+
     def decode(self, token: int, pos: int, n_steps: int) -> np.ndarray:
         out = np.zeros(max(n_steps, 1), dtype=np.int32)
         _check("tos_model_decode", _lib().tos_model_decode(self.h, token, pos, n_steps, _p(out)))
