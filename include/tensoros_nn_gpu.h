@@ -251,6 +251,32 @@ size_t tos_model_device_bytes(const tos_model_t *m);
 /* 1 when each token runs as the one fused kernel (see fused_step) */
 int tos_model_fused(const tos_model_t *m);
 
+/* ------------------------------------------------------------ GGUF files
+ * The container of runtime/nn (gguf.c:204-423): v2/v3 headers, metadata,
+ * tensor infos; tensor data is used in place (the caller's buffer, or a
+ * read-only mapping of the file).  tos_gguf_model_desc maps a llama-family
+ * file onto tos_model_desc_t (llm.c:1374-1448, 1521-1545): architecture
+ * from "<general.architecture>.*" keys, tensors blk.N.attn_q.weight etc.,
+ * output.weight tied to token_embd when absent; max_seq = the file's
+ * context length, kv_type F16, EXACT arithmetic (the caller may change
+ * them).  The descriptor's pointers stay valid until tos_gguf_close. */
+typedef struct tos_gguf tos_gguf_t;
+int tos_gguf_open(tos_gguf_t **g, const void *data, uint64_t size);
+int tos_gguf_open_file(tos_gguf_t **g, const char *path);
+void tos_gguf_close(tos_gguf_t *g);
+uint32_t tos_gguf_version(const tos_gguf_t *g);
+int64_t tos_gguf_n_tensors(const tos_gguf_t *g);
+int64_t tos_gguf_n_kv(const tos_gguf_t *g);
+int64_t tos_gguf_find_tensor(const tos_gguf_t *g, const char *name);   /* index or -1 */
+/* dims[d] = ne[d] (fastest first; 1 beyond n_dims); bytes 0 for a type
+ * whose block size is unknown */
+int tos_gguf_tensor_info(const tos_gguf_t *g, int64_t i, const char **name, int *type, int *n_dims,
+                         uint64_t dims[4], const void **data, uint64_t *bytes);
+int tos_gguf_get_u32(const tos_gguf_t *g, const char *key, uint32_t *out);   /* any integer type */
+int tos_gguf_get_f32(const tos_gguf_t *g, const char *key, float *out);
+int tos_gguf_get_str(const tos_gguf_t *g, const char *key, const char **str, uint64_t *len);
+int tos_gguf_model_desc(tos_gguf_t *g, tos_model_desc_t *desc);
+
 /* ------------------------------------------ multi-GPU (one node, NCCL)
  * No counterpart in the reference (a single-CPU decoder).  A model is
  * row-sharded over `world` ranks, one process and one GPU per rank: rank r

@@ -102,6 +102,19 @@ NN_FUNCS = {
     "tos_model_stream": (vp, [vp]),
     "tos_model_logits_dev": (vp, [vp]),
     "tos_model_device_bytes": (sz, [vp]),
+    "tos_gguf_open": (i32, [C.POINTER(vp), vp, C.c_uint64]),
+    "tos_gguf_open_file": (i32, [C.POINTER(vp), C.c_char_p]),
+    "tos_gguf_close": (None, [vp]),
+    "tos_gguf_version": (C.c_uint32, [vp]),
+    "tos_gguf_n_tensors": (C.c_int64, [vp]),
+    "tos_gguf_n_kv": (C.c_int64, [vp]),
+    "tos_gguf_find_tensor": (C.c_int64, [vp, C.c_char_p]),
+    "tos_gguf_tensor_info": (i32, [vp, C.c_int64, C.POINTER(C.c_char_p), ip, ip, C.POINTER(C.c_uint64),
+                                   C.POINTER(vp), C.POINTER(C.c_uint64)]),
+    "tos_gguf_get_u32": (i32, [vp, C.c_char_p, C.POINTER(C.c_uint32)]),
+    "tos_gguf_get_f32": (i32, [vp, C.c_char_p, C.POINTER(C.c_float)]),
+    "tos_gguf_get_str": (i32, [vp, C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(C.c_uint64)]),
+    "tos_gguf_model_desc": (i32, [vp, vp]),
     "tos_model_fused": (i32, [vp]),
     "tos_shard_range": (i32, [i32, i32, i32, i32, ip, ip]),
     "tos_shard_plan": (i32, [C.POINTER(ModelDesc), i32, i32, C.POINTER(ShardPlan)]),

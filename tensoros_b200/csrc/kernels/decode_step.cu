@@ -956,6 +956,14 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       const int t = t0 + ((lane >> 2) & 7) * kNW;
       if ((lane & 3) == 0 && t < n) sc[t] = dot * scale;
     }
+    // the V rows of this warp's first PV pass (first 128 dims) start loading
+    // now: their latency overlaps the softmax
+    Raw4<ESZ> vpre[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int t = w + u * kNW;
+      vpre[u] = (t < n && 4 * lane < hd) ? ldcg_raw<ESZ>(vc + ((size_t)t * kv_dim + 4 * lane) * ESZ) : raw_zero<ESZ>();
+    }
     named_sync(B_WORKERS, kWorkers);
     // llm.c:509-521: max, e_t = llm_expf(s_t - max), sum (tree), 1/(sum + 1e-10)
     float m = -INFINITY;
@@ -986,7 +994,10 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int t = t0 + u * kNW;
-            vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (sl == 0 && t0 == w)
+              vv[u] = widen<ESZ>(vpre[u]);
+            else
+              vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
