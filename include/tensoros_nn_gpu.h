@@ -130,6 +130,8 @@ int tos_argmax_dev(const float *x, int n, int *out_index, void *stream);
  * `world` equal slices, each slice gives a (value, index) pair and the pairs
  * reduce with llm_argmax's rule (llm.c:1129-1140); same kernels as a sharded
  * model's last step.  No counterpart in the reference. */
+int tos_sample_dev(const float *logits, int n, float temperature, uint32_t entropy, int *out_index,
+                   void *stream);
 int tos_argmax_sharded_dev(const float *x, int n, int world, int *out_index, void *stream);
 
 /* Single-query attention over a KV cache [ctx][n_kv*head_dim] (kv_type F32 or
@@ -171,6 +173,11 @@ void tos_axpy_f32(float *dst, float scale, const float *src, int n);            
 void tos_vadd_f32(float *dst, const float *src, int n);                                           /* llm.c:599 */
 void tos_vmul_f32(float *dst, const float *src, int n);                                           /* llm.c:617 */
 int tos_argmax(const float *logits, int n);                                                       /* llm.c:1129 */
+/* llm_sample (llm.c:1177-1246): top-40, temperature, nucleus 0.9, one draw.
+ * The reference draws from the CPU timestamp; here the caller passes the
+ * 32-bit word (mixed and reduced to r in [0,1) exactly as the reference
+ * mixes its timestamp).  temperature <= 0.001: llm_argmax.  Finite logits. */
+int tos_sample(const float *logits, int n, float temperature, uint32_t entropy);
 /* quantize4.h:64-67: fp32-scale 20-byte Q4 blocks */
 float tos_q4_dot_block(const void *block20, const float *x);
 void tos_q4_gemv(float *out, const void *blocks20, const float *x, int out_dim, int in_dim);

@@ -155,8 +155,12 @@ class Oracle(_Ops):
         L.orc_model_create.restype, L.orc_model_create.argtypes = vp, [C.POINTER(_Desc)]
         L.orc_model_kcache.restype, L.orc_model_kcache.argtypes = vp, [vp, i32]
         L.orc_model_vcache.restype, L.orc_model_vcache.argtypes = vp, [vp, i32]
+        L.orc_sample.restype, L.orc_sample.argtypes = i32, [vp, i32, f32, C.c_uint32]
 
     def fp32_to_fp16(self, x): return int(self.lib.orc_fp32_to_fp16(float(x)))
+
+    def sample(self, logits, temperature, entropy):
+        return int(self.lib.orc_sample(_p(_f32(logits)), len(logits), float(temperature), int(entropy) & 0xFFFFFFFF))
 
     def gemv_mt(self, w, x, out_dim, in_dim, t, threads=8):
         out = np.empty(out_dim, dtype=np.float32)

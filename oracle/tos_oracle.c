@@ -369,6 +369,71 @@ int orc_argmax(const float *x, int n)
     return best;
 }
 
+/* llm.c:1143-1175: the first k indices insertion-sorted by value
+ * (descending), then every later element inserted if strictly larger than
+ * the smallest kept one and bubbled up */
+static void orc_partial_sort_desc(int *idx, const float *v, int n, int k)
+{
+    for (int i = 0; i < k && i < n; i++) idx[i] = i;
+    for (int i = 1; i < k && i < n; i++) {
+        int key = idx[i];
+        float kv = v[key];
+        int j = i - 1;
+        while (j >= 0 && v[idx[j]] < kv) { idx[j + 1] = idx[j]; j--; }
+        idx[j + 1] = key;
+    }
+    for (int i = k; i < n; i++) {
+        int last = (k < n) ? k - 1 : n - 1;
+        if (v[i] > v[idx[last]]) {
+            idx[last] = i;
+            int j = last - 1;
+            while (j >= 0 && v[idx[j]] < v[idx[j + 1]]) { int t = idx[j]; idx[j] = idx[j + 1]; idx[j + 1] = t; j--; }
+        }
+    }
+}
+
+/* llm.c:1177-1246 llm_sample: top-40, softmax of (l - max)/T with
+ * llm_expf, nucleus 0.9, renormalise, inverse-CDF draw; the TSC read
+ * (llm.c:1226-1233) is replaced by the caller's 32-bit entropy word, mixed
+ * and reduced to r in [0, 1) as the reference does */
+int orc_sample(const float *logits, int n, float temperature, uint32_t entropy)
+{
+    if (temperature <= 0.001f) return orc_argmax(logits, n);
+    int idx[40];
+    float pr[40];
+    int k = 40 < n ? 40 : n;
+    orc_partial_sort_desc(idx, logits, n, k);
+    float mx = logits[idx[0]], sum = 0.0f;
+    for (int i = 0; i < k; i++) {
+        pr[i] = orc_expf((logits[idx[i]] - mx) / temperature);
+        sum += pr[i];
+    }
+    float inv = 1.0f / (sum + 1e-10f);
+    for (int i = 0; i < k; i++) pr[i] *= inv;
+    float cum = 0.0f;
+    int cut = k;
+    for (int i = 0; i < k; i++) {
+        cum += pr[i];
+        if (cum >= 0.9f) { cut = i + 1; break; }
+    }
+    if (cut < k) {
+        sum = 0.0f;
+        for (int i = 0; i < cut; i++) sum += pr[i];
+        inv = 1.0f / (sum + 1e-10f);
+        for (int i = 0; i < cut; i++) pr[i] *= inv;
+    }
+    uint32_t lo = entropy;
+    lo = lo ^ (lo >> 16);
+    lo = lo * 0x45d9f3bU;
+    float r = (float)(lo % 10000) / 10000.0f;
+    float cdf = 0.0f;
+    for (int i = 0; i < cut; i++) {
+        cdf += pr[i];
+        if (cdf >= r) return idx[i];
+    }
+    return idx[cut - 1];
+}
+
 static float kv_at(const void *c, int kv_type, size_t idx)
 {
     if (kv_type == ORC_TYPE_F16) return orc_fp16_to_fp32(((const uint16_t *)c)[idx]);

@@ -50,6 +50,7 @@ void orc_axpy_f32(float *dst, float s, const float *src, int n);
 void orc_vadd_f32(float *dst, const float *src, int n);
 void orc_vmul_f32(float *dst, const float *src, int n);
 int orc_argmax(const float *x, int n);
+int orc_sample(const float *logits, int n, float temperature, uint32_t entropy);
 
 /* Single-query attention over a KV cache laid out [pos][n_kv*hd]
  * (kv_type ORC_TYPE_F32 or ORC_TYPE_F16). */

@@ -115,6 +115,8 @@ NN_FUNCS = {
     "tos_gguf_get_f32": (i32, [vp, C.c_char_p, C.POINTER(C.c_float)]),
     "tos_gguf_get_str": (i32, [vp, C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(C.c_uint64)]),
     "tos_gguf_model_desc": (i32, [vp, vp]),
+    "tos_sample": (i32, [vp, i32, f32, C.c_uint32]),
+    "tos_sample_dev": (i32, [vp, i32, f32, C.c_uint32, vp, vp]),
     "tos_model_fused": (i32, [vp]),
     "tos_shard_range": (i32, [i32, i32, i32, i32, ip, ip]),
     "tos_shard_plan": (i32, [C.POINTER(ModelDesc), i32, i32, C.POINTER(ShardPlan)]),

@@ -618,6 +618,31 @@ int tos_argmax(const float *logits, int n)
     return e ? 0 : r;
 }
 
+/* llm_sample (llm.c:1177-1246) with the caller's entropy word in place of
+ * the timestamp; temperature <= 0.001 is llm_argmax */
+int tos_sample(const float *logits, int n, float temperature, uint32_t entropy)
+{
+    if (!logits || n <= 0) { tos_set_status(TOS_EINVAL); return 0; }
+    if (tos_ensure_init()) { tos_set_status(TOS_ENODEV); return 0; }
+    size_t ox = 0, oo = al((size_t)n * 4);
+    if (!tos_scratch(oo + 8)) { tos_set_status(TOS_ENOMEM); return 0; }
+    int r = 0;
+    int e = h2d(ox, logits, (size_t)n * 4);
+    if (!e) e = tosk_sample((const float *)tos_g.scratch, n, temperature, entropy,
+                            (int *)((char *)tos_g.scratch + oo), tos_g.stream);
+    if (!e) e = finish_to_host(&r, oo, 4);
+    tos_set_status(tos_from_cuda(e));
+    return e ? 0 : r;
+}
+
+int tos_sample_dev(const float *logits, int n, float temperature, uint32_t entropy, int *out_index, void *stream)
+{
+    DEV_PROLOGUE();
+    if (!logits || n <= 0 || !out_index) return tos_set_status(TOS_EINVAL);
+    return tos_set_status(tos_from_cuda(tosk_sample(logits, n, temperature, entropy, out_index,
+                                                    tos_pick_stream(stream))));
+}
+
 float tos_q4_dot_block(const void *block20, const float *x)
 {
     float r = 0.0f;

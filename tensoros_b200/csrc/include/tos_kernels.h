@@ -138,6 +138,8 @@ int tosk_argmax(const float *x, int n, int *out_idx, float *out_val, int pdl, cu
 /* one rank's slice of a row-sharded vector: pair = {value bits, index+offset
  * or -1}; first_rule for the slice that starts the vector (rank 0) */
 int tosk_argmax_slice(const float *x, int n, int offset, int first_rule, int *pair, int pdl, cudaStream_t st);
+/* llm_sample (llm.c:1177-1246) with the timestamp replaced by `entropy` */
+int tosk_sample(const float *x, int n, float temperature, uint32_t entropy, int *out_idx, cudaStream_t st);
 /* llm_argmax of each of `rows` consecutive rows of n (batched decode) */
 int tosk_argmax_rows(const float *x, int n, int rows, int *out_idx, cudaStream_t st);
 /* reduce world pairs (rank order) to the reference's argmax */

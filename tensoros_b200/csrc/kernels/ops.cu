@@ -309,6 +309,163 @@ __global__ void argmax_pairs_kernel(const int* __restrict__ pairs, int world, in
   pdl_trigger();
 }
 
+// llm_sample (llm.c:1143-1246) on the device, one CTA of 1024 threads.
+// The reference keeps the 40 largest logits ordered by (value descending,
+// index ascending) - its insertion-based partial sort resolves equal values
+// that way - then runs a short serial recipe.  Here the 40th largest value
+// is found by a 4-pass radix select on order-preserving keys (-0.0 counted
+// as +0.0, as float comparison does), the 40 candidates are gathered (for
+// equal values at the threshold the lowest indices, by a prefix count in
+// index order) and sorted, and thread 0 runs the reference's serial steps in
+// its rounding order: softmax of (l - max)/T with llm_expf, nucleus 0.9,
+// renormalisation, and the inverse-CDF draw with r from the entropy word
+// mixed as the reference mixes its timestamp.  Finite logits.
+constexpr int kSampleK = 40;
+
+__device__ __forceinline__ uint32_t order_key(float v) {
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0;   // -0.0 == +0.0
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ x, int n, float temperature,
+                                                      uint32_t entropy, int* __restrict__ out) {
+  __shared__ unsigned hist[256];
+  __shared__ unsigned s_prefix, s_need;
+  __shared__ unsigned wsum[32];
+  __shared__ int s_cnt;
+  __shared__ float cv[kSampleK];
+  __shared__ int ci[kSampleK];
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = n < kSampleK ? n : kSampleK;
+  if (tid == 0) {
+    s_prefix = 0;
+    s_need = (unsigned)k;
+    s_cnt = 0;
+  }
+  unsigned pmask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const unsigned prefix = s_prefix;
+    for (int i = tid; i < n; i += blockDim.x) {
+      const uint32_t kk = order_key(x[i]);
+      if ((kk & pmask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned need = s_need, cum = 0;
+      for (int bin = 255; bin >= 0; --bin) {
+        if (cum + hist[bin] >= need) {
+          s_prefix = prefix | ((unsigned)bin << shift);
+          s_need = need - cum;
+          break;
+        }
+        cum += hist[bin];
+      }
+    }
+    pmask |= 255u << shift;
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const unsigned need = s_need;   // elements equal to the threshold to keep (lowest indices)
+  // keys above the threshold: all kept; equal ones: rank in index order
+  const int chunk = (n + blockDim.x - 1) / blockDim.x;
+  const int i0 = tid * chunk, i1 = min(n, i0 + chunk);
+  unsigned eq = 0;
+  for (int i = i0; i < i1; ++i) eq += order_key(x[i]) == T;
+  unsigned incl = eq;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    unsigned w = lane < nw ? wsum[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned v = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += v;
+    }
+    if (lane < nw) wsum[lane] = w;   // inclusive per-warp totals
+  }
+  __syncthreads();
+  unsigned rank = (warp > 0 ? wsum[warp - 1] : 0u) + incl - eq;   // equal keys before this chunk
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t kk = order_key(x[i]);
+    bool take = kk > T;
+    if (kk == T) {
+      take = rank < need;
+      ++rank;
+    }
+    if (take) {
+      const int slot = atomicAdd(&s_cnt, 1);
+      if (slot < kSampleK) {
+        cv[slot] = x[i];
+        ci[slot] = i;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid != 0) return;
+  const int m = min(s_cnt, kSampleK);
+  // (value descending, index ascending)
+  for (int a = 1; a < m; ++a) {
+    const float v = cv[a];
+    const int ix = ci[a];
+    int j = a - 1;
+    while (j >= 0 && (cv[j] < v || (cv[j] == v && ci[j] > ix))) {
+      cv[j + 1] = cv[j];
+      ci[j + 1] = ci[j];
+      --j;
+    }
+    cv[j + 1] = v;
+    ci[j + 1] = ix;
+  }
+  float pr[kSampleK];
+  const float mx = cv[0];
+  float sum = 0.0f;
+  for (int a = 0; a < m; ++a) {
+    pr[a] = ref_expf(__fdiv_rn(__fsub_rn(cv[a], mx), temperature));
+    sum = __fadd_rn(sum, pr[a]);
+  }
+  float inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
+  for (int a = 0; a < m; ++a) pr[a] = __fmul_rn(pr[a], inv);
+  float cum = 0.0f;
+  int cut = m;
+  for (int a = 0; a < m; ++a) {
+    cum = __fadd_rn(cum, pr[a]);
+    if (cum >= 0.9f) {
+      cut = a + 1;
+      break;
+    }
+  }
+  if (cut < m) {
+    sum = 0.0f;
+    for (int a = 0; a < cut; ++a) sum = __fadd_rn(sum, pr[a]);
+    inv = __fdiv_rn(1.0f, __fadd_rn(sum, 1e-10f));
+    for (int a = 0; a < cut; ++a) pr[a] = __fmul_rn(pr[a], inv);
+  }
+  uint32_t lo = entropy;
+  lo = lo ^ (lo >> 16);
+  lo = lo * 0x45d9f3bU;
+  const float r = __fdiv_rn((float)(lo % 10000u), 10000.0f);
+  float cdf = 0.0f;
+  int pick = ci[cut - 1];
+  for (int a = 0; a < cut; ++a) {
+    cdf = __fadd_rn(cdf, pr[a]);
+    if (cdf >= r) {
+      pick = ci[a];
+      break;
+    }
+  }
+  *out = pick;
+}
+
 // Greedy decode on the device: record the token the last argmax produced
 // (io[2]) in ring[io[4]], then advance the position io[1] and the counter.
 __global__ void decode_advance_kernel(int* __restrict__ io, int* __restrict__ ring) {
@@ -401,6 +558,14 @@ extern "C" int tosk_argmax(const float* x, int n, int* out_idx, float* out_val, 
   int first_rule = 1, offset = 0;
   void* args[] = {&x, &n, &out_idx, &out_val, &first_rule, &offset};
   return launch_pdl((const void*)argmax_kernel, dim3(1), dim3(1024), args, pdl, st);
+}
+
+extern "C" int tosk_sample(const float* x, int n, float temperature, uint32_t entropy, int* out_idx,
+                           cudaStream_t st) {
+  if (n <= 0 || !x || !out_idx) return (int)cudaErrorInvalidValue;
+  if (temperature <= 0.001f) return tosk_argmax(x, n, out_idx, nullptr, 0, st);   // llm.c:1179-1180
+  void* args[] = {&x, &n, &temperature, &entropy, &out_idx};
+  return launch_pdl((const void*)sample_kernel, dim3(1), dim3(1024), args, 0, st);
 }
 
 extern "C" int tosk_argmax_rows(const float* x, int n, int rows, int* out_idx, cudaStream_t st) {
