@@ -9,26 +9,30 @@
 // kernel still holds).  Here one CTA per SM stays resident for the token:
 //
 //   * warp 0 (the producer) streams the weight planes of EVERY projection of
-//     the step, in execution order, through a 5-slot shared-memory ring
-//     (cp.async.bulk, mbarrier complete_tx).  Weights depend on nothing, so
-//     the producer only waits for free slots: while the other warps wait at
-//     a grid barrier or run attention, the next projection's rows are
-//     already landing.
-//   * warps 4..15 (compute) evaluate block values of the ring's stages
-//     exactly as the FAST GEMV does (integer dp4a dot products on 24-bit
-//     fixed-point x, gemv_fastmath.cuh) into a partials tile;
+//     the step, in execution order, through a 3-slot shared-memory ring of
+//     41.5 KB stages (cp.async.bulk with an L2 evict-first policy, mbarrier
+//     complete_tx).  Weights depend on nothing, so the producer only waits
+//     for free slots: while the other warps wait at a grid barrier or run
+//     attention, the next projection's rows are already landing.
+//   * warps 4..15 (compute) turn the phase's input vector into fixed-point
+//     records (cp.async of every chunk at once; RMSNorm fused) and evaluate
+//     block values of the ring's stages as the FAST GEMV does (integer dp4a
+//     dot products on 24-bit fixed-point x, gemv_fastmath.cuh) into a
+//     partials tile;
 //   * warps 1..3 (chain) add each row's partials in a fixed tree order and
 //     run the fused epilogue (RoPE + KV store, residual add, SiLU*up, logits
-//     with a running argmax);
+//     with a running argmax); during the q|k|v projection they prefetch
+//     into L2 the K and V rows the CTA's attention reads next;
 //   * between dependent phases all 148 CTAs meet at a grid barrier (an
 //     atomic counter in global memory, release/acquire at GPU scope, every
-//     wait bounded); attention runs on the 15 worker warps (the split-K scores / softmax*V passes of attention.cu's FAST
-//     mode).
+//     wait bounded).  Attention runs on the 15 worker warps: up to 1024
+//     positions one CTA per head in one phase, beyond that the split-K
+//     scores / softmax*V passes of attention.cu's FAST mode.
 //
 // Each CTA owns the same contiguous row range of a given projection in every
 // layer, so the residual rows it adds to are the rows it wrote (no extra
 // barrier for the residual), and every vector another CTA wrote is read
-// through L2 (ld.global.cg).
+// through L2 (ld.global.cg, cp.async.cg).
 //
 // Numerics: FAST (tolerance 1e-4 normwise to the reference, greedy ids equal
 // to the exact path on every tested configuration).  Block values and the

@@ -136,6 +136,24 @@ def test_step_long_context(gpu):
         per_op.close()
 
 
+def test_step_long_context_split_k(gpu):
+    """past 1024 positions attention switches to the two-phase split-K form
+    (64-position chunks over all CTAs): fused decode at positions 1100.. agrees
+    with the per-operator kernels"""
+    synth = W.make_model(W.LLAMA2_7B, 13, n_layers=1)
+    prompt = W.tokens(1104, W.LLAMA2_7B["vocab_size"], 13)
+    fused, per_op = fast_model(synth), fast_model(synth, per_op=True)
+    try:
+        assert fused.prefill(prompt[:1100], 0) == per_op.prefill(prompt[:1100], 0)
+        for i in range(1100, 1104):
+            lf = fused.forward(int(prompt[i]), i)
+            lp = per_op.forward(int(prompt[i]), i)
+            assert normwise(lf, lp) <= CLOSE, (i, normwise(lf, lp))
+    finally:
+        fused.close()
+        per_op.close()
+
+
 def test_step_off_for_exact_and_opt_out(gpu):
     synth = W.make_model(W.SHARD_SMALL, 3)
     for kw, want in [(dict(), False), (dict(fused_step=1), False),
