@@ -687,45 +687,6 @@ __device__ __forceinline__ float4 ldcg4(const uint8_t* p) {
   }
 }
 
-// Four consecutive elements of a cache row, loaded now and widened later
-// (so a prefetch holds 8 bytes a lane for fp16 caches).
-template <int ESZ>
-struct Raw4 {
-  uint2 u;
-};
-template <>
-struct Raw4<4> {
-  float4 f;
-};
-template <int ESZ>
-__device__ __forceinline__ Raw4<ESZ> ldcg_raw(const uint8_t* p) {
-  Raw4<ESZ> r;
-  if constexpr (ESZ == 2)
-    r.u = __ldcg(reinterpret_cast<const uint2*>(p));
-  else
-    r.f = __ldcg(reinterpret_cast<const float4*>(p));
-  return r;
-}
-template <int ESZ>
-__device__ __forceinline__ float4 widen(const Raw4<ESZ>& r) {
-  if constexpr (ESZ == 2) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.u.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.u.y));
-    return make_float4(a.x, a.y, b.x, b.y);
-  } else {
-    return r.f;
-  }
-}
-template <int ESZ>
-__device__ __forceinline__ Raw4<ESZ> raw_zero() {
-  Raw4<ESZ> r;
-  if constexpr (ESZ == 2)
-    r.u = make_uint2(0u, 0u);
-  else
-    r.f = make_float4(0.f, 0.f, 0.f, 0.f);
-  return r;
-}
-
 __device__ __forceinline__ float warp_max_f(float m) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -960,14 +921,6 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       const int t = t0 + ((lane >> 2) & 7) * kNW;
       if ((lane & 3) == 0 && t < n) sc[t] = dot * scale;
     }
-    // the V rows of this warp's first PV pass (first 128 dims) start loading
-    // now: their latency overlaps the softmax
-    Raw4<ESZ> vpre[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int t = w + u * kNW;
-      vpre[u] = (t < n && 4 * lane < hd) ? ldcg_raw<ESZ>(vc + ((size_t)t * kv_dim + 4 * lane) * ESZ) : raw_zero<ESZ>();
-    }
     named_sync(B_WORKERS, kWorkers);
     // llm.c:509-521: max, e_t = llm_expf(s_t - max), sum (tree), 1/(sum + 1e-10)
     float m = -INFINITY;
@@ -998,10 +951,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int t = t0 + u * kNW;
-            if (sl == 0 && t0 == w)
-              vv[u] = widen<ESZ>(vpre[u]);
-            else
-              vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
