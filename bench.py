@@ -353,7 +353,7 @@ def run_ours(args, world, rank, local):
 
     prompt_next = {}
 
-    def timed_decode(model, clk=None):
+    def timed_decode(model, clk=None, prompt=prompt):
         """prompt token by token, W warm-up steps, then K chained steps
         (value) and K host round-trip steps (e2e); returns (ms, e2e ms, the
         2K greedy ids)"""
@@ -429,7 +429,8 @@ def run_ours(args, world, rank, local):
     sharded_ms = None
     if replicas:
         model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(force=True))
-        sharded_ms, _, _ = timed_decode(model)
+        # one sequence: every rank feeds the same prompt
+        sharded_ms, _, _ = timed_decode(model, prompt=W.tokens(args.prefill, cfg["vocab_size"], W.SEED))
         model.close()
     if world > 1:
         tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0, sharded_ms or 0.0], device="cuda")
