@@ -9,24 +9,35 @@
 // q*d (Q8_0, at most 19) is, after a per-row power-of-two scale, exactly
 // W_hi + W_lo with W_hi, W_lo fp16.  Each activation row is scaled by a power
 // of two and split into X_hi + X_lo (fp16, 22 significant bits).  The kernel
-// accumulates X_hi W_hi + X_lo W_hi + X_hi W_lo in fp32 TMEM (the dropped
-// X_lo W_lo is below 2^-22 relative) and undoes both scales exactly in the
+// accumulates W_hi X_hi + W_hi X_lo + W_lo X_hi in fp32 TMEM (the dropped
+// W_lo X_lo is below 2^-22 relative) and undoes both scales exactly in the
 // epilogue: results agree with the fp32 GEMV to ~1e-6 (normwise).
 //
-// Design (sm_100a, one CTA per 128x128 output tile and K slice):
-//   * prep kernel: X (fp32, row-major) -> per-row scale and X_hi / X_lo in
-//     the UMMA K-major SWIZZLE_128B layout, one 16 KB block per 64-wide K
-//     chunk, so the GEMM fetches each with a single cp.async.bulk.
-//   * warp 0: TMEM allocation and the A (activation) bulk copies;
-//     warp 1: one elected thread issues the tcgen05.mma (3 per 16-wide K step)
-//     and commits each stage back to the producers;
-//     warps 2..9: dequantise 128 weight rows x 64 columns per stage straight
-//     into the swizzled B tiles (2 threads per row), then run the epilogue
-//     (tcgen05.ld of the fp32 accumulator, exact unscaling, store).
-//   * S-stage shared-memory ring; every wait is bounded and reports through
-//     *err; TMEM is always released.
-//   * K is split over CTAs when the tile grid alone does not fill the GPU;
-//     partial tiles are added in split order by a reduce kernel.
+// Design (sm_100a).  The weights are the MMA's M side (128 rows of a tile,
+// one per TMEM lane) and the tokens its N side (N = tokens rounded up to 16,
+// at most 128 a tile), so a 16-token decode step issues 1/8 of the tensor
+// work of a 128-token prefill chunk and both stream the same weight bytes.
+// A persistent grid (one CTA per SM) walks work units (tile, K slice):
+//   * warp 0 streams the raw GGUF blocks of its units' rows, 8 blocks (4 K
+//     chunks of 64) a row per stage, with one cp.async.bulk per row into a
+//     shared-memory ring (mbarrier complete_tx).  Weights depend on nothing,
+//     so the ring fills before the previous kernel has finished;
+//   * warps 2..17, two groups of eight taking alternate K chunks, turn the
+//     raw blocks into the fp16 hi / lo A tiles (UMMA K-major SWIZZLE_128B,
+//     one row and one block a thread); the first thread of a group also
+//     bulk-copies the chunk's prepared activation parts (the B tiles);
+//   * warp 1: one elected thread issues the tcgen05.mma (3 per 16-wide K
+//     step) into one of two TMEM accumulators and commits each chunk back;
+//   * warps 18..21 (epilogue) read the accumulator of the previous unit
+//     (tcgen05.ld) while the next one accumulates, unscale it and store it.
+//     When K is split, each slice stores its partial tile and the warp that
+//     finishes a tile's rows last adds the slices in slice order
+//     (deterministic).
+// Q4_0 chunks are dequantised in a permuted K order (word e of every 16-byte
+// group holds elements e and e + 4, the order in which two mask operations
+// take the nibbles out of a 32-bit word); the activation prep writes the
+// same order, so the products are unchanged.  Every wait is bounded and
+// reports through *err; TMEM is always released.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -35,14 +46,24 @@
 
 namespace tos {
 
-constexpr int kBM = 128;                  // tokens per tile (TMEM lanes)
-constexpr int kBN = 128;                  // weight rows per tile (TMEM columns)
-constexpr int kBK = 64;                   // K per stage: one 128-byte fp16 row
-constexpr int kPart = kBM * kBK * 2;      // 16 KB: one operand part of a stage
-constexpr int kStageBytes = 4 * kPart;    // A_hi, A_lo, B_hi, B_lo
-constexpr int kGStages = 3;
-constexpr int kDqWarps = 8;               // dequantising / epilogue warps
-constexpr int kGThreads = 32 * (2 + kDqWarps);
+constexpr int kWR = 128;                  // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kTok = 128;                 // most tokens per tile (MMA N)
+constexpr int kBK = 64;                   // K per chunk: one 128-byte fp16 row
+constexpr int kAPart = kWR * kBK * 2;     // 16 KB: one weight operand part of a chunk
+constexpr int kRawBlk = 8;                // GGUF blocks a row per raw stage
+constexpr int kRawCh = kRawBlk / 2;       // K chunks per raw stage
+constexpr int kDqWarps = 8;               // dequantising warps per group
+constexpr int kDqGroups = 2;
+constexpr int kEpWarps = 4;
+constexpr int kDq0 = 2;                                  // first dequantising warp
+constexpr int kEp0 = kDq0 + kDqGroups * kDqWarps;        // first epilogue warp
+constexpr int kGThreads = 32 * (kEp0 + kEpWarps);        // 704
+constexpr int kMaxS = 4;                  // operand stages (A hi/lo + B hi/lo of one chunk)
+constexpr int kMaxR = 8;                  // raw stages
+constexpr int kHdrBytes = 256;
+constexpr int kMaxSmem = 227 * 1024;
+static_assert(kEp0 % 4 == 2, "the epilogue warps cover the four TMEM lane quarters");
+static_assert((2 * kMaxR + 2 * kMaxS + 5) * 8 + 8 <= kHdrBytes, "header");
 
 // ---------------------------------------------------------------------------
 // tcgen05 / descriptor helpers (PTX ISA 8.7, sm_100a)
@@ -60,16 +81,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor: fp32 accumulate, fp16 A and B, both K-major,
-// N = kBN, M = kBM.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+// M = 128; N (a multiple of 16, 16..256) goes to bits 17..22 as N / 8.
+constexpr uint32_t kIdescM128 = (1u << 4) | ((uint32_t)(kWR >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_n(int n) { return kIdescM128 | ((uint32_t)(n >> 3) << 17); }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -99,22 +121,19 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive fp32 accumulator columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// 16 consecutive fp32 accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a K-major SWIZZLE_128B
@@ -136,7 +155,7 @@ __device__ __forceinline__ float pow2_to_2p13(float m) {
 // hi + lo: Veltkamp split at 11 bits (t = v (2^13 + 1), hi = t - (t - v),
 // lo = v - hi, all exact in round-to-nearest fp32), then one packed
 // conversion per pair.  hi has 11 significant bits (exact in fp16); lo is
-// exact for weights (at most 15 bits in all) and keeps 11 more bits of an
+// exact for weights (at most 19 bits in all) and keeps 11 more bits of an
 // activation.
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi2, uint32_t& lo2) {
   const float ta = __fmul_rn(a, 8193.0f), tb = __fmul_rn(b, 8193.0f);
@@ -147,31 +166,61 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi2, uint32_t
   lo2 = *reinterpret_cast<const uint32_t*>(&L);
 }
 
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+
 struct GemmArgs {
   const uint8_t* qs;    // weight quants [N][nb][qb]
   const uint16_t* sc;   // weight scales [N][nbp] (fp16)
   const float* rws;     // per-row power-of-two weight scales [N]
-  int qb, nb, nbp;      // 16 (Q4_0) or 32 (Q8_0) bytes per block
-  int N, K;
-  const uint8_t* xa;    // prepared activations [mtiles][nkc][hi, lo][16 KB]
-  const float* xs;      // per-row activation scales [Mpad]
-  float* out;           // splits == 1: Y [M][N]; else partials [split][Mpad][N]
-  int M, Mpad, mtiles, ntiles;
-  int splits, kc_per_split, nkc;
+  int nb, nbp, N, K, nkc;
+  const uint8_t* xa;    // prepared activations [mtiles][nkc][hi, lo][NB rows x 128 B]
+  const float* xs;      // per-row inverse activation scales [mtiles * NB]
+  float* y;             // Y [M][N]
+  float* part;          // K-slice partials [splits][M][N]
+  int* cnt;             // per-tile count of finished K slices (zeroed by the prep kernel)
+  int M, NB, mtiles, ntiles, splits, kcps, units;
+  int S, R;             // operand and raw stages in the rings
+  uint32_t op_bytes, raw_bytes, raw_stride, tcols;
   int* err;
 };
 
+// One work unit: a 128-row weight tile, a token tile and a K slice.
+struct Unit {
+  int mt, tile, split, n0, kc0, nk, ntok;
+};
+__device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
+  Unit w;
+  w.split = u % a.splits;
+  w.tile = u / a.splits;
+  const int nt = w.tile % a.ntiles;
+  w.mt = w.tile / a.ntiles;
+  w.n0 = nt * kWR;
+  w.kc0 = w.split * a.kcps;
+  w.nk = min(a.nkc, w.kc0 + a.kcps) - w.kc0;
+  w.ntok = min(a.NB, (a.M - w.mt * kTok + 15) & ~15);
+  return w;
+}
+
 // ---------------------------------------------------------------------------
-// prep: X[M][K] fp32 -> per-row power-of-two scale and fp16 hi/lo parts in
-// the swizzled K-major layout (rows beyond M are zero)
+// prep: X[M][K] fp32 -> per-row power-of-two scale s (stored as 1/s, exact)
+// and fp16 hi/lo parts of X*s in the swizzled K-major layout, token tiles of
+// NB rows (rows beyond M are zero).  perm: the Q4_0 K order (word e of a
+// 16-byte group = elements e and e + 4 of its eight) instead of the natural
+// one.  Also clears the per-tile counters of the GEMM that follows.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict__ x, int M, int K,
-                                                        uint8_t* __restrict__ xa, float* __restrict__ xs) {
+__global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict__ x, int M, int K, int NB,
+                                                        int perm, uint8_t* __restrict__ xa,
+                                                        float* __restrict__ xs, int* __restrict__ cnt,
+                                                        int ncnt) {
   __shared__ float red[4];
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.x;           // padded row
-  const int mt = m / kBM, r = m % kBM;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
+  const int p = blockIdx.x;            // prepared row
+  const int mt = p / NB, r = p % NB;
+  const int m = mt * kTok + r;
   const int nkc = K / kBK;
   const bool valid = m < M;
   const float* xr = x + (size_t)m * K;
@@ -183,116 +232,118 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float s = pow2_to_2p13(mx);
-  if (threadIdx.x == 0) xs[m] = s;
-  // one 16-byte chunk (8 elements) per thread and step
+  if (threadIdx.x == 0) xs[p] = 1.0f / s;
+  const size_t part = (size_t)NB * 128;
+  // one 16-byte group (8 elements) per thread and step
   for (int q = threadIdx.x; q < K / 8; q += blockDim.x) {
     const int kc = q / 8, c = q % 8;
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float v0 = valid ? __fmul_rn(xr[8 * q + 2 * e], s) : 0.0f;
-      const float v1 = valid ? __fmul_rn(xr[8 * q + 2 * e + 1], s) : 0.0f;
+      const int i0 = perm ? e : 2 * e, i1 = perm ? e + 4 : 2 * e + 1;
+      const float v0 = valid ? __fmul_rn(xr[8 * q + i0], s) : 0.0f;
+      const float v1 = valid ? __fmul_rn(xr[8 * q + i1], s) : 0.0f;
       split2(v0, v1, hi[e], lo[e]);
     }
-    uint8_t* blk = xa + ((size_t)mt * nkc + kc) * 2 * kPart;
+    uint8_t* blk = xa + ((size_t)mt * nkc + kc) * 2 * part;
     *reinterpret_cast<uint4*>(blk + sw128_off(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(blk + kPart + sw128_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(blk + part + sw128_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
 }
 
-// split-K partials added in split order
-__global__ void gemm_reduce_kernel(const float* __restrict__ part, int splits, int M, int Mpad, int N,
-                                   float* __restrict__ y) {
-  pdl_wait();
-  pdl_trigger();
-  const size_t total = (size_t)M * N;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    float acc = part[i];
-    for (int s = 1; s < splits; ++s) acc += part[(size_t)s * Mpad * N + i];
-    y[i] = acc;
+// Q4_0 block (16 quant bytes; byte j = elements 2j (low nibble) and 2j + 1
+// (high nibble), llm.c:162-165) times d*ws into fp16 hi / lo words, in the
+// permuted K order: words 4k..4k+3 cover elements 8k..8k+7 as (e, e + 4).
+// D = d*ws (11 significant bits, exact) = Dh (top 7 bits) + Dl (4 bits);
+// (n - 8) Dh and (n - 8) Dl are exact in fp16.  A nibble n becomes 1024 + n
+// (or 1024 + 16 n for a high nibble, paired with Dh/16 and Dl/16) through
+// the 0x6400 exponent, so one subtraction gives (n - 8) (or 16 (n - 8)).
+__device__ __forceinline__ void dequant_q4(const uint4 q, float d, float ws, uint32_t (&hi)[16],
+                                           uint32_t (&lo)[16]) {
+  const float D = __fmul_rn(d, ws);
+  const float Dh = __uint_as_float(__float_as_uint(D) & ~((1u << 17) - 1u));
+  const float Dl = __fsub_rn(D, Dh);
+  const __half2 h1 = __float2half2_rn(Dh), l1 = __float2half2_rn(Dl);
+  const __half2 h16 = __float2half2_rn(__fmul_rn(Dh, 0.0625f));
+  const __half2 l16 = __float2half2_rn(__fmul_rn(Dl, 0.0625f));
+  const __half2 k1032 = __float2half2_rn(1032.0f), k1152 = __float2half2_rn(1152.0f);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w8 = w[k] >> 8;
+    const __half2 v0 = __hsub2(u2h((w[k] & 0x000F000Fu) | 0x64006400u), k1032);   // elements 0, 4
+    const __half2 v1 = __hsub2(u2h((w[k] & 0x00F000F0u) | 0x64006400u), k1152);   // 1, 5 (x16)
+    const __half2 v2 = __hsub2(u2h((w8 & 0x000F000Fu) | 0x64006400u), k1032);     // 2, 6
+    const __half2 v3 = __hsub2(u2h((w8 & 0x00F000F0u) | 0x64006400u), k1152);     // 3, 7 (x16)
+    hi[4 * k + 0] = h2u(__hmul2(v0, h1));
+    lo[4 * k + 0] = h2u(__hmul2(v0, l1));
+    hi[4 * k + 1] = h2u(__hmul2(v1, h16));
+    lo[4 * k + 1] = h2u(__hmul2(v1, l16));
+    hi[4 * k + 2] = h2u(__hmul2(v2, h1));
+    lo[4 * k + 2] = h2u(__hmul2(v2, l1));
+    hi[4 * k + 3] = h2u(__hmul2(v3, h16));
+    lo[4 * k + 3] = h2u(__hmul2(v3, l16));
   }
 }
 
-// Dequantises one 32-element block (quants in q0[, q1], scale d) into fp16
-// hi / lo pairs scaled by ws, exactly (Q4_0: 15 significant bits at most,
-// Q8_0: 19, split 11 + 8 by split2).
-template <int QB>
-__device__ __forceinline__ void dequant_block(const uint4 q0, const uint4 q1, float d, float ws,
-                                              uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+// Q8_0 block (32 int8 quants, llm.c:199-200) times d*ws into fp16 hi / lo
+// pairs in the natural K order (19 significant bits, split 11 + 8).
+__device__ __forceinline__ void dequant_q8(const uint4 q0, const uint4 q1, float d, float ws,
+                                           uint32_t (&hi)[16], uint32_t (&lo)[16]) {
   const float ds = __fmul_rn(d, ws);   // exact (power-of-two ws)
-  if constexpr (QB == 16) {
-    // Q4_0: (n - 8) is exact in fp16, and so are its products with the two
-    // parts of D = d*ws (11 significant bits) split 7 + 4: the weight is
-    // W_hi + W_lo = (n-8) D_hi + (n-8) D_lo without rounding, in packed
-    // half2 arithmetic.  Nibbles become 1024 + n through the 0x6400 magic.
-    const float D = ds;
-    const float Dh = __uint_as_float(__float_as_uint(D) & ~((1u << 17) - 1u));   // top 7 bits
-    const __half2 dh2 = __float2half2_rn(Dh);
-    const __half2 dl2 = __float2half2_rn(__fsub_rn(D, Dh));
-    const __half2 k1032 = __float2half2_rn(1032.0f);
-    const uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
+  const float kM = 8388736.0f;         // 2^23 + 128
+  const uint32_t w[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
+                         q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t lw = w[k] & 0x0F0F0F0Fu, hw = (w[k] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        // byte j = 4k + p: element 2j = low nibble, 2j+1 = high (llm.c:162-165)
-        const uint32_t sel = (uint32_t)(p | (p << 4) | ((4 + p) << 8) | ((4 + p) << 12));
-        const uint32_t t = (__byte_perm(lw, hw, sel) & 0x00FF00FFu) | 0x64006400u;
-        const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&t), k1032);
-        const __half2 H = __hmul2(v, dh2), L = __hmul2(v, dl2);
-        hi[4 * k + p] = *reinterpret_cast<const uint32_t*>(&H);
-        lo[4 * k + p] = *reinterpret_cast<const uint32_t*>(&L);
-      }
-    }
-  } else {
-    const float kM = 8388736.0f;       // 2^23 + 128
-    const uint32_t w[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
-                           q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t word = w[j >> 1];
-      const uint32_t b0 = (uint32_t)((2 * j) & 3), b1 = (uint32_t)((2 * j + 1) & 3);
-      const float e0 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | b0)), kM);
-      const float e1 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | b1)), kM);
-      split2(__fmul_rn(e0, ds), __fmul_rn(e1, ds), hi[j], lo[j]);   // llm.c:199-200
-    }
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t word = w[j >> 1];
+    const uint32_t b0 = (uint32_t)((2 * j) & 3), b1 = (uint32_t)((2 * j + 1) & 3);
+    const float e0 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | b0)), kM);
+    const float e1 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | b1)), kM);
+    split2(__fmul_rn(e0, ds), __fmul_rn(e1, ds), hi[j], lo[j]);
   }
+}
+
+// Every lane of the warp waits (each acquires the barrier's phase); the warp
+// continues only if all of them saw it complete.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const bool good = mbar_wait(bar, parity, err, code);
+  return __all_sync(0xffffffffu, good);
 }
 
 template <int QB>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a) {
   extern __shared__ uint8_t gsm[];
-  // header (barriers, TMEM address, row scales), then 1024-aligned stages
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(gsm);
-  uint64_t* b_full = a_full + kGStages;
-  uint64_t* empty = b_full + kGStages;
-  uint64_t* done = empty + kGStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  float* s_inv_ws = reinterpret_cast<float*>(gsm + 128);            // [kBN]
-  const uint32_t sbase = (smem_u32(gsm) + 640 + 1023) & ~1023u;
-  uint8_t* stages = gsm + (sbase - smem_u32(gsm));
-
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(gsm);   // [R]: raw stage landed
+  uint64_t* raw_empty = raw_full + kMaxR;                  // [R]: every dequantising warp is done with it
+  uint64_t* op_full = raw_empty + kMaxR;                   // [S]: A parts written, B parts landed
+  uint64_t* op_empty = op_full + kMaxS;                    // [S]: the chunk's MMAs have read it
+  uint64_t* tm_full = op_empty + kMaxS;                    // [2]: accumulator final
+  uint64_t* tm_empty = tm_full + 2;                        // [2]: accumulator read out
+  uint64_t* drain = tm_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  const uint32_t sbase = (smem_u32(gsm) + kHdrBytes + 1023) & ~1023u;
+  uint8_t* ops = gsm + (sbase - smem_u32(gsm));
+  uint8_t* raws = ops + (size_t)a.S * a.op_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int t = blockIdx.x;
-  const int nt = t % a.ntiles;
-  t /= a.ntiles;
-  const int mt = t % a.mtiles;
-  const int split = t / a.mtiles;
-  const int n0 = nt * kBN;
-  const int kc0 = split * a.kc_per_split;
-  const int nk = min(a.nkc, kc0 + a.kc_per_split) - kc0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGStages; ++s) {
-      mbar_init(&a_full[s], 1);
-      mbar_init(&b_full[s], kDqWarps);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < a.R; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kDqGroups * kDqWarps);
     }
-    mbar_init(done, 1);
+    for (int s = 0; s < a.S; ++s) {
+      mbar_init(&op_full[s], kDqWarps + 1);   // the group's warps + the B copies' expect_tx
+      mbar_init(&op_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tm_full[b], 1);
+      mbar_init(&tm_empty[b], kEpWarps);
+    }
+    mbar_init(drain, 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, kBN);   // fp32 accumulator: 128 lanes x 128 columns
+  if (warp == 0) tmem_alloc(tmem_slot, a.tcols);   // two accumulators of NB fp32 columns
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -300,123 +351,193 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
   pdl_trigger();
 
   if (warp == 0) {
-    // ---------------- activation tiles: one bulk copy per part ----------------
-    if (lane == 0) {
-      pdl_wait();   // the prepared activations come from the previous kernel
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % kGStages;
-        if (i >= kGStages && !mbar_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err, 21)) break;
-        uint8_t* st = stages + (size_t)s * kStageBytes;
-        const uint8_t* src = a.xa + ((size_t)mt * a.nkc + kc0 + i) * 2 * kPart;
-        mbar_arrive_expect_tx(&a_full[s], 2 * kPart);
-        bulk_g2s(st, src, kPart, &a_full[s]);
-        bulk_g2s(st + kPart, src + kPart, kPart, &a_full[s]);
+    // ---------------- raw weight stages: one bulk copy per row and plane ----------------
+    int j = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const Unit w = unit_of(a, u);
+      const int rows = min(kWR, a.N - w.n0);
+      for (int c = 0; c < w.nk; c += kRawCh, ++j) {
+        const int slot = j % a.R;
+        if (j >= a.R && !warp_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 21)) {
+          ok = false;
+          break;
+        }
+        const int b0 = 2 * (w.kc0 + c);   // a multiple of 8: the scale copy is 16-byte aligned
+        const uint32_t qbytes = (uint32_t)(2 * min(kRawCh, w.nk - c) * QB);
+        if (lane == 0) mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)rows * (qbytes + 16u));
+        __syncwarp();
+        uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
+        uint8_t* rs = rq + (size_t)kWR * a.raw_stride;
+        for (int r = lane; r < rows; r += 32) {
+          const size_t n = (size_t)(w.n0 + r);
+          bulk_g2s(rq + (size_t)r * a.raw_stride, a.qs + (n * a.nb + b0) * QB, qbytes, &raw_full[slot]);
+          bulk_g2s(rs + 16 * r, a.sc + n * a.nbp + b0, 16u, &raw_full[slot]);
+        }
       }
     }
+    // copies still in flight land before the CTA leaves (each slot's last
+    // stage is the newest phase of its barrier)
+    for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 28);
   } else if (warp == 1) {
     // ---------------- MMA issue (one thread) ----------------
     if (lane == 0) {
-      bool ok = true;
-      for (int i = 0; i < nk && ok; ++i) {
-        const int s = i % kGStages;
-        ok = mbar_wait(&a_full[s], (i / kGStages) & 1, a.err, 22) &&
-             mbar_wait(&b_full[s], (i / kGStages) & 1, a.err, 23);
-        if (!ok) break;
+      int i = 0, v = 0;
+      bool ok = true, issued = false;
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x, ++v) {
+        const Unit w = unit_of(a, u);
+        const int buf = v & 1;
+        if (v >= 2 && !mbar_wait(&tm_empty[buf], ((v >> 1) - 1) & 1, a.err, 22)) break;
         tc_fence_after();
-        const uint32_t base = smem_u32(stages + (size_t)s * kStageBytes);
+        const uint32_t idesc = idesc_n(w.ntok);
+        const uint32_t d = taddr + (uint32_t)(buf * a.NB);
+        for (int c = 0; c < w.nk; ++c, ++i) {
+          const int s = i % a.S;
+          if (!mbar_wait(&op_full[s], (i / a.S) & 1, a.err, 23)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(ops + (size_t)s * a.op_bytes);
+          const uint32_t bh0 = base + 2 * kAPart, bl0 = bh0 + (uint32_t)a.NB * 128u;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t ah = sw128_desc(base + 32 * kk);
-          const uint64_t al = sw128_desc(base + kPart + 32 * kk);
-          const uint64_t bh = sw128_desc(base + 2 * kPart + 32 * kk);
-          const uint64_t bl = sw128_desc(base + 3 * kPart + 32 * kk);
-          umma_f16(taddr, ah, bh, (i > 0 || kk > 0) ? 1u : 0u);
-          umma_f16(taddr, al, bh, 1u);
-          umma_f16(taddr, ah, bl, 1u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ah = sw128_desc(base + 32 * kk), al = sw128_desc(base + kAPart + 32 * kk);
+            const uint64_t bh = sw128_desc(bh0 + 32 * kk), bl = sw128_desc(bl0 + 32 * kk);
+            umma_f16(d, ah, bh, idesc, (c > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(d, ah, bl, idesc, 1u);
+            umma_f16(d, al, bh, idesc, 1u);
+          }
+          issued = true;
+          umma_commit(&op_empty[s]);   // the chunk's operands may be refilled once read
         }
-        umma_commit(&empty[s]);   // operands of stage s may be refilled once read
+        if (!ok) break;
+        umma_commit(&tm_full[buf]);    // this unit's accumulator is final
       }
-      umma_commit(done);          // the accumulator is final
-    }
-  } else {
-    // ---------------- weight dequantisation, then the epilogue ----------------
-    const int tid = threadIdx.x - 64;       // 0..255
-    const int r = tid >> 1, h = tid & 1;    // weight row in the tile, half of the 64 columns
-    const int n = n0 + r;
-    const bool valid = n < a.N;
-    const float ws = valid ? a.rws[n] : 1.0f;
-    if (h == 0) s_inv_ws[r] = 1.0f / ws;   // exact: power of two
-    // raw blocks are loaded kPf stages ahead (registers), so the global
-    // latency overlaps the dequantisation of the stages before
-    constexpr int kPf = 3;
-    uint4 qv[kPf], qv2[kPf];
-    float dv[kPf];
-    auto fetch = [&](int i, uint4& q0, uint4& q1, float& d) {
-      if (valid && i < nk) {
-        const int b = 2 * (kc0 + i) + h;
-        const uint8_t* src = a.qs + ((size_t)n * a.nb + b) * QB;
-        q0 = *reinterpret_cast<const uint4*>(src);
-        if constexpr (QB == 32) q1 = *reinterpret_cast<const uint4*>(src + 16);
-        d = h2f(a.sc[(size_t)n * a.nbp + b]);
+      if (issued) {
+        umma_commit(drain);            // nothing of this thread is in flight past here
+        mbar_wait(drain, 0, a.err, 27);
       }
-    };
-#pragma unroll
-    for (int u = 0; u < kPf; ++u) {
-      qv[u] = qv2[u] = make_uint4(0, 0, 0, 0);
-      dv[u] = 0.0f;
-      fetch(u, qv[u], qv2[u], dv[u]);
     }
+  } else if (warp < kEp0) {
+    // ---------------- dequantisation: group g takes the chunks i with i % 2 == g ----------------
+    const int g = (warp - kDq0) / kDqWarps;
+    const int tid = (int)threadIdx.x - 32 * (kDq0 + g * kDqWarps);   // 0..255
+    const int r = tid >> 1, h = tid & 1;   // weight row in the tile, block of the chunk
+    const bool leader = tid == 0;
+    if (leader) pdl_wait();                // the B parts come from the prep kernel
+    int i = 0, j = 0, last_s = -1, last_i = 0;
     bool ok = true;
-    for (int i0 = 0; i0 < nk && ok; i0 += kPf) {
-#pragma unroll
-      for (int u = 0; u < kPf; ++u) {
-        const int i = i0 + u;
-        if (i >= nk) break;
-        const int s = i % kGStages;
-        if (i >= kGStages && !mbar_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err, 24)) { ok = false; break; }
-        uint32_t hi[16], lo[16];
-        if (valid) {
-          dequant_block<QB>(qv[u], qv2[u], dv[u], ws, hi, lo);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) hi[e] = lo[e] = 0u;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const Unit w = unit_of(a, u);
+      const bool valid = w.n0 + r < a.N;
+      const float ws = valid ? a.rws[w.n0 + r] : 1.0f;
+      for (int c0 = 0; c0 < w.nk; c0 += kRawCh, ++j) {
+        const int slot = j % a.R;
+        if (!warp_wait(&raw_full[slot], (j / a.R) & 1, a.err, 24)) {
+          ok = false;
+          break;
         }
-        fetch(i + kPf, qv[u], qv2[u], dv[u]);
-        uint8_t* st = stages + (size_t)s * kStageBytes;
+        const uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
+        const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + (size_t)kWR * a.raw_stride);
+        const int cn = min(kRawCh, w.nk - c0);
+        for (int c = 0; c < cn; ++c, ++i) {
+          if ((i & 1) != g) continue;
+          const int s = i % a.S;
+          if (i >= a.S && !warp_wait(&op_empty[s], ((i / a.S) - 1) & 1, a.err, 25)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ops + (size_t)s * a.op_bytes;
+          if (leader) {
+            const uint32_t bbytes = (uint32_t)w.ntok * 128u;
+            const size_t part = (size_t)a.NB * 128;
+            const uint8_t* src = a.xa + ((size_t)w.mt * a.nkc + w.kc0 + c0 + c) * 2 * part;
+            mbar_arrive_expect_tx(&op_full[s], 2 * bbytes);
+            bulk_g2s(st + 2 * kAPart, src, bbytes, &op_full[s]);
+            bulk_g2s(st + 2 * kAPart + part, src + part, bbytes, &op_full[s]);
+            last_s = s;
+            last_i = i;
+          }
+          uint32_t hi[16], lo[16];
+          if (valid) {
+            const uint8_t* qp = rq + (size_t)r * a.raw_stride + (2 * c + h) * QB;
+            const float dd = h2f(rs[8 * r + 2 * c + h]);
+            if constexpr (QB == 16) {
+              dequant_q4(*reinterpret_cast<const uint4*>(qp), dd, ws, hi, lo);
+            } else {
+              dequant_q8(*reinterpret_cast<const uint4*>(qp), *reinterpret_cast<const uint4*>(qp + 16), dd, ws,
+                         hi, lo);
+            }
+          } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          *reinterpret_cast<uint4*>(st + 2 * kPart + sw128_off(r, 4 * h + c)) =
-              make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
-          *reinterpret_cast<uint4*>(st + 3 * kPart + sw128_off(r, 4 * h + c)) =
-              make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+            for (int e = 0; e < 16; ++e) hi[e] = lo[e] = 0u;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = sw128_off(r, 4 * h + q);
+            *reinterpret_cast<uint4*>(st + off) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+            *reinterpret_cast<uint4*>(st + kAPart + off) =
+                make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&op_full[s]);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
+        if (!ok) break;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&b_full[s]);
+        if (lane == 0) mbar_arrive(&raw_empty[slot]);
       }
     }
-    // epilogue: warp w reads TMEM lanes 32*(w%4).. and columns 64*((w-2)/4)..
-    asm volatile("barrier.sync 1, %0;" ::"r"(32 * kDqWarps) : "memory");   // s_inv_ws complete
-    if (ok && mbar_wait(done, 0, a.err, 25)) {
+    // after a failed wait, the last B copies land before the CTA leaves (on
+    // success the MMAs have read every chunk)
+    if (!ok && last_s >= 0) mbar_wait(&op_full[last_s], (last_i / a.S) & 1, a.err, 29);
+  } else {
+    // ---------------- epilogue: warp q reads TMEM lanes 32q..32q+31 ----------------
+    pdl_wait();   // Y, the partials, the counters and the scales: after the previous kernels
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    int v = 0;
+    for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++v) {
+      const Unit w = unit_of(a, u);
+      const int buf = v & 1;
+      if (!warp_wait(&tm_full[buf], (v >> 1) & 1, a.err, 26)) break;
       tc_fence_after();
-      pdl_wait();   // the activation scales come from the previous kernel (already complete here)
-      const int q = warp & 3;
-      const int cb = 64 * ((warp - 2) >> 2);
-      const int m = mt * kBM + 32 * q + lane;
-      const float inv_s = 1.0f / a.xs[m];   // exact: power of two
+      const int n = w.n0 + r;
+      const bool vn = n < a.N;
+      const float inv_ws = vn ? 1.0f / a.rws[n] : 0.0f;   // exact: power of two
+      const int m0 = w.mt * kTok;
+      const int mend = min(a.M, m0 + w.ntok);
+      float* dst = a.splits == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
+      for (int c0 = 0; c0 < w.ntok; c0 += 16) {
+        float vv[16];
+        tmem_ld16(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.NB + c0), vv);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float v[32];
-        tmem_ld32(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(cb + 32 * half), v);
-        const int c0 = cb + 32 * half;
-        if (a.splits == 1) {
-          if (m < a.M)
-            for (int j = 0; j < 32; ++j)
-              if (n0 + c0 + j < a.N) a.out[(size_t)m * a.N + n0 + c0 + j] = (v[j] * inv_s) * s_inv_ws[c0 + j];
-        } else {
-          float* p = a.out + ((size_t)split * a.Mpad + m) * a.N;
-          for (int j = 0; j < 32; ++j)
-            if (n0 + c0 + j < a.N) p[n0 + c0 + j] = (v[j] * inv_s) * s_inv_ws[c0 + j];
+        for (int e = 0; e < 16; ++e) {
+          const int m = m0 + c0 + e;
+          if (vn && m < mend) dst[(size_t)m * a.N + n] = __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[buf]);
+      if (a.splits > 1) {
+        // the warp that stores the last K slice of its 32 rows adds the
+        // slices in slice order
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&a.cnt[4 * w.tile + q], 1) == a.splits - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          if (vn)
+            for (int m = m0; m < mend; ++m) {
+              float acc = __ldcg(a.part + (size_t)m * a.N + n);
+              for (int s2 = 1; s2 < a.splits; ++s2)
+                acc = __fadd_rn(acc, __ldcg(a.part + ((size_t)s2 * a.M + m) * a.N + n));
+              a.y[(size_t)m * a.N + n] = acc;
+            }
         }
       }
     }
@@ -425,7 +546,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(taddr, kBN);
+    tmem_dealloc(taddr, a.tcols);
   }
 }
 
@@ -456,27 +577,63 @@ extern "C" int tosk_qmat_row_scales(tosk_qmat_t* m, cudaStream_t st) {
 
 namespace {
 struct GemmPlan {
-  int mtiles, ntiles, nkc, splits, kcps, Mpad;
-  size_t off_xs, off_part, bytes;
+  int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, S, R;
+  uint32_t op_bytes, raw_bytes, raw_stride, tcols;
+  size_t off_xs, off_cnt, off_part, bytes, smem;
 };
 
-GemmPlan gemm_plan(int M, int N, int K) {
-  GemmPlan p;
-  p.mtiles = (M + kBM - 1) / kBM;
-  p.Mpad = p.mtiles * kBM;
-  p.ntiles = (N + kBN - 1) / kBN;
+size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Ring sizes from the token tile, then the K split: the persistent grid runs
+// ceil(units / grid) units a CTA, so the split count trades idle SMs in the
+// last round of units against the partial tiles' traffic.  A chunk costs
+// the slowest of its weight bytes at the per-SM share of HBM bandwidth, its
+// three MMAs and its dequantisation (estimates in ns).  Deterministic in
+// (M, N, K, qb) on a given device.
+GemmPlan gemm_plan(int M, int N, int K, int qb) {
+  GemmPlan p = {};
+  p.mtiles = (M + kTok - 1) / kTok;
+  p.NB = min(kTok, (M + 15) & ~15);
+  p.ntiles = (N + kWR - 1) / kWR;
   p.nkc = K / kBK;
+  p.raw_stride = (uint32_t)(kRawBlk * qb + 32);   // a 32-byte skew between rows: conflict-free reads
+  p.raw_bytes = (uint32_t)kWR * p.raw_stride + (uint32_t)kWR * 16u;
+  p.op_bytes = (uint32_t)(2 * kAPart + 2 * p.NB * 128);
+  p.S = p.NB <= 64 ? 3 : 2;
+  const size_t avail = (size_t)kMaxSmem - kHdrBytes - 1024;
+  p.R = (int)min((size_t)kMaxR, (avail - (size_t)p.S * p.op_bytes) / p.raw_bytes);
+  p.tcols = 32;
+  while (p.tcols < (uint32_t)(2 * p.NB)) p.tcols <<= 1;
+  p.smem = (size_t)kHdrBytes + 1024 + (size_t)p.S * p.op_bytes + (size_t)p.R * p.raw_bytes;
+
   const int tiles = p.mtiles * p.ntiles;
   const int sms = tosk_num_sms();
-  int splits = sms / tiles;                        // fill the GPU in one wave
-  if (splits > p.nkc) splits = p.nkc;
-  if (splits < 1) splits = 1;
-  p.kcps = (p.nkc + splits - 1) / splits;
-  p.splits = (p.nkc + p.kcps - 1) / p.kcps;        // every split gets >= 1 chunk
-  const size_t xa = (size_t)p.mtiles * p.nkc * 2 * kPart;
-  p.off_xs = xa;
-  p.off_part = (p.off_xs + (size_t)p.Mpad * 4 + 255) & ~(size_t)255;
-  p.bytes = p.off_part + (p.splits > 1 ? (size_t)p.splits * p.Mpad * N * 4 : 0);
+  const double t_mem = 256.0 * (qb + 2) / (6500.0 / sms);
+  const double t_mma = 3.0 * kWR * p.NB * kBK / 5600.0;
+  const double t_dq = qb == 16 ? 95.0 : 250.0;
+  const double tc = fmax(t_mem, fmax(t_mma, t_dq));
+  double best = 1e300;
+  const int kmax = (p.nkc + 3) & ~3;
+  for (int kcps = 4; kcps <= kmax; kcps += 4) {
+    const int splits = (p.nkc + kcps - 1) / kcps;
+    if (splits > 64) continue;
+    const int units = tiles * splits;
+    const int grid = min(sms, units);
+    const int per = (units + grid - 1) / grid;
+    const double t = per * (min(kcps, p.nkc) * tc + (splits > 1 ? 350.0 : 200.0));
+    if (t < best * 0.999) {
+      best = t;
+      p.kcps = kcps;
+      p.splits = splits;
+      p.units = units;
+      p.grid = grid;
+    }
+  }
+  const size_t part = (size_t)p.NB * 128;
+  p.off_xs = up256((size_t)p.mtiles * p.nkc * 2 * part);
+  p.off_cnt = up256(p.off_xs + (size_t)p.mtiles * p.NB * 4);
+  p.off_part = up256(p.off_cnt + (size_t)tiles * 4 * 4);
+  p.bytes = p.off_part + (p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0);
   return p;
 }
 
@@ -496,65 +653,77 @@ int launch_ex(Kern kern, int grid, int threads, size_t smem, int pdl, cudaStream
 }
 }  // namespace
 
+// Largest workspace of any call with at most M rows (a caller sizes the
+// workspace once for its longest batch and then runs shorter ones).
 extern "C" size_t tosk_gemm_ws_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || K % kBK) return 0;
-  return gemm_plan(M, N, K).bytes;
+  size_t best = 0;
+  for (int m = 16;; m += 16) {
+    const int mm = min(m, M);
+    for (int qb = 16; qb <= 32; qb += 16) {
+      const size_t b = gemm_plan(mm, N, K, qb).bytes;
+      if (b > best) best = b;
+    }
+    if (mm == M) break;
+  }
+  return best;
 }
 
 extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y, void* ws, size_t ws_bytes,
                            int* err, int pdl, cudaStream_t st) {
-  if (!w || !x || !y || !ws || M <= 0) return (int)cudaErrorInvalidValue;
+  if (!w || !x || !y || !ws || M <= 0 || (w->qb != 16 && w->qb != 32)) return (int)cudaErrorInvalidValue;
   const int N = w->rows, K = w->cols;
   if (K % kBK || (reinterpret_cast<uintptr_t>(ws) & 255)) return (int)cudaErrorInvalidValue;
-  const GemmPlan p = gemm_plan(M, N, K);
-  if (ws_bytes < p.bytes) return (int)cudaErrorInvalidValue;
+  const GemmPlan p = gemm_plan(M, N, K, w->qb);
+  if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
   uint8_t* xa = (uint8_t*)ws;
   float* xs = (float*)((uint8_t*)ws + p.off_xs);
+  int* cnt = (int*)((uint8_t*)ws + p.off_cnt);
   float* part = (float*)((uint8_t*)ws + p.off_part);
   {
-    int Mi = M, Ki = K;
-    void* args[] = {(void*)&x, &Mi, &Ki, &xa, &xs};
-    const int e = launch_ex(gemm_prep_kernel, p.Mpad, 128, 0, pdl, st, args);
+    int Mi = M, Ki = K, NBi = p.NB, perm = w->qb == 16 ? 1 : 0, ncnt = p.mtiles * p.ntiles * 4;
+    void* args[] = {(void*)&x, &Mi, &Ki, &NBi, &perm, &xa, &xs, &cnt, &ncnt};
+    const int e = launch_ex(gemm_prep_kernel, p.mtiles * p.NB, 128, 0, pdl, st, args);
     if (e) return e;
   }
   GemmArgs a = {};
   a.qs = w->qs;
   a.sc = w->sc;
   a.rws = w->rws;
-  a.qb = w->qb;
   a.nb = w->nb;
   a.nbp = w->nbp;
   a.N = N;
   a.K = K;
+  a.nkc = p.nkc;
   a.xa = xa;
   a.xs = xs;
-  a.out = p.splits > 1 ? part : y;
+  a.y = y;
+  a.part = part;
+  a.cnt = cnt;
   a.M = M;
-  a.Mpad = p.Mpad;
+  a.NB = p.NB;
   a.mtiles = p.mtiles;
   a.ntiles = p.ntiles;
   a.splits = p.splits;
-  a.kc_per_split = p.kcps;
-  a.nkc = p.nkc;
+  a.kcps = p.kcps;
+  a.units = p.units;
+  a.S = p.S;
+  a.R = p.R;
+  a.op_bytes = p.op_bytes;
+  a.raw_bytes = p.raw_bytes;
+  a.raw_stride = p.raw_stride;
+  a.tcols = p.tcols;
   a.err = err;
-  const size_t smem = 640 + 1024 + (size_t)kGStages * kStageBytes;
   static bool attr_done[2] = {false, false};
   const int qi = w->qb == 16 ? 0 : 1;
   if (!attr_done[qi]) {
     const cudaError_t e = qi == 0
-        ? cudaFuncSetAttribute(gemm_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-        : cudaFuncSetAttribute(gemm_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ? cudaFuncSetAttribute(gemm_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)
+        : cudaFuncSetAttribute(gemm_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     if (e != cudaSuccess) return (int)e;
     attr_done[qi] = true;
   }
   void* gargs[] = {&a};
-  const int grid = p.ntiles * p.mtiles * p.splits;
-  int e = qi == 0 ? launch_ex(gemm_tc_kernel<16>, grid, kGThreads, smem, pdl, st, gargs)
-                  : launch_ex(gemm_tc_kernel<32>, grid, kGThreads, smem, pdl, st, gargs);
-  if (e || p.splits == 1) return e;
-  int splits = p.splits, Mi = M, Mp = p.Mpad, Ni = N;
-  void* rargs[] = {&part, &splits, &Mi, &Mp, &Ni, &y};
-  int rgrid = (int)(((size_t)M * N + 255) / 256);
-  if (rgrid > 4096) rgrid = 4096;
-  return launch_ex(gemm_reduce_kernel, rgrid, 256, 0, pdl, st, rargs);
+  return qi == 0 ? launch_ex(gemm_tc_kernel<16>, p.grid, kGThreads, p.smem, pdl, st, gargs)
+                 : launch_ex(gemm_tc_kernel<32>, p.grid, kGThreads, p.smem, pdl, st, gargs);
 }
