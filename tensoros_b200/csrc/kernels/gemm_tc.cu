@@ -180,24 +180,36 @@ struct GemmArgs {
   float* part;          // K-slice partials [splits][M][N]
   int* cnt;             // per-tile count of finished K slices (zeroed by the prep kernel)
   int M, NB, mtiles, ntiles, splits, kcps, units;
+  int full;             // tiles 0..full-1 run whole; the rest in `splits` K slices each
   int S, R;             // operand and raw stages in the rings
   uint32_t op_bytes, raw_bytes, raw_stride, tcols;
   int* err;
 };
 
-// One work unit: a 128-row weight tile, a token tile and a K slice.
+// One work unit: a 128-row weight tile, a token tile and a K slice (ns
+// slices of that tile in all; ns == 1 for a whole tile).
 struct Unit {
-  int mt, tile, split, n0, kc0, nk, ntok;
+  int mt, tile, split, ns, n0, kc0, nk, ntok;
 };
 __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
   Unit w;
-  w.split = u % a.splits;
-  w.tile = u / a.splits;
+  if (u < a.full) {
+    w.tile = u;
+    w.split = 0;
+    w.ns = 1;
+    w.kc0 = 0;
+    w.nk = a.nkc;
+  } else {
+    const int v = u - a.full;
+    w.tile = a.full + v / a.splits;
+    w.split = v % a.splits;
+    w.ns = a.splits;
+    w.kc0 = w.split * a.kcps;
+    w.nk = min(a.nkc, w.kc0 + a.kcps) - w.kc0;
+  }
   const int nt = w.tile % a.ntiles;
   w.mt = w.tile / a.ntiles;
   w.n0 = nt * kWR;
-  w.kc0 = w.split * a.kcps;
-  w.nk = min(a.nkc, w.kc0 + a.kcps) - w.kc0;
   w.ntok = min(a.NB, (a.M - w.mt * kTok + 15) & ~15);
   return w;
 }
@@ -508,38 +520,61 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
       const float inv_ws = vn ? 1.0f / a.rws[n] : 0.0f;   // exact: power of two
       const int m0 = w.mt * kTok;
       const int mend = min(a.M, m0 + w.ntok);
-      float* dst = a.splits == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
+      const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.NB);
+      float* dst = w.ns == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
       for (int c0 = 0; c0 < w.ntok; c0 += 16) {
         float vv[16];
-        tmem_ld16(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.NB + c0), vv);
+        tmem_ld16(tcol + (uint32_t)c0, vv);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int m = m0 + c0 + e;
           if (vn && m < mend) dst[(size_t)m * a.N + n] = __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tm_empty[buf]);
-      if (a.splits > 1) {
+      if (w.ns > 1) {
         // the warp that stores the last K slice of its 32 rows adds the
-        // slices in slice order
+        // slices in slice order, two slices x 16 tokens of L2 loads in
+        // flight at a time
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(&a.cnt[4 * w.tile + q], 1) == a.splits - 1;
+        if (lane == 0) last = atomicAdd(&a.cnt[4 * w.tile + q], 1) == w.ns - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
+        if (last && vn) {
           __threadfence();
-          if (vn)
-            for (int m = m0; m < mend; ++m) {
-              float acc = __ldcg(a.part + (size_t)m * a.N + n);
-              for (int s2 = 1; s2 < a.splits; ++s2)
-                acc = __fadd_rn(acc, __ldcg(a.part + ((size_t)s2 * a.M + m) * a.N + n));
-              a.y[(size_t)m * a.N + n] = acc;
+          for (int c0 = 0; c0 < w.ntok; c0 += 16) {
+            float acc[16];
+            for (int s0 = 0; s0 < w.ns; s0 += 2) {
+              float t[2][16];
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const int m = m0 + c0 + e;
+                  t[k][e] = (s0 + k < w.ns && m < mend)
+                                ? __ldcg(a.part + ((size_t)(s0 + k) * a.M + m) * a.N + n)
+                                : 0.0f;
+                }
+              }
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                if (s0 + k < w.ns) {
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) acc[e] = s0 + k == 0 ? t[k][e] : __fadd_rn(acc[e], t[k][e]);
+                }
+              }
             }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int m = m0 + c0 + e;
+              if (m < mend) a.y[(size_t)m * a.N + n] = acc[e];
+            }
+          }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[buf]);
     }
   }
   tc_fence_before();
@@ -577,19 +612,21 @@ extern "C" int tosk_qmat_row_scales(tosk_qmat_t* m, cudaStream_t st) {
 
 namespace {
 struct GemmPlan {
-  int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, S, R;
+  int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, S, R, full;
   uint32_t op_bytes, raw_bytes, raw_stride, tcols;
   size_t off_xs, off_cnt, off_part, bytes, smem;
 };
 
 size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// Ring sizes from the token tile, then the K split: the persistent grid runs
-// ceil(units / grid) units a CTA, so the split count trades idle SMs in the
-// last round of units against the partial tiles' traffic.  A chunk costs
-// the slowest of its weight bytes at the per-SM share of HBM bandwidth, its
-// three MMAs and its dequantisation (estimates in ns).  Deterministic in
-// (M, N, K, qb) on a given device.
+// Ring sizes from the token tile, then the schedule: every CTA first runs
+// the same number of whole tiles, then the tiles left over (fewer than the
+// SMs) are cut into K slices so that they spread over the grid.  The slice
+// count trades idle SMs in that last round against the slices' reduction.
+// A chunk costs the slowest of its weight bytes at the per-SM share of HBM
+// bandwidth, its three MMAs and its dequantisation; a reduction costs about
+// one L2 round trip per two slices and 16 tokens (estimates in ns).
+// Deterministic in (M, N, K, qb) on a given device.
 GemmPlan gemm_plan(int M, int N, int K, int qb) {
   GemmPlan p = {};
   p.mtiles = (M + kTok - 1) / kTok;
@@ -612,23 +649,28 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   const double t_mma = 3.0 * kWR * p.NB * kBK / 5600.0;
   const double t_dq = qb == 16 ? 95.0 : 250.0;
   const double tc = fmax(t_mem, fmax(t_mma, t_dq));
+  const int rounds = tiles / sms;
+  const int rem = tiles - rounds * sms;
+  p.full = rounds * sms;
+  p.kcps = (p.nkc + 3) & ~3;
+  p.splits = 1;
   double best = 1e300;
-  const int kmax = (p.nkc + 3) & ~3;
-  for (int kcps = 4; kcps <= kmax; kcps += 4) {
-    const int splits = (p.nkc + kcps - 1) / kcps;
-    if (splits > 64) continue;
-    const int units = tiles * splits;
-    const int grid = min(sms, units);
-    const int per = (units + grid - 1) / grid;
-    const double t = per * (min(kcps, p.nkc) * tc + (splits > 1 ? 350.0 : 200.0));
-    if (t < best * 0.999) {
-      best = t;
-      p.kcps = kcps;
-      p.splits = splits;
-      p.units = units;
-      p.grid = grid;
+  if (rem > 0) {
+    for (int kcps = 4; kcps <= ((p.nkc + 3) & ~3); kcps += 4) {
+      const int splits = (p.nkc + kcps - 1) / kcps;
+      if (splits > 64) continue;
+      const int last = (rem * splits + sms - 1) / sms;
+      const double red = splits > 1 ? ((p.NB + 15) / 16) * ((splits + 1) / 2) * 700.0 : 0.0;
+      const double t = last * (min(kcps, p.nkc) * tc + 200.0) + red;
+      if (t < best * 0.999) {
+        best = t;
+        p.kcps = kcps;
+        p.splits = splits;
+      }
     }
   }
+  p.units = p.full + rem * p.splits;
+  p.grid = min(sms, p.units);
   const size_t part = (size_t)p.NB * 128;
   p.off_xs = up256((size_t)p.mtiles * p.nkc * 2 * part);
   p.off_cnt = up256(p.off_xs + (size_t)p.mtiles * p.NB * 4);
@@ -707,6 +749,7 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   a.splits = p.splits;
   a.kcps = p.kcps;
   a.units = p.units;
+  a.full = p.full;
   a.S = p.S;
   a.R = p.R;
   a.op_bytes = p.op_bytes;
