@@ -19,12 +19,15 @@
 // work of a 128-token prefill chunk and both stream the same weight bytes.
 // A persistent grid (one CTA per SM) walks work units (tile, K slice):
 //   * warp 0 streams the raw GGUF blocks of its units' rows, 8 blocks (4 K
-//     chunks of 64) a row per stage, with one cp.async.bulk per row into a
-//     shared-memory ring (mbarrier complete_tx).  Weights depend on nothing,
-//     so the ring fills before the previous kernel has finished;
+//     chunks of 64) a row per stage: one TMA tensor load of the 128 x 128-byte
+//     quant box (two for Q8_0), swizzled 128B, and one of the 128 x 16-byte
+//     scale box, into a shared-memory ring (mbarrier complete_tx).  Weights
+//     depend on nothing, so the ring fills before the previous kernel has
+//     finished;
 //   * warps 2..17, two groups of eight taking alternate K chunks, turn the
 //     raw blocks into the fp16 hi / lo A tiles (UMMA K-major SWIZZLE_128B,
-//     one row and one block a thread); the first thread of a group also
+//     one row and one block a thread, consecutive lanes on consecutive rows:
+//     no bank conflicts on either side); the first thread of a group also
 //     bulk-copies the chunk's prepared activation parts (the B tiles);
 //   * warp 1: one elected thread issues the tcgen05.mma (3 per 16-wide K
 //     step) into one of two TMEM accumulators and commits each chunk back;
@@ -38,6 +41,8 @@
 // take the nibbles out of a 32-bit word); the activation prep writes the
 // same order, so the products are unchanged.  Every wait is bounded and
 // reports through *err; TMEM is always released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -57,7 +62,8 @@ constexpr int kDqGroups = 2;
 constexpr int kEpWarps = 4;
 constexpr int kDq0 = 2;                                  // first dequantising warp
 constexpr int kEp0 = kDq0 + kDqGroups * kDqWarps;        // first epilogue warp
-constexpr int kGThreads = 32 * (kEp0 + kEpWarps);        // 704
+constexpr int kGThreads = 32 * (kEp0 + kEpWarps);        // 704: six warps on some SM
+                                                         // sub-partitions, 80 registers a thread
 constexpr int kMaxS = 4;                  // operand stages (A hi/lo + B hi/lo of one chunk)
 constexpr int kMaxR = 8;                  // raw stages
 constexpr int kHdrBytes = 256;
@@ -170,8 +176,8 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
 
 struct GemmArgs {
-  const uint8_t* qs;    // weight quants [N][nb][qb]
-  const uint16_t* sc;   // weight scales [N][nbp] (fp16)
+  CUtensorMap tq;       // weight quants [N][nb * qb] bytes: 128-byte x 128-row boxes, swizzled 128B
+  CUtensorMap ts;       // weight scales [N][nbp] fp16: 8 x 128 boxes
   const float* rws;     // per-row power-of-two weight scales [N]
   int nb, nbp, N, K, nkc;
   const uint8_t* xa;    // prepared activations [mtiles][nkc][hi, lo][NB rows x 128 B]
@@ -182,7 +188,7 @@ struct GemmArgs {
   int M, NB, mtiles, ntiles, splits, kcps, units;
   int full;             // tiles 0..full-1 run whole; the rest in `splits` K slices each
   int S, R;             // operand and raw stages in the rings
-  uint32_t op_bytes, raw_bytes, raw_stride, tcols;
+  uint32_t op_bytes, raw_bytes, tcols;
   int* err;
 };
 
@@ -318,13 +324,24 @@ __device__ __forceinline__ void dequant_q8(const uint4 q0, const uint4 q1, float
 
 // Every lane of the warp waits (each acquires the barrier's phase); the warp
 // continues only if all of them saw it complete.
+// 2-D TMA tensor load into this CTA's shared memory, completion counted on
+// `bar` in bytes.  No multicast.  x (innermost, in elements) times the
+// element size is a multiple of 16 at every call site.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   const bool good = mbar_wait(bar, parity, err, code);
   return __all_sync(0xffffffffu, good);
 }
 
 template <int QB>
-__global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ uint8_t gsm[];
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(gsm);   // [R]: raw stage landed
   uint64_t* raw_empty = raw_full + kMaxR;                  // [R]: every dequantising warp is done with it
@@ -363,34 +380,34 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
   pdl_trigger();
 
   if (warp == 0) {
-    // ---------------- raw weight stages: one bulk copy per row and plane ----------------
-    int j = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
-      const Unit w = unit_of(a, u);
-      const int rows = min(kWR, a.N - w.n0);
-      for (int c = 0; c < w.nk; c += kRawCh, ++j) {
-        const int slot = j % a.R;
-        if (j >= a.R && !warp_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 21)) {
-          ok = false;
-          break;
+    // ---------------- raw weight stages: TMA boxes of 128 rows x 8 blocks ----------------
+    // (rows past N and blocks past the row end read as zeros)
+    constexpr int kQBoxes = QB / 16;
+    if (lane == 0) {
+      int j = 0;
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+        const Unit w = unit_of(a, u);
+        bool ok = true;
+        for (int c = 0; c < w.nk; c += kRawCh, ++j) {
+          const int slot = j % a.R;
+          if (j >= a.R && !mbar_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 21)) {
+            ok = false;
+            break;
+          }
+          const int b0 = 2 * (w.kc0 + c);   // a multiple of 8: every box starts 16-byte aligned
+          uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
+          mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(kQBoxes * 16384 + 2048));
+#pragma unroll
+          for (int qb = 0; qb < kQBoxes; ++qb)
+            tma_load_2d(rq + 16384 * qb, &a.tq, b0 * QB + 128 * qb, w.n0, &raw_full[slot]);
+          tma_load_2d(rq + 16384 * kQBoxes, &a.ts, b0, w.n0, &raw_full[slot]);
         }
-        const int b0 = 2 * (w.kc0 + c);   // a multiple of 8: the scale copy is 16-byte aligned
-        const uint32_t qbytes = (uint32_t)(2 * min(kRawCh, w.nk - c) * QB);
-        if (lane == 0) mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)rows * (qbytes + 16u));
-        __syncwarp();
-        uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
-        uint8_t* rs = rq + (size_t)kWR * a.raw_stride;
-        for (int r = lane; r < rows; r += 32) {
-          const size_t n = (size_t)(w.n0 + r);
-          bulk_g2s(rq + (size_t)r * a.raw_stride, a.qs + (n * a.nb + b0) * QB, qbytes, &raw_full[slot]);
-          bulk_g2s(rs + 16 * r, a.sc + n * a.nbp + b0, 16u, &raw_full[slot]);
-        }
+        if (!ok) break;
       }
+      // loads still in flight land before the CTA leaves (each slot's last
+      // stage is the newest phase of its barrier)
+      for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 28);
     }
-    // copies still in flight land before the CTA leaves (each slot's last
-    // stage is the newest phase of its barrier)
-    for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 28);
   } else if (warp == 1) {
     // ---------------- MMA issue (one thread) ----------------
     if (lane == 0) {
@@ -435,7 +452,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
     // ---------------- dequantisation: group g takes the chunks i with i % 2 == g ----------------
     const int g = (warp - kDq0) / kDqWarps;
     const int tid = (int)threadIdx.x - 32 * (kDq0 + g * kDqWarps);   // 0..255
-    const int r = tid >> 1, h = tid & 1;   // weight row in the tile, block of the chunk
+    const int r = tid & (kWR - 1), h = tid >> 7;   // weight row in the tile, block of the chunk
     const bool leader = tid == 0;
     if (leader) pdl_wait();                // the B parts come from the prep kernel
     int i = 0, j = 0, last_s = -1, last_i = 0;
@@ -451,7 +468,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
           break;
         }
         const uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
-        const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + (size_t)kWR * a.raw_stride);
+        const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + 16384 * (QB / 16));
         const int cn = min(kRawCh, w.nk - c0);
         for (int c = 0; c < cn; ++c, ++i) {
           if ((i & 1) != g) continue;
@@ -473,13 +490,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const GemmArgs a)
           }
           uint32_t hi[16], lo[16];
           if (valid) {
-            const uint8_t* qp = rq + (size_t)r * a.raw_stride + (2 * c + h) * QB;
-            const float dd = h2f(rs[8 * r + 2 * c + h]);
+            const int blk = 2 * c + h;    // block of the raw stage, 0..7
+            const float dd = h2f(rs[8 * r + blk]);
             if constexpr (QB == 16) {
-              dequant_q4(*reinterpret_cast<const uint4*>(qp), dd, ws, hi, lo);
+              dequant_q4(*reinterpret_cast<const uint4*>(rq + sw128_off(r, blk)), dd, ws, hi, lo);
             } else {
-              dequant_q8(*reinterpret_cast<const uint4*>(qp), *reinterpret_cast<const uint4*>(qp + 16), dd, ws,
-                         hi, lo);
+              const uint8_t* box = rq + 16384 * (blk >> 2);
+              dequant_q8(*reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3))),
+                         *reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3) + 1)), dd, ws, hi, lo);
             }
           } else {
 #pragma unroll
@@ -613,7 +631,7 @@ extern "C" int tosk_qmat_row_scales(tosk_qmat_t* m, cudaStream_t st) {
 namespace {
 struct GemmPlan {
   int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, S, R, full;
-  uint32_t op_bytes, raw_bytes, raw_stride, tcols;
+  uint32_t op_bytes, raw_bytes, tcols;
   size_t off_xs, off_cnt, off_part, bytes, smem;
 };
 
@@ -633,8 +651,7 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   p.NB = min(kTok, (M + 15) & ~15);
   p.ntiles = (N + kWR - 1) / kWR;
   p.nkc = K / kBK;
-  p.raw_stride = (uint32_t)(kRawBlk * qb + 32);   // a 32-byte skew between rows: conflict-free reads
-  p.raw_bytes = (uint32_t)kWR * p.raw_stride + (uint32_t)kWR * 16u;
+  p.raw_bytes = (uint32_t)(16384 * (qb / 16) + 2048);   // quant box(es), then the scale box
   p.op_bytes = (uint32_t)(2 * kAPart + 2 * p.NB * 128);
   p.S = p.NB <= 64 ? 3 : 2;
   const size_t avail = (size_t)kMaxSmem - kHdrBytes - 1024;
@@ -695,6 +712,20 @@ int launch_ex(Kern kern, int grid, int threads, size_t smem, int pdl, cudaStream
 }
 }  // namespace
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on the driver library).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
 // Largest workspace of any call with at most M rows (a caller sizes the
 // workspace once for its longest batch and then runs shorter ones).
 extern "C" size_t tosk_gemm_ws_bytes(int M, int N, int K) {
@@ -729,8 +760,25 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
     if (e) return e;
   }
   GemmArgs a = {};
-  a.qs = w->qs;
-  a.sc = w->sc;
+  {
+    // tensor maps of the two weight planes (host-side encoding, no device work)
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return (int)cudaErrorNotSupported;
+    const cuuint32_t es[2] = {1, 1};
+    const cuuint64_t qdim[2] = {(cuuint64_t)w->nb * w->qb, (cuuint64_t)N};
+    const cuuint64_t qstr[1] = {(cuuint64_t)w->nb * w->qb};
+    const cuuint32_t qbox[2] = {128, (cuuint32_t)kWR};
+    const cuuint64_t sdim[2] = {(cuuint64_t)w->nbp, (cuuint64_t)N};
+    const cuuint64_t sstr[1] = {(cuuint64_t)w->nbp * 2};
+    const cuuint32_t sbox[2] = {(cuuint32_t)kRawBlk, (cuuint32_t)kWR};
+    if (enc(&a.tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)w->qs, qdim, qstr, qbox, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&a.ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void*)w->sc, sdim, sstr, sbox, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return (int)cudaErrorInvalidValue;
+  }
   a.rws = w->rws;
   a.nb = w->nb;
   a.nbp = w->nbp;
@@ -754,7 +802,6 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   a.R = p.R;
   a.op_bytes = p.op_bytes;
   a.raw_bytes = p.raw_bytes;
-  a.raw_stride = p.raw_stride;
   a.tcols = p.tcols;
   a.err = err;
   static bool attr_done[2] = {false, false};
