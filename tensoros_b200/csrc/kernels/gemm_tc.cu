@@ -27,15 +27,22 @@
 //   * warps 2..17, two groups of eight taking alternate K chunks, turn the
 //     raw blocks into the fp16 hi / lo A tiles (UMMA K-major SWIZZLE_128B,
 //     one row and one block a thread, consecutive lanes on consecutive rows:
-//     no bank conflicts on either side); the first thread of a group also
-//     bulk-copies the chunk's prepared activation parts (the B tiles);
-//   * warp 1: one elected thread issues the tcgen05.mma (3 per 16-wide K
-//     step) into one of two TMEM accumulators and commits each chunk back;
+//     no bank conflicts on either side) in a ring of A stages;
+//   * warp 22 bulk-copies the prepared activation parts (the B tiles) into
+//     their own ring, ahead of the MMAs: for up to 32 tokens one copy covers
+//     the four chunks of a weight stage (an L2-to-shared copy takes ~1.5 us
+//     whatever its size, so small tiles need many chunks in flight);
+//   * warp 1: one elected thread issues the tcgen05.mma into one of two TMEM
+//     accumulators and commits each chunk back.  Up to 64 tokens (where the
+//     MMA count, not the tensor pipe, sets the pace) the X_hi and X_lo parts
+//     form one N = 2 NB operand: 2 MMAs per 16-wide K step, W_hi [X_hi X_lo]
+//     and W_lo [X_hi X_lo], the two column halves added in the epilogue;
+//     beyond that 3 MMAs per step (W_hi X_hi, W_hi X_lo, W_lo X_hi);
 //   * warps 18..21 (epilogue) read the accumulator of the previous unit
 //     (tcgen05.ld) while the next one accumulates, unscale it and store it.
-//     When K is split, each slice stores its partial tile and the warp that
-//     finishes a tile's rows last adds the slices in slice order
-//     (deterministic).
+// Every CTA first runs the same number of whole tiles; the tiles left over
+// are cut into K slices whose partial tiles a second kernel adds in slice
+// order (deterministic).
 // Q4_0 chunks are dequantised in a permuted K order (word e of every 16-byte
 // group holds elements e and e + 4, the order in which two mask operations
 // take the nibbles out of a 32-bit word); the activation prep writes the
@@ -62,14 +69,16 @@ constexpr int kDqGroups = 2;
 constexpr int kEpWarps = 4;
 constexpr int kDq0 = 2;                                  // first dequantising warp
 constexpr int kEp0 = kDq0 + kDqGroups * kDqWarps;        // first epilogue warp
-constexpr int kGThreads = 32 * (kEp0 + kEpWarps);        // 704: six warps on some SM
+constexpr int kBw = kEp0 + kEpWarps;                     // activation copy warp
+constexpr int kGThreads = 32 * (kBw + 1);                // 736: six warps on some SM
                                                          // sub-partitions, 80 registers a thread
-constexpr int kMaxS = 4;                  // operand stages (A hi/lo + B hi/lo of one chunk)
+constexpr int kMaxSA = 4;                 // A stages (weight hi/lo of one chunk)
+constexpr int kMaxSB = 8;                 // B stages (activation hi/lo of one chunk)
 constexpr int kMaxR = 8;                  // raw stages
-constexpr int kHdrBytes = 256;
+constexpr int kHdrBytes = 512;
 constexpr int kMaxSmem = 227 * 1024;
 static_assert(kEp0 % 4 == 2, "the epilogue warps cover the four TMEM lane quarters");
-static_assert((2 * kMaxR + 2 * kMaxS + 5) * 8 + 8 <= kHdrBytes, "header");
+static_assert((2 * kMaxR + 2 * kMaxSA + 2 * kMaxSB + 5) * 8 + 8 <= kHdrBytes, "header");
 
 // ---------------------------------------------------------------------------
 // tcgen05 / descriptor helpers (PTX ISA 8.7, sm_100a)
@@ -184,18 +193,24 @@ struct GemmArgs {
   const float* xs;      // per-row inverse activation scales [mtiles * NB]
   float* y;             // Y [M][N]
   float* part;          // K-slice partials [splits][M][N]
-  int* cnt;             // per-tile count of finished K slices (zeroed by the prep kernel)
   int M, NB, mtiles, ntiles, splits, kcps, units;
   int full;             // tiles 0..full-1 run whole; the rest in `splits` K slices each
-  int S, R;             // operand and raw stages in the rings
-  uint32_t op_bytes, raw_bytes, tcols;
+  int SA, SB, R;        // A, B and raw stages in the rings
+  int bcs;              // chunks per B stage: kRawCh (one copy per weight stage) or 1
+  int cat;              // 1: [X_hi X_lo] as one operand, accumulators of 2 NB columns
+  uint32_t b_bytes, raw_bytes, tcols;   // b_bytes: one B stage
   int* err;
 };
 
 // One work unit: a 128-row weight tile, a token tile and a K slice (ns
-// slices of that tile in all; ns == 1 for a whole tile).
+// slices of that tile in all; ns == 1 for a whole tile).  Its nst raw stages
+// (4 chunks each, the last one possibly shorter) run in the order
+// rot, rot + 1, ..., nst - 1, 0, ..., rot - 1 with rot = tile % nst, so CTAs
+// that run units at the same time read different activation chunks (one
+// order for all of them piles every CTA onto the same L2 lines); the order
+// depends on the tile only, so results are the same run to run.
 struct Unit {
-  int mt, tile, split, ns, n0, kc0, nk, ntok;
+  int mt, tile, split, ns, n0, kc0, nk, ntok, nst, rot;
 };
 __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
   Unit w;
@@ -217,7 +232,15 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
   w.mt = w.tile / a.ntiles;
   w.n0 = nt * kWR;
   w.ntok = min(a.NB, (a.M - w.mt * kTok + 15) & ~15);
+  w.nst = (w.nk + kRawCh - 1) / kRawCh;
+  w.rot = w.tile % w.nst;
   return w;
+}
+
+// First chunk (relative to kc0) and chunk count of the q-th raw stage run.
+__device__ __forceinline__ int stage_c0(const Unit& w, int q) {
+  const int st = q + w.rot < w.nst ? q + w.rot : q + w.rot - w.nst;
+  return kRawCh * st;
 }
 
 // ---------------------------------------------------------------------------
@@ -225,17 +248,15 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u) {
 // and fp16 hi/lo parts of X*s in the swizzled K-major layout, token tiles of
 // NB rows (rows beyond M are zero).  perm: the Q4_0 K order (word e of a
 // 16-byte group = elements e and e + 4 of its eight) instead of the natural
-// one.  Also clears the per-tile counters of the GEMM that follows.
+// one.  Grid: (prepared row, part of K); every CTA of a row finds the row's
+// maximum, then converts its part.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict__ x, int M, int K, int NB,
                                                         int perm, uint8_t* __restrict__ xa,
-                                                        float* __restrict__ xs, int* __restrict__ cnt,
-                                                        int ncnt) {
+                                                        float* __restrict__ xs) {
   __shared__ float red[4];
   pdl_wait();
   pdl_trigger();
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
   const int p = blockIdx.x;            // prepared row
   const int mt = p / NB, r = p % NB;
   const int m = mt * kTok + r;
@@ -250,10 +271,12 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float s = pow2_to_2p13(mx);
-  if (threadIdx.x == 0) xs[p] = 1.0f / s;
+  if (threadIdx.x == 0 && blockIdx.y == 0) xs[p] = 1.0f / s;
   const size_t part = (size_t)NB * 128;
+  const int ng = K / 8;
+  const int g1 = (int)(((long long)(blockIdx.y + 1) * ng) / gridDim.y);
   // one 16-byte group (8 elements) per thread and step
-  for (int q = threadIdx.x; q < K / 8; q += blockDim.x) {
+  for (int q = (int)(((long long)blockIdx.y * ng) / gridDim.y) + threadIdx.x; q < g1; q += blockDim.x) {
     const int kc = q / 8, c = q % 8;
     uint32_t hi[4], lo[4];
 #pragma unroll
@@ -335,6 +358,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// True in exactly one lane of a full warp (the lowest).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
+
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   const bool good = mbar_wait(bar, parity, err, code);
   return __all_sync(0xffffffffu, good);
@@ -345,15 +379,18 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   extern __shared__ uint8_t gsm[];
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(gsm);   // [R]: raw stage landed
   uint64_t* raw_empty = raw_full + kMaxR;                  // [R]: every dequantising warp is done with it
-  uint64_t* op_full = raw_empty + kMaxR;                   // [S]: A parts written, B parts landed
-  uint64_t* op_empty = op_full + kMaxS;                    // [S]: the chunk's MMAs have read it
-  uint64_t* tm_full = op_empty + kMaxS;                    // [2]: accumulator final
+  uint64_t* a_full = raw_empty + kMaxR;                    // [SA]: the chunk's A parts written
+  uint64_t* a_empty = a_full + kMaxSA;                     // [SA]: the chunk's MMAs have read them
+  uint64_t* b_full = a_empty + kMaxSA;                     // [SB]: the chunk's B parts landed
+  uint64_t* b_empty = b_full + kMaxSB;                     // [SB]: the chunk's MMAs have read them
+  uint64_t* tm_full = b_empty + kMaxSB;                    // [2]: accumulator final
   uint64_t* tm_empty = tm_full + 2;                        // [2]: accumulator read out
   uint64_t* drain = tm_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const uint32_t sbase = (smem_u32(gsm) + kHdrBytes + 1023) & ~1023u;
-  uint8_t* ops = gsm + (sbase - smem_u32(gsm));
-  uint8_t* raws = ops + (size_t)a.S * a.op_bytes;
+  uint8_t* aring = gsm + (sbase - smem_u32(gsm));
+  uint8_t* bring = aring + (size_t)a.SA * (2 * kAPart);
+  uint8_t* raws = bring + (size_t)a.SB * a.b_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -361,9 +398,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kDqGroups * kDqWarps);
     }
-    for (int s = 0; s < a.S; ++s) {
-      mbar_init(&op_full[s], kDqWarps + 1);   // the group's warps + the B copies' expect_tx
-      mbar_init(&op_empty[s], 1);
+    for (int s = 0; s < a.SA; ++s) {
+      mbar_init(&a_full[s], kDqWarps);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < a.SB; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tm_full[b], 1);
@@ -388,13 +429,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
         const Unit w = unit_of(a, u);
         bool ok = true;
-        for (int c = 0; c < w.nk; c += kRawCh, ++j) {
+        for (int q = 0; q < w.nst; ++q, ++j) {
           const int slot = j % a.R;
           if (j >= a.R && !mbar_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 21)) {
             ok = false;
             break;
           }
-          const int b0 = 2 * (w.kc0 + c);   // a multiple of 8: every box starts 16-byte aligned
+          const int b0 = 2 * (w.kc0 + stage_c0(w, q));   // a multiple of 8: every box starts 16-byte aligned
           uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
           mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(kQBoxes * 16384 + 2048));
 #pragma unroll
@@ -408,60 +449,104 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       // stage is the newest phase of its barrier)
       for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 28);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issue (one thread) ----------------
+  } else if (warp == kBw) {
+    // ---------------- activation (B) parts: one bulk copy per B stage ----------------
     if (lane == 0) {
-      int i = 0, v = 0;
-      bool ok = true, issued = false;
-      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x, ++v) {
+      pdl_wait();   // the prepared activations come from the prep kernel
+      const uint32_t cbytes = 2u * (uint32_t)a.NB * 128u;   // hi and lo parts of one chunk
+      int i = 0;    // B stages issued
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
         const Unit w = unit_of(a, u);
-        const int buf = v & 1;
-        if (v >= 2 && !mbar_wait(&tm_empty[buf], ((v >> 1) - 1) & 1, a.err, 22)) break;
-        tc_fence_after();
-        const uint32_t idesc = idesc_n(w.ntok);
-        const uint32_t d = taddr + (uint32_t)(buf * a.NB);
-        for (int c = 0; c < w.nk; ++c, ++i) {
-          const int s = i % a.S;
-          if (!mbar_wait(&op_full[s], (i / a.S) & 1, a.err, 23)) {
-            ok = false;
-            break;
+        bool ok = true;
+        for (int q = 0; q < w.nst && ok; ++q) {
+          const int c0 = stage_c0(w, q), cn = min(kRawCh, w.nk - c0);
+          for (int c = c0; c < c0 + cn; c += a.bcs, ++i) {
+            const int s = i % a.SB;
+            if (i >= a.SB && !mbar_wait(&b_empty[s], ((i / a.SB) - 1) & 1, a.err, 29)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bytes = (uint32_t)min(a.bcs, c0 + cn - c) * cbytes;
+            mbar_arrive_expect_tx(&b_full[s], bytes);
+            bulk_g2s(bring + (size_t)s * a.b_bytes, a.xa + ((size_t)w.mt * a.nkc + w.kc0 + c) * cbytes, bytes,
+                     &b_full[s]);
           }
-          tc_fence_after();
-          const uint32_t base = smem_u32(ops + (size_t)s * a.op_bytes);
-          const uint32_t bh0 = base + 2 * kAPart, bl0 = bh0 + (uint32_t)a.NB * 128u;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ah = sw128_desc(base + 32 * kk), al = sw128_desc(base + kAPart + 32 * kk);
-            const uint64_t bh = sw128_desc(bh0 + 32 * kk), bl = sw128_desc(bl0 + 32 * kk);
-            umma_f16(d, ah, bh, idesc, (c > 0 || kk > 0) ? 1u : 0u);
-            umma_f16(d, ah, bl, idesc, 1u);
-            umma_f16(d, al, bh, idesc, 1u);
-          }
-          issued = true;
-          umma_commit(&op_empty[s]);   // the chunk's operands may be refilled once read
         }
         if (!ok) break;
-        umma_commit(&tm_full[buf]);    // this unit's accumulator is final
       }
-      if (issued) {
-        umma_commit(drain);            // nothing of this thread is in flight past here
-        mbar_wait(drain, 0, a.err, 27);
+      for (int ii = max(0, i - a.SB); ii < i; ++ii) mbar_wait(&b_full[ii % a.SB], (ii / a.SB) & 1, a.err, 30);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue ----------------
+    // The whole warp runs the loop, so the descriptors are warp-uniform;
+    // one elected lane (always lane 0) issues the MMAs and their commits.
+    int i = 0, v = 0, jb = 0;   // chunks, units and B stages so far
+    bool ok = true, issued = false;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x, ++v) {
+      const Unit w = unit_of(a, u);
+      const int buf = v & 1;
+      if (v >= 2 && !warp_wait(&tm_empty[buf], ((v >> 1) - 1) & 1, a.err, 22)) break;
+      tc_fence_after();
+      const uint32_t idesc = a.cat ? idesc_n(2 * a.NB) : idesc_n(w.ntok);
+      const uint32_t d = taddr + (uint32_t)(buf * (a.cat ? 2 * a.NB : a.NB));
+      int c = 0;   // chunks of this unit so far (run order)
+      for (int q = 0; q < w.nst && ok; ++q) {
+       const int cn = min(kRawCh, w.nk - stage_c0(w, q));
+       for (int cc = 0; cc < cn; ++cc, ++c, ++i) {
+        const int sa = i % a.SA;
+        const bool bfirst = cc % a.bcs == 0, blast = cc % a.bcs == a.bcs - 1 || cc == cn - 1;
+        const int sb = jb % a.SB;
+        if (!warp_wait(&a_full[sa], (i / a.SA) & 1, a.err, 23) ||
+            (bfirst && !warp_wait(&b_full[sb], (jb / a.SB) & 1, a.err, 23))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ab = smem_u32(aring + (size_t)sa * (2 * kAPart));
+        const uint32_t bh0 = smem_u32(bring + (size_t)sb * a.b_bytes) + (uint32_t)(cc % a.bcs) * 256u * a.NB;
+        const uint32_t bl0 = bh0 + (uint32_t)a.NB * 128u;
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ah = sw128_desc(ab + 32 * kk), al = sw128_desc(ab + kAPart + 32 * kk);
+            const uint64_t bh = sw128_desc(bh0 + 32 * kk), bl = sw128_desc(bl0 + 32 * kk);
+            umma_f16(d, ah, bh, idesc, (c > 0 || kk > 0) ? 1u : 0u);   // c counts chunks in run order
+            if (a.cat) {
+              umma_f16(d, al, bh, idesc, 1u);   // bh spans the hi and the lo rows
+            } else {
+              umma_f16(d, ah, bl, idesc, 1u);
+              umma_f16(d, al, bh, idesc, 1u);
+            }
+          }
+          umma_commit(&a_empty[sa]);   // the chunk's operands may be refilled once read
+          if (blast) umma_commit(&b_empty[sb]);
+        }
+        __syncwarp();
+        issued = true;
+        if (blast) ++jb;
+       }
       }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&tm_full[buf]);   // this unit's accumulator is final
+      __syncwarp();
+    }
+    if (issued) {
+      if (elect_one()) umma_commit(drain);   // nothing of this warp is in flight past here
+      __syncwarp();
+      mbar_wait(drain, 0, a.err, 27);
     }
   } else if (warp < kEp0) {
     // ---------------- dequantisation: group g takes the chunks i with i % 2 == g ----------------
     const int g = (warp - kDq0) / kDqWarps;
     const int tid = (int)threadIdx.x - 32 * (kDq0 + g * kDqWarps);   // 0..255
     const int r = tid & (kWR - 1), h = tid >> 7;   // weight row in the tile, block of the chunk
-    const bool leader = tid == 0;
-    if (leader) pdl_wait();                // the B parts come from the prep kernel
-    int i = 0, j = 0, last_s = -1, last_i = 0;
+    int i = 0, j = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
       const Unit w = unit_of(a, u);
       const bool valid = w.n0 + r < a.N;
       const float ws = valid ? a.rws[w.n0 + r] : 1.0f;
-      for (int c0 = 0; c0 < w.nk; c0 += kRawCh, ++j) {
+      for (int q = 0; q < w.nst; ++q, ++j) {
         const int slot = j % a.R;
         if (!warp_wait(&raw_full[slot], (j / a.R) & 1, a.err, 24)) {
           ok = false;
@@ -469,25 +554,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
         }
         const uint8_t* rq = raws + (size_t)slot * a.raw_bytes;
         const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + 16384 * (QB / 16));
-        const int cn = min(kRawCh, w.nk - c0);
+        const int cn = min(kRawCh, w.nk - stage_c0(w, q));
         for (int c = 0; c < cn; ++c, ++i) {
           if ((i & 1) != g) continue;
-          const int s = i % a.S;
-          if (i >= a.S && !warp_wait(&op_empty[s], ((i / a.S) - 1) & 1, a.err, 25)) {
+          const int s = i % a.SA;
+          if (i >= a.SA && !warp_wait(&a_empty[s], ((i / a.SA) - 1) & 1, a.err, 25)) {
             ok = false;
             break;
           }
-          uint8_t* st = ops + (size_t)s * a.op_bytes;
-          if (leader) {
-            const uint32_t bbytes = (uint32_t)w.ntok * 128u;
-            const size_t part = (size_t)a.NB * 128;
-            const uint8_t* src = a.xa + ((size_t)w.mt * a.nkc + w.kc0 + c0 + c) * 2 * part;
-            mbar_arrive_expect_tx(&op_full[s], 2 * bbytes);
-            bulk_g2s(st + 2 * kAPart, src, bbytes, &op_full[s]);
-            bulk_g2s(st + 2 * kAPart + part, src + part, bbytes, &op_full[s]);
-            last_s = s;
-            last_i = i;
-          }
+          uint8_t* st = aring + (size_t)s * (2 * kAPart);
           uint32_t hi[16], lo[16];
           if (valid) {
             const int blk = 2 * c + h;    // block of the raw stage, 0..7
@@ -512,19 +587,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
           __syncwarp();
-          if (lane == 0) mbar_arrive(&op_full[s]);
+          if (lane == 0) mbar_arrive(&a_full[s]);
         }
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[slot]);
       }
     }
-    // after a failed wait, the last B copies land before the CTA leaves (on
-    // success the MMAs have read every chunk)
-    if (!ok && last_s >= 0) mbar_wait(&op_full[last_s], (last_i / a.S) & 1, a.err, 29);
   } else {
     // ---------------- epilogue: warp q reads TMEM lanes 32q..32q+31 ----------------
-    pdl_wait();   // Y, the partials, the counters and the scales: after the previous kernels
+    pdl_wait();   // Y and the partials: after the previous kernels
     const int q = warp & 3;
     const int r = 32 * q + lane;
     int v = 0;
@@ -538,56 +610,23 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       const float inv_ws = vn ? 1.0f / a.rws[n] : 0.0f;   // exact: power of two
       const int m0 = w.mt * kTok;
       const int mend = min(a.M, m0 + w.ntok);
-      const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.NB);
+      const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * (a.cat ? 2 * a.NB : a.NB));
+      // a whole tile goes to Y; a K slice to its partial plane (added by
+      // the slice-sum kernel)
       float* dst = w.ns == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
       for (int c0 = 0; c0 < w.ntok; c0 += 16) {
         float vv[16];
         tmem_ld16(tcol + (uint32_t)c0, vv);
+        if (a.cat) {
+          float vl[16];
+          tmem_ld16(tcol + (uint32_t)(a.NB + c0), vl);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) vv[e] = __fadd_rn(vv[e], vl[e]);
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int m = m0 + c0 + e;
           if (vn && m < mend) dst[(size_t)m * a.N + n] = __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws);
-        }
-      }
-      if (w.ns > 1) {
-        // the warp that stores the last K slice of its 32 rows adds the
-        // slices in slice order, two slices x 16 tokens of L2 loads in
-        // flight at a time
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&a.cnt[4 * w.tile + q], 1) == w.ns - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last && vn) {
-          __threadfence();
-          for (int c0 = 0; c0 < w.ntok; c0 += 16) {
-            float acc[16];
-            for (int s0 = 0; s0 < w.ns; s0 += 2) {
-              float t[2][16];
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                  const int m = m0 + c0 + e;
-                  t[k][e] = (s0 + k < w.ns && m < mend)
-                                ? __ldcg(a.part + ((size_t)(s0 + k) * a.M + m) * a.N + n)
-                                : 0.0f;
-                }
-              }
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                if (s0 + k < w.ns) {
-#pragma unroll
-                  for (int e = 0; e < 16; ++e) acc[e] = s0 + k == 0 ? t[k][e] : __fadd_rn(acc[e], t[k][e]);
-                }
-              }
-            }
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int m = m0 + c0 + e;
-              if (m < mend) a.y[(size_t)m * a.N + n] = acc[e];
-            }
-          }
         }
       }
       tc_fence_before();
@@ -600,6 +639,26 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(taddr, a.tcols);
+  }
+}
+
+// The K slices of the tiles past `full`, added in slice order.
+__global__ void __launch_bounds__(256) gemm_slice_sum_kernel(const float* __restrict__ part, int splits, int M,
+                                                             int N, int NB, int full, int ntiles, int rem,
+                                                             float* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t per = (size_t)NB * kWR;   // tokens x columns of one tile
+  const size_t total = (size_t)rem * per;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = full + (int)(i / per);
+    const int wi = (int)(i % per);
+    const int m = (t / ntiles) * kTok + wi / kWR;
+    const int n = (t % ntiles) * kWR + wi % kWR;
+    if (m >= M || n >= N) continue;
+    float acc = part[(size_t)m * N + n];
+    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[((size_t)s * M + m) * N + n]);
+    y[(size_t)m * N + n] = acc;
   }
 }
 
@@ -630,9 +689,9 @@ extern "C" int tosk_qmat_row_scales(tosk_qmat_t* m, cudaStream_t st) {
 
 namespace {
 struct GemmPlan {
-  int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, S, R, full;
-  uint32_t op_bytes, raw_bytes, tcols;
-  size_t off_xs, off_cnt, off_part, bytes, smem;
+  int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, SA, SB, R, full, bcs, cat;
+  uint32_t b_bytes, raw_bytes, tcols;
+  size_t off_xs, off_part, bytes, smem;
 };
 
 size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -642,8 +701,8 @@ size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
 // SMs) are cut into K slices so that they spread over the grid.  The slice
 // count trades idle SMs in that last round against the slices' reduction.
 // A chunk costs the slowest of its weight bytes at the per-SM share of HBM
-// bandwidth, its three MMAs and its dequantisation; a reduction costs about
-// one L2 round trip per two slices and 16 tokens (estimates in ns).
+// bandwidth, its MMAs' tensor time, their issue and its dequantisation; the
+// slice sum costs a launch and its traffic (estimates in ns).
 // Deterministic in (M, N, K, qb) on a given device.
 GemmPlan gemm_plan(int M, int N, int K, int qb) {
   GemmPlan p = {};
@@ -652,20 +711,29 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   p.ntiles = (N + kWR - 1) / kWR;
   p.nkc = K / kBK;
   p.raw_bytes = (uint32_t)(16384 * (qb / 16) + 2048);   // quant box(es), then the scale box
-  p.op_bytes = (uint32_t)(2 * kAPart + 2 * p.NB * 128);
-  p.S = p.NB <= 64 ? 3 : 2;
+  p.bcs = p.NB <= 32 ? kRawCh : 1;
+  p.b_bytes = (uint32_t)(2 * p.NB * 128 * p.bcs);
+  p.SA = p.NB <= 32 ? 2 : p.NB <= 64 ? 3 : 2;
+  p.SB = p.NB <= 32 ? 4 : p.NB >= 96 ? 3 : 4;
   const size_t avail = (size_t)kMaxSmem - kHdrBytes - 1024;
-  p.R = (int)min((size_t)kMaxR, (avail - (size_t)p.S * p.op_bytes) / p.raw_bytes);
+  for (;; --p.SB) {
+    const size_t used = (size_t)p.SA * 2 * kAPart + (size_t)p.SB * p.b_bytes;
+    p.R = used < avail ? (int)min((size_t)kMaxR, (avail - used) / p.raw_bytes) : 0;
+    if (p.R >= 2 || p.SB == 2) break;
+  }
+  p.cat = p.NB <= 64 ? 1 : 0;
   p.tcols = 32;
-  while (p.tcols < (uint32_t)(2 * p.NB)) p.tcols <<= 1;
-  p.smem = (size_t)kHdrBytes + 1024 + (size_t)p.S * p.op_bytes + (size_t)p.R * p.raw_bytes;
+  while (p.tcols < (uint32_t)(2 * p.NB * (p.cat ? 2 : 1))) p.tcols <<= 1;
+  p.smem = (size_t)kHdrBytes + 1024 + (size_t)p.SA * 2 * kAPart + (size_t)p.SB * p.b_bytes +
+           (size_t)p.R * p.raw_bytes;
 
   const int tiles = p.mtiles * p.ntiles;
   const int sms = tosk_num_sms();
   const double t_mem = 256.0 * (qb + 2) / (6500.0 / sms);
   const double t_mma = 3.0 * kWR * p.NB * kBK / 5600.0;
   const double t_dq = qb == 16 ? 95.0 : 250.0;
-  const double tc = fmax(t_mem, fmax(t_mma, t_dq));
+  const double t_issue = (p.cat ? 8 : 12) * 44.0;   // one tcgen05.mma issued every ~85 cycles (measured)
+  const double tc = fmax(fmax(t_mem, t_issue), fmax(t_mma, t_dq));
   const int rounds = tiles / sms;
   const int rem = tiles - rounds * sms;
   p.full = rounds * sms;
@@ -677,7 +745,7 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
       const int splits = (p.nkc + kcps - 1) / kcps;
       if (splits > 64) continue;
       const int last = (rem * splits + sms - 1) / sms;
-      const double red = splits > 1 ? ((p.NB + 15) / 16) * ((splits + 1) / 2) * 700.0 : 0.0;
+      const double red = splits > 1 ? 2500.0 + (splits + 1.0) * rem * p.NB * kWR * 4.0 / 6500.0 : 0.0;
       const double t = last * (min(kcps, p.nkc) * tc + 200.0) + red;
       if (t < best * 0.999) {
         best = t;
@@ -690,16 +758,15 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   p.grid = min(sms, p.units);
   const size_t part = (size_t)p.NB * 128;
   p.off_xs = up256((size_t)p.mtiles * p.nkc * 2 * part);
-  p.off_cnt = up256(p.off_xs + (size_t)p.mtiles * p.NB * 4);
-  p.off_part = up256(p.off_cnt + (size_t)tiles * 4 * 4);
+  p.off_part = up256(p.off_xs + (size_t)p.mtiles * p.NB * 4);
   p.bytes = p.off_part + (p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0);
   return p;
 }
 
 template <typename Kern>
-int launch_ex(Kern kern, int grid, int threads, size_t smem, int pdl, cudaStream_t st, void** args) {
+int launch_ex(Kern kern, dim3 grid, int threads, size_t smem, int pdl, cudaStream_t st, void** args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -751,12 +818,13 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
   uint8_t* xa = (uint8_t*)ws;
   float* xs = (float*)((uint8_t*)ws + p.off_xs);
-  int* cnt = (int*)((uint8_t*)ws + p.off_cnt);
   float* part = (float*)((uint8_t*)ws + p.off_part);
   {
-    int Mi = M, Ki = K, NBi = p.NB, perm = w->qb == 16 ? 1 : 0, ncnt = p.mtiles * p.ntiles * 4;
-    void* args[] = {(void*)&x, &Mi, &Ki, &NBi, &perm, &xa, &xs, &cnt, &ncnt};
-    const int e = launch_ex(gemm_prep_kernel, p.mtiles * p.NB, 128, 0, pdl, st, args);
+    int Mi = M, Ki = K, NBi = p.NB, perm = w->qb == 16 ? 1 : 0;
+    void* args[] = {(void*)&x, &Mi, &Ki, &NBi, &perm, &xa, &xs};
+    const int rows = p.mtiles * p.NB;
+    const int kparts = max(1, min(K / 8 / 128, (4 * tosk_num_sms() + rows - 1) / rows));
+    const int e = launch_ex(gemm_prep_kernel, dim3(rows, kparts), 128, 0, pdl, st, args);
     if (e) return e;
   }
   GemmArgs a = {};
@@ -789,7 +857,6 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   a.xs = xs;
   a.y = y;
   a.part = part;
-  a.cnt = cnt;
   a.M = M;
   a.NB = p.NB;
   a.mtiles = p.mtiles;
@@ -798,9 +865,12 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   a.kcps = p.kcps;
   a.units = p.units;
   a.full = p.full;
-  a.S = p.S;
+  a.SA = p.SA;
+  a.SB = p.SB;
+  a.bcs = p.bcs;
+  a.cat = p.cat;
   a.R = p.R;
-  a.op_bytes = p.op_bytes;
+  a.b_bytes = p.b_bytes;
   a.raw_bytes = p.raw_bytes;
   a.tcols = p.tcols;
   a.err = err;
@@ -814,6 +884,13 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
     attr_done[qi] = true;
   }
   void* gargs[] = {&a};
-  return qi == 0 ? launch_ex(gemm_tc_kernel<16>, p.grid, kGThreads, p.smem, pdl, st, gargs)
-                 : launch_ex(gemm_tc_kernel<32>, p.grid, kGThreads, p.smem, pdl, st, gargs);
+  const int e = qi == 0 ? launch_ex(gemm_tc_kernel<16>, p.grid, kGThreads, p.smem, pdl, st, gargs)
+                        : launch_ex(gemm_tc_kernel<32>, p.grid, kGThreads, p.smem, pdl, st, gargs);
+  const int tiles = p.mtiles * p.ntiles;
+  if (e || p.splits == 1 || tiles == p.full) return e;
+  int sp = p.splits, Mi = M, Ni = N, NBi = p.NB, full = p.full, nti = p.ntiles, rem = tiles - p.full;
+  void* rargs[] = {&part, &sp, &Mi, &Ni, &NBi, &full, &nti, &rem, &y};
+  const size_t total = (size_t)rem * p.NB * kWR;
+  const int rgrid = (int)min((size_t)tosk_num_sms() * 8, (total + 255) / 256);
+  return launch_ex(gemm_slice_sum_kernel, rgrid, 256, 0, pdl, st, rargs);
 }

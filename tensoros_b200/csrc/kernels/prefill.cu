@@ -3,7 +3,9 @@
 // row-wise work between them for n tokens at positions pos0 .. pos0+n-1.
 // Reference: llm_forward_token per token (runtime/nn/llm.c:641-743).
 //   pf_embed_kernel      llm_embed (llm.c:365-410), one CTA per token
-//   pf_rmsnorm_kernel    llm_rmsnorm (llm.c:416-452) in the reference's order
+//   pf_rmsnorm_kernel    llm_rmsnorm (llm.c:416-452) with a fixed-order tree
+//                        sum of squares (FAST numerics: the GEMMs it feeds
+//                        are not bit-exact either)
 //   pf_rope_store_kernel RoPE of q and k (llm.c:460-500, table of the decode
 //                        path) and the K/V cache store (llm.c:673-681)
 //   pf_attention_kernel  causal single-query attention of every token over
@@ -47,32 +49,32 @@ __global__ void pf_embed_kernel(float* __restrict__ x, const uint8_t* __restrict
 
 // The reference's order: four serial lane sums over i = 0, 4, 8, ..., then
 // ((f0+f1)+f2)+f3 and the scalar tail; ss = 1/sqrt(ss/dim + eps); (x*ss)*w.
-__global__ void pf_rmsnorm_kernel(float* __restrict__ y, const float* __restrict__ x, const float* __restrict__ w,
-                                  int dim, float eps) {
-  __shared__ float lanes[4];
+// One CTA (256 threads) per row: strided per-thread sums of squares, warp
+// butterflies, then the eight warp sums in warp order (deterministic).
+__global__ void __launch_bounds__(256) pf_rmsnorm_kernel(float* __restrict__ y, const float* __restrict__ x,
+                                                         const float* __restrict__ w, int dim, float eps) {
+  __shared__ float wsum[8];
   __shared__ float s_ss;
   pdl_wait();
   pdl_trigger();
   const float* xr = x + (size_t)blockIdx.x * dim;
   float* yr = y + (size_t)blockIdx.x * dim;
-  if (threadIdx.x < 4) {
-    float acc = 0.0f;
-    for (int i0 = 0; i0 + 4 <= dim; i0 += 4) {
-      const float v = xr[i0 + threadIdx.x];
-      acc = __fadd_rn(acc, __fmul_rn(v, v));
-    }
-    lanes[threadIdx.x] = acc;
-  }
+  float acc = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) acc = fmaf(xr[i], xr[i], acc);
+  for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float ss = __fadd_rn(__fadd_rn(__fadd_rn(lanes[0], lanes[1]), lanes[2]), lanes[3]);
-    for (int i = dim & ~3; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    float ss = wsum[0];
+    for (int i = 1; i < 8; ++i) ss = __fadd_rn(ss, wsum[i]);
     s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
   }
   __syncthreads();
   const float ss = s_ss;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], ss), w[i]);
 }
+
+constexpr int kRopeRows = 1024;   // rows of one token per CTA
 
 // qkv rows [q_rows | kv_rows | kv_rows] per token; q (roped) -> q_out,
 // k (roped) and v -> the caches at position pos0 + t.
@@ -94,7 +96,8 @@ __global__ void pf_rope_store_kernel(const float* __restrict__ qkv, int q_rows, 
   }
   const int nrow = q_rows + 2 * kv_rows;
   const float* row = qkv + (size_t)t * nrow;
-  for (int r = threadIdx.x; r < nrow; r += blockDim.x) {
+  const int rend = min(nrow, (int)(blockIdx.y + 1) * kRopeRows);   // grid.y splits a token's rows
+  for (int r = blockIdx.y * kRopeRows + threadIdx.x; r < rend; r += blockDim.x) {
     const float y = row[r];
     float v = y;
     if (r < q_rows + kv_rows) {
@@ -239,7 +242,8 @@ extern "C" int tosk_pf_rope_store(const float* qkv, int q_rows, int kv_rows, int
   size_t cstride = 0;
   void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type,
                   (void*)&pos_arr, (void*)&slot, &cstride};
-  return launch_pf((const void*)pf_rope_store_kernel, dim3(n), dim3(256), 0, args, st);
+  return launch_pf((const void*)pf_rope_store_kernel, dim3(n, (q_rows + 2 * kv_rows + kRopeRows - 1) / kRopeRows),
+                   dim3(256), 0, args, st);
 }
 
 extern "C" int tosk_bd_rope_store(const float* qkv, int q_rows, int kv_rows, int hd, const float2* cs,
@@ -249,7 +253,8 @@ extern "C" int tosk_bd_rope_store(const float* qkv, int q_rows, int kv_rows, int
   int pos0 = 0;
   void* args[] = {(void*)&qkv, &q_rows, &kv_rows, &hd, (void*)&cs, &pos0, &q_out, &kc, &vc, &kv_type,
                   (void*)&pos, (void*)&slot, &cstride};
-  return launch_pf((const void*)pf_rope_store_kernel, dim3(n), dim3(256), 0, args, st);
+  return launch_pf((const void*)pf_rope_store_kernel, dim3(n, (q_rows + 2 * kv_rows + kRopeRows - 1) / kRopeRows),
+                   dim3(256), 0, args, st);
 }
 
 extern "C" int tosk_pf_attention(const float* q, const void* kc, const void* vc, int kv_type, int n_heads, int n_kv,
