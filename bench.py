@@ -553,6 +553,8 @@ def main():
     ap.add_argument("--gemv-copies", type=int, default=32)
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the prefill tensor-core GEMM (128x22016x4096 Q4_0) and print it")
+    ap.add_argument("--gemm-m", type=int, default=128,
+                    help="--gemm-only: token rows of the gate|up GEMM (16 = a batch-16 decode step)")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.gemv_only:
@@ -563,9 +565,10 @@ def main():
         torch.cuda.set_device(local)
         lib = _lib()
         assert lib.tos_init(local) == 0, "tos_init failed"
-        us, flops = gemm_roofline(lib, torch)
-        print(json.dumps({"kernel": "gemm_tc Q4_0 128x22016x4096", "launch_us": us,
-                          "TFLOP/s": flops / (us * 1e-6) / 1e12}), flush=True)
+        us, flops = gemm_roofline(lib, torch, m=args.gemm_m)
+        print(json.dumps({"kernel": f"gemm_tc Q4_0 {args.gemm_m}x22016x4096", "launch_us": us,
+                          "TFLOP/s": flops / (us * 1e-6) / 1e12,
+                          "weight_GB/s": 22016 * 4096 // 32 * 18 / (us * 1e-6) / 1e9}), flush=True)
     elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
