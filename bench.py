@@ -75,19 +75,27 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        # nvidia-smi numbers GPUs physically; CUDA_VISIBLE_DEVICES may remap
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        self.gpu = vis[gpu_index] if gpu_index < len(vis) else str(gpu_index)
         self.proc = None
         self.lines = []
+        self.start = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # the sampler is running (first line out) before the region starts
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.start = len(self.lines)
         return self
 
     def _read(self):
@@ -96,6 +104,11 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
+            # a region shorter than the 200 ms interval still gets the sample
+            # that closes it
+            t0 = time.time()
+            while len(self.lines) <= self.start and time.time() - t0 < 1.0 and self.proc.poll() is None:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -105,7 +118,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.start:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
