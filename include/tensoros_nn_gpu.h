@@ -107,7 +107,9 @@ int tos_gemv_mode_dev(const tos_weight_t *w, const float *x, const float *norm_w
  * fp16 hi/lo split of the dequantised weights and a 22-bit split of the
  * activations, fp32 accumulation: normwise error ~1e-6 against the fp32
  * GEMV.  in_dim a multiple of 64; ws: tos_gemm_workspace_bytes bytes,
- * 256-byte aligned. */
+ * 256-byte aligned.  tos_gemm_workspace_bytes(m, ...) covers every call with
+ * at most m rows, so one workspace sized for the longest batch serves the
+ * shorter ones.  Results are bit-identical run to run. */
 size_t tos_gemm_workspace_bytes(int m, int out_dim, int in_dim);
 int tos_gemm_dev(const tos_weight_t *w, const float *x, int m, float *y, void *ws, size_t ws_bytes,
                  void *stream);
