@@ -150,11 +150,42 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* qh = q + ((size_t)t * n_heads + h) * hd;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  for (int j = warp; j < n; j += 4) {
-    float acc = 0.0f;
-    for (int d = lane; d < hd; d += 32) acc = fmaf(qh[d], kv_load(kc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), acc);
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) sc[j] = acc * scale;
+  if (kv_type == TOSK_F16 && hd % 32 == 0 && hd <= 256) {
+    // 8 positions per warp step, 4 lanes a position, each lane a contiguous
+    // quarter of the head in 16-byte loads; q from shared memory
+    __shared__ float qsh[256];
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) qsh[d] = qh[d];
+    __syncthreads();
+    const int sub = lane & 3, dpl = hd >> 2;
+    const float* qs = qsh + sub * dpl;
+    for (int j0 = warp * 8; j0 < n; j0 += 32) {
+      const int j = j0 + (lane >> 2);
+      float acc = 0.0f;
+      if (j < n) {
+        const uint4* kr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(kc) +
+                                                         (size_t)j * kv_dim + (size_t)kvh * hd + sub * dpl);
+        for (int v = 0; v < dpl / 8; ++v) {
+          const uint4 w = kr[v];
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ww[e]));
+            acc = fmaf(qs[8 * v + 2 * e], f.x, acc);
+            acc = fmaf(qs[8 * v + 2 * e + 1], f.y, acc);
+          }
+        }
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (sub == 0 && j < n) sc[j] = acc * scale;
+    }
+  } else {
+    for (int j = warp; j < n; j += 4) {
+      float acc = 0.0f;
+      for (int d = lane; d < hd; d += 32) acc = fmaf(qh[d], kv_load(kc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), acc);
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) sc[j] = acc * scale;
+    }
   }
   __syncthreads();
   float m = -INFINITY;
@@ -175,14 +206,20 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
   __syncthreads();
   const float inv = 1.0f / ((red[0] + red[1]) + (red[2] + red[3]) + 1e-10f);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float a0 = 0.0f, a1 = 0.0f;
+    // eight independent chains (eight V rows in flight), added in a fixed order
+    float a[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const size_t col = (size_t)kvh * hd + d;
     int j = 0;
-    for (; j + 2 <= n; j += 2) {
-      a0 = fmaf(sc[j], kv_load(vc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), a0);
-      a1 = fmaf(sc[j + 1], kv_load(vc, kv_type, (size_t)(j + 1) * kv_dim + (size_t)kvh * hd + d), a1);
+    for (; j + 8 <= n; j += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = kv_load(vc, kv_type, (size_t)(j + k) * kv_dim + col);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = fmaf(sc[j + k], v[k], a[k]);
     }
-    if (j < n) a0 = fmaf(sc[j], kv_load(vc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), a0);
-    out[((size_t)t * n_heads + h) * hd + d] = (a0 + a1) * inv;
+    for (; j < n; ++j) a[j & 7] = fmaf(sc[j], kv_load(vc, kv_type, (size_t)j * kv_dim + col), a[j & 7]);
+    const float s = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+    out[((size_t)t * n_heads + h) * hd + d] = s * inv;
   }
 }
 
