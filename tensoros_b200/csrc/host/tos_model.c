@@ -647,16 +647,16 @@ static int pf_chunk(tos_model_t *m, const int *tokens, int n, int pos0)
     if (!e) e = tosk_pf_embed(m->pf_x, m->embd, d->embd_type, dim, m->pf_toks, n, st);
     for (int l = 0; !e && l < d->n_layers; l++) {
         void *kc = (char *)m->kc + kv_layer * l, *vc = (char *)m->vc + kv_layer * l;
-        e = tosk_pf_rmsnorm(m->pf_xn, m->pf_x, m->norms + (size_t)(2 * l) * dim, dim, d->norm_eps, n, st);
-        if (!e) e = tosk_gemm_q(&m->wqkv[l], m->pf_xn, n, m->pf_qkv, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        e = tosk_gemm_q_norm(&m->wqkv[l], m->pf_x, m->norms + (size_t)(2 * l) * dim, d->norm_eps, n, m->pf_qkv,
+                             m->pf_ws, m->pf_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_rope_store(m->pf_qkv, m->q_dim, m->kv_dim, hd, m->rope, pos0, m->pf_q, kc, vc,
                                        d->kv_type, n, st);
         if (!e) e = tosk_pf_attention(m->pf_q, kc, vc, d->kv_type, d->n_heads, d->n_kv_heads, hd, pos0, n,
                                       m->pf_att, st);
         if (!e) e = tosk_gemm_q(&m->wo[l], m->pf_att, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
-        if (!e) e = tosk_pf_rmsnorm(m->pf_xn, m->pf_x, m->norms + (size_t)(2 * l + 1) * dim, dim, d->norm_eps, n, st);
-        if (!e) e = tosk_gemm_q(&m->wgu[l], m->pf_xn, n, m->pf_gu, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_gemm_q_norm(&m->wgu[l], m->pf_x, m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps, n,
+                                     m->pf_gu, m->pf_ws, m->pf_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_swiglu(m->pf_h, m->pf_gu, (size_t)n * ff, st);
         if (!e) e = tosk_gemm_q(&m->wdown[l], m->pf_h, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
@@ -756,22 +756,22 @@ int tos_model_decode_batch(tos_model_t *m, const int *slot, const int *tokens, c
     if (!e) e = tosk_pf_embed(m->bd_x, m->embd, d->embd_type, dim, m->bd_io, n, st);
     for (int l = 0; !e && l < d->n_layers; l++) {
         void *kc = (char *)m->bd_kc + kv_layer * l, *vc = (char *)m->bd_vc + kv_layer * l;
-        e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)(2 * l) * dim, dim, d->norm_eps, n, st);
-        if (!e) e = tosk_gemm_q(&m->wqkv[l], m->bd_xn, n, m->bd_qkv, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        e = tosk_gemm_q_norm(&m->wqkv[l], m->bd_x, m->norms + (size_t)(2 * l) * dim, d->norm_eps, n, m->bd_qkv,
+                             m->bd_ws, m->bd_ws_bytes, err, 1, st);
         if (!e) e = tosk_bd_rope_store(m->bd_qkv, m->q_dim, m->kv_dim, hd, m->rope, m->bd_io + C, m->bd_io + 3 * C,
                                        m->bd_q, kc, vc, cstride, d->kv_type, n, st);
         if (!e) e = tosk_bd_attention(m->bd_q, kc, vc, cstride, d->kv_type, d->n_heads, d->n_kv_heads, hd,
                                       m->bd_io + C, m->bd_io + 3 * C, d->max_seq, n, m->bd_att, st);
         if (!e) e = tosk_gemm_q(&m->wo[l], m->bd_att, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
-        if (!e) e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)(2 * l + 1) * dim, dim, d->norm_eps, n, st);
-        if (!e) e = tosk_gemm_q(&m->wgu[l], m->bd_xn, n, m->bd_gu, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_gemm_q_norm(&m->wgu[l], m->bd_x, m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps, n,
+                                     m->bd_gu, m->bd_ws, m->bd_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_swiglu(m->bd_h, m->bd_gu, (size_t)n * ff, st);
         if (!e) e = tosk_gemm_q(&m->wdown[l], m->bd_h, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
         if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
     }
-    if (!e) e = tosk_pf_rmsnorm(m->bd_xn, m->bd_x, m->norms + (size_t)2 * d->n_layers * dim, dim, d->norm_eps, n, st);
-    if (!e) e = tosk_gemm_q(&m->lm, m->bd_xn, n, m->bd_logits, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+    if (!e) e = tosk_gemm_q_norm(&m->lm, m->bd_x, m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps, n,
+                                 m->bd_logits, m->bd_ws, m->bd_ws_bytes, err, 1, st);
     if (!e) e = tosk_argmax_rows(m->bd_logits, d->vocab_size, n, m->bd_io + 2 * C, st);
     if (!e) e = cudaMemcpyAsync(m->bd_host + 2 * C, m->bd_io + 2 * C, (size_t)n * sizeof(int),
                                 cudaMemcpyDeviceToHost, st);

@@ -108,6 +108,11 @@ int tosk_pf_swiglu(float *h, const float *gu, size_t n, cudaStream_t st);
 int tosk_qmat_row_scales(tosk_qmat_t *m, cudaStream_t st);
 int tosk_gemm_q(const tosk_qmat_t *w, const float *x, int M, float *y, void *ws, size_t ws_bytes,
                 int *err, int pdl, cudaStream_t st);
+/* the same with each row of x RMS-normalised by norm_w first (llm_rmsnorm,
+ * llm.c:416-452, tree sum of squares): the norm runs inside the GEMM's
+ * activation prep */
+int tosk_gemm_q_norm(const tosk_qmat_t *w, const float *x, const float *norm_w, float eps, int M, float *y,
+                     void *ws, size_t ws_bytes, int *err, int pdl, cudaStream_t st);
 
 /* per-block exact partials: blocks in GGUF layout, n_blocks consecutive,
  * x of length 32*n_blocks, out[n_blocks] (q4_0_dot32 / q8_0_dot32) */

@@ -249,12 +249,17 @@ __device__ __forceinline__ int stage_c0(const Unit& w, int q) {
 // NB rows (rows beyond M are zero).  perm: the Q4_0 K order (word e of a
 // 16-byte group = elements e and e + 4 of its eight) instead of the natural
 // one.  Grid: (prepared row, part of K); every CTA of a row finds the row's
-// maximum, then converts its part.
+// maximum, then converts its part.  nw non-null: the row is first RMS-
+// normalised as llm_rmsnorm does (llm.c:416-452: ss = 1/sqrt(sum x^2 / K +
+// eps), then (x ss) w) with a fixed-order tree sum of squares, so the norm
+// feeding a GEMM needs no launch of its own.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict__ x, int M, int K, int NB,
                                                         int perm, uint8_t* __restrict__ xa,
-                                                        float* __restrict__ xs) {
+                                                        float* __restrict__ xs, const float* __restrict__ nw,
+                                                        float eps) {
   __shared__ float red[4];
+  __shared__ float s_ss;
   pdl_wait();
   pdl_trigger();
   const int p = blockIdx.x;            // prepared row
@@ -263,9 +268,26 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
   const int nkc = K / kBK;
   const bool valid = m < M;
   const float* xr = x + (size_t)m * K;
+  float ss = 1.0f;
+  if (nw) {
+    float acc = 0.0f;
+    if (valid)
+      for (int i = threadIdx.x; i < K; i += blockDim.x) acc = fmaf(xr[i], xr[i], acc);
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float t = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
+      s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
+    }
+    __syncthreads();
+    ss = s_ss;
+  }
+  // element i of the (normalised) row
+  auto val = [&](int i) { return nw ? __fmul_rn(__fmul_rn(xr[i], ss), nw[i]) : xr[i]; };
   float mx = 0.0f;
   if (valid)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(xr[i]));
+    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(val(i)));
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
@@ -282,8 +304,8 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i0 = perm ? e : 2 * e, i1 = perm ? e + 4 : 2 * e + 1;
-      const float v0 = valid ? __fmul_rn(xr[8 * q + i0], s) : 0.0f;
-      const float v1 = valid ? __fmul_rn(xr[8 * q + i1], s) : 0.0f;
+      const float v0 = valid ? __fmul_rn(val(8 * q + i0), s) : 0.0f;
+      const float v1 = valid ? __fmul_rn(val(8 * q + i1), s) : 0.0f;
       split2(v0, v1, hi[e], lo[e]);
     }
     uint8_t* blk = xa + ((size_t)mt * nkc + kc) * 2 * part;
@@ -809,8 +831,9 @@ extern "C" size_t tosk_gemm_ws_bytes(int M, int N, int K) {
   return best;
 }
 
-extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y, void* ws, size_t ws_bytes,
-                           int* err, int pdl, cudaStream_t st) {
+namespace {
+int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int M, float* y, void* ws,
+           size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
   if (!w || !x || !y || !ws || M <= 0 || (w->qb != 16 && w->qb != 32)) return (int)cudaErrorInvalidValue;
   const int N = w->rows, K = w->cols;
   if (K % kBK || (reinterpret_cast<uintptr_t>(ws) & 255)) return (int)cudaErrorInvalidValue;
@@ -821,7 +844,8 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   float* part = (float*)((uint8_t*)ws + p.off_part);
   {
     int Mi = M, Ki = K, NBi = p.NB, perm = w->qb == 16 ? 1 : 0;
-    void* args[] = {(void*)&x, &Mi, &Ki, &NBi, &perm, &xa, &xs};
+    float epsv = eps;
+    void* args[] = {(void*)&x, &Mi, &Ki, &NBi, &perm, &xa, &xs, (void*)&nw, &epsv};
     const int rows = p.mtiles * p.NB;
     const int kparts = max(1, min(K / 8 / 128, (4 * tosk_num_sms() + rows - 1) / rows));
     const int e = launch_ex(gemm_prep_kernel, dim3(rows, kparts), 128, 0, pdl, st, args);
@@ -893,4 +917,16 @@ extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y
   const size_t total = (size_t)rem * p.NB * kWR;
   const int rgrid = (int)min((size_t)tosk_num_sms() * 8, (total + 255) / 256);
   return launch_ex(gemm_slice_sum_kernel, rgrid, 256, 0, pdl, st, rargs);
+}
+}  // namespace
+
+extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y, void* ws, size_t ws_bytes,
+                           int* err, int pdl, cudaStream_t st) {
+  return gemm_q(w, x, nullptr, 0.0f, M, y, ws, ws_bytes, err, pdl, st);
+}
+
+extern "C" int tosk_gemm_q_norm(const tosk_qmat_t* w, const float* x, const float* norm_w, float eps, int M,
+                                float* y, void* ws, size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
+  if (!norm_w) return (int)cudaErrorInvalidValue;
+  return gemm_q(w, x, norm_w, eps, M, y, ws, ws_bytes, err, pdl, st);
 }
