@@ -62,7 +62,7 @@ struct tos_model {
     /* batched prompt pass (allocated on first use): up to pf_cap tokens */
     int pf_cap;
     int *pf_toks;
-    float *pf_x, *pf_xn, *pf_qkv, *pf_q, *pf_att, *pf_gu, *pf_h, *pf_tmp;
+    float *pf_x, *pf_qkv, *pf_q, *pf_att, *pf_gu, *pf_h, *pf_tmp;
     void *pf_ws;
     size_t pf_ws_bytes;
     /* batched decode (allocated on first use): up to bd_cap sequences, each
@@ -71,7 +71,7 @@ struct tos_model {
     void *bd_kc, *bd_vc;
     int *bd_io;               /* device: tokens[cap], positions[cap], next[cap], slots[cap] */
     int *bd_host;             /* pinned mirror */
-    float *bd_x, *bd_xn, *bd_qkv, *bd_q, *bd_att, *bd_gu, *bd_h, *bd_tmp, *bd_logits;
+    float *bd_x, *bd_qkv, *bd_q, *bd_att, *bd_gu, *bd_h, *bd_tmp, *bd_logits;
     void *bd_ws;
     size_t bd_ws_bytes;
 };
@@ -141,8 +141,8 @@ void tos_model_destroy(tos_model_t *m)
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
                     m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
-                    m->pf_toks, m->pf_x, m->pf_xn, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
-                    m->pf_tmp, m->pf_ws, m->bd_kc, m->bd_vc, m->bd_io, m->bd_x, m->bd_xn, m->bd_qkv,
+                    m->pf_toks, m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
+                    m->pf_tmp, m->pf_ws, m->bd_kc, m->bd_vc, m->bd_io, m->bd_x, m->bd_qkv,
                     m->bd_q, m->bd_att, m->bd_gu, m->bd_h, m->bd_tmp, m->bd_logits, m->bd_ws};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
@@ -613,7 +613,6 @@ static int pf_alloc(tos_model_t *m)
     const int nqkv = m->q_dim + 2 * m->kv_dim;
     int e = dmalloc(m, (void **)&m->pf_toks, (size_t)C * sizeof(int));
     if (!e) e = dmalloc(m, (void **)&m->pf_x, (size_t)C * dim * 4);
-    if (!e) e = dmalloc(m, (void **)&m->pf_xn, (size_t)C * dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_qkv, (size_t)C * nqkv * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_q, (size_t)C * m->q_dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_att, (size_t)C * m->q_dim * 4);
@@ -704,7 +703,6 @@ static int bd_alloc(tos_model_t *m)
     if (!e) e = dmalloc(m, (void **)&m->bd_io, (size_t)4 * C * sizeof(int));
     if (!e) e = cudaMallocHost((void **)&m->bd_host, (size_t)4 * C * sizeof(int));
     if (!e) e = dmalloc(m, (void **)&m->bd_x, (size_t)C * dim * 4);
-    if (!e) e = dmalloc(m, (void **)&m->bd_xn, (size_t)C * dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_qkv, (size_t)C * nqkv * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_q, (size_t)C * m->q_dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_att, (size_t)C * m->q_dim * 4);

@@ -89,7 +89,6 @@ int tosk_gemv(const tosk_qmat_t *w, const float *x, const tosk_norm_t *norm,
 size_t tosk_gemm_ws_bytes(int M, int N, int K);
 /* batched prompt pass (prefill.cu): n tokens, row-major [n][...] */
 int tosk_pf_embed(float *x, const void *embd, int type, int dim, const int *toks, int n, cudaStream_t st);
-int tosk_pf_rmsnorm(float *y, const float *x, const float *w, int dim, float eps, int n, cudaStream_t st);
 int tosk_pf_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const float2 *cs, int pos0,
                        float *q_out, void *kc, void *vc, int kv_type, int n, cudaStream_t st);
 int tosk_pf_attention(const float *q, const void *kc, const void *vc, int kv_type, int n_heads, int n_kv,

@@ -1,11 +1,9 @@
 // prefill.cu - per-token kernels of the batched prompt pass (prefill): the
 // projections run as tensor-core GEMMs (gemm_tc.cu); these kernels do the
-// row-wise work between them for n tokens at positions pos0 .. pos0+n-1.
+// row-wise work between them for n tokens at positions pos0 .. pos0+n-1
+// (the RMSNorms run inside the GEMMs' activation prep, gemm_tc.cu).
 // Reference: llm_forward_token per token (runtime/nn/llm.c:641-743).
 //   pf_embed_kernel      llm_embed (llm.c:365-410), one CTA per token
-//   pf_rmsnorm_kernel    llm_rmsnorm (llm.c:416-452) with a fixed-order tree
-//                        sum of squares (FAST numerics: the GEMMs it feeds
-//                        are not bit-exact either)
 //   pf_rope_store_kernel RoPE of q and k (llm.c:460-500, table of the decode
 //                        path) and the K/V cache store (llm.c:673-681)
 //   pf_attention_kernel  causal single-query attention of every token over
@@ -49,31 +47,6 @@ __global__ void pf_embed_kernel(float* __restrict__ x, const uint8_t* __restrict
 
 // The reference's order: four serial lane sums over i = 0, 4, 8, ..., then
 // ((f0+f1)+f2)+f3 and the scalar tail; ss = 1/sqrt(ss/dim + eps); (x*ss)*w.
-// One CTA (256 threads) per row: strided per-thread sums of squares, warp
-// butterflies, then the eight warp sums in warp order (deterministic).
-__global__ void __launch_bounds__(256) pf_rmsnorm_kernel(float* __restrict__ y, const float* __restrict__ x,
-                                                         const float* __restrict__ w, int dim, float eps) {
-  __shared__ float wsum[8];
-  __shared__ float s_ss;
-  pdl_wait();
-  pdl_trigger();
-  const float* xr = x + (size_t)blockIdx.x * dim;
-  float* yr = y + (size_t)blockIdx.x * dim;
-  float acc = 0.0f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) acc = fmaf(xr[i], xr[i], acc);
-  for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-  if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float ss = wsum[0];
-    for (int i = 1; i < 8; ++i) ss = __fadd_rn(ss, wsum[i]);
-    s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
-  }
-  __syncthreads();
-  const float ss = s_ss;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], ss), w[i]);
-}
-
 constexpr int kRopeRows = 1024;   // rows of one token per CTA
 
 // qkv rows [q_rows | kv_rows | kv_rows] per token; q (roped) -> q_out,
@@ -265,11 +238,6 @@ int ew_grid(size_t n) {
 extern "C" int tosk_pf_embed(float* x, const void* embd, int type, int dim, const int* toks, int n, cudaStream_t st) {
   void* args[] = {&x, (void*)&embd, &type, &dim, (void*)&toks};
   return launch_pf((const void*)pf_embed_kernel, dim3(n), dim3(256), 0, args, st);
-}
-
-extern "C" int tosk_pf_rmsnorm(float* y, const float* x, const float* w, int dim, float eps, int n, cudaStream_t st) {
-  void* args[] = {&y, (void*)&x, (void*)&w, &dim, &eps};
-  return launch_pf((const void*)pf_rmsnorm_kernel, dim3(n), dim3(256), 0, args, st);
 }
 
 extern "C" int tosk_pf_rope_store(const float* qkv, int q_rows, int kv_rows, int hd, const float2* cs, int pos0,
