@@ -80,3 +80,14 @@ def test_invalid_arguments_rejected_on_host(lib):
     h = ctypes.c_void_p()
     assert lib.tos_model_create(ctypes.byref(h), None) == -1
     assert lib.tos_attention_workspace_bytes(0, 16) == 0
+
+
+def test_gemm_workspace_covers_shorter_batches(lib):
+    """tos_gemm_workspace_bytes(m, ...) is enough for every call with at
+    most m rows (a caller sizes one workspace for its longest batch); the
+    size is host arithmetic, so this runs without a GPU."""
+    for n, k in ((4096, 4096), (22016, 4096), (4096, 11008), (288, 768), (32000, 4096)):
+        sizes = [lib.tos_gemm_workspace_bytes(m, n, k) for m in range(1, 300)]
+        assert all(s > 0 for s in sizes)
+        assert all(b >= a for a, b in zip(sizes, sizes[1:])), (n, k)
+    assert lib.tos_gemm_workspace_bytes(16, 4096, 4000) == 0   # in_dim not a multiple of 64
