@@ -54,8 +54,8 @@ sys.path.insert(0, str(ROOT))
 GEMV_BYTES_4096 = 4096 * 128 * 18 + 4096 * 4 + 4096 * 4   # 9,469,952 B per launch
 METRIC = "decode tokens/sec (Llama-2-7B-shaped, Q4_0, batch 1)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_step_kernel launch
-# of the 32-layer model (profiles/decode_step_llama2_7b_q4_0.md; context 8: the
-# KV rows of a longer context add 16 KB per position and layer)
+# of the 32-layer model, from a full-size ncu capture at context 8 (the KV rows
+# of a longer context add 16 KB per position and layer)
 STEP_TRAFFIC = 3721760768 + 13937152
 
 
@@ -484,8 +484,8 @@ def run_ours(args, world, rank, local):
                    "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                    "frac": achieved / peak,
                    # dram__bytes_read.sum + dram__bytes_write.sum of one launch
-                   # of this kernel and shape (profiles/gemv_q4_0_fast_4096x4096.md,
-                   # profiles/gemv_q4_0_4096x4096.md for the exact arithmetic)
+                   # of this kernel and shape, from an ncu capture of each
+                   # arithmetic
                    "traffic": 9482496 if args.math == "fast" else 9485568,
                    "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0}
         step_us = t_ms / K * 1000.0

@@ -128,12 +128,13 @@ int tos_axpy_dev(float *dst, float s, const float *src, int n, void *stream);
 int tos_dot_dev(const float *a, const float *b, int n, float *out, void *stream);
 int tos_embed_dev(float *out, const void *embd, int type, int dim, int token, void *stream);
 int tos_argmax_dev(const float *x, int n, int *out_index, void *stream);
+/* llm_sample (llm.c:1177-1246) on device logits; see tos_sample */
+int tos_sample_dev(const float *logits, int n, float temperature, uint32_t entropy, int *out_index,
+                   void *stream);
 /* The distributed argmax of a row-sharded model, on one device: x is cut into
  * `world` equal slices, each slice gives a (value, index) pair and the pairs
  * reduce with llm_argmax's rule (llm.c:1129-1140); same kernels as a sharded
  * model's last step.  No counterpart in the reference. */
-int tos_sample_dev(const float *logits, int n, float temperature, uint32_t entropy, int *out_index,
-                   void *stream);
 int tos_argmax_sharded_dev(const float *x, int n, int world, int *out_index, void *stream);
 
 /* Single-query attention over a KV cache [ctx][n_kv*head_dim] (kv_type F32 or
@@ -155,6 +156,8 @@ int tos_attention_dev(float *out, const float *q, const void *k_cache, const voi
  * call on a device resolves the array's address (make it before any stream
  * capture).  All calls share the array: calls that overlap on the GPU race
  * and must be serialised by the caller.  Nothing needs to start at zero.
+ * A cudaDeviceReset invalidates the resolved address along with every other
+ * device object of the library: call tos_shutdown before a reset.
  * stream: the caller's CUDA stream (NULL = the legacy default stream). */
 int tos_attention_noalloc_dev(float *out, const float *q, const void *k_cache, const void *v_cache,
                               int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,

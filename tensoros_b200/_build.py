@@ -118,15 +118,21 @@ def build_nn(verbose=False, jobs=None) -> Path:
 
 
 def build_oracle(verbose=False, with_reference=None):
-    """Build the CPU checkers under oracle/ (test infrastructure)."""
-    ref = Path(os.environ.get("TOS_REFERENCE_DIR", "/root/reference"))
+    """Build the CPU checkers under oracle/ (test infrastructure).
+
+    The reference's own sources are compiled (oracle/_ref) only when the
+    environment variable TOS_REFERENCE_DIR names a TensorOS source tree."""
+    ref_dir = os.environ.get("TOS_REFERENCE_DIR", "")
+    ref = Path(ref_dir) if ref_dir else None
     targets = ["oracle"]
     if with_reference is None:
-        with_reference = (ref / "runtime" / "nn" / "llm.c").exists()
+        with_reference = ref is not None and (ref / "runtime" / "nn" / "llm.c").exists()
     if with_reference:
+        if ref is None:
+            raise RuntimeError("TOS_REFERENCE_DIR must name the TensorOS source tree")
         targets.append("ref")
     make = shutil.which("make") or "make"
-    _run([make, "-s", "-C", ROOT / "oracle", f"REF={ref}"] + targets, verbose)
+    _run([make, "-s", "-C", ROOT / "oracle"] + ([f"REF={ref}"] if ref else []) + targets, verbose)
 
 
 def build_all(verbose=False):

@@ -157,7 +157,22 @@ static uint64_t type_bytes(uint32_t type, uint64_t n)
     default: return 0;
     }
     if (n % blk) return 0;
+    if (n / blk > UINT64_MAX / bytes) return 0;   /* the byte size would wrap */
     return n / blk * bytes;
+}
+
+/* A mapped tensor has the shape the model reads from it: ne0 x ne1 elements
+ * (GGUF order, ne0 fastest), every further dimension 1, a known type, and
+ * data inside the file (its byte size, from the shape, was range-checked at
+ * open).  Without this a tensor smaller than the header implies would pass
+ * the container check and the model upload would read past it. */
+static int tensor_is(const gtensor_t *t, uint64_t ne0, uint64_t ne1)
+{
+    if (!t->data || t->bytes == 0 || t->dims[0] != ne0) return 0;
+    for (uint32_t d = 1; d < t->n_dims; d++)
+        if (t->dims[d] != (d == 1 ? ne1 : 1)) return 0;
+    if (t->n_dims < 2 && ne1 != 1) return 0;
+    return t->bytes == type_bytes(t->type, ne0 * ne1);
 }
 
 static int gstr_eq(gstr_t s, const char *c)
@@ -415,17 +430,25 @@ int tos_gguf_model_desc(tos_gguf_t *g, tos_model_desc_t *d)
     tos_set_status(TOS_OK);
     if (d->dim <= 0 || d->n_layers <= 0 || d->n_heads <= 0 || d->ff_dim <= 0) return tos_set_status(TOS_EINVAL);
     if (d->n_kv_heads <= 0) d->n_kv_heads = d->n_heads;
+    if (d->dim % d->n_heads || d->n_heads % d->n_kv_heads) return tos_set_status(TOS_EINVAL);
+    /* rows of each projection (llm.c:1541: head_dim = dim / n_heads) */
+    const uint64_t dim = (uint64_t)d->dim, ff = (uint64_t)d->ff_dim;
+    const uint64_t q_rows = dim, kv_rows = (uint64_t)d->n_kv_heads * (dim / (uint64_t)d->n_heads);
 
     int64_t ie = tos_gguf_find_tensor(g, "token_embd.weight");
     int64_t io = tos_gguf_find_tensor(g, "output_norm.weight");
     if (ie < 0 || io < 0 || !g->t[ie].data || !g->t[io].data) return tos_set_status(TOS_EINVAL);
     const gtensor_t *te = &g->t[ie];
-    if (d->vocab_size <= 0) d->vocab_size = te->n_dims >= 2 ? (int)te->dims[1] : 0;
-    if (d->vocab_size <= 0 || te->dims[0] != (uint64_t)d->dim) return tos_set_status(TOS_EINVAL);
+    if (d->vocab_size <= 0) d->vocab_size = te->n_dims >= 2 && te->dims[1] <= INT32_MAX ? (int)te->dims[1] : 0;
+    /* a vocab_size key must match the embedding's rows: the model uploads
+     * vocab_size rows of it */
+    if (d->vocab_size <= 0 || !tensor_is(te, dim, (uint64_t)d->vocab_size)) return tos_set_status(TOS_EINVAL);
+    if (!tensor_is(&g->t[io], dim, 1)) return tos_set_status(TOS_EINVAL);
     d->token_embd = te->data;
     d->embd_type = (int)te->type;
     int64_t ih = tos_gguf_find_tensor(g, "output.weight");
     if (ih >= 0 && g->t[ih].data) {
+        if (!tensor_is(&g->t[ih], dim, (uint64_t)d->vocab_size)) return tos_set_status(TOS_EINVAL);
         d->output_weight = g->t[ih].data;
         d->out_type = (int)g->t[ih].type;
     } else {
@@ -436,6 +459,9 @@ int tos_gguf_model_desc(tos_gguf_t *g, tos_model_desc_t *d)
     static const char *const suffix[9] = {"attn_norm.weight", "ffn_norm.weight", "attn_q.weight",
                                           "attn_k.weight", "attn_v.weight", "attn_output.weight",
                                           "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
+    /* (ne0, ne1) of each: columns read per row, rows */
+    const uint64_t shape[9][2] = {{dim, 1},     {dim, 1},  {dim, q_rows}, {dim, kv_rows}, {dim, kv_rows},
+                                  {q_rows, dim}, {dim, ff}, {dim, ff},     {ff, dim}};
     const int L = d->n_layers;
     free(g->ptrs);
     free(g->norm_f32);
@@ -456,7 +482,7 @@ int tos_gguf_model_desc(tos_gguf_t *g, tos_model_desc_t *d)
                 char name[96];
                 snprintf(name, sizeof(name), "blk.%d.%s", l, suffix[j]);
                 int64_t i = tos_gguf_find_tensor(g, name);
-                if (i < 0 || !g->t[i].data) return tos_set_status(TOS_EINVAL);
+                if (i < 0 || !tensor_is(&g->t[i], shape[j][0], shape[j][1])) return tos_set_status(TOS_EINVAL);
                 tn[j] = &g->t[i];
                 if (pass == 0) continue;
                 if (j < 2 && tn[j]->type != 0) {

@@ -105,7 +105,7 @@ static int upload_qmat(tos_model_t *m, tosk_qmat_t *dst, const void *const *hsrc
 {
     int total = 0;
     for (int i = 0; i < n; i++) total += rows[i];
-    int e = tosk_qmat_alloc(dst, type, total, cols);
+    int e = tosk_qmat_alloc(dst, type, total, cols, m->st);
     if (e) return e;
     m->dev_bytes += dst->bytes;
     const void *dsrc[4];
@@ -199,10 +199,11 @@ static int setup_step(tos_model_t *m)
         hl[l].v_cache = (char *)m->vc + kv_layer * l;
     }
     int e = dmalloc(m, (void **)&m->step_layers, (size_t)L * sizeof(*hl));
-    if (!e) e = cudaMemcpy(m->step_layers, hl, (size_t)L * sizeof(*hl), cudaMemcpyHostToDevice);
+    if (!e) e = cudaMemcpyAsync(m->step_layers, hl, (size_t)L * sizeof(*hl), cudaMemcpyHostToDevice, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);   /* hl is pageable and freed next */
     free(hl);
     if (!e) e = dmalloc(m, (void **)&m->step_sync, tosk_step_sync_bytes());
-    if (!e) e = cudaMemset(m->step_sync, 0, tosk_step_sync_bytes());
+    if (!e) e = cudaMemsetAsync(m->step_sync, 0, tosk_step_sync_bytes(), m->st);
     if (e) return e;
     tosk_step_t *s = &m->step;
     memset(s, 0, sizeof(*s));
@@ -305,22 +306,31 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
 #undef ROWS
     if (stage) cudaFree(stage);
 
+    /* Every device write of the set-up goes on the model's stream, which does
+     * not synchronise with the legacy default stream (cudaStreamNonBlocking):
+     * a plain cudaMemset or a pageable cudaMemcpy there could still be in
+     * flight when the first step runs on m->st, and a late clear of the KV
+     * cache or of io[] would then overwrite what that step wrote.  The host
+     * sources are pageable and stay valid until the final synchronise. */
     size_t eb = embd_row_bytes(dim, d->embd_type) * (size_t)d->vocab_size;
     if (!e) e = dmalloc(m, &m->embd, eb);
-    if (!e) e = cudaMemcpy(m->embd, d->token_embd, eb, cudaMemcpyHostToDevice);
+    if (!e) e = cudaMemcpyAsync(m->embd, d->token_embd, eb, cudaMemcpyHostToDevice, m->st);
     size_t nb = ((size_t)L * 2 + 1) * (size_t)dim * 4;
     if (!e) e = dmalloc(m, (void **)&m->norms, nb);
     for (int l = 0; !e && l < L; l++) {
-        e = cudaMemcpy(m->norms + (size_t)(2 * l) * dim, d->attn_norm[l], (size_t)dim * 4, cudaMemcpyHostToDevice);
-        if (!e) e = cudaMemcpy(m->norms + (size_t)(2 * l + 1) * dim, d->ffn_norm[l], (size_t)dim * 4, cudaMemcpyHostToDevice);
+        e = cudaMemcpyAsync(m->norms + (size_t)(2 * l) * dim, d->attn_norm[l], (size_t)dim * 4,
+                            cudaMemcpyHostToDevice, m->st);
+        if (!e) e = cudaMemcpyAsync(m->norms + (size_t)(2 * l + 1) * dim, d->ffn_norm[l], (size_t)dim * 4,
+                                    cudaMemcpyHostToDevice, m->st);
     }
-    if (!e) e = cudaMemcpy(m->norms + (size_t)2 * L * dim, d->output_norm, (size_t)dim * 4, cudaMemcpyHostToDevice);
+    if (!e) e = cudaMemcpyAsync(m->norms + (size_t)2 * L * dim, d->output_norm, (size_t)dim * 4,
+                                cudaMemcpyHostToDevice, m->st);
 
     size_t kvb = (size_t)L * d->max_seq * m->kv_dim * m->esz;
     if (!e) e = dmalloc(m, &m->kc, kvb);
     if (!e) e = dmalloc(m, &m->vc, kvb);
-    if (!e) e = cudaMemset(m->kc, 0, kvb);
-    if (!e) e = cudaMemset(m->vc, 0, kvb);
+    if (!e) e = cudaMemsetAsync(m->kc, 0, kvb, m->st);
+    if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
     int mx = dim > ff ? dim : ff;
     if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->q, (size_t)mx * 4);
@@ -334,7 +344,7 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
     m->ws_bytes = tosk_attention_ws_bytes(sp.n_heads, d->max_seq);
     if (!e) e = dmalloc(m, &m->ws, m->ws_bytes);
     if (!e) e = dmalloc(m, (void **)&m->io, 8 * sizeof(int));
-    if (!e) e = cudaMemset(m->io, 0, 8 * sizeof(int));
+    if (!e) e = cudaMemsetAsync(m->io, 0, 8 * sizeof(int), m->st);
     if (!e) e = dmalloc(m, (void **)&m->ring, (size_t)d->max_seq * sizeof(int));
     if (!e) e = cudaMallocHost((void **)&m->io_host, 8 * sizeof(int));
     if (!e) e = setup_step(m);
@@ -698,8 +708,8 @@ static int bd_alloc(tos_model_t *m)
     const size_t kvb = (size_t)d->n_layers * C * d->max_seq * m->kv_dim * m->esz;
     int e = dmalloc(m, &m->bd_kc, kvb);
     if (!e) e = dmalloc(m, &m->bd_vc, kvb);
-    if (!e) e = cudaMemset(m->bd_kc, 0, kvb);
-    if (!e) e = cudaMemset(m->bd_vc, 0, kvb);
+    if (!e) e = cudaMemsetAsync(m->bd_kc, 0, kvb, m->st);
+    if (!e) e = cudaMemsetAsync(m->bd_vc, 0, kvb, m->st);
     if (!e) e = dmalloc(m, (void **)&m->bd_io, (size_t)4 * C * sizeof(int));
     if (!e) e = cudaMallocHost((void **)&m->bd_host, (size_t)4 * C * sizeof(int));
     if (!e) e = dmalloc(m, (void **)&m->bd_x, (size_t)C * dim * 4);

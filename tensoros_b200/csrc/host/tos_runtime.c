@@ -81,7 +81,10 @@ int tos_init(int device)
     int e = cudaSetDevice(device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&tos_g.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc((void **)&tos_g.err_dev, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(tos_g.err_dev, 0, sizeof(int));
+    /* the library stream does not synchronise with the legacy default
+     * stream: every device write here goes on it, and is complete on return */
+    if (e == cudaSuccess) e = cudaMemsetAsync(tos_g.err_dev, 0, sizeof(int), tos_g.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(tos_g.stream);
     if (e != cudaSuccess) {
         pthread_mutex_unlock(&g_mu);
         return tos_set_status(tos_from_cuda(e));
@@ -133,9 +136,12 @@ int tos_synchronize(void)
 int tos_check_device_error(void)
 {
     int h = 0;
-    if (cudaMemcpy(&h, tos_g.err_dev, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return TOS_ECUDA;
+    if (cudaMemcpyAsync(&h, tos_g.err_dev, sizeof(int), cudaMemcpyDeviceToHost, tos_g.stream) != cudaSuccess ||
+        cudaStreamSynchronize(tos_g.stream) != cudaSuccess)
+        return TOS_ECUDA;
     if (h != 0) {
-        cudaMemset(tos_g.err_dev, 0, sizeof(int));
+        cudaMemsetAsync(tos_g.err_dev, 0, sizeof(int), tos_g.stream);
+        cudaStreamSynchronize(tos_g.stream);
         return TOS_ETIMEOUT;
     }
     return TOS_OK;
@@ -167,7 +173,7 @@ int tos_weight_create_dev(tos_weight_t **out, const void *dev_blocks, int out_di
     if (rc) return tos_set_status(rc);
     tos_weight_t *w = (tos_weight_t *)calloc(1, sizeof(*w));
     if (!w) return tos_set_status(TOS_ENOMEM);
-    int e = tosk_qmat_alloc(&w->m, type, out_dim, in_dim);
+    int e = tosk_qmat_alloc(&w->m, type, out_dim, in_dim, tos_pick_stream(stream));
     if (e) { free(w); return tos_set_status(tos_from_cuda(e)); }
     const void *srcs[1] = {dev_blocks};
     int rows[1] = {out_dim};

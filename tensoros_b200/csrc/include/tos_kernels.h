@@ -38,7 +38,9 @@ typedef struct {
 } tosk_qmat_t;
 
 /* ---- weight planes ---- */
-int tosk_qmat_alloc(tosk_qmat_t *m, int type, int rows, int cols);
+/* allocates the planes and clears the scale padding on stream st (the
+ * stream of the repack that fills them) */
+int tosk_qmat_alloc(tosk_qmat_t *m, int type, int rows, int cols, cudaStream_t st);
 void tosk_qmat_free(tosk_qmat_t *m);
 /* Repack GGUF blocks already on the device into m (row-concatenation of
  * n_src sources, or row interleave when interleave != 0: dst row

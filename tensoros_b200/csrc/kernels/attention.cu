@@ -27,6 +27,8 @@
 // the place of the 1/sum differ from the reference (tolerance 1e-4).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "tos_dev.cuh"
 #include "tos_kernels.h"
 
@@ -572,8 +574,12 @@ extern "C" int tosk_attention(float* out, const float* q, const void* k_cache, c
 //    workspace (tos_attention_workspace_bytes(n_heads, max_ctx)) is larger
 //    is rejected with TOS_ENOMEM before any work is queued.
 //  * The first call on a device resolves the array's device address with
-//    cudaGetSymbolAddress while that device is current; make that first call
-//    before any stream capture.
+//    cudaGetSymbolAddress while that device is current (once per device,
+//    std::call_once, so concurrent first calls are safe); make that first
+//    call before any stream capture.  A cudaDeviceReset destroys every device
+//    object this library holds on that device (its stream, registered
+//    weights, models and this address alike): call tos_shutdown first and do
+//    not use the library on that device afterwards.
 //  * Every call shares the one array.  Nothing in it has to start at zero:
 //    each call writes every workspace element before reading it.  Calls that
 //    overlap on the GPU (different streams, or concurrent host threads) race
@@ -586,8 +592,10 @@ constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 }  // namespace tos
 
-static void* g_noalloc_ptr[64];
-static int g_noalloc_ready[64];
+static constexpr int kNoAllocMaxDevices = 64;
+static std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+static void* g_noalloc_ptr[kNoAllocMaxDevices];
+static cudaError_t g_noalloc_status[kNoAllocMaxDevices];
 
 extern "C" int tos_attention_noalloc_dev(float* out, const float* q, const void* k_cache, const void* v_cache,
                                          int kv_type, int n_heads, int n_kv, int head_dim, int pos, int max_ctx,
@@ -601,14 +609,15 @@ extern "C" int tos_attention_noalloc_dev(float* out, const float* q, const void*
   if (need > tos::kNoAllocScratchBytes) return kNoMem;   // beyond the static scratch
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kNoDev;
-  if (dev < 0 || dev >= 64) return kInval;
-  if (!g_noalloc_ready[dev]) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return kInval;
+  // the array's address on this device (the symbol's host-side name is not a
+  // device address), resolved once with this device current
+  std::call_once(g_noalloc_once[dev], [dev] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, tos::g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return kCuda;
-    g_noalloc_ptr[dev] = p;
-    g_noalloc_ready[dev] = 1;
-  }
+    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, tos::g_noalloc_scratch);
+    g_noalloc_ptr[dev] = g_noalloc_status[dev] == cudaSuccess ? p : nullptr;
+  });
+  if (g_noalloc_status[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr) return kCuda;
   const int e = tosk_attention(out, q, k_cache, v_cache, kv_type, n_heads, n_kv, head_dim, nullptr, pos, max_ctx,
                                mode, g_noalloc_ptr[dev], tos::kNoAllocScratchBytes, nullptr, 0,
                                (cudaStream_t)stream);

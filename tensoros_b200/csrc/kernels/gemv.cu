@@ -529,7 +529,7 @@ extern "C" int tosk_num_sms(void) {
   return g_num_sms;
 }
 
-extern "C" int tosk_qmat_alloc(tosk_qmat_t* m, int type, int rows, int cols) {
+extern "C" int tosk_qmat_alloc(tosk_qmat_t* m, int type, int rows, int cols, cudaStream_t st) {
   if (!m || rows <= 0 || cols <= 0 || (cols % 32) != 0) return (int)cudaErrorInvalidValue;
   if (type != TOSK_Q4_0 && type != TOSK_Q8_0) return (int)cudaErrorInvalidValue;
   m->type = type;
@@ -555,7 +555,9 @@ extern "C" int tosk_qmat_alloc(tosk_qmat_t* m, int type, int rows, int cols) {
     return (int)e;
   }
   m->bytes = qbytes + sbytes + (size_t)rows * 4;
-  return (int)cudaMemset(m->sc, 0, sbytes);
+  // the padding of the scale rows is cleared on the stream that repacks into
+  // the planes next, so the clear cannot land after the repack
+  return (int)cudaMemsetAsync(m->sc, 0, sbytes, st);
 }
 
 extern "C" void tosk_qmat_free(tosk_qmat_t* m) {

@@ -45,8 +45,6 @@ __global__ void pf_embed_kernel(float* __restrict__ x, const uint8_t* __restrict
   for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)t * dim + i] = embed_elem(embd, type, dim, tok, i);
 }
 
-// The reference's order: four serial lane sums over i = 0, 4, 8, ..., then
-// ((f0+f1)+f2)+f3 and the scalar tail; ss = 1/sqrt(ss/dim + eps); (x*ss)*w.
 constexpr int kRopeRows = 1024;   // rows of one token per CTA
 
 // qkv rows [q_rows | kv_rows | kv_rows] per token; q (roped) -> q_out,

@@ -47,19 +47,32 @@ def init(device: int = 0):
     _check("tos_init", _lib().tos_init(device))
 
 
+def _forget_weights():
+    """tos_gemv / tos_vec_dot cache a quantised matrix by its host address, as
+    the reference uses GGUF tensors in place.  A numpy buffer can be freed and
+    its address reused by another array, so these wrappers drop the cache
+    after every call (the C drop-ins keep it for callers whose weights stay
+    put)."""
+    _lib().tos_weight_cache_clear()
+
+
 def gemv(weight: np.ndarray, x, out_dim: int, in_dim: int, type_: int) -> np.ndarray:
     out = np.empty(out_dim, dtype=np.float32)
     x = _f32(x)
     w = np.ascontiguousarray(weight)
     _lib().tos_gemv(_p(out), _p(w), _p(x), out_dim, in_dim, type_)
-    _check("tos_gemv")
+    st = _lib().tos_last_status()
+    _forget_weights()
+    _check("tos_gemv", st)
     return out
 
 
 def vec_dot(weight: np.ndarray, x, n: int, type_: int) -> float:
     x = _f32(x)
     r = _lib().tos_vec_dot(_p(np.ascontiguousarray(weight)), _p(x), n, type_)
-    _check("tos_vec_dot")
+    st = _lib().tos_last_status()
+    _forget_weights()
+    _check("tos_vec_dot", st)
     return np.float32(r)
 
 

@@ -91,3 +91,30 @@ def first_diff(a, b):
         return None
     i = int(bad[0])
     return f"{len(bad)} differ; first at {i}: {a[i]!r} vs {b[i]!r}"
+
+
+FAST_TOL = 1e-4     # the FAST-arithmetic bound against the reference
+FAST_FLOOR = 1e-3   # per-element part: elements with |ref| above this share of max|ref|
+
+
+def fast_errors(got, ref):
+    """The two halves of the FAST numerics contract: the normwise error
+    max|got - ref| / max|ref|, and the largest per-element relative error
+    |got - ref| / |ref| over the elements with |ref| > FAST_FLOOR * max|ref|."""
+    got = np.asarray(got, dtype=np.float64).ravel()
+    ref = np.asarray(ref, dtype=np.float64).ravel()
+    d = np.abs(got - ref)
+    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    norm = float(np.max(d)) / (scale if scale > 0 else 1.0) if ref.size else 0.0
+    big = np.abs(ref) > FAST_FLOOR * scale
+    elem = float(np.max(d[big] / np.abs(ref[big]))) if np.any(big) else 0.0
+    return norm, elem
+
+
+def assert_fast(got, ref, tol=FAST_TOL, what=""):
+    """Both halves of the FAST bound: normwise <= tol and per-element <= tol
+    where |ref| > 1e-3 * max|ref|."""
+    norm, elem = fast_errors(got, ref)
+    assert norm <= tol and elem <= tol, (what, "normwise", norm, "per-element", elem)
+    return norm, elem
+

@@ -29,7 +29,9 @@ def _kv(key, t, val):
     return out
 
 
-def gguf_bytes(synth, alignment=None, tied=False, extra_kv=(), norm_f16=False, version=3):
+def gguf_bytes(synth, alignment=None, tied=False, extra_kv=(), norm_f16=False, version=3, override=None):
+    """override: {tensor name: (dims, type, bytes)} replaces those tensors'
+    infos and data (malformed-file tests)."""
     c = synth.cfg
     dim, ff, L = c["dim"], c["ff_dim"], c["n_layers"]
     hd = dim // c["n_heads"]
@@ -65,6 +67,8 @@ def gguf_bytes(synth, alignment=None, tied=False, extra_kv=(), norm_f16=False, v
                     (f"blk.{l}.ffn_gate.weight", [dim, ff], wt, bytes(ly["wgate"])),
                     (f"blk.{l}.ffn_up.weight", [dim, ff], wt, bytes(ly["wup"])),
                     (f"blk.{l}.ffn_down.weight", [ff, dim], wt, bytes(ly["wdown"]))]
+    if override:
+        tensors = [(n, *override[n]) if n in override else (n, dm, t, b) for n, dm, t, b in tensors]
     align = alignment or 32
     head = struct.pack("<IIQQ", 0x46554747, version, len(tensors), len(kvs))
     head += b"".join(_kv(k, t, v) for k, t, v in kvs)

@@ -117,6 +117,60 @@ def test_gguf_rejects_malformed(lib):
     assert st == EINVAL
 
 
+def _desc_status(lib, blob):
+    st, h, buf = open_bytes(lib, blob)
+    if st != 0:
+        return st
+    try:
+        return read_desc(lib, h)[0]
+    finally:
+        lib.tos_gguf_close(h)
+
+
+def test_gguf_desc_rejects_tensors_smaller_than_the_model(lib):
+    """Every tensor the model maps must have the shape the descriptor
+    implies: a file whose tensors are smaller than its header says passes the
+    container's range check, and the model upload would then read past them."""
+    synth = small()
+    c = synth.cfg
+    dim, ff = c["dim"], c["ff_dim"]
+    wt = c["wtype"]
+    rb = (dim // 32) * (18 if wt == W.TYPE_Q4_0 else 34)
+    norm = np.asarray(synth.layers[0]["attn_norm"], np.float32)
+    assert _desc_status(lib, gguf_bytes(synth)) == 0
+    cases = {
+        # a norm 32 elements short
+        "short attn_norm": {"blk.0.attn_norm.weight": ([dim - 32], 0, norm[:dim - 32].tobytes())},
+        # q with one row fewer than n_heads * head_dim
+        "short attn_q": {"blk.1.attn_q.weight": ([dim, dim - 1], wt, bytes(synth.layers[1]["wq"])[:rb * (dim - 1)])},
+        # down with the input and output dimensions swapped
+        "swapped ffn_down": {"blk.0.ffn_down.weight": ([dim, ff], wt, bytes(synth.layers[0]["wdown"]))},
+        # a third dimension
+        "3-d output": {"output.weight": ([dim, c["vocab_size"] // 2, 2], c["out_type"], bytes(synth.output))},
+    }
+    for what, ov in cases.items():
+        assert _desc_status(lib, gguf_bytes(synth, override=ov)) == EINVAL, what
+    # a well-formed norm of a quantised type: valid but not supported
+    ov = {"output_norm.weight": ([dim], W.TYPE_Q8_0, b"\0" * ((dim // 32) * 34))}
+    assert _desc_status(lib, gguf_bytes(synth, override=ov)) == ENOTSUP
+    # a vocab_size key larger than the embedding's row count
+    big = [("llama.vocab_size", 4, c["vocab_size"] + 32)]
+    assert _desc_status(lib, gguf_bytes(synth, extra_kv=big)) == EINVAL
+    ok = [("llama.vocab_size", 4, c["vocab_size"])]
+    assert _desc_status(lib, gguf_bytes(synth, extra_kv=ok)) == 0
+
+
+def test_gguf_rejects_wrapping_byte_size(lib):
+    """An F32 tensor whose element count fits in 64 bits but whose byte size
+    does not: its size must not wrap to a small value that passes the range
+    check."""
+    synth = small()
+    n = (1 << 62) + 1                      # 4 * n wraps past 2^64
+    ov = {"output_norm.weight": ([n], 0, b"\0" * 4)}
+    st = _desc_status(lib, gguf_bytes(synth, override=ov))
+    assert st == EINVAL
+
+
 def test_gguf_file_mapping(lib, tmp_path):
     synth = small()
     p = tmp_path / "m.gguf"

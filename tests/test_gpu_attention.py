@@ -4,7 +4,7 @@ normwise relative error of 1e-4."""
 import numpy as np
 import pytest
 
-from conftest import bits_equal, first_diff
+from conftest import assert_fast, bits_equal, first_diff
 from tensoros_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -51,8 +51,7 @@ def test_attention_benchmark_config(gpu, oracle, ctx):
     got = run_gpu(gpu, q, kc, vc, W.TYPE_F16, nh, nkv, hd, pos, ctx, 0)
     assert bits_equal(got, ref), first_diff(got, ref)
     fast = run_gpu(gpu, q, kc, vc, W.TYPE_F16, nh, nkv, hd, pos, ctx, 1)
-    err = np.abs(fast - ref).max() / np.abs(ref).max()
-    assert err <= TOL, err
+    assert_fast(fast, ref, TOL, ("attention", ctx))
 
 
 @pytest.mark.parametrize("nh,nkv,hd,ctx,kv", [(8, 2, 64, 300, 0), (6, 6, 48, 272, 0), (4, 1, 128, 1, 1),
@@ -65,7 +64,7 @@ def test_attention_shapes(gpu, oracle, nh, nkv, hd, ctx, kv):
     got = run_gpu(gpu, q, kc, vc, kv, nh, nkv, hd, pos, ctx, 0)
     assert bits_equal(got, ref), first_diff(got, ref)
     fast = run_gpu(gpu, q, kc, vc, kv, nh, nkv, hd, pos, ctx, 1)
-    assert np.abs(fast - ref).max() / np.abs(ref).max() <= TOL
+    assert_fast(fast, ref, TOL, ("attention", nh, nkv, hd, ctx, kv))
 
 
 def test_attention_prefix_of_cache(gpu, oracle):

@@ -7,6 +7,7 @@ reference's result for that sequence alone: logits within the FAST bound
 import numpy as np
 import pytest
 
+from conftest import assert_fast
 from tensoros_b200 import ops
 from tensoros_b200 import workloads as W
 
@@ -64,7 +65,7 @@ def test_batch_gqa_vs_oracle(gpu, oracle):
             want_next = []
             for t, tok in enumerate(consumed):
                 lr = ref.forward(int(tok), t)
-                assert normwise(logs[i][t], lr) <= TOL, (i, t, normwise(logs[i][t], lr))
+                assert_fast(logs[i][t], lr, TOL, ("batch", i, t))
                 if t >= len(p) - 1:
                     want_next.append((int(np.argmax(lr)), lr))
         finally:
@@ -91,7 +92,7 @@ def test_batch_7b_layers_sixteen(gpu):
             for t in range(3):
                 ls = single.forward(int(prompts[i][t]), t)
                 ids, lg = batch[t]
-                assert normwise(lg[i], ls) <= TOL, (i, t, normwise(lg[i], ls))
+                assert_fast(lg[i], ls, TOL, ("batch vs single", i, t))
             assert int(ids[i]) == int(np.argmax(ls))
     finally:
         model.close()
