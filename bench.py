@@ -136,6 +136,25 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def cpu_info() -> dict:
+    """The host CPU the baselines ran on: model name, online CPUs, and the
+    CPUs this process may use."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except Exception:
+        usable = os.cpu_count()
+    return {"cpu_model": model, "nproc": os.cpu_count(), "usable_cpus": usable}
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -178,20 +197,23 @@ def run_reference(args, world, rank):
     from tensoros_b200 import workloads as W
     cfg = dict(W.LLAMA2_7B, kv_type=W.TYPE_F32)
     synth = W.make_model(cfg, W.SEED)
+    # a bounded sample: at ~3 s per token on one core, the run times n
+    # tokens after w warm-up tokens (the line reports those counts)
     n = max(1, min(args.steps, args.ref_tokens))
     w = min(args.warmup, 1)
     value, kind, dt = ref_cpu_decode(synth, n, args.prefill, w)
     sample = (f"{n} decode tokens (after {w} warm-up) at positions {args.prefill + w}.. of the 7B Q4_0 model, "
               f"fp32 KV cache (the reference's only cache type), prefix positions left zero instead of a "
-              f"{args.prefill}-token CPU prefill; reference runtime/nn/llm.c built hosted, 1 core")
+              f"{args.prefill}-token CPU prefill; reference runtime/nn/llm.c built hosted, 1 core, {dt:.1f} s")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+        "steps": n, "warmup": w, "steps_requested": args.steps, "ms_per_step": 1000.0 / value,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, random-init weights)",
         "config": {"workload": "llama2-7b-shape-q4_0 decode, batch 1", "global_batch": 1,
                    "seq_len": args.prefill, "parallelism": "none (CPU)"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample},
+        "cpu_baseline": dict({"value": value, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample},
+                             **cpu_info()),
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -199,40 +221,263 @@ def run_reference(args, world, rank):
 
 def gemv_roofline(lib, torch, mode, n_copies=32, reps=4):
     """Isolated Q4_0 GEMV 4096x4096, L2-cold by rotating weight copies."""
+    from tensoros_b200 import workloads as W
+    return time_gemv(lib, torch, W.TYPE_Q4_0, 4096, 4096, (mode,), n_copies, reps)[mode]
+
+
+def time_gemv(lib, torch, t, rows, cols, modes, n_copies, reps=4):
+    """{mode: ms per launch} of one GEMV (tos_gemv_mode_dev) in a CUDA graph
+    of back-to-back launches over n_copies weight copies (L2-cold when the
+    copies exceed L2)."""
     import ctypes
     from tensoros_b200 import workloads as W
     hs = []
     try:
         for c in range(n_copies):
-            w = W.q4_0(4096, 4096, W.SEED, 9000 + c)
+            w = W.quant(t, rows, cols, W.SEED, 9000 + c)
             h = ctypes.c_void_p()
-            assert lib.tos_weight_create(ctypes.byref(h), w.ctypes.data, 4096, 4096, W.TYPE_Q4_0) == 0
+            assert lib.tos_weight_create(ctypes.byref(h), w.ctypes.data, rows, cols, t) == 0
             hs.append(h)
-        x = torch.from_numpy(W.normal_f32(4096, W.SEED, 9999)).cuda()
-        y = torch.empty(4096, device="cuda")
+        x = torch.from_numpy(W.normal_f32(cols, W.SEED, 9999)).cuda()
+        y = torch.empty(rows, device="cuda")
         s = torch.cuda.Stream()
-        with torch.cuda.stream(s):
-            sp = s.cuda_stream
-            for h in hs[:4]:
-                assert lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp) == 0
-            s.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=s):
-                for _ in range(reps):
-                    for h in hs:
-                        lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp)
-            g.replay()
-            s.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(s)
-            g.replay()
-            e1.record(s)
-            e1.synchronize()
-        ms = e0.elapsed_time(e1) / (reps * n_copies)
-        return ms
+        res = {}
+        for mode in modes:
+            with torch.cuda.stream(s):
+                sp = s.cuda_stream
+                for h in hs[:4]:
+                    assert lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp) == 0
+                s.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(reps):
+                        for h in hs:
+                            lib.tos_gemv_mode_dev(h, x.data_ptr(), None, 0.0, y.data_ptr(), mode, sp)
+                g.replay()
+                s.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                g.replay()
+                e1.record(s)
+                e1.synchronize()
+            res[mode] = e0.elapsed_time(e1) / (reps * n_copies)
+            del g
+        return res
     finally:
         for h in hs:
             lib.tos_weight_destroy(h)
+
+
+L2_BYTES = 126 << 20
+ROTATE_BYTES = 256 << 20   # rotated inputs: more than twice L2, so every launch is L2-cold
+
+
+def q8_0_sweep(lib, torch, peak):
+    """The Q8_0 GEMV shapes of the weight sweep (batch 1, fp32 in/out), FAST
+    and EXACT arithmetic: algorithmic bytes R*(C/32)*34 + 4C + 4R per
+    launch, L2-cold."""
+    from tensoros_b200 import workloads as W
+    out = []
+    for rows, cols in [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]:
+        wbytes = rows * (cols // 32) * 34
+        copies = max(2, -(-ROTATE_BYTES // wbytes))
+        ms = time_gemv(lib, torch, W.TYPE_Q8_0, rows, cols, (1, 0), copies, reps=3)
+        alg = wbytes + 4 * cols + 4 * rows
+        row = {"rows": rows, "cols": cols, "algorithmic_bytes": alg, "copies_rotated": copies}
+        for name, mode in (("fast", 1), ("exact", 0)):
+            gbs = alg / (ms[mode] / 1000.0) / 1e9
+            row[name] = {"launch_us": ms[mode] * 1000.0, "GB/s": gbs, "frac": gbs / peak}
+        out.append(row)
+    return out
+
+
+def attention_sweep(lib, torch, peak):
+    """Single-query decode attention, 32 heads x 128, fp16 KV cache at
+    contexts 512 / 2048 / 4096 (tos_attention_dev, EXACT and FAST): K and V
+    rows read once per call, L2-cold by rotating cache copies; seeded
+    N(0,1) data."""
+    nh, hd = 32, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234)
+    res = []
+    s = torch.cuda.Stream()
+    for ctx in (512, 2048, 4096):
+        kvb = 2 * ctx * nh * hd * 2
+        copies = max(2, -(-ROTATE_BYTES // kvb))
+        ks = [torch.randn(ctx * nh * hd, generator=g, device="cuda").half() for _ in range(copies)]
+        vs = [torch.randn(ctx * nh * hd, generator=g, device="cuda").half() for _ in range(copies)]
+        q = torch.randn(nh * hd, generator=g, device="cuda")
+        out = torch.empty(nh * hd, device="cuda")
+        wsb = lib.tos_attention_workspace_bytes(nh, ctx)
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        row = {"ctx": ctx, "heads": nh, "head_dim": hd, "algorithmic_bytes": kvb + 2 * nh * hd * 4,
+               "copies_rotated": copies}
+        for name, mode in (("exact", 0), ("fast", 1)):
+            with torch.cuda.stream(s):
+                def call(c):
+                    return lib.tos_attention_dev(out.data_ptr(), q.data_ptr(), ks[c].data_ptr(), vs[c].data_ptr(), 1,
+                                                 nh, nh, hd, ctx - 1, ctx, mode, ws.data_ptr(), wsb, s.cuda_stream)
+                for c in range(copies):
+                    assert call(c) == 0
+                s.synchronize()
+                reps = 3
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=s):
+                    for _ in range(reps):
+                        for c in range(copies):
+                            call(c)
+                gr.replay()
+                s.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                gr.replay()
+                e1.record(s)
+                e1.synchronize()
+            us = e0.elapsed_time(e1) * 1000.0 / (reps * copies)
+            gbs = row["algorithmic_bytes"] / (us * 1e-6) / 1e9
+            row[name] = {"call_us": us, "GB/s": gbs, "frac": gbs / peak}
+            del gr
+        res.append(row)
+        del ks, vs
+    return res
+
+
+def tiny_llama_run(torch):
+    """The tiny Llama config: the reference's golden 16-token prompt, then 256
+    greedy tokens; the ids are compared with the reference's own golden run
+    and the decode is timed (device-chained steps, CUDA events)."""
+    import numpy as np
+    from tensoros_b200 import ops
+    from tensoros_b200 import workloads as W
+    g = np.load(ROOT / "tests" / "golden" / "tiny_llama.npz")
+    synth = W.make_model(W.TINY_LLAMA, int(g["seed"][0]))
+    prompt, want = [int(t) for t in g["prompt"]], [int(t) for t in g["ids"]]
+    res = {"prompt_tokens": len(prompt), "generated": len(want)}
+    for name, kw in (("exact", {}), ("fast", dict(attn_mode=1, gemv_mode=1, fused_step=1))):
+        model = ops.Model(synth, **kw)
+        try:
+            nxt = 0
+            for i, t in enumerate(prompt):
+                nxt = model.forward_argmax(t, i)
+            stream = torch.cuda.ExternalStream(model.stream())
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            toks = model.decode(nxt, len(prompt), len(want) - 1)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            ids = [nxt] + [int(t) for t in toks]
+            res[name] = {"tokens_per_s": (len(want) - 1) / (ms / 1000.0), "ms": ms,
+                         "ids_identical_to_reference": ids == want, "fused": model.fused}
+        finally:
+            model.close()
+    return res
+
+
+def long_context_run(synth, torch, weight_bytes, peak, K=32):
+    """The 7B model deep into its 4096-position fp16 cache: prefill to
+    position 2048 and ~4000 (tensor-core prefill), then K greedy steps
+    chained on the device (fused FAST step) at each; bytes per token =
+    weights + the K and V rows of the context."""
+    from tensoros_b200 import ops
+    from tensoros_b200 import workloads as W
+    cfg = synth.cfg
+    L = cfg["n_layers"]
+    prompt = [int(t) for t in W.tokens(4000, cfg["vocab_size"], W.SEED + 7)]
+    model = ops.Model(synth, attn_mode=1, gemv_mode=1, fused_step=1)
+    out = []
+    try:
+        nxt = model.prefill(prompt[:2048], 0)
+        stream = torch.cuda.ExternalStream(model.stream())
+        for start in (2048, 4000 - K):
+            if start > 2048:
+                nxt = model.prefill(prompt[2048 + K:start], 2048 + K)
+            model.decode(nxt, start, 1)   # warm-up: the same graph, one step
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            toks = model.decode(nxt, start, K)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            ctx_mid = start + K // 2
+            step_bytes = weight_bytes + L * 2 * (ctx_mid + 1) * cfg["dim"] * 2
+            us = ms * 1000.0 / K
+            out.append({"positions": [start, start + K - 1], "tokens_per_s": K / (ms / 1000.0), "ms_per_step": ms / K,
+                        "GB/s": step_bytes / (us * 1e-6) / 1e9, "frac": step_bytes / (us * 1e-6) / 1e9 / peak,
+                        "kv_bytes_per_step": L * 2 * (ctx_mid + 1) * cfg["dim"] * 2})
+            nxt = int(toks[-1])
+    finally:
+        model.close()
+    return out
+
+
+def cpu_batch_worker(n_seq: int, n_tokens: int, start_pos: int):
+    """Batch-16 CPU baseline: n_seq independent single-core runs of the
+    reference's llm_forward_token on the 7B model, one process per CPU, run
+    at the same time; forked from this process, which never touches CUDA.
+    Prints one JSON line."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle
+    from tensoros_b200 import workloads as W
+    cfg = dict(W.LLAMA2_7B, kv_type=W.TYPE_F32, max_seq=start_pos + n_tokens + 8)
+    synth = W.make_model(cfg, W.SEED)
+    kind = "reference" if pyoracle.reference_available() else "port"
+    cpus = sorted(os.sched_getaffinity(0))
+    n = min(n_seq, len(cpus))
+    kids = []
+    for i in range(n):
+        r, w = os.pipe()
+        pid = os.fork()
+        if pid == 0:
+            os.close(r)
+            try:
+                os.sched_setaffinity(0, {cpus[i]})
+                ops = pyoracle.reference() if kind == "reference" else pyoracle.oracle()
+                model = ops.model(synth) if kind == "reference" else ops.model(synth, kv_type=0)
+                tok, pos = 1 + i, start_pos
+                model.forward(tok, pos)   # warm-up
+                pos += 1
+                t0 = time.perf_counter()
+                for _ in range(n_tokens):
+                    tok = int(model.forward(tok, pos).argmax())
+                    pos += 1
+                os.write(w, json.dumps({"s": time.perf_counter() - t0}).encode())
+            finally:
+                os._exit(0)
+        os.close(w)
+        kids.append((pid, r))
+    secs = []
+    for pid, r in kids:
+        data = b""
+        while True:
+            chunk = os.read(r, 4096)
+            if not chunk:
+                break
+            data += chunk
+        os.close(r)
+        os.waitpid(pid, 0)
+        if data:
+            secs.append(json.loads(data)["s"])
+    total = len(secs) * n_tokens / max(secs) if secs else None
+    print(json.dumps({"value": total, "unit": "tokens/s", "cores": len(secs), "kind": kind,
+                      "sample": f"{len(secs)} independent sequences, one process and one core each, run "
+                                f"concurrently: {n_tokens} decode tokens each (after 1 warm-up) at positions "
+                                f"{start_pos + 1}.. of the 7B Q4_0 model (fp32 KV, prefix positions zero); "
+                                f"aggregate = sequences x tokens / the slowest sequence's time",
+                      "per_sequence_s": secs}), flush=True)
+
+
+def cpu_batch_baseline(n_seq=16, n_tokens=2, start_pos=128):
+    """Runs cpu_batch_worker in a fresh CUDA-free process."""
+    try:
+        r = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--cpu-batch-worker",
+                            str(n_seq), str(n_tokens), str(start_pos)], capture_output=True, text=True, timeout=900)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        return dict(json.loads(line[-1]), **cpu_info()) if line else {"error": r.stderr[-500:]}
+    except Exception as e:   # the baseline is reported, not required
+        return {"error": str(e)}
 
 
 def run_gemv_only(args, local):
@@ -495,12 +740,22 @@ def run_ours(args, world, rank, local):
                    # dram bytes of one launch at context 8, plus the KV rows of this context
                    "traffic": STEP_TRAFFIC + L * 2 * (ctx - 8) * 4096 * 2,
                    "algorithmic_bytes_per_launch": step_bytes, "launch_us": step_us}
+        extra = {}
+        if world == 1 and not args.no_extra:
+            extra["q8_0_gemv_sweep"] = q8_0_sweep(lib, torch, peak)
+            extra["attention"] = attention_sweep(lib, torch, peak)
+            extra["tiny_llama"] = tiny_llama_run(torch)
+            extra["long_context"] = long_context_run(synth, torch, weight_bytes, peak)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, kind, dt = ref_cpu_decode(synth, args.ref_tokens, args.prefill, 1)
-            cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
-                   "sample": f"{args.ref_tokens} decode tokens of the same 7B Q4_0 model (fp32 KV, the "
-                             f"reference's cache type) at positions {args.prefill + 1}.., one host core, {dt:.1f} s"}
+            cpu = dict({"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
+                        "sample": f"{args.ref_tokens} decode tokens of the same 7B Q4_0 model (fp32 KV, the "
+                                  f"reference's cache type) at positions {args.prefill + 1}.., one host core, "
+                                  f"{dt:.1f} s"}, **cpu_info())
+            if args.batch > 1 and not args.no_extra:
+                # the batch-16 decode's baseline: 16 single-core reference runs
+                cpu["batch16"] = cpu_batch_baseline(16, 2, args.prefill)
         res = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": warm, "ms_per_step": t_ms / K, "higher_is_better": True,
@@ -534,6 +789,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "setup_s": round(t_gen, 1),
         }
+        res.update(extra)
         print(json.dumps(res), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -564,11 +820,19 @@ def main():
     ap.add_argument("--gemv-only", action="store_true",
                     help="time only the isolated Q4_0 4096x4096 GEMV (the roofline leg) and print it")
     ap.add_argument("--gemv-copies", type=int, default=32)
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other workloads (Q8_0 GEMV sweep, attention, tiny llama, long context, "
+                         "batch-16 CPU baseline)")
+    ap.add_argument("--cpu-batch-worker", nargs=3, type=int, metavar=("SEQS", "TOKENS", "POS"),
+                    help=argparse.SUPPRESS)
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the prefill tensor-core GEMM (128x22016x4096 Q4_0) and print it")
     ap.add_argument("--gemm-m", type=int, default=128,
                     help="--gemm-only: token rows of the gate|up GEMM (16 = a batch-16 decode step)")
     args = ap.parse_args()
+    if args.cpu_batch_worker:
+        cpu_batch_worker(*args.cpu_batch_worker)
+        return
     world, rank, local = dist_setup(args)
     if args.gemv_only:
         run_gemv_only(args, local)

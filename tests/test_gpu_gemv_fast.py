@@ -8,7 +8,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, assert_fast, fast_errors
+from conftest import GOLDEN, assert_fast, dequant_abs_matvec, logits_scale
 from tensoros_b200 import ops
 from tensoros_b200 import workloads as W
 
@@ -64,7 +64,7 @@ def test_fast_gemv_shapes(gpu, oracle, t, rows, cols):
     finally:
         g.close()
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "FAST results must be deterministic"
-    err, _ = assert_fast(a, ref, TOL, (t, rows, cols))
+    err, _ = assert_fast(a, ref, TOL, (t, rows, cols), dequant_abs_matvec(w, t, rows, cols, x))
     assert err <= TYPICAL, err
 
 
@@ -78,7 +78,7 @@ def test_fast_gemv_ragged(gpu, oracle, t, rows, cols):
         got = g(x, FAST)
     finally:
         g.close()
-    assert_fast(got, oracle.gemv(w, x, rows, cols, t), TOL, (t, rows, cols))
+    assert_fast(got, oracle.gemv(w, x, rows, cols, t), TOL, (t, rows, cols), dequant_abs_matvec(w, t, rows, cols, x))
 
 
 def test_fast_gemv_special_activations(gpu, oracle):
@@ -93,11 +93,13 @@ def test_fast_gemv_special_activations(gpu, oracle):
             assert np.all(z == 0.0)
             x = W.normal_f32(cols, 3, 701)
             x[:6] = [0.0, -0.0, 1e-40, -3e-39, 1e30, -1e30]
-            assert_fast(g(x, FAST), oracle.gemv(w, x, rows, cols, t), TOL, "special values")
+            assert_fast(g(x, FAST), oracle.gemv(w, x, rows, cols, t), TOL, "special values",
+                        dequant_abs_matvec(w, t, rows, cols, x))
             x = W.normal_f32(cols, 3, 702)
             x[::97] *= 100.0                 # outlier features
             x[256:512] *= 1e-6               # a quiet stretch
-            assert_fast(g(x, FAST), oracle.gemv(w, x, rows, cols, t), TOL, "outliers")
+            assert_fast(g(x, FAST), oracle.gemv(w, x, rows, cols, t), TOL, "outliers",
+                        dequant_abs_matvec(w, t, rows, cols, x))
         finally:
             g.close()
 
@@ -112,7 +114,8 @@ def test_fast_gemv_fused_norm(gpu, oracle):
         for eps in (1e-6, 1e-5):
             got = g(x, FAST, gw, eps)
             xn = oracle.rmsnorm(x, gw, cols, 0, eps)
-            assert_fast(got, oracle.gemv(w, xn, rows, cols, t), TOL, ("fused norm", eps))
+            assert_fast(got, oracle.gemv(w, xn, rows, cols, t), TOL, ("fused norm", eps),
+                        dequant_abs_matvec(w, t, rows, cols, xn))
         # EXACT through the same entry point is bit-identical to tos_gemv_norm_dev's contract
         exact = g(x, 0, gw, 1e-6)
         xn = oracle.rmsnorm(x, gw, cols, 0, 1e-6)
@@ -136,15 +139,20 @@ def test_fast_gemv_rejects_bad_mode(gpu):
         g.close()
 
 
-def test_tiny_llama_fast_greedy_matches_reference(gpu):
+def test_tiny_llama_fast_greedy_matches_reference(gpu, oracle):
     """FAST GEMV + FAST attention: the greedy ids of the reference's own run
-    (golden), and first-step logits within the bound."""
+    (golden), and first-step logits within the bound (per-element scale:
+    the LM head's terms, from the oracle's hidden state of the same step)."""
     g = np.load(GOLDEN / "tiny_llama.npz")
     m = W.make_model(W.TINY_LLAMA, int(g["seed"][0]))
+    om = oracle.model(m)
+    om.forward(int(g["prompt"][0]), 0)
+    scale = logits_scale(m, om.hidden())
+    om.close()
     model = ops.Model(m, attn_mode=1, gemv_mode=FAST)
     try:
         lg = model.forward(int(g["prompt"][0]), 0)
-        assert_fast(lg, g["logits0"], TOL, "tiny-llama first logits")
+        assert_fast(lg, g["logits0"], TOL, "tiny-llama first logits", scale)
         model.reset()
         ids = model.generate_greedy(g["prompt"], len(g["ids"]))
         assert np.array_equal(ids, g["ids"]), np.nonzero(ids != g["ids"])[0][:5]

@@ -14,7 +14,7 @@ per-operator FAST kernels of the same model:
 import numpy as np
 import pytest
 
-from conftest import assert_fast, fast_errors
+from conftest import assert_fast, fast_errors, logits_scale
 from tensoros_b200 import ops
 from tensoros_b200 import workloads as W
 
@@ -45,8 +45,10 @@ def compare_with_oracle(oracle, cfg, seed, n_steps, n_gen, layers=None):
             lr = ref.forward(int(t), i)
             lf = fused.forward(int(t), i)
             lp = per_op.forward(int(t), i)
-            ef, _ = assert_fast(lf, lr, TOL, ("fused step", i))
+            sc = logits_scale(synth, ref.hidden())
+            ef, _ = assert_fast(lf, lr, TOL, ("fused step", i), sc)
             ep, _ = fast_errors(lp, lr)
+            assert_fast(lp, lr, TOL, ("per-operator FAST", i), sc)
             assert ef <= 4 * ep + 2e-6, (i, ef, ep)
         ref.close()
         ref = oracle.model(synth)
@@ -185,7 +187,7 @@ def test_step_7b_full_depth_vs_oracle(gpu, oracle):
         for pos, t in enumerate(toks):
             lr = om.forward(int(t), pos)
             lf = fused.forward(int(t), pos)
-            assert_fast(lf, lr, TOL, ("7B fused step", pos))
+            assert_fast(lf, lr, TOL, ("7B fused step", pos), logits_scale(synth, om.hidden()))
             assert int(np.argmax(lf)) == int(np.argmax(lr)), pos
     finally:
         fused.close()
@@ -198,8 +200,11 @@ def test_step_7b_full_depth_split_k(gpu):
     switches to the split-K form: one token sequence fed to the fused FAST
     model and to the EXACT per-operator model (bit-identical to the reference
     and its restatement: tests/test_gpu_model.py), logits compared at
-    positions 1024..1027 within both halves of the FAST bound.  (The oracle
-    itself would need ~3 s per position for the 1028 positions.)"""
+    positions 1024..1027 within the normwise FAST bound, same greedy token.
+    (The oracle itself would need ~3 s per position for the 1028 positions;
+    the per-element half needs the reference's hidden state, which only the
+    oracle exposes: tests/test_gpu_step.py::test_step_7b_full_depth_vs_oracle
+    checks it on this model shape.)"""
     cfg = dict(W.LLAMA2_7B)
     synth = W.make_model(cfg, 17)
     toks = W.tokens(1028, cfg["vocab_size"], 17)
@@ -212,7 +217,7 @@ def test_step_7b_full_depth_split_k(gpu):
         for pos in range(1024, 1028):
             lf = fused.forward(int(toks[pos]), pos)
             le = exact.forward(int(toks[pos]), pos)
-            assert_fast(lf, le, TOL, ("7B split-K", pos))
+            assert_fast(lf, le, TOL, ("7B split-K", pos))   # normwise
             assert int(np.argmax(lf)) == int(np.argmax(le)), pos
     finally:
         fused.close()
