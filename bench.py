@@ -172,22 +172,28 @@ def ref_cpu_decode(synth, n_tokens: int, start_pos: int, warmup: int):
     else:
         ops, kind = pyoracle.oracle(), "port"
         model = ops.model(synth, kv_type=0)
+    saved = None
     try:
-        os.sched_setaffinity(0, {sorted(os.sched_getaffinity(0))[0]})
+        saved = os.sched_getaffinity(0)
+        os.sched_setaffinity(0, {sorted(saved)[0]})
     except Exception:
         pass
-    tok = 1
-    pos = start_pos
-    for _ in range(warmup):
-        model.forward(tok, pos)
-        pos += 1
-    t0 = time.perf_counter()
-    for _ in range(n_tokens):
-        lg = model.forward(tok, pos)
-        tok = int(lg.argmax())
-        pos += 1
-    dt = time.perf_counter() - t0
-    model.close()
+    try:
+        tok = 1
+        pos = start_pos
+        for _ in range(warmup):
+            model.forward(tok, pos)
+            pos += 1
+        t0 = time.perf_counter()
+        for _ in range(n_tokens):
+            lg = model.forward(tok, pos)
+            tok = int(lg.argmax())
+            pos += 1
+        dt = time.perf_counter() - t0
+    finally:
+        model.close()
+        if saved:
+            os.sched_setaffinity(0, saved)   # the process's other work keeps all its CPUs
     return n_tokens / dt, kind, dt
 
 

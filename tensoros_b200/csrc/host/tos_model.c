@@ -58,6 +58,11 @@ struct tos_model {
     tosk_step_t step;
     tosk_step_layer_t *step_layers;   /* device [n_layers] */
     unsigned *step_sync;
+    /* sharded: x | att | h | flags | pairs in one allocation shared with the
+     * peers through CUDA IPC; peer_base[r] is rank r's, mapped here */
+    void *xch;
+    size_t xoff_att, xoff_h, xoff_flags, xoff_pairs, xch_bytes;
+    void *peer_base[TOSK_MAX_WORLD];
     size_t dev_bytes;
     /* batched prompt pass (allocated on first use): up to pf_cap tokens */
     int pf_cap;
@@ -129,6 +134,18 @@ void tos_model_destroy(tos_model_t *m)
     /* graphs holding collectives go before the communicator */
     if (m->have_graph > 0) cudaGraphExecDestroy(m->gexec);
     if (m->have_chain > 0) cudaGraphExecDestroy(m->gexec_chain);
+    int mapped = 0;
+    for (int r = 0; r < TOSK_MAX_WORLD; r++)
+        if (m->peer_base[r] && r != m->sp.rank) {
+            cudaIpcCloseMemHandle(m->peer_base[r]);
+            mapped = 1;
+        }
+    if (mapped && m->comm && m->pairs) {
+        /* every rank has closed its mappings of the others' exchange
+         * buffers before any rank frees its own */
+        tos_nccl_all_gather(m->pairs + 2 * m->sp.rank, m->pairs, 2, 1, m->comm, m->st);
+        cudaStreamSynchronize(m->st);
+    }
     if (m->comm) tos_nccl_comm_destroy(m->comm);
     for (int L = 0; m->wqkv && L < m->d.n_layers; L++) {
         tosk_qmat_free(&m->wqkv[L]);
@@ -138,6 +155,10 @@ void tos_model_destroy(tos_model_t *m)
     }
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
+    if (m->xch) {   /* x, att and h live in the exchange buffer */
+        cudaFree(m->xch);
+        m->x = m->att = m->h = NULL;
+    }
     void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
                     m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
@@ -178,11 +199,46 @@ static int validate(const tos_model_desc_t *d)
 /* The fused per-token kernel (decode_step.cu) runs the step when the
  * descriptor asks for it (fused_step), the model uses FAST arithmetic on one
  * GPU and the device and shapes allow it. */
+/* Sharded fused step: every rank maps every other rank's exchange buffer
+ * (CUDA IPC handles swapped with one all-gather on the model's
+ * communicator); the kernel's epilogues then store into the peers' vectors
+ * directly over NVLink. */
+static int map_peers(tos_model_t *m)
+{
+    const int G = m->sp.world, R = m->sp.rank;
+    cudaIpcMemHandle_t mine;
+    int e = cudaIpcGetMemHandle(&mine, m->xch);
+    if (e) return e;
+    const size_t hb = sizeof(cudaIpcMemHandle_t);   /* 64 bytes */
+    char *dh = NULL;
+    char all[TOSK_MAX_WORLD * sizeof(cudaIpcMemHandle_t)];
+    e = cudaMalloc((void **)&dh, hb * (size_t)G);
+    if (!e) e = cudaMemcpyAsync(dh + hb * (size_t)R, &mine, hb, cudaMemcpyHostToDevice, m->st);
+    if (!e) e = tos_nccl_all_gather(dh + hb * (size_t)R, dh, hb / 4, 1, m->comm, m->st);
+    if (!e) e = cudaMemcpyAsync(all, dh, hb * (size_t)G, cudaMemcpyDeviceToHost, m->st);
+    if (!e) e = cudaStreamSynchronize(m->st);
+    if (dh) cudaFree(dh);
+    for (int r = 0; !e && r < G; r++) {
+        if (r == R) {
+            m->peer_base[r] = m->xch;
+            continue;
+        }
+        cudaIpcMemHandle_t hr;
+        memcpy(&hr, all + hb * (size_t)r, hb);
+        e = cudaIpcOpenMemHandle(&m->peer_base[r], hr, cudaIpcMemLazyEnablePeerAccess);
+    }
+    return e;
+}
+
 static int setup_step(tos_model_t *m)
 {
     const tos_model_desc_t *d = &m->d;
-    if (m->sp.world != 1 || d->gemv_mode != TOS_GEMV_FAST || d->attn_mode != TOS_ATTN_FAST || !d->fused_step)
-        return 0;
+    if (d->gemv_mode != TOS_GEMV_FAST || d->attn_mode != TOS_ATTN_FAST || !d->fused_step) return 0;
+    if (m->sp.world > TOSK_MAX_WORLD) return 0;
+    if (m->sp.world > 1) {
+        int e = map_peers(m);
+        if (e) return e;
+    }
     const int L = d->n_layers;
     tosk_step_layer_t *hl = (tosk_step_layer_t *)calloc((size_t)L, sizeof(*hl));
     if (!hl) return cudaErrorMemoryAllocation;
@@ -235,6 +291,29 @@ static int setup_step(tos_model_t *m)
     s->max_seq = d->max_seq;
     s->kv_type = d->kv_type;
     s->eps = d->norm_eps;
+    s->vocab = m->sp.n_vocab;
+    s->n_heads = m->sp.n_heads;
+    s->n_kv = m->sp.n_kv_heads;
+    if (m->sp.world > 1) {
+        const tos_shard_plan_t *sp = &m->sp;
+        s->world = sp->world;
+        s->rank = sp->rank;
+        s->n_rows = sp->n_rows;
+        s->n_ff = sp->n_ff;
+        s->q_full = d->n_heads * m->hd;
+        s->q0 = sp->q_row0;
+        s->row0 = sp->row0;
+        s->ff0 = sp->ff0;
+        s->vocab0 = sp->vocab0;
+        for (int r = 0; r < sp->world; r++) {
+            char *b = (char *)m->peer_base[r];
+            s->peer_x[r] = (float *)b;
+            s->peer_att[r] = (float *)(b + m->xoff_att);
+            s->peer_h[r] = (float *)(b + m->xoff_h);
+            s->peer_flags[r] = (unsigned *)(b + m->xoff_flags);
+            s->peer_pairs[r] = (int *)(b + m->xoff_pairs);
+        }
+    }
     /* shapes or devices the fused kernel does not cover keep the per-operator path */
     m->fused = tosk_step_check(s) == 0;
     cudaGetLastError();
@@ -332,10 +411,29 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
     if (!e) e = cudaMemsetAsync(m->kc, 0, kvb, m->st);
     if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
     int mx = dim > ff ? dim : ff;
-    if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
+    if (world > 1) {
+        /* the full vectors every rank assembles (x, att, h), its barrier
+         * flags and argmax pairs: one allocation the peers can map */
+#define AL(v) (((v) + 255) & ~(size_t)255)
+        m->xoff_att = AL((size_t)dim * 4);
+        m->xoff_h = m->xoff_att + AL((size_t)mx * 4);
+        m->xoff_flags = m->xoff_h + AL((size_t)ff * 4);
+        m->xoff_pairs = m->xoff_flags + AL(TOSK_MAX_WORLD * sizeof(unsigned));
+        m->xch_bytes = m->xoff_pairs + AL(TOSK_MAX_WORLD * 2 * sizeof(int));
+#undef AL
+        if (!e) e = dmalloc(m, &m->xch, m->xch_bytes);
+        if (!e) e = cudaMemsetAsync(m->xch, 0, m->xch_bytes, m->st);
+        if (!e) {
+            m->x = (float *)m->xch;
+            m->att = (float *)((char *)m->xch + m->xoff_att);
+            m->h = (float *)((char *)m->xch + m->xoff_h);
+        }
+    } else {
+        if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
+        if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
+        if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
+    }
     if (!e) e = dmalloc(m, (void **)&m->q, (size_t)mx * 4);
-    if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
-    if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
     if (!e) e = dmalloc(m, (void **)&m->logits, (size_t)sp.n_vocab * 4);
     if (!e && world > 1) e = dmalloc(m, (void **)&m->logits_full, (size_t)d->vocab_size * 4);
     if (!e && world > 1) e = dmalloc(m, (void **)&m->pairs, (size_t)world * 2 * sizeof(int));
@@ -407,7 +505,11 @@ static int enqueue_token(tos_model_t *m, int chained)
 {
     if (m->fused) {
         m->step.chained = chained;
-        return tosk_step_launch(&m->step, m->st);
+        int e = tosk_step_launch(&m->step, m->st);
+        /* sharded: each rank holds its vocabulary rows; a plain step hands
+         * out the whole logits vector */
+        if (!e && m->sp.world > 1 && !chained) e = gather_to(m, m->logits, m->logits_full, m->sp.n_vocab);
+        return e;
     }
     const tos_model_desc_t *d = &m->d;
     cudaStream_t st = m->st;

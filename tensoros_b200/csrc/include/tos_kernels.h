@@ -173,6 +173,9 @@ typedef struct {
     void *k_cache, *v_cache;   /* this layer's [max_seq][kv_dim] */
 } tosk_step_layer_t;
 
+/* most GPUs a fused step is sharded over (one node) */
+#define TOSK_MAX_WORLD 8
+
 typedef struct {
     const tosk_step_layer_t *layers;  /* device array [n_layers] */
     int n_layers;
@@ -192,6 +195,23 @@ typedef struct {
     unsigned *sync;                   /* tosk_step_sync_bytes(), zero before the first launch */
     int dim, ff, n_heads, n_kv, hd, vocab, max_seq, kv_type;
     float eps;
+    /* Row sharding over `world` GPUs of one node (world 1: everything here).
+     * n_heads / n_kv / vocab above are this rank's heads and logit rows;
+     * dim and ff are the full vector lengths (the projections' columns).
+     * This rank computes residual rows [row0, row0 + n_rows), SwiGLU rows
+     * [ff0, ff0 + n_ff), attention-output elements [q0, q0 + n_heads*hd) of
+     * q_full, and vocabulary rows [vocab0, vocab0 + vocab).  x, att and h are
+     * the full vectors; its epilogues store each produced element into every
+     * rank's copy (peer_x[r] etc.: rank r's vector as mapped here, [rank] =
+     * x itself) and the ranks meet at flag barriers: peer_flags[r] is rank
+     * r's array of one epoch per writer, peer_pairs[r] its [world][2] argmax
+     * pairs.  io[5] holds the epoch base (0 on a fresh model). */
+    int world, rank;
+    int n_rows, n_ff, q_full;
+    int q0, row0, ff0, vocab0;
+    float *peer_x[TOSK_MAX_WORLD], *peer_att[TOSK_MAX_WORLD], *peer_h[TOSK_MAX_WORLD];
+    unsigned *peer_flags[TOSK_MAX_WORLD];
+    int *peer_pairs[TOSK_MAX_WORLD];
 } tosk_step_t;
 
 size_t tosk_step_sync_bytes(void);

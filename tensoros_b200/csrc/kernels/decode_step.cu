@@ -98,6 +98,8 @@ struct Hdr {
   uint64_t pempty[kChain];
   int abort;
   int tok, pos, skip;
+  unsigned ebase;   // epoch of the last cross-GPU barrier before this step (sharded)
+  unsigned efinal;  // epoch of this step's argmax exchange (sharded)
   float wpart[kCompute];
   float av[kChain];
   int ai[kChain];
@@ -215,6 +217,18 @@ __device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target
   return !*reinterpret_cast<volatile int*>(&h->abort);
 }
 
+// Release / acquire at system scope on a word that another GPU reads or
+// writes (peer memory mapped into this process, or this GPU's memory that a
+// peer writes).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // A projection's geometry in registers: read once from the kernel
 // parameters and kept opaque to the compiler, which would otherwise reload
 // it inside the stage loops (a constant load with a computed index issues
@@ -268,6 +282,55 @@ __device__ __forceinline__ void arg_better(float& v, int& i, float v2, int i2) {
     v = v2;
     i = i2;
   }
+}
+
+// Barrier of every worker thread of every CTA on every rank of a sharded
+// step.  Each CTA fences its stores (to this GPU and to the peers) at system
+// scope and counts itself in on this GPU's grid counter; the CTA that
+// completes the count publishes `epoch` in every rank's flag array (slot
+// `rank`, release at system scope), and every CTA waits until all ranks'
+// slots in its own array reach `epoch` (acquire).  Epochs only grow, so no
+// flag is ever reset while a peer may still read it.  Every wait is bounded
+// like grid_sync's; returns false, in every worker thread of the CTA alike,
+// when the step must stop.
+__device__ __forceinline__ bool xgpu_sync(Hdr* h, const Params& p, unsigned target, unsigned epoch, int* err) {
+  named_sync(B_WORKERS, kWorkers);
+  if (threadIdx.x == 32 && !*reinterpret_cast<volatile int*>(&h->abort)) {
+    __threadfence_system();
+    if (atomicAdd(p.s.sync, 1u) == target - 1) {
+      // every CTA of this GPU has arrived: publish this rank's epoch
+      __threadfence_system();
+      for (int r = 0; r < p.s.world; ++r) st_release_sys(p.s.peer_flags[r] + p.s.rank, epoch);
+    }
+    const unsigned* mine = p.s.peer_flags[p.s.rank];
+    const long long t0 = clock64();
+    for (int i = 0;; ++i) {
+      bool all = true;
+      for (int r = 0; r < p.s.world && all; ++r) all = (int)(ld_acquire_sys(mine + r) - epoch) >= 0;
+      if (all) break;
+      __nanosleep(32);
+      if ((i & 7) == 7) {
+        if (*reinterpret_cast<volatile int*>(err)) {
+          h->abort = 1;
+          break;
+        }
+        if (clock64() - t0 > kWaitCycles) {
+          atomicCAS(err, 0, 21);
+          h->abort = 1;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  named_sync(B_WORKERS, kWorkers);
+  return !*reinterpret_cast<volatile int*>(&h->abort);
+}
+
+// Stores v at index i of every rank's copy of a vector (peers[rank] is the
+// local one); one rank: the local store only.
+__device__ __forceinline__ void store_all(const Params& p, float* const* peers, size_t i, float v) {
+  for (int r = 0; r < p.s.world; ++r) peers[r][i] = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -396,8 +459,10 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
         // rows it owns in the o / down phases (their residual adds are its own)
         const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (4 * q + i >= orb && 4 * q + i < ore) p.s.x[4 * q + i] = e[i];
+        for (int i = 0; i < 4; ++i) {
+          const int lr = 4 * q + i - p.s.row0;   // the o phase's local row
+          if (lr >= orb && lr < ore) p.s.x[4 * q + i] = e[i];
+        }
         X4[q] = v;
       }
     } else {
@@ -550,12 +615,13 @@ __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind
         reinterpret_cast<float*>(is_k ? L.k_cache : L.v_cache)[idx] = v;
     }
   } else if (kind == K_O || kind == K_D) {
-    p.s.x[r] = __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + r), y);   // llm.c:717-718, 732-733
+    const int gr = p.s.row0 + r;   // residual row (all of x on one GPU)
+    store_all(p, p.s.peer_x, gr, __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + gr), y));   // llm.c:717-718, 732-733
   } else if (kind == K_GU) {
-    if ((r & 1) == 0) p.s.h[r >> 1] = __fmul_rn(ref_silu(y), partner);   // llm.c:726-729
+    if ((r & 1) == 0) store_all(p, p.s.peer_h, p.s.ff0 + (r >> 1), __fmul_rn(ref_silu(y), partner));   // llm.c:726-729
   } else {
     p.s.logits[r] = y;
-    if (!(y != y)) arg_better(bv, bi, y, r);
+    if (!(y != y)) arg_better(bv, bi, y, p.s.vocab0 + r);
   }
 }
 
@@ -589,9 +655,47 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
   for (unsigned k = 0; k < gridDim.x; ++k)
     arg_better(best, idx, __int_as_float(__ldcg(pairs + 2 * k)), __ldcg(pairs + 2 * k + 1));
   // llm.c:1130: x[0] is the starting candidate; it stays when NaN or unbeaten
-  const float x0 = __ldcg(p.s.logits);
-  if (x0 != x0 || idx < 0) idx = 0;
+  // (logit 0 is the first row of rank 0's slice)
+  const bool x0_nan = p.s.rank == 0 && __ldcg(p.s.logits) != __ldcg(p.s.logits);
   int* io = p.s.io;
+  if (p.s.world > 1) {
+    // every rank's (value, index) pair into every rank's pair array (rank 0
+    // marks a NaN logit 0 with index -2), published with the step's final
+    // epoch; every rank then reduces the same pairs in rank order
+    for (int r = 0; r < p.s.world; ++r) {
+      p.s.peer_pairs[r][2 * p.s.rank] = __float_as_int(best);
+      p.s.peer_pairs[r][2 * p.s.rank + 1] = x0_nan ? -2 : idx;
+    }
+    __threadfence_system();
+    for (int r = 0; r < p.s.world; ++r) st_release_sys(p.s.peer_flags[r] + p.s.rank, h->efinal);
+    const unsigned* mine = p.s.peer_flags[p.s.rank];
+    const long long t0 = clock64();
+    bool ok = true;
+    for (int it = 0;; ++it) {
+      bool all = true;
+      for (int r = 0; r < p.s.world && all; ++r) all = (int)(ld_acquire_sys(mine + r) - h->efinal) >= 0;
+      if (all) break;
+      __nanosleep(32);
+      if ((it & 7) == 7 && clock64() - t0 > kWaitCycles) {
+        atomicCAS(io + 3, 0, 22);
+        ok = false;
+        break;
+      }
+    }
+    best = 0.0f;
+    idx = -1;
+    bool nan0 = false;
+    const int* all_pairs = p.s.peer_pairs[p.s.rank];
+    for (int r = 0; ok && r < p.s.world; ++r) {
+      const int pi = __ldcg(all_pairs + 2 * r + 1);
+      if (pi == -2) nan0 = true;
+      else arg_better(best, idx, __int_as_float(__ldcg(all_pairs + 2 * r)), pi);
+    }
+    if (nan0 || idx < 0) idx = 0;
+    io[5] = (int)h->efinal;
+  } else if (x0_nan || idx < 0) {
+    idx = 0;
+  }
   io[2] = idx;
   if (p.s.chained) {
     const int k = io[4];
@@ -628,7 +732,7 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
   {
     const int ct = (int)threadIdx.x - 32;   // 0 .. 32 * kChain - 1
     if (pre_res)
-      for (int i = ct; i < re - rb; i += 32 * kChain) h->res[i] = __ldcg(p.s.x + rb + i);
+      for (int i = ct; i < re - rb; i += 32 * kChain) h->res[i] = __ldcg(p.s.x + p.s.row0 + rb + i);
     if (kind == K_QKV) {
       for (int i = ct; i < (p.s.hd >> 1); i += 32 * kChain) h->cs[i] = p.s.rope[(size_t)pos * (p.s.hd >> 1) + i];
       if (pos + 1 <= kHeadMaxN) {
@@ -848,7 +952,7 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
       for (int d = gt; d < hd; d += 128) {
         float o = 0.0f;
         for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
-        p.s.att[(size_t)hh * hd + d] = o * inv;
+        store_all(p, p.s.peer_att, p.s.q0 + (size_t)hh * hd + d, o * inv);
       }
     }
     named_sync(B_GROUP0 + grp, 128);   // es / red / wpart / s_last are reused by the next item
@@ -973,7 +1077,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
     for (int d = wt; d < hd; d += kWorkers) {
       float o = part[d];
       for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
-      p.s.att[(size_t)hh * hd + d] = o * inv;
+      store_all(p, p.s.peer_att, p.s.q0 + (size_t)hh * hd + d, o * inv);
     }
     named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
   }
@@ -1016,6 +1120,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     h->skip = *reinterpret_cast<volatile int*>(err) != 0;
     h->pos = p.s.io[1];
     h->tok = p.s.chained ? p.s.io[2] : p.s.io[0];
+    // four cross-GPU barriers a layer (after attention, o, gate|up, down),
+    // then the argmax exchange
+    h->ebase = (unsigned)p.s.io[5];
+    h->efinal = h->ebase + 4u * (unsigned)p.s.n_layers + 1u;
     mbar_fence_init();
   }
   __syncthreads();
@@ -1029,7 +1137,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   // else split-K scores then softmax*V), o, gate|up, down; then the LM head.
   // One call site per role keeps every role inlined once.
   const bool short_ctx = h->pos + 1 <= kHeadMaxN;
-  unsigned nsync = 0;
+  unsigned nsync = 0, nx = 0;
   const int nph = 6 * p.s.n_layers + 1;
   for (int ph = 0; ph < nph; ++ph) {
     const int l = ph / 6, r = ph - 6 * l;
@@ -1045,7 +1153,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     } else {
       attn_pv<ESZ>(p, h, P, l);
     }
-    if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) return;
+    // sharded: the vectors the next phase reads in full (attention output,
+    // residual, SwiGLU output) come from every rank; the q|k|v -> attention
+    // and scores -> softmax*V hand-offs stay on this GPU
+    const bool cross = p.s.world > 1 && (r >= 2 || (r == 1 && short_ctx));
+    if (cross) {
+      if (!xgpu_sync(h, p, (++nsync) * gridDim.x, h->ebase + (++nx), err)) return;
+    } else if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) {
+      return;
+    }
   }
 }
 
@@ -1112,10 +1228,33 @@ static int plan(const tosk_step_t* s, Params* p) {
     if (!v || (reinterpret_cast<uintptr_t>(v) & 15)) return (int)cudaErrorInvalidValue;
   memset(p, 0, sizeof(*p));
   p->s = *s;
+  tosk_step_t& t = p->s;
+  if (t.world <= 1) {
+    // one GPU: every row is local, every vector has only its own copy
+    t.world = 1;
+    t.rank = 0;
+    t.n_rows = s->dim;
+    t.n_ff = s->ff;
+    t.q_full = q_dim;
+    t.q0 = t.row0 = t.ff0 = t.vocab0 = 0;
+    t.peer_x[0] = s->x;
+    t.peer_att[0] = s->att;
+    t.peer_h[0] = s->h;
+  } else {
+    if (t.world > TOSK_MAX_WORLD || t.rank < 0 || t.rank >= t.world) return (int)cudaErrorInvalidValue;
+    if (t.n_rows <= 0 || t.n_ff <= 0 || t.q_full < q_dim || t.q0 < 0 || t.q0 + q_dim > t.q_full ||
+        t.row0 < 0 || t.row0 + t.n_rows > s->dim || t.ff0 < 0 || t.ff0 + t.n_ff > s->ff || t.vocab0 < 0)
+      return (int)cudaErrorInvalidValue;
+    for (int r = 0; r < t.world; ++r)
+      if (!t.peer_x[r] || !t.peer_att[r] || !t.peer_h[r] || !t.peer_flags[r] || !t.peer_pairs[r])
+        return (int)cudaErrorInvalidValue;
+    if (t.peer_x[t.rank] != s->x || t.peer_att[t.rank] != s->att || t.peer_h[t.rank] != s->h)
+      return (int)cudaErrorInvalidValue;
+  }
   int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
-  if (!e) e = make_geo(s->dim, q_dim, s->wtype, 1, p->g[K_O]);
-  if (!e) e = make_geo(2 * s->ff, s->dim, s->wtype, 2, p->g[K_GU]);
-  if (!e) e = make_geo(s->dim, s->ff, s->wtype, 1, p->g[K_D]);
+  if (!e) e = make_geo(t.n_rows, t.q_full, s->wtype, 1, p->g[K_O]);
+  if (!e) e = make_geo(2 * t.n_ff, s->dim, s->wtype, 2, p->g[K_GU]);
+  if (!e) e = make_geo(t.n_rows, s->ff, s->wtype, 1, p->g[K_D]);
   if (!e) e = make_geo(s->vocab, s->dim, s->lm_type, 1, p->g[K_LM]);
   if (e) return e;
   p->maxc = (s->max_seq + kChunk - 1) / kChunk;

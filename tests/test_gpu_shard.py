@@ -1,8 +1,10 @@
-"""Row-sharded decoder on 2 GPUs (one process per GPU, NCCL all-gathers):
-every rank's logits and greedy tokens equal the one-GPU model's, bit for bit,
-in EXACT and in FAST arithmetic (each row is computed by the same kernels on
-the same inputs; the exchanges are copies).  Needs two GPUs; skipped
-otherwise."""
+"""Row-sharded decoder on 2 GPUs (one process per GPU): every rank's logits
+and greedy tokens equal the one-GPU model's, bit for bit, in EXACT and in
+FAST arithmetic with a kernel per operator (NCCL all-gathers), and with the
+fused FAST step, whose epilogues store each rank's rows into the peers'
+vectors over NVLink and whose ranks meet at flag barriers (each row is
+computed by the same arithmetic on the same inputs; the exchanges are
+copies).  Needs two GPUs; skipped otherwise."""
 import socket
 
 import numpy as np
@@ -31,7 +33,11 @@ def _run(model, toks):
     return logits, ids
 
 
-def rank_main(rank, world, port, cfg_name, mode, out_path):
+VARIANTS = {"exact": dict(attn_mode=0, gemv_mode=0), "fast": dict(attn_mode=1, gemv_mode=1),
+            "fused": dict(attn_mode=1, gemv_mode=1, fused_step=1)}
+
+
+def rank_main(rank, world, port, cfg_name, variant, out_path):
     import os
     import sys
     from pathlib import Path
@@ -50,36 +56,39 @@ def rank_main(rank, world, port, cfg_name, mode, out_path):
         dist.broadcast_object_list(obj, src=0)
         cfg, layers = CFGS[cfg_name]
         synth = W.make_model(cfg, 23, n_layers=layers)
-        model = ops.Model(synth, attn_mode=mode, gemv_mode=mode, shard=(rank, world, obj[0]))
+        model = ops.Model(synth, shard=(rank, world, obj[0]), **VARIANTS[variant])
         try:
+            fused = model.fused
             toks = W.tokens(N_STEPS, cfg["vocab_size"], 23)
             logits, ids = _run(model, toks)
         finally:
             model.close()
-        np.savez(f"{out_path}.{rank}.npz", logits=logits, ids=ids)
+        np.savez(f"{out_path}.{rank}.npz", logits=logits, ids=ids, fused=fused)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("cfg_name", list(CFGS))
-@pytest.mark.parametrize("mode", [0, 1])
-def test_sharded_equals_one_gpu(gpu, cfg_name, mode, tmp_path):
+@pytest.mark.parametrize("variant", list(VARIANTS))
+def test_sharded_equals_one_gpu(gpu, cfg_name, variant, tmp_path):
     import torch
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
     out = str(tmp_path / "run")
-    mp.start_processes(rank_main, args=(WORLD, _free_port(), cfg_name, mode, out), nprocs=WORLD, join=True,
+    mp.start_processes(rank_main, args=(WORLD, _free_port(), cfg_name, variant, out), nprocs=WORLD, join=True,
                        start_method="spawn")
     cfg, layers = CFGS[cfg_name]
     synth = W.make_model(cfg, 23, n_layers=layers)
-    model = ops.Model(synth, attn_mode=mode, gemv_mode=mode)
+    model = ops.Model(synth, **VARIANTS[variant])
     try:
+        assert model.fused == (variant == "fused")
         ref_logits, ref_ids = _run(model, W.tokens(N_STEPS, cfg["vocab_size"], 23))
     finally:
         model.close()
     for r in range(WORLD):
         got = np.load(f"{out}.{r}.npz")
+        assert bool(got["fused"]) == (variant == "fused"), r
         assert np.array_equal(got["logits"].view(np.uint32), ref_logits.view(np.uint32)), r
         assert np.array_equal(got["ids"], ref_ids), r
 
