@@ -58,10 +58,11 @@ struct tos_model {
     tosk_step_t step;
     tosk_step_layer_t *step_layers;   /* device [n_layers] */
     unsigned *step_sync;
-    /* sharded: x | att | h | flags | pairs in one allocation shared with the
-     * peers through CUDA IPC; peer_base[r] is rank r's, mapped here */
+    /* sharded fused step: the exchange words (tosk_step_ll_words), one
+     * allocation shared with the peers through CUDA IPC; peer_base[r] is
+     * rank r's, mapped here */
     void *xch;
-    size_t xoff_att, xoff_h, xoff_flags, xoff_pairs, xch_bytes;
+    size_t xch_bytes;
     void *peer_base[TOSK_MAX_WORLD];
     size_t dev_bytes;
     /* batched prompt pass (allocated on first use): up to pf_cap tokens */
@@ -155,11 +156,7 @@ void tos_model_destroy(tos_model_t *m)
     }
     free(m->wqkv); free(m->wo); free(m->wgu); free(m->wdown);
     tosk_qmat_free(&m->lm);
-    if (m->xch) {   /* x, att and h live in the exchange buffer */
-        cudaFree(m->xch);
-        m->x = m->att = m->h = NULL;
-    }
-    void *bufs[] = {m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
+    void *bufs[] = {m->xch, m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
                     m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
                     m->pf_toks, m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
@@ -206,8 +203,13 @@ static int validate(const tos_model_desc_t *d)
 static int map_peers(tos_model_t *m)
 {
     const int G = m->sp.world, R = m->sp.rank;
+    /* epochs start above 0: a zeroed area holds no word of any exchange */
+    m->xch_bytes = tosk_step_ll_words(m->d.n_heads * m->hd, m->d.dim, m->d.ff_dim) * 8;
+    int e = dmalloc(m, &m->xch, m->xch_bytes);
+    if (!e) e = cudaMemsetAsync(m->xch, 0, m->xch_bytes, m->st);
+    if (e) return e;
     cudaIpcMemHandle_t mine;
-    int e = cudaIpcGetMemHandle(&mine, m->xch);
+    e = cudaIpcGetMemHandle(&mine, m->xch);
     if (e) return e;
     const size_t hb = sizeof(cudaIpcMemHandle_t);   /* 64 bytes */
     char *dh = NULL;
@@ -305,14 +307,7 @@ static int setup_step(tos_model_t *m)
         s->row0 = sp->row0;
         s->ff0 = sp->ff0;
         s->vocab0 = sp->vocab0;
-        for (int r = 0; r < sp->world; r++) {
-            char *b = (char *)m->peer_base[r];
-            s->peer_x[r] = (float *)b;
-            s->peer_att[r] = (float *)(b + m->xoff_att);
-            s->peer_h[r] = (float *)(b + m->xoff_h);
-            s->peer_flags[r] = (unsigned *)(b + m->xoff_flags);
-            s->peer_pairs[r] = (int *)(b + m->xoff_pairs);
-        }
+        for (int r = 0; r < sp->world; r++) s->peer_ll[r] = (unsigned long long *)m->peer_base[r];
     }
     /* shapes or devices the fused kernel does not cover keep the per-operator path */
     m->fused = tosk_step_check(s) == 0;
@@ -411,29 +406,10 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
     if (!e) e = cudaMemsetAsync(m->kc, 0, kvb, m->st);
     if (!e) e = cudaMemsetAsync(m->vc, 0, kvb, m->st);
     int mx = dim > ff ? dim : ff;
-    if (world > 1) {
-        /* the full vectors every rank assembles (x, att, h), its barrier
-         * flags and argmax pairs: one allocation the peers can map */
-#define AL(v) (((v) + 255) & ~(size_t)255)
-        m->xoff_att = AL((size_t)dim * 4);
-        m->xoff_h = m->xoff_att + AL((size_t)mx * 4);
-        m->xoff_flags = m->xoff_h + AL((size_t)ff * 4);
-        m->xoff_pairs = m->xoff_flags + AL(TOSK_MAX_WORLD * sizeof(unsigned));
-        m->xch_bytes = m->xoff_pairs + AL(TOSK_MAX_WORLD * 2 * sizeof(int));
-#undef AL
-        if (!e) e = dmalloc(m, &m->xch, m->xch_bytes);
-        if (!e) e = cudaMemsetAsync(m->xch, 0, m->xch_bytes, m->st);
-        if (!e) {
-            m->x = (float *)m->xch;
-            m->att = (float *)((char *)m->xch + m->xoff_att);
-            m->h = (float *)((char *)m->xch + m->xoff_h);
-        }
-    } else {
-        if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
-        if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
-        if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
-    }
+    if (!e) e = dmalloc(m, (void **)&m->x, (size_t)dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->q, (size_t)mx * 4);
+    if (!e) e = dmalloc(m, (void **)&m->att, (size_t)mx * 4);
+    if (!e) e = dmalloc(m, (void **)&m->h, (size_t)ff * 4);
     if (!e) e = dmalloc(m, (void **)&m->logits, (size_t)sp.n_vocab * 4);
     if (!e && world > 1) e = dmalloc(m, (void **)&m->logits_full, (size_t)d->vocab_size * 4);
     if (!e && world > 1) e = dmalloc(m, (void **)&m->pairs, (size_t)world * 2 * sizeof(int));

@@ -200,19 +200,22 @@ typedef struct {
      * dim and ff are the full vector lengths (the projections' columns).
      * This rank computes residual rows [row0, row0 + n_rows), SwiGLU rows
      * [ff0, ff0 + n_ff), attention-output elements [q0, q0 + n_heads*hd) of
-     * q_full, and vocabulary rows [vocab0, vocab0 + vocab).  x, att and h are
-     * the full vectors; its epilogues store each produced element into every
-     * rank's copy (peer_x[r] etc.: rank r's vector as mapped here, [rank] =
-     * x itself) and the ranks meet at flag barriers: peer_flags[r] is rank
-     * r's array of one epoch per writer, peer_pairs[r] its [world][2] argmax
-     * pairs.  io[5] holds the epoch base (0 on a fresh model). */
+     * q_full, and vocabulary rows [vocab0, vocab0 + vocab); x holds the
+     * residual rows it computes.  The vectors the ranks exchange (attention
+     * output, residual after o, SwiGLU output, residual after down, argmax
+     * pairs) travel as 8-byte words {value, epoch}: its epilogues store each
+     * produced element into every rank's exchange area (peer_ll[r]: rank r's
+     * area as mapped here, [rank] the local one), and the phase that reads a
+     * vector waits on the epochs of its words (tosk_step_ll_words long).
+     * io[5] holds the epoch base (0 on a fresh model). */
     int world, rank;
     int n_rows, n_ff, q_full;
     int q0, row0, ff0, vocab0;
-    float *peer_x[TOSK_MAX_WORLD], *peer_att[TOSK_MAX_WORLD], *peer_h[TOSK_MAX_WORLD];
-    unsigned *peer_flags[TOSK_MAX_WORLD];
-    int *peer_pairs[TOSK_MAX_WORLD];
+    unsigned long long *peer_ll[TOSK_MAX_WORLD];
 } tosk_step_t;
+
+/* 8-byte words of one rank's exchange area for a sharded step */
+size_t tosk_step_ll_words(int q_full, int dim, int ff);
 
 size_t tosk_step_sync_bytes(void);
 /* 0 when the fused step supports this configuration on this device */

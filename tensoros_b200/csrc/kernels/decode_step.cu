@@ -217,15 +217,24 @@ __device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target
   return !*reinterpret_cast<volatile int*>(&h->abort);
 }
 
-// Release / acquire at system scope on a word that another GPU reads or
-// writes (peer memory mapped into this process, or this GPU's memory that a
-// peer writes).
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Exchange words of a sharded step: {value bits, epoch} as one 8-byte
+// access, so a reader that sees the epoch sees the value with it (no fence
+// between them; the same idea as NCCL's low-latency protocol).  Volatile
+// accesses: every poll goes to L2, where the peers' NVLink stores land.
+__device__ __forceinline__ void ll_store(unsigned long long* p, uint32_t v, uint32_t e) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(e) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void ll_store2(unsigned long long* p, uint32_t v0, uint32_t v1, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v0), "r"(e), "r"(v1), "r"(e)
+               : "memory");
+}
+// two words (16-byte aligned): x, z values; y, w epochs
+__device__ __forceinline__ uint4 ll_load2(const unsigned long long* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
@@ -284,53 +293,58 @@ __device__ __forceinline__ void arg_better(float& v, int& i, float v2, int i2) {
   }
 }
 
-// Barrier of every worker thread of every CTA on every rank of a sharded
-// step.  Each CTA fences its stores (to this GPU and to the peers) at system
-// scope and counts itself in on this GPU's grid counter; the CTA that
-// completes the count publishes `epoch` in every rank's flag array (slot
-// `rank`, release at system scope), and every CTA waits until all ranks'
-// slots in its own array reach `epoch` (acquire).  Epochs only grow, so no
-// flag is ever reset while a peer may still read it.  Every wait is bounded
-// like grid_sync's; returns false, in every worker thread of the CTA alike,
-// when the step must stop.
-__device__ __forceinline__ bool xgpu_sync(Hdr* h, const Params& p, unsigned target, unsigned epoch, int* err) {
-  named_sync(B_WORKERS, kWorkers);
-  if (threadIdx.x == 32 && !*reinterpret_cast<volatile int*>(&h->abort)) {
-    __threadfence_system();
-    if (atomicAdd(p.s.sync, 1u) == target - 1) {
-      // every CTA of this GPU has arrived: publish this rank's epoch
-      __threadfence_system();
-      for (int r = 0; r < p.s.world; ++r) st_release_sys(p.s.peer_flags[r] + p.s.rank, epoch);
-    }
-    const unsigned* mine = p.s.peer_flags[p.s.rank];
-    const long long t0 = clock64();
-    for (int i = 0;; ++i) {
-      bool all = true;
-      for (int r = 0; r < p.s.world && all; ++r) all = (int)(ld_acquire_sys(mine + r) - epoch) >= 0;
-      if (all) break;
-      __nanosleep(32);
-      if ((i & 7) == 7) {
-        if (*reinterpret_cast<volatile int*>(err)) {
-          h->abort = 1;
-          break;
-        }
-        if (clock64() - t0 > kWaitCycles) {
-          atomicCAS(err, 0, 21);
-          h->abort = 1;
-          break;
-        }
+// Word offsets of the exchange area (the same on every rank): attention
+// output [q_full], residual after o [dim], SwiGLU output [ff], residual
+// after down [dim], argmax pairs [2 * TOSK_MAX_WORLD].
+enum { X_ATT = 0, X_XO = 1, X_H = 2, X_XD = 3 };
+__device__ __forceinline__ size_t ll_off(const Params& p, int kind) {
+  const size_t q = (size_t)p.s.q_full, d = (size_t)p.s.dim, f = (size_t)p.s.ff;
+  switch (kind) {
+    case X_ATT: return 0;
+    case X_XO: return q;
+    case X_H: return q + d;
+    case X_XD: return q + d + f;
+    default: return q + 2 * d + f;   // pairs
+  }
+}
+// Epoch of exchange `kind` of layer `layer` in this step.
+__device__ __forceinline__ uint32_t ll_epoch(const Hdr* h, int layer, int kind) {
+  return h->ebase + 4u * (uint32_t)layer + (uint32_t)kind + 1u;
+}
+// Element i of an exchanged vector into every rank's area.
+__device__ __forceinline__ void ll_store_all(const Params& p, int kind, size_t i, float v, uint32_t e) {
+  const size_t w = ll_off(p, kind) + i;
+  for (int r = 0; r < p.s.world; ++r) ll_store(p.s.peer_ll[r] + w, __float_as_uint(v), e);
+}
+// Waits (bounded) until both words of a pair carry epoch e; false when the
+// step must stop.  (Out of line: the spin is the rare path.)
+__device__ __noinline__ bool ll_wait(const unsigned long long* w, uint4& v, uint32_t e, Hdr* h, int* err) {
+  const long long t0 = clock64();
+  for (int i = 0;; ++i) {
+    __nanosleep(20);
+    v = ll_load2(w);
+    if (v.y == e && v.w == e) return true;
+    if ((i & 15) == 15) {
+      if (*reinterpret_cast<volatile int*>(&h->abort)) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        atomicCAS(err, 0, 21);
+        h->abort = 1;
+        return false;
       }
     }
-    __threadfence();
   }
-  named_sync(B_WORKERS, kWorkers);
-  return !*reinterpret_cast<volatile int*>(&h->abort);
 }
-
-// Stores v at index i of every rank's copy of a vector (peers[rank] is the
-// local one); one rank: the local store only.
-__device__ __forceinline__ void store_all(const Params& p, float* const* peers, size_t i, float v) {
-  for (int r = 0; r < p.s.world; ++r) peers[r][i] = v;
+__device__ __forceinline__ bool ll_ready(const unsigned long long* w, uint4& v, uint32_t e, Hdr* h, int* err) {
+  return (v.y == e && v.w == e) || ll_wait(w, v, e, h, err);
+}
+// Every worker thread of this CTA (the phases of a sharded step hand their
+// vectors over through the exchange words, not through grid barriers);
+// false, in all of them alike, when the step must stop.
+__device__ __forceinline__ bool cta_sync(Hdr* h) {
+  named_sync(B_WORKERS, kWorkers);
+  const bool ok = !*reinterpret_cast<volatile int*>(&h->abort);
+  named_sync(B_WORKERS, kWorkers);
+  return ok;
 }
 
 // ---------------------------------------------------------------------------
@@ -409,6 +423,36 @@ __device__ __forceinline__ float4 embed_chunk(const void* embd, int type, int di
   return v;
 }
 
+// Sharded step: the phase's input vector from every rank's exchange words
+// into X4 (nq 16-byte chunks): four rounds of chunks in flight per thread, a
+// chunk read again until its words carry the exchange's epoch.  Out of line,
+// so its registers do not weigh on the block-value loop.
+__device__ __noinline__ void ll_input(const Params& p, Hdr* h, float4* X4, int nq, int xk, int el, int ct, int* err) {
+  const unsigned long long* ll = p.s.peer_ll[p.s.rank] + ll_off(p, xk);
+  const uint32_t ep = ll_epoch(h, el, xk);
+  for (int qb = ct; qb < nq; qb += 4 * 32 * kCompute) {
+    uint4 w[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = qb + u * 32 * kCompute;
+      if (q < nq) {
+        w[u][0] = ll_load2(ll + 4 * (size_t)q);
+        w[u][1] = ll_load2(ll + 4 * (size_t)q + 2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = qb + u * 32 * kCompute;
+      if (q < nq) {
+        ll_ready(ll + 4 * (size_t)q, w[u][0], ep, h, err);
+        ll_ready(ll + 4 * (size_t)q + 2, w[u][1], ep, h, err);
+        X4[q] = make_float4(__uint_as_float(w[u][0].x), __uint_as_float(w[u][0].z), __uint_as_float(w[u][1].x),
+                            __uint_as_float(w[u][1].z));
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // compute warps: the phase's input vector in fixed point, then block values
 // ---------------------------------------------------------------------------
@@ -465,6 +509,9 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
         }
         X4[q] = v;
       }
+    } else if (p.s.world > 1) {
+      const int xk = kind == K_O ? X_ATT : kind == K_GU ? X_XO : kind == K_D ? X_H : X_XD;
+      ll_input(p, h, X4, nq, xk, (kind == K_QKV || kind == K_LM) ? layer - 1 : layer, ct, err);
     } else {
       for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(X4 + q, reinterpret_cast<const float4*>(src) + q);
     }
@@ -616,9 +663,15 @@ __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind
     }
   } else if (kind == K_O || kind == K_D) {
     const int gr = p.s.row0 + r;   // residual row (all of x on one GPU)
-    store_all(p, p.s.peer_x, gr, __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + gr), y));   // llm.c:717-718, 732-733
+    const float v = __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + gr), y);   // llm.c:717-718, 732-733
+    p.s.x[gr] = v;
+    if (p.s.world > 1) ll_store_all(p, kind == K_O ? X_XO : X_XD, gr, v, ll_epoch(h, layer, kind == K_O ? X_XO : X_XD));
   } else if (kind == K_GU) {
-    if ((r & 1) == 0) store_all(p, p.s.peer_h, p.s.ff0 + (r >> 1), __fmul_rn(ref_silu(y), partner));   // llm.c:726-729
+    if ((r & 1) == 0) {
+      const float v = __fmul_rn(ref_silu(y), partner);   // llm.c:726-729
+      if (p.s.world > 1) ll_store_all(p, X_H, p.s.ff0 + (r >> 1), v, ll_epoch(h, layer, X_H));
+      else p.s.h[r >> 1] = v;
+    }
   } else {
     p.s.logits[r] = y;
     if (!(y != y)) arg_better(bv, bi, y, p.s.vocab0 + r);
@@ -659,37 +712,22 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
   const bool x0_nan = p.s.rank == 0 && __ldcg(p.s.logits) != __ldcg(p.s.logits);
   int* io = p.s.io;
   if (p.s.world > 1) {
-    // every rank's (value, index) pair into every rank's pair array (rank 0
-    // marks a NaN logit 0 with index -2), published with the step's final
-    // epoch; every rank then reduces the same pairs in rank order
-    for (int r = 0; r < p.s.world; ++r) {
-      p.s.peer_pairs[r][2 * p.s.rank] = __float_as_int(best);
-      p.s.peer_pairs[r][2 * p.s.rank + 1] = x0_nan ? -2 : idx;
-    }
-    __threadfence_system();
-    for (int r = 0; r < p.s.world; ++r) st_release_sys(p.s.peer_flags[r] + p.s.rank, h->efinal);
-    const unsigned* mine = p.s.peer_flags[p.s.rank];
-    const long long t0 = clock64();
-    bool ok = true;
-    for (int it = 0;; ++it) {
-      bool all = true;
-      for (int r = 0; r < p.s.world && all; ++r) all = (int)(ld_acquire_sys(mine + r) - h->efinal) >= 0;
-      if (all) break;
-      __nanosleep(32);
-      if ((it & 7) == 7 && clock64() - t0 > kWaitCycles) {
-        atomicCAS(io + 3, 0, 22);
-        ok = false;
-        break;
-      }
-    }
+    // every rank's (value, index) pair into every rank's pair words (rank 0
+    // marks a NaN logit 0 with index -2) with the step's final epoch; every
+    // rank then reduces the same pairs in rank order
+    const size_t pw = ll_off(p, 4);
+    for (int r = 0; r < p.s.world; ++r)
+      ll_store2(p.s.peer_ll[r] + pw + 2 * p.s.rank, __float_as_uint(best), (uint32_t)(x0_nan ? -2 : idx), h->efinal);
+    const unsigned long long* mine = p.s.peer_ll[p.s.rank] + pw;
     best = 0.0f;
     idx = -1;
     bool nan0 = false;
-    const int* all_pairs = p.s.peer_pairs[p.s.rank];
-    for (int r = 0; ok && r < p.s.world; ++r) {
-      const int pi = __ldcg(all_pairs + 2 * r + 1);
+    for (int r = 0; r < p.s.world; ++r) {
+      uint4 v = ll_load2(mine + 2 * r);
+      if (!ll_ready(mine + 2 * r, v, h->efinal, h, io + 3)) break;
+      const int pi = (int)v.z;
       if (pi == -2) nan0 = true;
-      else arg_better(best, idx, __int_as_float(__ldcg(all_pairs + 2 * r)), pi);
+      else arg_better(best, idx, __uint_as_float(v.x), pi);
     }
     if (nan0 || idx < 0) idx = 0;
     io[5] = (int)h->efinal;
@@ -952,7 +990,8 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
       for (int d = gt; d < hd; d += 128) {
         float o = 0.0f;
         for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
-        store_all(p, p.s.peer_att, p.s.q0 + (size_t)hh * hd + d, o * inv);
+        if (p.s.world > 1) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+        else p.s.att[(size_t)hh * hd + d] = o * inv;
       }
     }
     named_sync(B_GROUP0 + grp, 128);   // es / red / wpart / s_last are reused by the next item
@@ -1077,7 +1116,8 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
     for (int d = wt; d < hd; d += kWorkers) {
       float o = part[d];
       for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
-      store_all(p, p.s.peer_att, p.s.q0 + (size_t)hh * hd + d, o * inv);
+      if (p.s.world > 1) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+      else p.s.att[(size_t)hh * hd + d] = o * inv;
     }
     named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
   }
@@ -1137,7 +1177,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   // else split-K scores then softmax*V), o, gate|up, down; then the LM head.
   // One call site per role keeps every role inlined once.
   const bool short_ctx = h->pos + 1 <= kHeadMaxN;
-  unsigned nsync = 0, nx = 0;
+  unsigned nsync = 0;
   const int nph = 6 * p.s.n_layers + 1;
   for (int ph = 0; ph < nph; ++ph) {
     const int l = ph / 6, r = ph - 6 * l;
@@ -1154,12 +1194,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       attn_pv<ESZ>(p, h, P, l);
     }
     // sharded: the vectors the next phase reads in full (attention output,
-    // residual, SwiGLU output) come from every rank; the q|k|v -> attention
-    // and scores -> softmax*V hand-offs stay on this GPU
-    const bool cross = p.s.world > 1 && (r >= 2 || (r == 1 && short_ctx));
-    if (cross) {
-      if (!xgpu_sync(h, p, (++nsync) * gridDim.x, h->ebase + (++nx), err)) return;
-    } else if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) {
+    // residual, SwiGLU output) come from every rank through the exchange
+    // words, which the readers wait on; only the q|k|v -> attention and
+    // scores -> softmax*V hand-offs (q, the KV rows, the scores: this GPU's
+    // own) need the grid barrier
+    const bool grid = p.s.world == 1 || r == 0 || (r == 1 && !short_ctx);
+    if (grid) {
+      if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) return;
+    } else if (!cta_sync(h)) {
       return;
     }
   }
@@ -1172,6 +1214,10 @@ using namespace tos;
 using namespace tos::step;
 
 extern "C" size_t tosk_step_sync_bytes(void) { return 256 + (size_t)kMaxGrid * 8; }
+
+extern "C" size_t tosk_step_ll_words(int q_full, int dim, int ff) {
+  return (size_t)q_full + 2 * (size_t)dim + (size_t)ff + 2 * TOSK_MAX_WORLD;
+}
 
 static inline int round_up_i(int v, int a) { return (v + a - 1) / a * a; }
 static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -1237,19 +1283,14 @@ static int plan(const tosk_step_t* s, Params* p) {
     t.n_ff = s->ff;
     t.q_full = q_dim;
     t.q0 = t.row0 = t.ff0 = t.vocab0 = 0;
-    t.peer_x[0] = s->x;
-    t.peer_att[0] = s->att;
-    t.peer_h[0] = s->h;
   } else {
     if (t.world > TOSK_MAX_WORLD || t.rank < 0 || t.rank >= t.world) return (int)cudaErrorInvalidValue;
     if (t.n_rows <= 0 || t.n_ff <= 0 || t.q_full < q_dim || t.q0 < 0 || t.q0 + q_dim > t.q_full ||
-        t.row0 < 0 || t.row0 + t.n_rows > s->dim || t.ff0 < 0 || t.ff0 + t.n_ff > s->ff || t.vocab0 < 0)
+        t.row0 < 0 || t.row0 + t.n_rows > s->dim || t.ff0 < 0 || t.ff0 + t.n_ff > s->ff || t.vocab0 < 0 ||
+        t.q_full % 32 != 0)
       return (int)cudaErrorInvalidValue;
     for (int r = 0; r < t.world; ++r)
-      if (!t.peer_x[r] || !t.peer_att[r] || !t.peer_h[r] || !t.peer_flags[r] || !t.peer_pairs[r])
-        return (int)cudaErrorInvalidValue;
-    if (t.peer_x[t.rank] != s->x || t.peer_att[t.rank] != s->att || t.peer_h[t.rank] != s->h)
-      return (int)cudaErrorInvalidValue;
+      if (!t.peer_ll[r] || (reinterpret_cast<uintptr_t>(t.peer_ll[r]) & 15)) return (int)cudaErrorInvalidValue;
   }
   int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
   if (!e) e = make_geo(t.n_rows, t.q_full, s->wtype, 1, p->g[K_O]);
