@@ -216,6 +216,14 @@ class Reference(_Ops):
         L.ref_model_create.restype, L.ref_model_create.argtypes = vp, [C.POINTER(_RefDesc)]
         L.q4_dot_block.restype, L.q4_dot_block.argtypes = f32, [vp, vp]
         L.q4_gemv.restype, L.q4_gemv.argtypes = None, [vp, vp, vp, i32, i32]
+        L.ref_sample_at.restype, L.ref_sample_at.argtypes = i32, [vp, i32, f32, C.c_uint32]
+
+    def sample_at(self, logits, temperature, tsc_lo):
+        """The reference's own llm_sample with its timestamp read returning
+        tsc_lo (oracle/ref_llm_hosted.c); -1 where the timestamp cannot be
+        scripted on this host."""
+        x = _f32(logits)
+        return int(self.lib.ref_sample_at(_p(x), len(x), float(temperature), int(tsc_lo) & 0xFFFFFFFF))
 
     def embed(self, embd, t, dim, tok):
         out = np.empty(dim, dtype=np.float32)

@@ -18,6 +18,7 @@
  *    the portable C path of llm_gemv (llm.c:343-348), as fact 3 of the survey
  *    of the reference requires.
  */
+#define _GNU_SOURCE   /* ucontext register names for the timestamp trap below */
 #include "runtime/nn/llm.h"
 
 #undef LLM_MAX_DIM
@@ -172,3 +173,66 @@ int ref_generate_greedy(void *p, const int *prompt, int n_prompt, int n_gen, int
     free(logits);
     return g;
 }
+
+/* ---- llm_sample with a chosen timestamp ----
+ *
+ * llm_sample (llm.c:1177-1246) draws from the CPU timestamp (rdtsc,
+ * llm.c:1228-1230).  To pin the whole sampler, the draw included, the
+ * harness makes rdtsc trap for the calling thread (prctl PR_SET_TSC,
+ * PR_TSC_SIGSEGV), answers the trap with the chosen value in EDX:EAX and
+ * steps over the two-byte instruction, then restores both.  The reference
+ * code runs unmodified; only its timestamp source is scripted. */
+#if defined(__x86_64__) && defined(__linux__)
+#include <signal.h>
+#include <sys/prctl.h>
+#include <ucontext.h>
+
+static volatile uint32_t g_tsc_lo;
+static volatile int g_tsc_used;
+
+static void tsc_trap(int sig, siginfo_t *si, void *ctx)
+{
+    (void)si;
+    ucontext_t *uc = (ucontext_t *)ctx;
+    const unsigned char *ip = (const unsigned char *)uc->uc_mcontext.gregs[REG_RIP];
+    if (ip[0] == 0x0F && ip[1] == 0x31) {   /* rdtsc */
+        uc->uc_mcontext.gregs[REG_RAX] = g_tsc_lo;
+        uc->uc_mcontext.gregs[REG_RDX] = 0;
+        uc->uc_mcontext.gregs[REG_RIP] += 2;
+        g_tsc_used++;
+        return;
+    }
+    /* any other fault: restore the default action and let it happen again */
+    signal(sig, SIG_DFL);
+}
+
+/* llm_sample(logits, n, temperature) with rdtsc returning tsc_lo.  Returns
+ * the reference's token, -1 when the timestamp cannot be scripted here (no
+ * PR_SET_TSC), or -2 when the reference did not read the timestamp (the
+ * greedy limit). */
+int ref_sample_at(const float *logits, int n, float temperature, uint32_t tsc_lo)
+{
+    struct sigaction sa, old;
+    memset(&sa, 0, sizeof(sa));
+    sa.sa_sigaction = tsc_trap;
+    sa.sa_flags = SA_SIGINFO;
+    sigemptyset(&sa.sa_mask);
+    if (sigaction(SIGSEGV, &sa, &old) != 0) return -1;
+    g_tsc_lo = tsc_lo;
+    g_tsc_used = 0;
+    if (prctl(PR_SET_TSC, PR_TSC_SIGSEGV, 0, 0, 0) != 0) {
+        sigaction(SIGSEGV, &old, NULL);
+        return -1;
+    }
+    int tok = llm_sample(logits, n, temperature);
+    prctl(PR_SET_TSC, PR_TSC_ENABLE, 0, 0, 0);
+    sigaction(SIGSEGV, &old, NULL);
+    return g_tsc_used ? tok : (temperature <= 0.001f ? tok : -2);
+}
+#else
+int ref_sample_at(const float *logits, int n, float temperature, uint32_t tsc_lo)
+{
+    (void)logits; (void)n; (void)temperature; (void)tsc_lo;
+    return -1;
+}
+#endif

@@ -8,8 +8,12 @@ pin both the C restatement (oracle/tos_oracle.c) and the GPU path:
   ops.npz            per-operator inputs and reference outputs
   tiny_llama.npz     tiny-llama (6L/288d, Q8_0, fp32 KV) greedy ids + logits
   llama7b_short.npz  Llama-2-7B-shaped Q4_0 model, fp32 KV, 4 prompt + 4 greedy
+  sample.npz         llm_sample's tokens for seeded logits, temperatures and
+                     timestamp words (the reference's own sampler, its
+                     timestamp read scripted: oracle/ref_llm_hosted.c)
 
 Run from the repository root after building:  python tests/golden/make_golden.py
+(`python tests/golden/make_golden.py sample` writes sample.npz alone)
 """
 from __future__ import annotations
 
@@ -158,5 +162,50 @@ def main():
     print("llama7b_short.npz:", ids7)
 
 
+SAMPLE_TEMPS = [0.0005, 0.2, 0.7, 1.0, 1.9]
+SAMPLE_WORDS = 24
+
+
+def sample_cases():
+    """Logit vectors for llm_sample (llm.c:1143-1246): plain, ties across the
+    top-40 cut, ties exactly at the 40th value, signed zeros, fewer than 40
+    candidates, many duplicates."""
+    c0 = W.normal_f32(32000, SEED, 200, 0.0, 3.0)
+    c1 = W.normal_f32(32000, SEED, 201).copy()
+    c1[(np.arange(60) * 523 + 7) % 32000] = 4.0
+    c2 = W.normal_f32(5000, SEED, 202).copy()
+    c2[(np.arange(7) * 701 + 3) % 5000] = np.sort(c2)[-40]
+    c3 = np.zeros(1000, np.float32)
+    c3[::3] = -0.0
+    c3[500] = 1.0
+    c4 = W.normal_f32(17, SEED, 203, 0.0, 2.0)
+    c5 = (np.round(W.normal_f32(32000, SEED, 204) * 4) / 4).astype(np.float32)
+    return [c0, c1, c2, c3, c4, c5]
+
+
+def sample_golden(R):
+    cases = sample_cases()
+    # timestamp words: a fixed LCG sequence (the reference mixes them itself)
+    words = np.empty((len(cases), len(SAMPLE_TEMPS), SAMPLE_WORDS), np.uint32)
+    v = 0x2545F491
+    for idx in np.ndindex(words.shape):
+        v = (v * 1664525 + 1013904223) & 0xFFFFFFFF
+        words[idx] = v
+    toks = np.empty(words.shape, np.int32)
+    for ci, x in enumerate(cases):
+        for ti, t in enumerate(SAMPLE_TEMPS):
+            for k in range(SAMPLE_WORDS):
+                toks[ci, ti, k] = R.sample_at(x, t, int(words[ci, ti, k]))
+    if np.any(toks < 0):
+        raise SystemExit("the timestamp read could not be scripted on this host")
+    g = {f"x{i}": x for i, x in enumerate(cases)}
+    np.savez_compressed(OUT / "sample.npz", temps=np.array(SAMPLE_TEMPS, np.float32), words=words, tokens=toks, **g)
+    print("sample.npz:", toks.size, "draws")
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["sample"]:
+        sample_golden(pyoracle.reference())
+    else:
+        main()
+        sample_golden(pyoracle.reference())

@@ -1,14 +1,29 @@
-"""Device sampling (tos_sample / tos_sample_dev) against the oracle's
-restatement of llm_sample (llm.c:1143-1246) with the same 32-bit entropy
-word in place of the reference's timestamp: the same token for every
-(logits, temperature, entropy), including equal logits at the top-40
-boundary, +0.0 / -0.0, vocabularies shorter than 40 and the greedy limit."""
+"""Device sampling (tos_sample / tos_sample_dev) with a 32-bit entropy word
+in place of the reference's timestamp: the reference's own llm_sample token
+(llm.c:1143-1246, tests/golden/sample.npz, drawn with its timestamp read
+scripted to the same word) for every committed case, and the oracle's
+restatement on further random words: equal logits at the top-40 boundary,
++0.0 / -0.0, vocabularies shorter than 40 and the greedy limit."""
 import numpy as np
 import pytest
 
+from conftest import GOLDEN
 from tensoros_b200 import _ffi
 
 pytestmark = pytest.mark.gpu
+
+
+def test_sample_matches_reference_draws(gpu):
+    lib = _ffi.nn()
+    g = np.load(GOLDEN / "sample.npz")
+    temps, words, toks = g["temps"], g["words"], g["tokens"]
+    for ci in range(toks.shape[0]):
+        x = np.ascontiguousarray(g[f"x{ci}"])
+        for ti, t in enumerate(temps):
+            for k in range(toks.shape[2]):
+                got = lib.tos_sample(x.ctypes.data, len(x), float(t), int(words[ci, ti, k]))
+                assert lib.tos_last_status() == 0
+                assert got == toks[ci, ti, k], (ci, float(t), k, got, int(toks[ci, ti, k]))
 
 
 def cases():
