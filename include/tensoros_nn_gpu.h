@@ -263,6 +263,31 @@ size_t tos_model_device_bytes(const tos_model_t *m);
 /* 1 when each token runs as the one fused kernel (see fused_step) */
 int tos_model_fused(const tos_model_t *m);
 
+/* ---------------------------------------------- fp32 transformer engine
+ * The reference's other decoder, runtime/nn/transformer.c (fp32 weights,
+ * KV cache [layer][head][seq][head_dim], eps 1e-5, the activations of
+ * runtime/tensor/tensor_cpu.c), on the GPU with its results bit for bit. */
+void tos_tf_rmsnorm(float *out, const float *x, const float *w, int dim);                   /* transformer.c:92 */
+void tos_tf_swiglu_ffn(float *out, const float *x, const float *w1, const float *w2,
+                       const float *w3, int dim, int ff_dim);                             /* transformer.c:121 */
+/* Mirrors tf_model_t / tf_block_weights_t (transformer.h): host fp32 arrays,
+ * per-layer pointer arrays of num_layers entries; wq/wk/wv/wo [dim][dim],
+ * w1/w3 [ff_dim][dim], w2 [dim][ff_dim], tok_embed [vocab_size][dim]. */
+typedef struct {
+    int dim, num_heads, ff_dim, num_layers, vocab_size, max_seq;
+    const float *const *wq, *const *wk, *const *wv, *const *wo;
+    const float *const *w1, *const *w2, *const *w3;
+    const float *const *rms_att, *const *rms_ffn;
+    const float *tok_embed, *rms_final;
+} tos_tf_desc_t;
+typedef struct tos_tf_model tos_tf_model_t;
+int tos_tf_model_create(tos_tf_model_t **m, const tos_tf_desc_t *desc);           /* kv_cache_init, transformer.c:46 */
+void tos_tf_model_destroy(tos_tf_model_t *m);
+int tos_tf_reset(tos_tf_model_t *m);                                               /* kv_cache_reset, transformer.c:67 */
+int tos_tf_cached_attention(tos_tf_model_t *m, float *out, const float *q, const float *k, const float *v,
+                            int layer, int head, int pos);                         /* transformer.c:193 */
+int tos_tf_forward_token(tos_tf_model_t *m, float *logits, const float *tok_embed, int pos); /* transformer.c:255 */
+
 /* ------------------------------------------------------------ GGUF files
  * The container of runtime/nn (gguf.c:204-423): v2/v3 headers, metadata,
  * tensor infos; tensor data is used in place (the caller's buffer, or a

@@ -217,6 +217,29 @@ class Reference(_Ops):
         L.q4_dot_block.restype, L.q4_dot_block.argtypes = f32, [vp, vp]
         L.q4_gemv.restype, L.q4_gemv.argtypes = None, [vp, vp, vp, i32, i32]
         L.ref_sample_at.restype, L.ref_sample_at.argtypes = i32, [vp, i32, f32, C.c_uint32]
+        L.ref_tf_rmsnorm.restype, L.ref_tf_rmsnorm.argtypes = None, [vp, vp, vp, i32]
+        L.ref_tf_swiglu_ffn.restype, L.ref_tf_swiglu_ffn.argtypes = None, [vp, vp, vp, vp, vp, i32, i32]
+        L.ref_tf_model_init.restype, L.ref_tf_model_init.argtypes = i32, [vp]
+        L.ref_tf_forward_token.restype, L.ref_tf_forward_token.argtypes = None, [vp, vp, i32]
+        L.ref_tf_cached_attention.restype, L.ref_tf_cached_attention.argtypes = None, [vp, vp, vp, vp, i32, i32, i32]
+        L.ref_tf_reset.restype, L.ref_tf_reset.argtypes = None, []
+
+    # ---- the fp32 transformer engine (runtime/nn/transformer.c), its own code
+    def tf_rmsnorm(self, x, w):
+        x, w = _f32(x), _f32(w)
+        out = np.empty(len(x), np.float32)
+        self.lib.ref_tf_rmsnorm(_p(out), _p(x), _p(w), len(x))
+        return out
+
+    def tf_swiglu_ffn(self, x, w1, w2, w3, dim, ff_dim):
+        out = np.empty(dim, np.float32)
+        self.lib.ref_tf_swiglu_ffn(_p(out), _p(_f32(x)), _p(_f32(w1)), _p(_f32(w2)), _p(_f32(w3)), dim, ff_dim)
+        return out
+
+    def tf_model(self, tf):
+        """The engine over a workloads.TfModel (one at a time: its KV store is
+        static)."""
+        return _TfRef(self, tf)
 
     def sample_at(self, logits, temperature, tsc_lo):
         """The reference's own llm_sample with its timestamp read returning
@@ -289,6 +312,30 @@ class _Model:
         out = np.zeros(max(1, n_gen), dtype=np.int32)
         n = getattr(self.ops.lib, self.px + "generate_greedy")(self.h, _p(p), len(p), n_gen, _p(out))
         return out[:n]
+
+
+class _TfRef:
+    def __init__(self, ref, tf):
+        from tensoros_b200 import _ffi
+        self.ref, self.tf = ref, tf
+        self.desc = tf.fill_desc(_ffi.TfDesc())
+        if ref.lib.ref_tf_model_init(C.byref(self.desc)) != 0:
+            raise ValueError("shape beyond the harness limits")
+
+    def forward(self, token, pos):
+        c = self.tf.cfg
+        row = np.ascontiguousarray(self.tf.tok_embed[token * c["dim"]:(token + 1) * c["dim"]])
+        out = np.empty(c["vocab_size"], np.float32)
+        self.ref.lib.ref_tf_forward_token(_p(out), _p(row), pos)
+        return out
+
+    def cached_attention(self, q, k, v, layer, head, pos):
+        out = np.empty(len(q), np.float32)
+        self.ref.lib.ref_tf_cached_attention(_p(out), _p(_f32(q)), _p(_f32(k)), _p(_f32(v)), layer, head, pos)
+        return out
+
+    def reset(self):
+        self.ref.lib.ref_tf_reset()
 
 
 def _fill_ref(d, synth):

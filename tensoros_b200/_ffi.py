@@ -43,6 +43,13 @@ class ShardPlan(C.Structure):
                                    "vocab0", "n_vocab")]
 
 
+class TfDesc(C.Structure):
+    """tos_tf_desc_t (the fp32 engine of runtime/nn/transformer.c)"""
+    _fields_ = [(n, i32) for n in ("dim", "num_heads", "ff_dim", "num_layers", "vocab_size", "max_seq")] + \
+               [(n, C.POINTER(vp)) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "rms_att", "rms_ffn")] + \
+               [("tok_embed", vp), ("rms_final", vp)]
+
+
 # name -> (restype, argtypes)
 NN_FUNCS = {
     "tos_status_string": (C.c_char_p, [i32]),
@@ -125,6 +132,13 @@ NN_FUNCS = {
     "tos_argmax_sharded_dev": (i32, [vp, i32, i32, vp, vp]),
     "tos_gemm_workspace_bytes": (sz, [i32, i32, i32]),
     "tos_gemm_dev": (i32, [vp, vp, i32, vp, vp, sz, vp]),
+    "tos_tf_rmsnorm": (None, [vp, vp, vp, i32]),
+    "tos_tf_swiglu_ffn": (None, [vp, vp, vp, vp, vp, i32, i32]),
+    "tos_tf_model_create": (i32, [C.POINTER(vp), C.POINTER(TfDesc)]),
+    "tos_tf_model_destroy": (None, [vp]),
+    "tos_tf_reset": (i32, [vp]),
+    "tos_tf_cached_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32]),
+    "tos_tf_forward_token": (i32, [vp, vp, vp, i32]),
 }
 
 SYNTH_FUNCS = {

@@ -163,6 +163,19 @@ int tosk_attention(float *out, const float *q, const void *k_cache, const void *
 
 int tosk_num_sms(void);
 
+/* ---- fp32 transformer engine (tf_engine.cu; runtime/nn/transformer.c) ---- */
+/* y = W x, W rows x cols row-major; chunk_order 1: sum += ((p0+p1)+p2)+p3
+ * over groups of four, 0: sum += w*x in order */
+int tosk_tf_matvec(const float *W, const float *x, float *y, int rows, int cols, int chunk_order, cudaStream_t st);
+int tosk_tf_rmsnorm(float *out, const float *x, const float *w, int dim, cudaStream_t st);
+int tosk_tf_silu_mul(float *g, const float *u, int n, cudaStream_t st);
+int tosk_tf_add(float *x, const float *y, int n, cudaStream_t st);
+/* tf_cached_attention for heads [h0, h0+nh) of one layer: head i's q/k/v at
+ * q/k/v + i*qstride, output at out + i*ostride; cache [layers][n_heads][max_seq][hd] */
+int tosk_tf_attention(float *out, int ostride, const float *q, const float *k, const float *v, int qstride,
+                      float *kc, float *vc, int layer, int h0, int nh, int n_heads, int hd, int max_seq,
+                      int pos, cudaStream_t st);
+
 /* ---- fused decode step (decode_step.cu): one cooperative kernel per token
  * runs every layer, the LM head and the greedy argmax with FAST arithmetic
  * (tosk_gemv FAST block values, FAST attention) ---- */

@@ -183,3 +183,53 @@ def make_model(cfg: dict, seed: int = SEED, n_layers: int | None = None) -> Synt
 
 def prompt_tokens(cfg: dict, seed: int = SEED) -> np.ndarray:
     return tokens(cfg["n_prompt"], cfg["vocab_size"], seed)
+
+
+# The fp32 transformer engine (runtime/nn/transformer.c): no quantisation,
+# tied output embedding, eps 1e-5.  Parity shapes within the engine's
+# raised harness limits (dim <= 512, max_seq <= 1024).
+TF_SMALL = dict(name="tf-engine-2L-64d", dim=64, num_heads=4, ff_dim=128, num_layers=2, vocab_size=32, max_seq=128)
+TF_MEDIUM = dict(name="tf-engine-4L-256d", dim=256, num_heads=8, ff_dim=688, num_layers=4, vocab_size=1000,
+                 max_seq=512)
+
+
+@dataclass
+class TfModel:
+    cfg: dict
+    seed: int
+    layers: list = field(default_factory=list)
+    tok_embed: np.ndarray = None
+    rms_final: np.ndarray = None
+    _keep: list = field(default_factory=list)
+
+    def fill_desc(self, desc):
+        """Fill a ctypes struct with tos_tf_desc_t / the harness's ref_tf_desc_t fields."""
+        c = self.cfg
+        for k in ("dim", "num_heads", "ff_dim", "num_layers", "vocab_size", "max_seq"):
+            setattr(desc, k, c[k])
+        for key in ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "rms_att", "rms_ffn"):
+            arr = (C.c_void_p * len(self.layers))(*[_ptr(l[key]) for l in self.layers])
+            self._keep.append(arr)
+            setattr(desc, key, C.cast(arr, C.POINTER(C.c_void_p)))
+        desc.tok_embed = _ptr(self.tok_embed)
+        desc.rms_final = _ptr(self.rms_final)
+        return desc
+
+
+def make_tf_model(cfg: dict, seed: int = SEED) -> TfModel:
+    """fp32 weights ~N(0, 1/dim) (rows of a projection keep activations near
+    unit scale), norm weights 1 + 0.1 N(0,1), embeddings N(0,1)."""
+    d, f = cfg["dim"], cfg["ff_dim"]
+    m = TfModel(cfg=dict(cfg), seed=seed)
+    s_d, s_f = 1.0 / np.sqrt(d), 1.0 / np.sqrt(f)
+    for l in range(cfg["num_layers"]):
+        base = 3_000_000 + 100 * l
+        m.layers.append(dict(
+            wq=normal_f32(d * d, seed, base + 0, 0.0, s_d), wk=normal_f32(d * d, seed, base + 1, 0.0, s_d),
+            wv=normal_f32(d * d, seed, base + 2, 0.0, s_d), wo=normal_f32(d * d, seed, base + 3, 0.0, s_d),
+            w1=normal_f32(f * d, seed, base + 4, 0.0, s_d), w2=normal_f32(d * f, seed, base + 5, 0.0, s_f),
+            w3=normal_f32(f * d, seed, base + 6, 0.0, s_d),
+            rms_att=normal_f32(d, seed, base + 7, 1.0, 0.1), rms_ffn=normal_f32(d, seed, base + 8, 1.0, 0.1)))
+    m.tok_embed = normal_f32(cfg["vocab_size"] * d, seed, 3_999_000)
+    m.rms_final = normal_f32(d, seed, 3_999_001, 1.0, 0.1)
+    return m

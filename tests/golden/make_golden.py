@@ -11,6 +11,9 @@ pin both the C restatement (oracle/tos_oracle.c) and the GPU path:
   sample.npz         llm_sample's tokens for seeded logits, temperatures and
                      timestamp words (the reference's own sampler, its
                      timestamp read scripted: oracle/ref_llm_hosted.c)
+  tf.npz             the fp32 transformer engine (runtime/nn/transformer.c):
+                     tf_rmsnorm, tf_swiglu_ffn, tf_cached_attention and
+                     tf_forward_token logits of two seeded models
 
 Run from the repository root after building:  python tests/golden/make_golden.py
 (`python tests/golden/make_golden.py sample` writes sample.npz alone)
@@ -203,9 +206,35 @@ def sample_golden(R):
     print("sample.npz:", toks.size, "draws")
 
 
+def tf_golden(R):
+    """The reference engine's outputs for the seeded cases of tests/tf_cases.py
+    (inputs regenerated by the tests, not stored)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import tf_cases as T
+    g = {}
+    for dim in T.RMS_DIMS:
+        g[f"rms_{dim}_out"] = R.tf_rmsnorm(*T.rms_case(dim))
+    for dim, ff in T.FFN_SHAPES:
+        g[f"ffn_{dim}_out"] = R.tf_swiglu_ffn(*T.ffn_case(dim, ff), dim, ff)
+    for tag in T.MODELS:
+        tf, toks = T.model_case(tag)
+        m = R.tf_model(tf)
+        g[f"model_{tag}_logits"] = np.stack([m.forward(int(t), p) for p, t in enumerate(toks)])
+    tf, _ = T.model_case("small")
+    m = R.tf_model(tf)
+    qkv = T.attn_qkv()
+    g["attn_out"] = np.stack([m.cached_attention(qkv[p, 0], qkv[p, 1], qkv[p, 2], T.ATTN["layer"], T.ATTN["head"], p)
+                              for p in range(T.ATTN["steps"])])
+    np.savez_compressed(OUT / "tf.npz", **g)
+    print("tf.npz:", len(g), "arrays")
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["sample"]:
         sample_golden(pyoracle.reference())
+    elif sys.argv[1:] == ["tf"]:
+        tf_golden(pyoracle.reference())
     else:
         main()
         sample_golden(pyoracle.reference())
+        tf_golden(pyoracle.reference())
