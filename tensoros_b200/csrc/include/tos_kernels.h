@@ -220,7 +220,9 @@ typedef struct {
      * produced element into every rank's exchange area (peer_ll[r]: rank r's
      * area as mapped here, [rank] the local one), and the phase that reads a
      * vector waits on the epochs of its words (tosk_step_ll_words long).
-     * io[5] holds the epoch base (0 on a fresh model). */
+     * On one GPU peer_ll[0] may name a local area (the phases then hand
+     * their vectors over the same way instead of at grid barriers) or be
+     * NULL.  io[5] holds the epoch base (0 on a fresh model). */
     int world, rank;
     int n_rows, n_ff, q_full;
     int q0, row0, ff0, vocab0;

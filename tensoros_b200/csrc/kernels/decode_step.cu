@@ -82,6 +82,7 @@ struct Geo {
 
 struct Params {
   tosk_step_t s;
+  int ll;          // vectors handed between phases as exchange words (peer_ll set; always when sharded)
   Geo g[K_N];
   float* S;        // attention workspace (the FAST attention layout)
   float* cmax;
@@ -509,7 +510,7 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
         }
         X4[q] = v;
       }
-    } else if (p.s.world > 1) {
+    } else if (p.ll) {
       const int xk = kind == K_O ? X_ATT : kind == K_GU ? X_XO : kind == K_D ? X_H : X_XD;
       ll_input(p, h, X4, nq, xk, (kind == K_QKV || kind == K_LM) ? layer - 1 : layer, ct, err);
     } else {
@@ -665,11 +666,11 @@ __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind
     const int gr = p.s.row0 + r;   // residual row (all of x on one GPU)
     const float v = __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + gr), y);   // llm.c:717-718, 732-733
     p.s.x[gr] = v;
-    if (p.s.world > 1) ll_store_all(p, kind == K_O ? X_XO : X_XD, gr, v, ll_epoch(h, layer, kind == K_O ? X_XO : X_XD));
+    if (p.ll) ll_store_all(p, kind == K_O ? X_XO : X_XD, gr, v, ll_epoch(h, layer, kind == K_O ? X_XO : X_XD));
   } else if (kind == K_GU) {
     if ((r & 1) == 0) {
       const float v = __fmul_rn(ref_silu(y), partner);   // llm.c:726-729
-      if (p.s.world > 1) ll_store_all(p, X_H, p.s.ff0 + (r >> 1), v, ll_epoch(h, layer, X_H));
+      if (p.ll) ll_store_all(p, X_H, p.s.ff0 + (r >> 1), v, ll_epoch(h, layer, X_H));
       else p.s.h[r >> 1] = v;
     }
   } else {
@@ -693,20 +694,34 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
     h->ai[cw] = bi;
   }
   named_sync(B_CHAIN, 32 * kChain);
-  if (threadIdx.x != 32) return;
-  float v = h->av[0];
-  int i = h->ai[0];
-  for (int c = 1; c < kChain; ++c) arg_better(v, i, h->av[c], h->ai[c]);
+  if (threadIdx.x >= 64) return;   // warp 1 finishes
   int* pairs = reinterpret_cast<int*>(p.s.sync + 64);
-  pairs[2 * blockIdx.x] = __float_as_int(v);
-  pairs[2 * blockIdx.x + 1] = i;
-  __threadfence();
-  if (atomicAdd(p.s.sync + 1, 1u) != gridDim.x - 1) return;
-  __threadfence();
+  int last = 0;
+  if (threadIdx.x == 32) {
+    float v = h->av[0];
+    int i = h->ai[0];
+    for (int c = 1; c < kChain; ++c) arg_better(v, i, h->av[c], h->ai[c]);
+    pairs[2 * blockIdx.x] = __float_as_int(v);
+    pairs[2 * blockIdx.x + 1] = i;
+    __threadfence();
+    last = atomicAdd(p.s.sync + 1, 1u) == gridDim.x - 1;
+    if (last) __threadfence();
+  }
+  if (!__shfl_sync(0xffffffffu, last, 0)) return;
+  // the last CTA: the warp loads the CTAs' pairs side by side and reduces
+  // them (arg_better is associative and commutative, so the order of the
+  // combination does not change the result)
   float best = 0.0f;
   int idx = -1;
-  for (unsigned k = 0; k < gridDim.x; ++k)
+  for (unsigned k = lane; k < gridDim.x; k += 32)
     arg_better(best, idx, __int_as_float(__ldcg(pairs + 2 * k)), __ldcg(pairs + 2 * k + 1));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_down_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_down_sync(0xffffffffu, idx, o);
+    arg_better(best, idx, v2, i2);
+  }
+  if (lane != 0) return;
   // llm.c:1130: x[0] is the starting candidate; it stays when NaN or unbeaten
   // (logit 0 is the first row of rank 0's slice)
   const bool x0_nan = p.s.rank == 0 && __ldcg(p.s.logits) != __ldcg(p.s.logits);
@@ -730,10 +745,12 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
       else arg_better(best, idx, __uint_as_float(v.x), pi);
     }
     if (nan0 || idx < 0) idx = 0;
-    io[5] = (int)h->efinal;
   } else if (x0_nan || idx < 0) {
     idx = 0;
   }
+  // the next step's exchange words carry later epochs than every word of
+  // this one
+  if (p.ll) io[5] = (int)h->efinal;
   io[2] = idx;
   if (p.s.chained) {
     const int k = io[4];
@@ -990,7 +1007,7 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
       for (int d = gt; d < hd; d += 128) {
         float o = 0.0f;
         for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
-        if (p.s.world > 1) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+        if (p.ll) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
         else p.s.att[(size_t)hh * hd + d] = o * inv;
       }
     }
@@ -1116,7 +1133,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
     for (int d = wt; d < hd; d += kWorkers) {
       float o = part[d];
       for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
-      if (p.s.world > 1) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+      if (p.ll) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
       else p.s.att[(size_t)hh * hd + d] = o * inv;
     }
     named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
@@ -1193,12 +1210,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     } else {
       attn_pv<ESZ>(p, h, P, l);
     }
-    // sharded: the vectors the next phase reads in full (attention output,
-    // residual, SwiGLU output) come from every rank through the exchange
-    // words, which the readers wait on; only the q|k|v -> attention and
-    // scores -> softmax*V hand-offs (q, the KV rows, the scores: this GPU's
-    // own) need the grid barrier
-    const bool grid = p.s.world == 1 || r == 0 || (r == 1 && !short_ctx);
+    // with exchange words, the vectors the next phase reads in full
+    // (attention output, residual, SwiGLU output; from every rank when
+    // sharded) carry their own readiness, which the readers wait on; only
+    // the q|k|v -> attention and scores -> softmax*V hand-offs (q, the KV
+    // rows, the scores) need the grid barrier
+    const bool grid = !p.ll || r == 0 || (r == 1 && !short_ctx);
     if (grid) {
       if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) return;
     } else if (!cta_sync(h)) {
@@ -1292,6 +1309,8 @@ static int plan(const tosk_step_t* s, Params* p) {
     for (int r = 0; r < t.world; ++r)
       if (!t.peer_ll[r] || (reinterpret_cast<uintptr_t>(t.peer_ll[r]) & 15)) return (int)cudaErrorInvalidValue;
   }
+  if (t.world == 1 && t.peer_ll[0] && (reinterpret_cast<uintptr_t>(t.peer_ll[0]) & 15)) return (int)cudaErrorInvalidValue;
+  p->ll = t.peer_ll[0] != nullptr;
   int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
   if (!e) e = make_geo(t.n_rows, t.q_full, s->wtype, 1, p->g[K_O]);
   if (!e) e = make_geo(2 * t.n_ff, s->dim, s->wtype, 2, p->g[K_GU]);
