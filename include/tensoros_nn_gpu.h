@@ -288,6 +288,60 @@ int tos_tf_cached_attention(tos_tf_model_t *m, float *out, const float *q, const
                             int layer, int head, int pos);                         /* transformer.c:193 */
 int tos_tf_forward_token(tos_tf_model_t *m, float *logits, const float *tok_embed, int pos); /* transformer.c:255 */
 
+/* ------------------------------------- GPU dispatch of the tensor engine
+ * The reference's intended GPU entry points (kernel/drivers/gpu/gpu.h:80-96,
+ * stubs in gpu.c:155-225 that compute nothing) and the engine's routing
+ * rule (runtime/tensor/tensor_engine.c:28-67), backed here by kernels that
+ * give the engine's CPU operators' results bit for bit
+ * (runtime/tensor/tensor_cpu.c: tensor_cpu_matmul, _softmax, _layernorm,
+ * element-wise ops, tensor_cpu_attention).  Tensors are F32, contiguous
+ * row-major; data_virt is host memory when device_id is 0 and device memory
+ * of the library's GPU otherwise.  Each returns 0, or -1 for what the
+ * reference rejects (a gpu_id it has no GPU for, mismatched shapes) and for
+ * what is not supported here; tos_last_status() gives the reason. */
+typedef struct {                 /* tensor_desc_t, kernel/core/kernel.h:30-40 */
+    uint32_t ndim;
+    uint64_t shape[8];
+    uint64_t strides[8];         /* bytes (not read: contiguous tensors only) */
+    int32_t dtype;               /* TENSOR_DTYPE_*: 0 = F32 */
+    uint64_t data_phys;
+    uint64_t data_virt;
+    uint64_t size_bytes;
+    uint32_t device_id;          /* 0 = host memory, 1+ = this GPU */
+    uint32_t flags;
+} tos_tensor_desc_t;
+
+/* tir_opcode_t values the routing rule looks at (runtime/pseudocode/pseudocode_jit.h:186-217) */
+enum {
+    TOS_TIR_MATMUL = 4, TOS_TIR_CONV2D = 5, TOS_TIR_ATTENTION = 6, TOS_TIR_SOFTMAX = 7,
+    TOS_TIR_LAYERNORM = 8, TOS_TIR_RELU = 9, TOS_TIR_GELU = 10, TOS_TIR_ADD = 12, TOS_TIR_MUL = 13,
+    TOS_TIR_EMBEDDING = 23
+};
+enum { TOS_BACKEND_CPU = 0, TOS_BACKEND_GPU = 1 };   /* engine_backend_t, tensor_engine.h:23-28 */
+
+/* select_backend (tensor_engine.c:28-67): which backend the engine sends an
+ * operation to, given the tensors' sizes and how many GPUs it has */
+int tos_tensor_select_backend(int op, const tos_tensor_desc_t *tensors, uint32_t count, uint32_t gpu_count);
+/* C[M][N] = A[M][K] B[K][N]; sets C's ndim, shape, dtype, size_bytes as
+ * tensor_matmul does (tensor_engine.c:83-88) */
+int tos_gpu_tensor_matmul(uint32_t gpu_id, tos_tensor_desc_t *C, const tos_tensor_desc_t *A,
+                          const tos_tensor_desc_t *B);                                          /* gpu.c:155 */
+/* out[seq][d] = softmax(Q K^T * scale) V for Q, K, V [seq][d] (no mask), as
+ * tensor_cpu_attention (which uses scale 1/sqrt(d): pass scale <= 0) */
+int tos_gpu_tensor_attention(uint32_t gpu_id, tos_tensor_desc_t *output, const tos_tensor_desc_t *Q,
+                             const tos_tensor_desc_t *K, const tos_tensor_desc_t *V, float scale); /* gpu.c:178 */
+/* softmax along the last axis (axis = ndim-1 or -1), tensor_cpu_softmax per row */
+int tos_gpu_tensor_softmax(uint32_t gpu_id, tos_tensor_desc_t *output, const tos_tensor_desc_t *input,
+                           int axis);                                                           /* gpu.c:195 */
+/* layer norm along the last axis (tensor_cpu_layernorm per row), then
+ * * gamma + beta per element when those are given (data_virt != 0) */
+int tos_gpu_tensor_layernorm(uint32_t gpu_id, tos_tensor_desc_t *output, const tos_tensor_desc_t *input,
+                             const tos_tensor_desc_t *gamma, const tos_tensor_desc_t *beta,
+                             float epsilon);                                                   /* gpu.c:202 */
+/* output = a op b, op 0 add, 1 mul, 2 sub, 3 div (gpu.h:94) */
+int tos_gpu_tensor_elementwise(uint32_t gpu_id, tos_tensor_desc_t *output, const tos_tensor_desc_t *a,
+                               const tos_tensor_desc_t *b, int op);                            /* gpu.c:211 */
+
 /* ------------------------------------------------------------ GGUF files
  * The container of runtime/nn (gguf.c:204-423): v2/v3 headers, metadata,
  * tensor infos; tensor data is used in place (the caller's buffer, or a

@@ -224,6 +224,64 @@ class Reference(_Ops):
         L.ref_tf_cached_attention.restype, L.ref_tf_cached_attention.argtypes = None, [vp, vp, vp, vp, i32, i32, i32]
         L.ref_tf_reset.restype, L.ref_tf_reset.argtypes = None, []
 
+    # ---- the tensor engine's CPU operators (runtime/tensor/tensor_cpu.c) and
+    # its routing rule (tensor_engine.c:28-67), their own code
+    def _engine_bind(self):
+        L = self.lib
+        if getattr(self, "_eng", False):
+            return L
+        L.tensor_cpu_matmul.restype, L.tensor_cpu_matmul.argtypes = None, [vp, vp, vp, i32, i32, i32]
+        L.tensor_cpu_softmax.restype, L.tensor_cpu_softmax.argtypes = None, [vp, vp, i32]
+        L.tensor_cpu_layernorm.restype, L.tensor_cpu_layernorm.argtypes = None, [vp, vp, i32, f32]
+        L.tensor_cpu_attention.restype, L.tensor_cpu_attention.argtypes = None, [vp, vp, vp, vp, i32, i32]
+        L.ref_select_backend.restype, L.ref_select_backend.argtypes = i32, [i32, vp, i32, i32]
+        self._eng = True
+        return L
+
+    def engine_matmul(self, A, B):
+        L = self._engine_bind()
+        A, B = _f32(A), _f32(B)
+        M, K = A.shape
+        N = B.shape[1]
+        C_ = np.empty((M, N), np.float32)
+        L.tensor_cpu_matmul(_p(C_), _p(A), _p(B), M, N, K)
+        return C_
+
+    def engine_softmax_rows(self, X):
+        L = self._engine_bind()
+        X = _f32(X)
+        out = np.empty_like(X)
+        for i in range(X.shape[0]):
+            row = np.array(X[i], np.float32, copy=True)   # a fresh, 16-byte aligned buffer
+            o = np.empty_like(row)
+            L.tensor_cpu_softmax(_p(o), _p(row), len(row))
+            out[i] = o
+        return out
+
+    def engine_layernorm_rows(self, X, eps):
+        L = self._engine_bind()
+        X = _f32(X)
+        out = np.empty_like(X)
+        for i in range(X.shape[0]):
+            row = np.array(X[i], np.float32, copy=True)   # a fresh, 16-byte aligned buffer
+            o = np.empty_like(row)
+            L.tensor_cpu_layernorm(_p(o), _p(row), len(row), float(eps))
+            out[i] = o
+        return out
+
+    def engine_attention(self, Q, K, V):
+        L = self._engine_bind()
+        Q, K, V = _f32(Q), _f32(K), _f32(V)
+        seq, hd = Q.shape
+        out = np.empty((seq, hd), np.float32)
+        L.tensor_cpu_attention(_p(out), _p(Q), _p(K), _p(V), seq, hd)
+        return out
+
+    def select_backend(self, op, sizes, gpu_count):
+        L = self._engine_bind()
+        a = np.ascontiguousarray(sizes, dtype=np.uint64)
+        return int(L.ref_select_backend(int(op), _p(a), len(a), int(gpu_count)))
+
     # ---- the fp32 transformer engine (runtime/nn/transformer.c), its own code
     def tf_rmsnorm(self, x, w):
         x, w = _f32(x), _f32(w)

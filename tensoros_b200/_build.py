@@ -38,7 +38,7 @@ CC_FLAGS = ["-std=c11", "-O2", "-fPIC", "-Wall", "-Wno-unused-function", "-D_GNU
 
 NN_CU = sorted((CSRC / "kernels").glob("*.cu"))
 NN_C = [CSRC / "host" / "tos_runtime.c", CSRC / "host" / "tos_model.c", CSRC / "host" / "tos_shard.c",
-        CSRC / "host" / "tos_gguf.c", CSRC / "host" / "tos_tf.c"]
+        CSRC / "host" / "tos_gguf.c", CSRC / "host" / "tos_tf.c", CSRC / "host" / "tos_tensor.c"]
 SYNTH_C = [CSRC / "host" / "tos_synth.c"]
 HEADERS = (sorted((CSRC / "include").glob("*")) + sorted((CSRC / "kernels").glob("*.cuh"))
            + sorted(INC.glob("*.h")))

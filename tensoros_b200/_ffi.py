@@ -50,6 +50,13 @@ class TfDesc(C.Structure):
                [("tok_embed", vp), ("rms_final", vp)]
 
 
+class TensorDesc(C.Structure):
+    """tos_tensor_desc_t (tensor_desc_t of kernel/core/kernel.h:30-40)"""
+    _fields_ = [("ndim", C.c_uint32), ("shape", C.c_uint64 * 8), ("strides", C.c_uint64 * 8), ("dtype", C.c_int32),
+                ("data_phys", C.c_uint64), ("data_virt", C.c_uint64), ("size_bytes", C.c_uint64),
+                ("device_id", C.c_uint32), ("flags", C.c_uint32)]
+
+
 # name -> (restype, argtypes)
 NN_FUNCS = {
     "tos_status_string": (C.c_char_p, [i32]),
@@ -139,6 +146,12 @@ NN_FUNCS = {
     "tos_tf_reset": (i32, [vp]),
     "tos_tf_cached_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32]),
     "tos_tf_forward_token": (i32, [vp, vp, vp, i32]),
+    "tos_tensor_select_backend": (i32, [i32, vp, C.c_uint32, C.c_uint32]),
+    "tos_gpu_tensor_matmul": (i32, [C.c_uint32, vp, vp, vp]),
+    "tos_gpu_tensor_attention": (i32, [C.c_uint32, vp, vp, vp, vp, f32]),
+    "tos_gpu_tensor_softmax": (i32, [C.c_uint32, vp, vp, i32]),
+    "tos_gpu_tensor_layernorm": (i32, [C.c_uint32, vp, vp, vp, vp, f32]),
+    "tos_gpu_tensor_elementwise": (i32, [C.c_uint32, vp, vp, vp, i32]),
 }
 
 SYNTH_FUNCS = {

@@ -163,6 +163,15 @@ int tosk_attention(float *out, const float *q, const void *k_cache, const void *
 
 int tosk_num_sms(void);
 
+/* ---- tensor-engine operators (tensor_ops.cu; runtime/tensor/tensor_cpu.c) ---- */
+int tosk_teng_matmul(float *C, const float *A, const float *B, int M, int N, int K, cudaStream_t st);
+int tosk_teng_softmax_rows(float *out, const float *x, int rows, int n, cudaStream_t st);
+int tosk_teng_layernorm_rows(float *out, const float *x, const float *gamma, const float *beta, int rows, int n,
+                             float eps, cudaStream_t st);
+int tosk_teng_elementwise(float *out, const float *a, const float *b, size_t n, int op, cudaStream_t st);
+/* S[i][j] = dot(Q_i, K_j) * scale, Q and K [seq][hd] */
+int tosk_teng_scores(float *S, const float *Q, const float *K, int seq, int hd, float scale, cudaStream_t st);
+
 /* ---- fp32 transformer engine (tf_engine.cu; runtime/nn/transformer.c) ---- */
 /* y = W x, W rows x cols row-major; chunk_order 1: sum += ((p0+p1)+p2)+p3
  * over groups of four, 0: sum += w*x in order */

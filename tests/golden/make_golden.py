@@ -14,6 +14,8 @@ pin both the C restatement (oracle/tos_oracle.c) and the GPU path:
   tf.npz             the fp32 transformer engine (runtime/nn/transformer.c):
                      tf_rmsnorm, tf_swiglu_ffn, tf_cached_attention and
                      tf_forward_token logits of two seeded models
+  engine.npz         the tensor engine's CPU operators (runtime/tensor/
+                     tensor_cpu.c: matmul, softmax, layer norm, attention)
 
 Run from the repository root after building:  python tests/golden/make_golden.py
 (`python tests/golden/make_golden.py sample` writes sample.npz alone)
@@ -229,8 +231,28 @@ def tf_golden(R):
     print("tf.npz:", len(g), "arrays")
 
 
+def engine_golden(R):
+    """The tensor engine's CPU operators (runtime/tensor/tensor_cpu.c) on the
+    seeded cases of tests/engine_cases.py."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import engine_cases as E
+    g = {}
+    for M, N, K in E.MATMUL:
+        g[f"matmul_{M}_{N}_{K}"] = R.engine_matmul(*E.matmul_case(M, N, K))
+    for rows, n in E.SOFTMAX:
+        g[f"softmax_{rows}_{n}"] = R.engine_softmax_rows(E.softmax_case(rows, n))
+    for rows, n in E.LAYERNORM:
+        g[f"layernorm_{rows}_{n}"] = R.engine_layernorm_rows(E.layernorm_case(rows, n), E.EPS)
+    for seq, hd in E.ATTENTION:
+        g[f"attention_{seq}_{hd}"] = R.engine_attention(*E.attention_case(seq, hd))
+    np.savez_compressed(OUT / "engine.npz", **g)
+    print("engine.npz:", len(g), "arrays")
+
+
 if __name__ == "__main__":
-    if sys.argv[1:] == ["sample"]:
+    if sys.argv[1:] == ["engine"]:
+        engine_golden(pyoracle.reference())
+    elif sys.argv[1:] == ["sample"]:
         sample_golden(pyoracle.reference())
     elif sys.argv[1:] == ["tf"]:
         tf_golden(pyoracle.reference())
@@ -238,3 +260,4 @@ if __name__ == "__main__":
         main()
         sample_golden(pyoracle.reference())
         tf_golden(pyoracle.reference())
+        engine_golden(pyoracle.reference())
