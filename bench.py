@@ -29,11 +29,13 @@ batch 1.  A step is one decoded token.
              compiled hosted) on one host core, rank 0 at N=1.
 
 --impl reference times that reference CPU implementation alone.
-With --gpus N > 1 (one process per GPU) every GPU holds the whole model and
-decodes its own sequence (data-parallel replicas, weak scaling): value is
-the tokens/s of all N sequences, timed as the slowest rank; "sharded" adds
-the same decode with one sequence row-sharded over the N GPUs (NCCL
-all-gathers, strong scaling), and --shard makes that the value.
+With --gpus N > 1 (one process per GPU) the value is one sequence
+row-sharded over the N GPUs (strong scaling): each token is one fused
+kernel per GPU whose epilogues store their rows straight into the peers'
+vectors over NVLink.  "sharded_check" compares its greedy ids and next-step
+logits with the one-GPU model's (rank 0); "replicas" adds N data-parallel
+replicas, each GPU decoding its own sequence with the whole model (weak
+scaling; --replicas makes that the value).
 batch_decode: 16 sequences per step through the tensor-core GEMMs.
 """
 from __future__ import annotations
@@ -601,9 +603,9 @@ def run_ours(args, world, rank, local):
     synth = W.make_model(cfg, W.SEED)
     fast = args.math == "fast"
     t_gen = time.perf_counter() - t_gen
-    # several GPUs: independent replicas, each decoding its own sequence
-    # (weak scaling), unless --shard row-shards one sequence over them
-    replicas = world > 1 and not args.shard
+    # several GPUs: one sequence row-sharded over them (strong scaling), or
+    # with --replicas independent replicas, each decoding its own sequence
+    replicas = world > 1 and args.replicas
     prompt = W.tokens(args.prefill, cfg["vocab_size"], W.SEED + (rank if replicas else 0))
     warm = max(3, args.warmup)
     K = args.steps
@@ -658,13 +660,30 @@ def run_ours(args, world, rank, local):
         return e0.elapsed_time(e1), e2.elapsed_time(e3), ids
 
     def shard(force=False):
-        """row-sharding over the ranks (one sequence, NCCL all-gathers); a
-        fresh communicator id for every model"""
+        """row-sharding over the ranks (one sequence); a fresh communicator
+        id for every model"""
         if world == 1 or (replicas and not force):
             return None
         obj = [ops.nccl_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
         return (rank, world, obj[0])
+
+    def untimed_sequence(model, prompt=prompt):
+        """the token sequence timed_decode produces, on one GPU, untimed:
+        the prompt, warm-up and chained steps, then host-driven steps"""
+        nxt = 0
+        for i, t in enumerate(prompt):
+            nxt = model.forward_argmax(int(t), i)
+        pos = args.prefill
+        toks = model.decode(nxt, pos, warm)
+        nxt, pos = int(toks[-1]), pos + warm
+        ids = [int(t) for t in model.decode(nxt, pos, K)]
+        nxt, pos = ids[-1], pos + K
+        for _ in range(K):
+            nxt = model.forward_argmax(nxt, pos)
+            ids.append(int(nxt))
+            pos += 1
+        return ids
 
     # ---- value / e2e: the selected arithmetic
     clk = ClockSampler(local)
@@ -675,6 +694,25 @@ def run_ours(args, world, rank, local):
     prefill = None
     if world == 1 and not args.no_prefill:
         prefill = time_prefill(model, prompt, prompt_next, torch)
+    sharded_check = None
+    if world > 1 and not replicas:
+        # the sharded model's next-step logits (every rank takes part), then
+        # on rank 0 the one-GPU model over the same tokens: greedy ids and
+        # logits compared
+        next_pos = args.prefill + warm + 2 * K
+        lg_sharded = model.forward(ids[-1], next_pos)
+        barrier()
+        if rank == 0:
+            one = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), fused_step=int(fast and not args.per_op))
+            ids_one = untimed_sequence(one)
+            lg_one = one.forward(ids_one[-1], next_pos)
+            one.close()
+            d = float(np.max(np.abs(lg_sharded.astype(np.float64) - lg_one)))
+            sharded_check = {"ids_identical_to_one_gpu": ids_one == ids, "ids_compared": len(ids),
+                             "next_logits_max_abs_diff": d,
+                             "next_logits_bitwise_equal": bool(np.array_equal(lg_sharded.view(np.uint32),
+                                                                                lg_one.view(np.uint32)))}
+        barrier()
     model.close()
     batch = None
     if world == 1 and args.batch > 1:
@@ -688,20 +726,26 @@ def run_ours(args, world, rank, local):
         model = ops.Model(synth, shard=shard())
         exact_ms, _, exact_ids = timed_decode(model)
         model.close()
-    # replicas: the same sequence row-sharded over all the GPUs, for the
-    # latency of one sequence (strong scaling)
-    sharded_ms = None
-    if replicas:
-        model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(force=True))
-        # one sequence: every rank feeds the same prompt
-        sharded_ms, _, _ = timed_decode(model, prompt=W.tokens(args.prefill, cfg["vocab_size"], W.SEED))
+    # beside the value: the other multi-GPU mode (data-parallel replicas
+    # beside the sharded value, or the sharded sequence beside replicas)
+    other_ms = None
+    if world > 1 and not args.no_replicas:
+        if replicas:
+            model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast), shard=shard(force=True),
+                              fused_step=int(fast and not args.per_op))
+            # one sequence: every rank feeds the same prompt
+            other_ms, _, _ = timed_decode(model, prompt=W.tokens(args.prefill, cfg["vocab_size"], W.SEED))
+        else:
+            model = ops.Model(synth, attn_mode=int(fast), gemv_mode=int(fast),
+                              fused_step=int(fast and not args.per_op))
+            other_ms, _, _ = timed_decode(model, prompt=W.tokens(args.prefill, cfg["vocab_size"], W.SEED + rank))
         model.close()
     if world > 1:
-        tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0, sharded_ms or 0.0], device="cuda")
+        tt = torch.tensor([t_ms, t_e2e, exact_ms or 0.0, other_ms or 0.0], device="cuda")
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         t_ms, t_e2e = float(tt[0]), float(tt[1])
         exact_ms = float(tt[2]) if exact_ms is not None else None
-        sharded_ms = float(tt[3]) if sharded_ms is not None else None
+        other_ms = float(tt[3]) if other_ms is not None else None
     # tokens of the whole job: one sequence per replica, or one sequence
     # row-sharded over all GPUs
     seqs = world if replicas else 1
@@ -740,12 +784,18 @@ def run_ours(args, world, rank, local):
                    "traffic": 9482496 if args.math == "fast" else 9485568,
                    "algorithmic_bytes_per_launch": GEMV_BYTES_4096, "launch_us": gemv_ms * 1000.0}
         step_us = t_ms / K * 1000.0
-        step_rl = {"bound": "hbm", "kernel": "decode_step_kernel (one launch per token, all layers)",
-                   "achieved": step_bytes / (step_us * 1e-6) / 1e9, "peak": peak, "peak_source": peak_kind,
-                   "unit": "GB/s", "frac": step_bytes / (step_us * 1e-6) / 1e9 / peak,
-                   # dram bytes of one launch at context 8, plus the KV rows of this context
-                   "traffic": STEP_TRAFFIC + L * 2 * (ctx - 8) * 4096 * 2,
-                   "algorithmic_bytes_per_launch": step_bytes, "launch_us": step_us}
+        # sharded: each GPU's launch streams its 1/N of the weights and KV rows
+        shards = world if (world > 1 and not replicas) else 1
+        launch_bytes = step_bytes / shards
+        step_rl = {"bound": "hbm", "kernel": "decode_step_kernel (one launch per token, all layers)"
+                   + (f", one of {shards} row-sharded launches" if shards > 1 else ""),
+                   "achieved": launch_bytes / (step_us * 1e-6) / 1e9, "peak": peak, "peak_source": peak_kind,
+                   "unit": "GB/s", "frac": launch_bytes / (step_us * 1e-6) / 1e9 / peak,
+                   # dram bytes of one (one-GPU) launch at context 8 from an ncu
+                   # capture, plus the KV rows of this context; no capture of a
+                   # multi-rank launch exists (ncu never wraps a multi-rank run)
+                   "traffic": STEP_TRAFFIC + L * 2 * (ctx - 8) * 4096 * 2 if shards == 1 else None,
+                   "algorithmic_bytes_per_launch": launch_bytes, "launch_us": step_us}
         extra = {}
         if world == 1 and not args.no_extra:
             extra["q8_0_gemv_sweep"] = q8_0_sweep(lib, torch, peak)
@@ -773,7 +823,8 @@ def run_ours(args, world, rank, local):
                        "step": "one fused kernel per token" if fused else "a kernel per operator (CUDA graph)",
                        "positions": [args.prefill + warm, args.prefill + warm + K - 1],
                        "parallelism": (f"{world} data-parallel replicas, one sequence each" if replicas else
-                                       f"row-sharded x{world} (heads, rows, vocabulary; NCCL all-gather)"
+                                       f"row-sharded x{world} (heads, rows, vocabulary; rows stored into the "
+                                       "peers' vectors over NVLink inside the fused step)"
                                        if world > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (3.72 GB of weights per step)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
@@ -785,10 +836,14 @@ def run_ours(args, world, rank, local):
             "prefill": prefill,
             "batch_decode": batch,
             "clocks": clk.summary(),
-            "sharded": None if sharded_ms is None else {
-                "value": K / (sharded_ms / 1000.0), "unit": "tokens/s", "ms_per_step": sharded_ms / K,
-                "scaling": "strong", "note": f"one sequence row-sharded over {world} GPUs, a kernel per "
-                                             "operator with NCCL all-gathers"},
+            "sharded": None if not (replicas and other_ms) else {
+                "value": K / (other_ms / 1000.0), "unit": "tokens/s", "ms_per_step": other_ms / K,
+                "scaling": "strong", "note": f"one sequence row-sharded over {world} GPUs"},
+            "replicas": None if (replicas or not other_ms) else {
+                "value": world * K / (other_ms / 1000.0), "unit": "tokens/s", "ms_per_step": other_ms / K,
+                "scaling": "weak", "note": f"{world} data-parallel replicas, one sequence each, the whole model "
+                                           "on every GPU (slowest rank's time)"},
+            "sharded_check": sharded_check,
             "exact": None if exact_ms is None else {
                 "value": K / (exact_ms / 1000.0), "unit": "tokens/s", "ms_per_step": exact_ms / K,
                 "greedy_ids_identical": exact_ids == ids, "ids_compared": len(ids)},
@@ -814,7 +869,10 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shard", action="store_true",
-                    help="with several GPUs, row-shard one sequence over them instead of one replica per GPU")
+                    help="with several GPUs, row-shard one sequence over them (the default)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with several GPUs, one data-parallel replica per GPU as the value instead")
+    ap.add_argument("--no-replicas", action="store_true", help="skip the second multi-GPU mode beside the value")
     ap.add_argument("--batch", type=int, default=16,
                     help="also time batched decode of this many sequences (0/1: skip)")
     ap.add_argument("--layers", type=int, default=0,

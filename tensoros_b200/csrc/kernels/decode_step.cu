@@ -462,7 +462,7 @@ __device__ __noinline__ void ll_input(const Params& p, Hdr* h, float4* X4, int n
 // eight lanes a block (xfix_group); with a fused RMSNorm the raw vector is
 // staged there first for the sum of squares.  Each compute thread then keeps
 // its block's record in registers for the whole phase.
-template <int QB>
+template <int QB, bool kLL>
 __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
                                              int kind, int layer, int& gs) {
   const Geo G = geo_regs(p, kind);
@@ -510,7 +510,7 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
         }
         X4[q] = v;
       }
-    } else if (p.ll) {
+    } else if (kLL) {
       const int xk = kind == K_O ? X_ATT : kind == K_GU ? X_XO : kind == K_D ? X_H : X_XD;
       ll_input(p, h, X4, nq, xk, (kind == K_QKV || kind == K_LM) ? layer - 1 : layer, ct, err);
     } else {
@@ -631,7 +631,7 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
 // ---------------------------------------------------------------------------
 // Lane i (< n) holds the sum of row r0 + i.  Paired epilogues see both rows
 // of a pair in lanes i, i ^ 1 (stages and row ranges start at even rows).
-template <int ESZ>
+template <int ESZ, bool kLL>
 __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind, int layer, float y, int r0, int n,
                                          int lane, int pos, int rb, bool pre_res, float& bv, int& bi) {
   const int r = r0 + lane;
@@ -666,11 +666,11 @@ __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind
     const int gr = p.s.row0 + r;   // residual row (all of x on one GPU)
     const float v = __fadd_rn(pre_res ? h->res[r - rb] : __ldcg(p.s.x + gr), y);   // llm.c:717-718, 732-733
     p.s.x[gr] = v;
-    if (p.ll) ll_store_all(p, kind == K_O ? X_XO : X_XD, gr, v, ll_epoch(h, layer, kind == K_O ? X_XO : X_XD));
+    if (kLL) ll_store_all(p, kind == K_O ? X_XO : X_XD, gr, v, ll_epoch(h, layer, kind == K_O ? X_XO : X_XD));
   } else if (kind == K_GU) {
     if ((r & 1) == 0) {
       const float v = __fmul_rn(ref_silu(y), partner);   // llm.c:726-729
-      if (p.ll) ll_store_all(p, X_H, p.s.ff0 + (r >> 1), v, ll_epoch(h, layer, X_H));
+      if (kLL) ll_store_all(p, X_H, p.s.ff0 + (r >> 1), v, ll_epoch(h, layer, X_H));
       else p.s.h[r >> 1] = v;
     }
   } else {
@@ -681,6 +681,7 @@ __device__ __forceinline__ void epilogue(const Params& p, const Hdr* h, int kind
 
 // Chain warps after the LM head: the CTA's (value, index), then the last CTA
 // to finish reduces all of them and writes the greedy token.
+template <bool kLL>
 __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv, int bi) {
   const int cw = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
 #pragma unroll
@@ -726,7 +727,7 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
   // (logit 0 is the first row of rank 0's slice)
   const bool x0_nan = p.s.rank == 0 && __ldcg(p.s.logits) != __ldcg(p.s.logits);
   int* io = p.s.io;
-  if (p.s.world > 1) {
+  if (kLL) {   // sharded
     // every rank's (value, index) pair into every rank's pair words (rank 0
     // marks a NaN logit 0 with index -2) with the step's final epoch; every
     // rank then reduces the same pairs in rank order
@@ -750,7 +751,7 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
   }
   // the next step's exchange words carry later epochs than every word of
   // this one
-  if (p.ll) io[5] = (int)h->efinal;
+  if (kLL) io[5] = (int)h->efinal;
   io[2] = idx;
   if (p.s.chained) {
     const int k = io[4];
@@ -763,7 +764,7 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
   atomicExch(p.s.sync + 1, 0u);
 }
 
-template <int ESZ>
+template <int ESZ, bool kLL>
 __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float* P, int kind, int layer, int& gs) {
   float bv = 0.0f;   // LM head: this lane's running (value, index) of llm_argmax
   int bi = -1;
@@ -826,9 +827,9 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
     const float y = __shfl_sync(0xffffffffu, t, min(lane, tr - 1) * nseg);
     __syncwarp();
     if (lane == 0) mbar_arrive(&h->pempty[cw]);
-    epilogue<ESZ>(p, h, kind, layer, y, r0, n, lane, pos, rb, pre_res, bv, bi);
+    epilogue<ESZ, kLL>(p, h, kind, layer, y, r0, n, lane, pos, rb, pre_res, bv, bi);
   }
-  if (kind == K_LM) argmax_finish(p, h, bv, bi);
+  if (kind == K_LM) argmax_finish<kLL>(p, h, bv, bi);
 }
 
 // ---------------------------------------------------------------------------
@@ -927,7 +928,7 @@ __device__ __noinline__ void attn_scores(const Params& p, Hdr* h, float* P, int 
 // e_t = llm_expf(s_t - max) with the head's global max (llm.c:509-517), the
 // chunk's e-sum and sum_t e_t v_t; the last chunk of a head to finish adds
 // the chunks in order and divides by the sum (llm.c:519-521, 703-712).
-template <int ESZ>
+template <int ESZ, bool kLL>
 __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int layer) {
   const int w = (int)(threadIdx.x >> 5) - 1;
   const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
@@ -1007,7 +1008,7 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
       for (int d = gt; d < hd; d += 128) {
         float o = 0.0f;
         for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
-        if (p.ll) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+        if (kLL) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
         else p.s.att[(size_t)hh * hd + d] = o * inv;
       }
     }
@@ -1021,7 +1022,7 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
 // takes positions w, w + kNW, ... eight at a time (all eight K or V rows in
 // flight); the eight dot products of a warp meet in one reduce-scatter.
 
-template <int ESZ>
+template <int ESZ, bool kLL>
 __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, int layer) {
   const int w = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
   const int wt = (int)threadIdx.x - 32;
@@ -1133,7 +1134,7 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
     for (int d = wt; d < hd; d += kWorkers) {
       float o = part[d];
       for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
-      if (p.ll) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+      if (kLL) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
       else p.s.att[(size_t)hh * hd + d] = o * inv;
     }
     named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
@@ -1143,19 +1144,22 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
 // ---------------------------------------------------------------------------
 // the step
 // ---------------------------------------------------------------------------
-template <int ESZ>
+template <int ESZ, bool kLL>
 __device__ __forceinline__ void gemv_phase(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
                                            int kind, int layer, int& gs) {
   if ((threadIdx.x >> 5) <= kChain)
-    chain_gemv<ESZ>(p, h, P, kind, layer, gs);
+    chain_gemv<ESZ, kLL>(p, h, P, kind, layer, gs);
   else if (p.g[kind].qb == 16)
-    compute_gemv<16>(p, h, X, P, ring, kind, layer, gs);
+    compute_gemv<16, kLL>(p, h, X, P, ring, kind, layer, gs);
   else
-    compute_gemv<32>(p, h, X, P, ring, kind, layer, gs);
+    compute_gemv<32, kLL>(p, h, X, P, ring, kind, layer, gs);
 }
 
-template <int ESZ>
+template <int ESZ, bool kLL>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ Params p) {
+  // kLL: the phases hand their vectors over as exchange words (a sharded
+  // step); otherwise through grid barriers.  Two instances, so that the
+  // one-GPU step carries none of the exchange code.
   extern __shared__ __align__(1024) uint8_t smem[];
   Hdr* h = reinterpret_cast<Hdr*>(smem);
   uint32_t* X = reinterpret_cast<uint32_t*>(smem + kHdr);
@@ -1200,22 +1204,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     const int l = ph / 6, r = ph - 6 * l;
     if (l == p.s.n_layers || r == 0 || r >= 3) {
       const int kind = l == p.s.n_layers ? K_LM : r == 0 ? K_QKV : r == 3 ? K_O : r == 4 ? K_GU : K_D;
-      gemv_phase<ESZ>(p, h, X, P, ring, kind, l, gs);
+      gemv_phase<ESZ, kLL>(p, h, X, P, ring, kind, l, gs);
       if (kind == K_LM) break;
     } else if (short_ctx) {
       if (r == 2) continue;
-      attn_head<ESZ>(p, h, reinterpret_cast<float*>(X), l);
+      attn_head<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
     } else if (r == 1) {
       attn_scores<ESZ>(p, h, P, l);
     } else {
-      attn_pv<ESZ>(p, h, P, l);
+      attn_pv<ESZ, kLL>(p, h, P, l);
     }
     // with exchange words, the vectors the next phase reads in full
     // (attention output, residual, SwiGLU output; from every rank when
     // sharded) carry their own readiness, which the readers wait on; only
     // the q|k|v -> attention and scores -> softmax*V hand-offs (q, the KV
     // rows, the scores) need the grid barrier
-    const bool grid = !p.ll || r == 0 || (r == 1 && !short_ctx);
+    const bool grid = !kLL || r == 0 || (r == 1 && !short_ctx);
     if (grid) {
       if (!grid_sync(h, p.s.sync, (++nsync) * gridDim.x, err)) return;
     } else if (!cta_sync(h)) {
@@ -1261,13 +1265,14 @@ static int make_geo(int R, int cols, int qtype, int unit, Geo& G) {
   return 0;
 }
 
-template <int ESZ>
+template <int ESZ, bool kLL>
 static int prepare_kernel(int* occ) {
   static int done = 0, occ_v = 0;
   if (!done) {
-    cudaError_t e = cudaFuncSetAttribute(decode_step_kernel<ESZ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(decode_step_kernel<ESZ, kLL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return (int)e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_v, decode_step_kernel<ESZ>, kThreads, kSmem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_v, decode_step_kernel<ESZ, kLL>, kThreads, kSmem);
     if (e != cudaSuccess) return (int)e;
     done = 1;
   }
@@ -1326,7 +1331,8 @@ static int plan(const tosk_step_t* s, Params* p) {
   p->cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(p->opart) +
                                   al256((size_t)s->n_heads * p->maxc * kMaxHd * 4));
   int occ = 0;
-  e = esz == 2 ? prepare_kernel<2>(&occ) : prepare_kernel<4>(&occ);
+  e = esz == 2 ? (p->ll ? prepare_kernel<2, true>(&occ) : prepare_kernel<2, false>(&occ))
+               : (p->ll ? prepare_kernel<4, true>(&occ) : prepare_kernel<4, false>(&occ));
   if (e) return e;
   // every CTA must be resident at once (grid barriers): one per SM
   if (occ < 1 || tosk_num_sms() > kMaxGrid) return (int)cudaErrorNotSupported;
@@ -1352,6 +1358,9 @@ extern "C" int tosk_step_launch(const tosk_step_t* s, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (s->kv_type == TOSK_F16) return (int)cudaLaunchKernelEx(&cfg, decode_step_kernel<2>, p);
-  return (int)cudaLaunchKernelEx(&cfg, decode_step_kernel<4>, p);
+  if (s->kv_type == TOSK_F16)
+    return (int)(p.ll ? cudaLaunchKernelEx(&cfg, decode_step_kernel<2, true>, p)
+                      : cudaLaunchKernelEx(&cfg, decode_step_kernel<2, false>, p));
+  return (int)(p.ll ? cudaLaunchKernelEx(&cfg, decode_step_kernel<4, true>, p)
+                    : cudaLaunchKernelEx(&cfg, decode_step_kernel<4, false>, p));
 }
