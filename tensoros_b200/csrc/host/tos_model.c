@@ -420,6 +420,8 @@ static int create_impl(tos_model_t **out, const tos_model_desc_t *d, int world, 
     if (!e) e = tosk_rope_table(m->rope, d->max_seq, m->hd, d->rope_base, m->st);
     m->ws_bytes = tosk_attention_ws_bytes(sp.n_heads, d->max_seq);
     if (!e) e = dmalloc(m, &m->ws, m->ws_bytes);
+    /* the fused step's per-head counters live in it and start at zero */
+    if (!e) e = cudaMemsetAsync(m->ws, 0, m->ws_bytes, m->st);
     if (!e) e = dmalloc(m, (void **)&m->io, 8 * sizeof(int));
     if (!e) e = cudaMemsetAsync(m->io, 0, 8 * sizeof(int), m->st);
     if (!e) e = dmalloc(m, (void **)&m->ring, (size_t)d->max_seq * sizeof(int));
@@ -605,6 +607,7 @@ static void clear_error(tos_model_t *m)
 {
     cudaMemsetAsync(m->io + 3, 0, sizeof(int), m->st);
     if (m->step_sync) cudaMemsetAsync(m->step_sync, 0, tosk_step_sync_bytes(), m->st);
+    if (m->step_sync && m->ws) cudaMemsetAsync(m->ws, 0, m->ws_bytes, m->st);   /* attention counters */
     /* one GPU: the exchange words restart from a cleared area at epoch 0 (a
      * step that stopped early leaves words of its epochs behind).  A sharded
      * model cannot restart its peers' epochs from here: after a timeout it is

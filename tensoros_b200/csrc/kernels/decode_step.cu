@@ -70,6 +70,7 @@ constexpr int kChunk = 64;               // attention positions per chunk
 constexpr int kMaxHd = 256;
 constexpr int kMaxGrid = 1024;
 constexpr int kHeadMaxN = 1024;          // longest context of the one-phase-per-head attention
+constexpr int kHeadSplit = 4;            // CTAs that share one head's one-phase attention (positions split)
 constexpr int kNW = kWorkers / 32;       // worker warps
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4, K_N = 5 };
 // named barriers (0 is __syncthreads)
@@ -83,6 +84,7 @@ struct Geo {
 struct Params {
   tosk_step_t s;
   int ll;          // vectors handed between phases as exchange words (peer_ll set; always when sharded)
+  int split;       // one-phase attention: kHeadSplit CTAs per head (grid a multiple of it, maxc >= it)
   Geo g[K_N];
   float* S;        // attention workspace (the FAST attention layout)
   float* cmax;
@@ -759,7 +761,9 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
     io[4] = k + 1;
     io[1] = io[1] + 1;
   }
-  // every CTA is past its last grid barrier: reset the counters for the next step
+  // every CTA is past its last grid barrier: reset the counters for the next
+  // step (the grid's, and the heads' of the split attention)
+  for (int hh = 0; hh < p.s.n_heads; ++hh) atomicExch(reinterpret_cast<unsigned*>(p.cnt) + hh, 0u);
   atomicExch(p.s.sync, 0u);
   atomicExch(p.s.sync + 1, 0u);
 }
@@ -798,11 +802,17 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
         const int hd = p.s.hd, group = p.s.n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
         const uint32_t rowb = (uint32_t)(hd * ESZ);
         const uint64_t keep = policy_evict_last();
-        for (int hh = blockIdx.x; hh < p.s.n_heads; hh += gridDim.x) {
+        const int per = p.split ? kHeadSplit : 1;
+        for (int c = blockIdx.x; c < p.s.n_heads * per; c += gridDim.x) {
+          const int hh = c / per, sp = c % per;
           const size_t off = (size_t)(hh / group) * hd * ESZ;
-          for (int t = ct; t < 2 * pos; t += 32 * kChain) {
-            const uint8_t* base = reinterpret_cast<const uint8_t*>(t < pos ? Ly.k_cache : Ly.v_cache);
-            prefetch_l2(base + (size_t)(t < pos ? t : t - pos) * kv_dim * ESZ + off, rowb, keep);
+          // this CTA's positions of the head (the whole head without the split)
+          const int ta = (int)(((long long)(pos + 1) * sp) / per);
+          const int tb = min(pos, (int)(((long long)(pos + 1) * (sp + 1)) / per));
+          const int m = max(0, tb - ta);
+          for (int t = ct; t < 2 * m; t += 32 * kChain) {
+            const uint8_t* base = reinterpret_cast<const uint8_t*>(t < m ? Ly.k_cache : Ly.v_cache);
+            prefetch_l2(base + (size_t)(ta + (t < m ? t : t - m)) * kv_dim * ESZ + off, rowb, keep);
           }
         }
       }
@@ -1141,6 +1151,190 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
   }
 }
 
+// Short contexts with the head split: kHeadSplit CTAs share a head, CTA
+// (head, s) taking positions [n*s/kHeadSplit, n*(s+1)/kHeadSplit).  Each
+// scores its positions (as attn_head: eight per warp per pass), publishes
+// its maximum and waits for the head's other CTAs (a per-head counter in
+// global memory, bounded wait; all CTAs are resident); then e_t =
+// llm_expf(s_t - the head's maximum), the partial sum and the partial
+// sum_t e_t v_t, published; the last of the head's CTAs adds the partials in
+// split order (fixed, so results do not depend on which CTA that is) and
+// writes the head's output.  The counter of head h reaches 2 * kHeadSplit
+// per layer; the step's last CTA resets it.
+template <int ESZ, bool kLL>
+__device__ __noinline__ void attn_split(const Params& p, Hdr* h, float* smf, int layer) {
+  const int w = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int wt = (int)threadIdx.x - 32;
+  const int n = h->pos + 1;
+  const int hd = p.s.hd, n_heads = p.s.n_heads, group = n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
+  int* err = p.s.io + 3;
+  float* sc = smf;                              // [n / kHeadSplit + 1]: scores, then e_t
+  float* part = smf + kHeadMaxN;                // [kNW][kMaxHd] PV partials
+  float* red = part + kNW * kMaxHd;             // [32]
+  int* flag = reinterpret_cast<int*>(red + 24);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].k_cache);
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].v_cache);
+  const unsigned arrive0 = 2u * kHeadSplit * (unsigned)layer;   // this layer's counts start here
+  for (int c = blockIdx.x; c < n_heads * kHeadSplit; c += gridDim.x) {
+    const int hh = c / kHeadSplit, sp = c % kHeadSplit;
+    const int t0 = (int)(((long long)n * sp) / kHeadSplit), t1 = (int)(((long long)n * (sp + 1)) / kHeadSplit);
+    const int m = t1 - t0;
+    const int kvh = hh / group;
+    const uint8_t* kc = kbase + (size_t)kvh * hd * ESZ;
+    const uint8_t* vc = vbase + (size_t)kvh * hd * ESZ;
+    float4 qv[kMaxHd / 128];
+#pragma unroll
+    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      qv[sl] = d < hd ? __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // scores of positions t0 + i, eight per warp per pass (llm.c:686-692)
+    for (int i0 = w; i0 < m; i0 += 8 * kNW) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+#pragma unroll 1
+      for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+        const int d = 128 * sl + 4 * lane;
+        if (d < hd) {
+          float4 kv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * kNW;
+            kv[u] = i < m ? ldcg4<ESZ>(kc + ((size_t)(t0 + i) * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            v[u] = fmaf(qv[sl].x, kv[u].x, fmaf(qv[sl].y, kv[u].y, fmaf(qv[sl].z, kv[u].z, fmaf(qv[sl].w, kv[u].w, v[u]))));
+        }
+      }
+#pragma unroll
+      for (int half = 4, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? v[half + i] : v[i];
+          const float send = up ? v[i] : v[half + i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      const int i = i0 + ((lane >> 2) & 7) * kNW;
+      if ((lane & 3) == 0 && i < m) sc[i] = dot * scale;
+    }
+    named_sync(B_WORKERS, kWorkers);
+    // this CTA's maximum, published; then the head's (llm.c:509-511)
+    float mx = -INFINITY;
+    for (int i = wt; i < m; i += kWorkers) mx = fmaxf(mx, sc[i]);
+    mx = warp_max_f(mx);
+    if (lane == 0) red[w] = mx;
+    named_sync(B_WORKERS, kWorkers);
+    if (threadIdx.x == 32) {
+      float ms = red[0];
+      for (int i = 1; i < kNW; ++i) ms = fmaxf(ms, red[i]);
+      p.cmax[(size_t)hh * p.maxc + sp] = ms;
+      __threadfence();
+      atomicAdd(reinterpret_cast<unsigned*>(p.cnt) + hh, 1u);
+      const long long tw = clock64();
+      for (int it = 0;; ++it) {
+        if (ld_acquire(reinterpret_cast<const unsigned*>(p.cnt) + hh) >= arrive0 + kHeadSplit) break;
+        if ((it & 7) == 7) {
+          if (*reinterpret_cast<volatile int*>(err)) {
+            h->abort = 1;
+            break;
+          }
+          if (clock64() - tw > kWaitCycles) {
+            atomicCAS(err, 0, 23);
+            h->abort = 1;
+            break;
+          }
+        }
+      }
+      __threadfence();
+      float M = -INFINITY;
+      for (int i = 0; i < kHeadSplit; ++i) M = fmaxf(M, __ldcg(p.cmax + (size_t)hh * p.maxc + i));
+      red[16] = M;
+    }
+    named_sync(B_WORKERS, kWorkers);
+    if (*reinterpret_cast<volatile int*>(&h->abort)) return;
+    const float M = red[16];
+    // e_t = llm_expf(s_t - M) and this CTA's sum (llm.c:514-517)
+    float l = 0.0f;
+    for (int i = wt; i < m; i += kWorkers) {
+      const float e = ref_expf(__fsub_rn(sc[i], M));
+      sc[i] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    named_sync(B_WORKERS, kWorkers);   // every thread has read red[16] and written its e_t
+    if (lane == 0) red[w] = l;
+    // sum_t e_t v_t[d] over this CTA's positions (llm.c:703-712)
+#pragma unroll 1
+    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
+      const int d = 128 * sl + 4 * lane;
+      if (d < hd) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i0 = w; i0 < m; i0 += 8 * kNW) {
+          float4 vv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * kNW;
+            vv[u] = i < m ? ldcg4<ESZ>(vc + ((size_t)(t0 + i) * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * kNW;
+            const float e = i < m ? sc[i] : 0.0f;
+            acc.x = fmaf(e, vv[u].x, acc.x);
+            acc.y = fmaf(e, vv[u].y, acc.y);
+            acc.z = fmaf(e, vv[u].z, acc.z);
+            acc.w = fmaf(e, vv[u].w, acc.w);
+          }
+        }
+        *reinterpret_cast<float4*>(part + w * kMaxHd + d) = acc;
+      }
+    }
+    named_sync(B_WORKERS, kWorkers);
+    // this CTA's partials (warp order), published; the last of the head's
+    // CTAs combines them in split order
+    float* op = p.opart + ((size_t)hh * p.maxc + sp) * kMaxHd;
+    for (int d = wt; d < hd; d += kWorkers) {
+      float o = part[d];
+      for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
+      op[d] = o;
+    }
+    if (threadIdx.x == 32) {
+      float L = red[0];
+      for (int i = 1; i < kNW; ++i) L += red[i];
+      p.lsum[(size_t)hh * p.maxc + sp] = L;
+    }
+    __threadfence();
+    named_sync(B_WORKERS, kWorkers);
+    if (threadIdx.x == 32) {
+      *flag = atomicAdd(reinterpret_cast<unsigned*>(p.cnt) + hh, 1u) == arrive0 + 2 * kHeadSplit - 1;
+      __threadfence();
+    }
+    named_sync(B_WORKERS, kWorkers);
+    if (*flag) {
+      const size_t b = (size_t)hh * p.maxc;
+      float Ls = __ldcg(p.lsum + b);
+      for (int i = 1; i < kHeadSplit; ++i) Ls += __ldcg(p.lsum + b + i);
+      const float inv = 1.0f / (Ls + 1e-10f);   // llm.c:519
+      for (int d = wt; d < hd; d += kWorkers) {
+        float o = __ldcg(p.opart + b * kMaxHd + d);
+        for (int i = 1; i < kHeadSplit; ++i) o += __ldcg(p.opart + (b + i) * kMaxHd + d);
+        if (kLL) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
+        else p.s.att[(size_t)hh * hd + d] = o * inv;
+      }
+    }
+    named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the step
 // ---------------------------------------------------------------------------
@@ -1208,7 +1402,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       if (kind == K_LM) break;
     } else if (short_ctx) {
       if (r == 2) continue;
-      attn_head<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
+      if (p.split) attn_split<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
+      else attn_head<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
     } else if (r == 1) {
       attn_scores<ESZ>(p, h, P, l);
     } else {
@@ -1316,6 +1511,9 @@ static int plan(const tosk_step_t* s, Params* p) {
   }
   if (t.world == 1 && t.peer_ll[0] && (reinterpret_cast<uintptr_t>(t.peer_ll[0]) & 15)) return (int)cudaErrorInvalidValue;
   p->ll = t.peer_ll[0] != nullptr;
+  // the head split needs kHeadSplit partial slots per head in the attention
+  // workspace and groups of CTAs that stay aligned across the grid
+  p->split = ((s->max_seq + kChunk - 1) / kChunk) >= kHeadSplit && tosk_num_sms() % kHeadSplit == 0;
   int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
   if (!e) e = make_geo(t.n_rows, t.q_full, s->wtype, 1, p->g[K_O]);
   if (!e) e = make_geo(2 * t.n_ff, s->dim, s->wtype, 2, p->g[K_GU]);
