@@ -68,7 +68,7 @@ struct tos_model {
     /* batched prompt pass (allocated on first use): up to pf_cap tokens */
     int pf_cap;
     int *pf_toks;
-    float *pf_x, *pf_qkv, *pf_q, *pf_att, *pf_gu, *pf_h, *pf_tmp;
+    float *pf_x, *pf_qkv, *pf_q, *pf_att, *pf_h;
     void *pf_ws;
     size_t pf_ws_bytes;
     /* batched decode (allocated on first use): up to bd_cap sequences, each
@@ -77,7 +77,7 @@ struct tos_model {
     void *bd_kc, *bd_vc;
     int *bd_io;               /* device: tokens[cap], positions[cap], next[cap], slots[cap] */
     int *bd_host;             /* pinned mirror */
-    float *bd_x, *bd_qkv, *bd_q, *bd_att, *bd_gu, *bd_h, *bd_tmp, *bd_logits;
+    float *bd_x, *bd_qkv, *bd_q, *bd_att, *bd_h, *bd_logits;
     void *bd_ws;
     size_t bd_ws_bytes;
 };
@@ -159,9 +159,9 @@ void tos_model_destroy(tos_model_t *m)
     void *bufs[] = {m->xch, m->embd, m->norms, m->kc, m->vc, m->x, m->q, m->att, m->h, m->logits,
                     m->step_layers, m->step_sync,
                     m->logits_full, m->pairs, m->rope, m->ws, m->io, m->ring,
-                    m->pf_toks, m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_gu, m->pf_h,
-                    m->pf_tmp, m->pf_ws, m->bd_kc, m->bd_vc, m->bd_io, m->bd_x, m->bd_qkv,
-                    m->bd_q, m->bd_att, m->bd_gu, m->bd_h, m->bd_tmp, m->bd_logits, m->bd_ws};
+                    m->pf_toks, m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_h,
+                    m->pf_ws, m->bd_kc, m->bd_vc, m->bd_io, m->bd_x, m->bd_qkv,
+                    m->bd_q, m->bd_att, m->bd_h, m->bd_logits, m->bd_ws};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
         if (bufs[i]) cudaFree(bufs[i]);
     if (m->io_host) cudaFreeHost(m->io_host);
@@ -718,9 +718,7 @@ static int pf_alloc(tos_model_t *m)
     if (!e) e = dmalloc(m, (void **)&m->pf_qkv, (size_t)C * nqkv * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_q, (size_t)C * m->q_dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_att, (size_t)C * m->q_dim * 4);
-    if (!e) e = dmalloc(m, (void **)&m->pf_gu, (size_t)C * 2 * ff * 4);
     if (!e) e = dmalloc(m, (void **)&m->pf_h, (size_t)C * ff * 4);
-    if (!e) e = dmalloc(m, (void **)&m->pf_tmp, (size_t)C * dim * 4);
     size_t ws = 0, t;
     t = tosk_gemm_ws_bytes(C, nqkv, dim); if (t > ws) ws = t;
     t = tosk_gemm_ws_bytes(C, dim, m->q_dim); if (t > ws) ws = t;
@@ -741,7 +739,7 @@ static int pf_chunk(tos_model_t *m, const int *tokens, int n, int pos0)
     const tos_model_desc_t *d = &m->d;
     cudaStream_t st = m->st;
     int *err = m->io + 3;
-    const int dim = d->dim, ff = d->ff_dim, hd = m->hd;
+    const int dim = d->dim, hd = m->hd;
     const int nqkv = m->q_dim + 2 * m->kv_dim;
     size_t kv_layer = (size_t)d->max_seq * m->kv_dim * m->esz;
     int e = cudaMemcpyAsync(m->pf_toks, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, st);
@@ -754,13 +752,13 @@ static int pf_chunk(tos_model_t *m, const int *tokens, int n, int pos0)
                                        d->kv_type, n, st);
         if (!e) e = tosk_pf_attention(m->pf_q, kc, vc, d->kv_type, d->n_heads, d->n_kv_heads, hd, pos0, n,
                                       m->pf_att, st);
-        if (!e) e = tosk_gemm_q(&m->wo[l], m->pf_att, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
-        if (!e) e = tosk_gemm_q_norm(&m->wgu[l], m->pf_x, m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps, n,
-                                     m->pf_gu, m->pf_ws, m->pf_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_swiglu(m->pf_h, m->pf_gu, (size_t)n * ff, st);
-        if (!e) e = tosk_gemm_q(&m->wdown[l], m->pf_h, n, m->pf_tmp, m->pf_ws, m->pf_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_add(m->pf_x, m->pf_tmp, (size_t)n * dim, st);
+        /* the residual adds and SiLU*up run in the GEMMs' epilogues */
+        if (!e) e = tosk_gemm_q_residual(&m->wo[l], m->pf_att, n, m->pf_x, m->pf_ws, m->pf_ws_bytes, err, 1,
+                                         st);
+        if (!e) e = tosk_gemm_q_norm_swiglu(&m->wgu[l], m->pf_x, m->norms + (size_t)(2 * l + 1) * dim,
+                                            d->norm_eps, n, m->pf_h, m->pf_ws, m->pf_ws_bytes, err, 1, st);
+        if (!e) e = tosk_gemm_q_residual(&m->wdown[l], m->pf_h, n, m->pf_x, m->pf_ws, m->pf_ws_bytes, err,
+                                         1, st);
     }
     (void)nqkv;
     if (!e) e = cudaMemcpyAsync(m->x, m->pf_x + (size_t)(n - 1) * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice, st);
@@ -808,9 +806,7 @@ static int bd_alloc(tos_model_t *m)
     if (!e) e = dmalloc(m, (void **)&m->bd_qkv, (size_t)C * nqkv * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_q, (size_t)C * m->q_dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_att, (size_t)C * m->q_dim * 4);
-    if (!e) e = dmalloc(m, (void **)&m->bd_gu, (size_t)C * 2 * ff * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_h, (size_t)C * ff * 4);
-    if (!e) e = dmalloc(m, (void **)&m->bd_tmp, (size_t)C * dim * 4);
     if (!e) e = dmalloc(m, (void **)&m->bd_logits, (size_t)C * d->vocab_size * 4);
     size_t ws = 0, t;
     t = tosk_gemm_ws_bytes(C, nqkv, dim); if (t > ws) ws = t;
@@ -846,7 +842,7 @@ int tos_model_decode_batch(tos_model_t *m, const int *slot, const int *tokens, c
     if (e) return tos_set_status(tos_from_cuda(e));
     cudaStream_t st = m->st;
     int *err = m->io + 3;
-    const int C = m->bd_cap, dim = d->dim, ff = d->ff_dim, hd = m->hd;
+    const int C = m->bd_cap, dim = d->dim, hd = m->hd;
     const size_t cstride = (size_t)d->max_seq * m->kv_dim;           /* elements per sequence */
     const size_t kv_layer = cstride * C * m->esz;                    /* bytes per layer */
     memcpy(m->bd_host, tokens, (size_t)n * sizeof(int));
@@ -862,13 +858,13 @@ int tos_model_decode_batch(tos_model_t *m, const int *slot, const int *tokens, c
                                        m->bd_q, kc, vc, cstride, d->kv_type, n, st);
         if (!e) e = tosk_bd_attention(m->bd_q, kc, vc, cstride, d->kv_type, d->n_heads, d->n_kv_heads, hd,
                                       m->bd_io + C, m->bd_io + 3 * C, d->max_seq, n, m->bd_att, st);
-        if (!e) e = tosk_gemm_q(&m->wo[l], m->bd_att, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
-        if (!e) e = tosk_gemm_q_norm(&m->wgu[l], m->bd_x, m->norms + (size_t)(2 * l + 1) * dim, d->norm_eps, n,
-                                     m->bd_gu, m->bd_ws, m->bd_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_swiglu(m->bd_h, m->bd_gu, (size_t)n * ff, st);
-        if (!e) e = tosk_gemm_q(&m->wdown[l], m->bd_h, n, m->bd_tmp, m->bd_ws, m->bd_ws_bytes, err, 1, st);
-        if (!e) e = tosk_pf_add(m->bd_x, m->bd_tmp, (size_t)n * dim, st);
+        /* the residual adds and SiLU*up run in the GEMMs' epilogues */
+        if (!e) e = tosk_gemm_q_residual(&m->wo[l], m->bd_att, n, m->bd_x, m->bd_ws, m->bd_ws_bytes, err, 1,
+                                         st);
+        if (!e) e = tosk_gemm_q_norm_swiglu(&m->wgu[l], m->bd_x, m->norms + (size_t)(2 * l + 1) * dim,
+                                            d->norm_eps, n, m->bd_h, m->bd_ws, m->bd_ws_bytes, err, 1, st);
+        if (!e) e = tosk_gemm_q_residual(&m->wdown[l], m->bd_h, n, m->bd_x, m->bd_ws, m->bd_ws_bytes, err,
+                                         1, st);
     }
     if (!e) e = tosk_gemm_q_norm(&m->lm, m->bd_x, m->norms + (size_t)2 * d->n_layers * dim, d->norm_eps, n,
                                  m->bd_logits, m->bd_ws, m->bd_ws_bytes, err, 1, st);

@@ -95,7 +95,6 @@ int tosk_pf_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const 
                        float *q_out, void *kc, void *vc, int kv_type, int n, cudaStream_t st);
 int tosk_pf_attention(const float *q, const void *kc, const void *vc, int kv_type, int n_heads, int n_kv,
                       int hd, int pos0, int n, float *out, cudaStream_t st);
-int tosk_pf_add(float *x, const float *y, size_t n, cudaStream_t st);
 /* batched decode: n tokens of n sequences, token t of sequence slot[t] at
  * position pos[t] (device arrays); slot s's cache at kc/vc + s*cstride elements */
 int tosk_bd_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const float2 *cs, const int *pos,
@@ -104,7 +103,6 @@ int tosk_bd_rope_store(const float *qkv, int q_rows, int kv_rows, int hd, const 
 int tosk_bd_attention(const float *q, const void *kc, const void *vc, size_t cstride, int kv_type, int n_heads,
                       int n_kv, int hd, const int *pos, const int *slot, int max_ctx, int n, float *out,
                       cudaStream_t st);
-int tosk_pf_swiglu(float *h, const float *gu, size_t n, cudaStream_t st);
 /* m->rws from m->sc (run after the planes are filled) */
 int tosk_qmat_row_scales(tosk_qmat_t *m, cudaStream_t st);
 int tosk_gemm_q(const tosk_qmat_t *w, const float *x, int M, float *y, void *ws, size_t ws_bytes,
@@ -114,6 +112,14 @@ int tosk_gemm_q(const tosk_qmat_t *w, const float *x, int M, float *y, void *ws,
  * activation prep */
 int tosk_gemm_q_norm(const tosk_qmat_t *w, const float *x, const float *norm_w, float eps, int M, float *y,
                      void *ws, size_t ws_bytes, int *err, int pdl, cudaStream_t st);
+/* res[M][N] += x . W^T (the residual add of llm.c:717-718, 732-733 in the
+ * GEMM's epilogue) */
+int tosk_gemm_q_residual(const tosk_qmat_t *w, const float *x, int M, float *res, void *ws, size_t ws_bytes,
+                         int *err, int pdl, cudaStream_t st);
+/* h[M][N/2] = SiLU(g) * u of the normalised GEMM's interleaved gate|up rows
+ * (llm.c:723-729) in its epilogue */
+int tosk_gemm_q_norm_swiglu(const tosk_qmat_t *w, const float *x, const float *norm_w, float eps, int M,
+                            float *h, void *ws, size_t ws_bytes, int *err, int pdl, cudaStream_t st);
 
 /* per-block exact partials: blocks in GGUF layout, n_blocks consecutive,
  * x of length 32*n_blocks, out[n_blocks] (q4_0_dot32 / q8_0_dot32) */

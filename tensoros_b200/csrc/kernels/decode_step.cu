@@ -14,15 +14,17 @@
 //     complete_tx).  Weights depend on nothing, so the producer only waits
 //     for free slots: while the other warps wait at a grid barrier or run
 //     attention, the next projection's rows are already landing.
-//   * warps 4..15 (compute) turn the phase's input vector into fixed-point
-//     records (cp.async of every chunk at once; RMSNorm fused) and evaluate
-//     block values of the ring's stages as the FAST GEMV does (integer dp4a
-//     dot products on 24-bit fixed-point x, gemv_fastmath.cuh) into a
-//     partials tile;
-//   * warps 1..3 (chain) add each row's partials in a fixed tree order and
-//     run the fused epilogue (RoPE + KV store, residual add, SiLU*up, logits
-//     with a running argmax); during the q|k|v projection they prefetch
-//     into L2 the K and V rows the CTA's attention reads next;
+//   * warps 4..15 (compute): thread (b, g) reads block b of the phase's
+//     input vector from L2 (RMSNorm weight applied), keeps its fixed-point
+//     record in registers and evaluates block b of rows g, g + rg, ... of
+//     each ring stage as the FAST GEMV does (integer dp4a dot products on
+//     24-bit fixed-point x, gemv_fastmath.cuh) into a partials tile;
+//   * warps 1..3 (chain) compute a RMSNorm phase's 1/rms from the whole
+//     input vector, add each row's partials in a fixed tree order, scale
+//     the row by 1/rms and run the fused epilogue (RoPE + KV store, residual
+//     add, SiLU*up, logits with a running argmax); during the q|k|v
+//     projection they prefetch into L2 the K and V rows the CTA's attention
+//     reads next;
 //   * between dependent phases all 148 CTAs meet at a grid barrier (an
 //     atomic counter in global memory, release/acquire at GPU scope, every
 //     wait bounded).  Attention runs on the 15 worker warps: up to 1024
@@ -61,7 +63,7 @@ constexpr int kSlot = 41472;             // ring slot: 18 rows of a 4096-column 
 constexpr int kSlots = 3;
 constexpr int kHdr = 2048;
 constexpr int kPreRows = 128;           // residual rows a CTA can stage for its epilogue
-constexpr int kXBytes = 58368;           // fixed-point records of x: 128 B a block, up to 456 blocks
+constexpr int kXBytes = 58368;           // the phase's input vector and norm weights; attention scratch
 constexpr int kPBytes = 28512;           // partials tile (also attention scratch)
 constexpr int kSmem = kHdr + kXBytes + kPBytes + kSlots * kSlot;
 static_assert(kSmem <= 227 * 1024, "shared memory");
@@ -70,11 +72,10 @@ constexpr int kChunk = 64;               // attention positions per chunk
 constexpr int kMaxHd = 256;
 constexpr int kMaxGrid = 1024;
 constexpr int kHeadMaxN = 1024;          // longest context of the one-phase-per-head attention
-constexpr int kHeadSplit = 4;            // CTAs that share one head's one-phase attention (positions split)
 constexpr int kNW = kWorkers / 32;       // worker warps
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4, K_N = 5 };
 // named barriers (0 is __syncthreads)
-enum { B_COMPUTE = 1, B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4 };
+enum { B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4 };
 
 // Geometry of one projection (the same in every layer).
 struct Geo {
@@ -84,7 +85,6 @@ struct Geo {
 struct Params {
   tosk_step_t s;
   int ll;          // vectors handed between phases as exchange words (peer_ll set; always when sharded)
-  int split;       // one-phase attention: kHeadSplit CTAs per head (grid a multiple of it, maxc >= it)
   Geo g[K_N];
   float* S;        // attention workspace (the FAST attention layout)
   float* cmax;
@@ -103,7 +103,7 @@ struct Hdr {
   int tok, pos, skip;
   unsigned ebase;   // epoch of the last cross-GPU barrier before this step (sharded)
   unsigned efinal;  // epoch of this step's argmax exchange (sharded)
-  float wpart[kCompute];
+  float cpart[kChain];   // the chain warps' partial sums of squares (RMSNorm)
   float av[kChain];
   int ai[kChain];
   // epilogue operands the chain warps stage while the compute warps build
@@ -426,6 +426,11 @@ __device__ __forceinline__ float4 embed_chunk(const void* embd, int type, int di
   return v;
 }
 
+// Shared-memory slot of 16-byte chunk q of the phase's input vector: chunk j
+// of block k at 8 k + (j ^ (k & 7)), so the compute threads, each reading
+// the eight chunks of its own block, spread over all banks.
+__device__ __forceinline__ int xsw(int q) { return (q & ~7) | ((q ^ (q >> 3)) & 7); }
+
 // Sharded step: the phase's input vector from every rank's exchange words
 // into X4 (nq 16-byte chunks): four rounds of chunks in flight per thread, a
 // chunk read again until its words carry the exchange's epoch.  Out of line,
@@ -449,27 +454,36 @@ __device__ __noinline__ void ll_input(const Params& p, Hdr* h, float4* X4, int n
       if (q < nq) {
         ll_ready(ll + 4 * (size_t)q, w[u][0], ep, h, err);
         ll_ready(ll + 4 * (size_t)q + 2, w[u][1], ep, h, err);
-        X4[q] = make_float4(__uint_as_float(w[u][0].x), __uint_as_float(w[u][0].z), __uint_as_float(w[u][1].x),
-                            __uint_as_float(w[u][1].z));
+        X4[xsw(q)] = make_float4(__uint_as_float(w[u][0].x), __uint_as_float(w[u][0].z), __uint_as_float(w[u][1].x),
+                                 __uint_as_float(w[u][1].z));
       }
     }
   }
 }
 
+// The RMSNorm weights of a phase (null: no norm).
+__device__ __forceinline__ const float* norm_weights(const Params& p, int kind, int layer) {
+  return kind == K_QKV ? p.s.layers[layer].norm_att
+       : kind == K_GU  ? p.s.layers[layer].norm_ffn
+       : kind == K_LM  ? p.s.norm_out : nullptr;
+}
+
 // ---------------------------------------------------------------------------
-// compute warps: the phase's input vector in fixed point, then block values
+// compute warps: the phase's input block in fixed point, then block values
 // ---------------------------------------------------------------------------
-// The input vector becomes per-block fixed-point records in shared memory
-// (128 B a block: limb words 0..23, c, s; 16-byte chunk j at slot j ^ (b & 7)),
-// eight lanes a block (xfix_group); with a fused RMSNorm the raw vector is
-// staged there first for the sum of squares.  Each compute thread then keeps
-// its block's record in registers for the whole phase.
+// The compute warps copy the phase's input vector (and a RMSNorm's weights)
+// into shared memory, every chunk once per CTA in coalesced 16-byte copies
+// (the vector is read by all CTAs, so L2 requests, not bytes, set the time);
+// after one barrier with the chain warps, compute thread (b, g) turns its
+// block b into a fixed-point record in registers (make_xfix) and evaluates
+// block b of rows g, g + rg, ... of every stage.  The RMSNorm's scalar 1/rms
+// is applied to the row sums by the chain warps (chain_gemv).
 template <int QB, bool kLL>
-__device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
+__device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, float* Xs, float* P, const uint8_t* ring,
                                              int kind, int layer, int& gs) {
   const Geo G = geo_regs(p, kind);
   int* err = p.s.io + 3;
-  const int ct = (int)threadIdx.x - 32 * (1 + kChain);   // 0 .. 511
+  const int ct = (int)threadIdx.x - 32 * (1 + kChain);   // 0 .. 32 * kCompute - 1
   const int lane = threadIdx.x & 31;
   const int nwb = (G.nb + 31) >> 5;
   int rg = kCompute / nwb;
@@ -481,25 +495,16 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
   int rb, re, nst;
   row_range(G, rb, re, nst);
 
+  const float* nw = norm_weights(p, kind, layer);
+  const int nq = G.nb * 8;   // 16-byte chunks
+  float4* X4 = reinterpret_cast<float4*>(Xs);
+  float4* W4 = X4 + nq;
+  const bool stage_w = nw && 2 * nq * 16 <= kXBytes;
   {
-    const bool emb = kind == K_QKV && layer == 0;
-    const float* src = (kind == K_O) ? p.s.att : (kind == K_D) ? p.s.h : p.s.x;
-    const float* nw = kind == K_QKV ? p.s.layers[layer].norm_att
-                    : kind == K_GU  ? p.s.layers[layer].norm_ffn
-                    : kind == K_LM  ? p.s.norm_out : nullptr;
-    const int nq = G.nb * 8;   // 16-byte chunks
-    float4* X4 = reinterpret_cast<float4*>(X);
-    int orb = 0, ore = 0;
-    if (emb) {
-      int ons;
+    const float4* src4 = reinterpret_cast<const float4*>((kind == K_O) ? p.s.att : (kind == K_D) ? p.s.h : p.s.x);
+    if (kind == K_QKV && layer == 0) {
+      int orb, ore, ons;
       row_range(p.g[K_O], orb, ore, ons);
-    }
-    // every chunk of x (and of the norm weights) is fetched at once with
-    // asynchronous copies into the record area (and the idle partials area)
-    const bool stage_w = nw && nq * 16 <= kPBytes;
-    float4* W4 = reinterpret_cast<float4*>(P);
-    const int nr = (nq + 32 * kCompute - 1) / (32 * kCompute);   // rounds
-    if (emb) {
       for (int q = ct; q < nq; q += 32 * kCompute) {
         const float4 v = embed_chunk(p.s.embd, p.s.embd_type, p.s.dim, h->tok, q);
         // the residual stream starts as the embedding: this CTA writes the
@@ -510,85 +515,38 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, uint32_t* 
           const int lr = 4 * q + i - p.s.row0;   // the o phase's local row
           if (lr >= orb && lr < ore) p.s.x[4 * q + i] = e[i];
         }
-        X4[q] = v;
+        X4[xsw(q)] = v;
       }
     } else if (kLL) {
       const int xk = kind == K_O ? X_ATT : kind == K_GU ? X_XO : kind == K_D ? X_H : X_XD;
       ll_input(p, h, X4, nq, xk, (kind == K_QKV || kind == K_LM) ? layer - 1 : layer, ct, err);
     } else {
-      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(X4 + q, reinterpret_cast<const float4*>(src) + q);
+      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(X4 + xsw(q), src4 + q);
     }
     if (stage_w)
-      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(W4 + q, reinterpret_cast<const float4*>(nw) + q);
-    cp_async_wait_all();   // a thread converts only the chunks it copied
-    float ss = 1.0f;
-    if (nw) {
-      // RMSNorm (llm.c:416-442): tree sum of squares (serial per thread,
-      // butterfly per warp, warps in order)
-      float acc = 0.0f;
-      for (int q = ct; q < nq; q += 32 * kCompute) {
-        const float4 v = X4[q];
-        acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) h->wpart[ct >> 5] = acc;
-      named_sync(B_COMPUTE, 32 * kCompute);
-      float s2 = 0.0f;
-      for (int w = 0; w < kCompute; ++w) s2 += h->wpart[w];
-      ss = 1.0f / sqrtf(s2 / (float)p.s.dim + p.s.eps);
-    }
-    // every lane runs the same number of rounds (xfix_group shuffles within
-    // eight-lane groups; a round's eight lanes share a block)
-    for (int k = 0; k < nr; ++k) {
-      const int q = k * 32 * kCompute + ct;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (q < nq) {
-        v = X4[q];
-        if (nw) {
-          const float4 wv = stage_w ? W4[q] : __ldg(reinterpret_cast<const float4*>(nw) + q);
-          v.x = __fmul_rn(__fmul_rn(v.x, ss), wv.x);
-          v.y = __fmul_rn(__fmul_rn(v.y, ss), wv.y);
-          v.z = __fmul_rn(__fmul_rn(v.z, ss), wv.z);
-          v.w = __fmul_rn(__fmul_rn(v.w, ss), wv.w);
-        }
-      }
-      uint32_t w0, w1, w2;
-      int wi, csum;
-      float sc;
-      xfix_group<QB>(v, q & 7, w0, w1, w2, wi, csum, sc);
-      __syncwarp();   // the raw chunks of this block are read before its record overwrites them
-      if (q < nq) {
-        const int blk = q >> 3;
-        uint32_t* rec = X + 32 * blk;
-        const int sw = blk & 7;
-        auto put = [&](int word, uint32_t val) { rec[(((word >> 2) ^ sw) << 2) | (word & 3)] = val; };
-        put(wi, w0);
-        put(8 + wi, w1);
-        put(16 + wi, w2);
-        if ((q & 7) == 0) {
-          put(24, (uint32_t)csum);
-          put(25, __float_as_uint(sc));
-        }
-      }
-    }
-    named_sync(B_COMPUTE, 32 * kCompute);
+      for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(W4 + xsw(q), reinterpret_cast<const float4*>(nw) + q);
+    cp_async_wait_all();
   }
+  named_sync(B_WORKERS, kWorkers);   // the vector is in shared memory (the chain warps read it too)
   XFix xf;
   if (active) {
-    const uint4* xv = reinterpret_cast<const uint4*>(X) + 8 * b;
-    uint32_t wds[28];
+    float v[32];
 #pragma unroll
-    for (int j = 0; j < 7; ++j) {
-      const uint4 u = xv[j ^ (b & 7)];
-      wds[4 * j] = u.x; wds[4 * j + 1] = u.y; wds[4 * j + 2] = u.z; wds[4 * j + 3] = u.w;
+    for (int j = 0; j < 8; ++j) {
+      const float4 e = X4[8 * b + (j ^ (b & 7))];
+      v[4 * j] = e.x; v[4 * j + 1] = e.y; v[4 * j + 2] = e.z; v[4 * j + 3] = e.w;
     }
+    if (nw) {
 #pragma unroll
-    for (int l = 0; l < 3; ++l)
-#pragma unroll
-      for (int w = 0; w < 8; ++w) xf.l[l][w] = wds[8 * l + w];
-    xf.c = (int)wds[24];
-    xf.s = __uint_as_float(wds[25]);
+      for (int j = 0; j < 8; ++j) {
+        const float4 e = stage_w ? W4[8 * b + (j ^ (b & 7))] : __ldg(reinterpret_cast<const float4*>(nw) + 8 * b + j);
+        v[4 * j] = __fmul_rn(v[4 * j], e.x);
+        v[4 * j + 1] = __fmul_rn(v[4 * j + 1], e.y);
+        v[4 * j + 2] = __fmul_rn(v[4 * j + 2], e.z);
+        v[4 * j + 3] = __fmul_rn(v[4 * j + 3], e.w);
+      }
+    }
+    make_xfix<QB>(v, xf);
   }
 
   for (int it = 0; it < nst; ++it, ++gs) {
@@ -761,15 +719,38 @@ __device__ __forceinline__ void argmax_finish(const Params& p, Hdr* h, float bv,
     io[4] = k + 1;
     io[1] = io[1] + 1;
   }
-  // every CTA is past its last grid barrier: reset the counters for the next
-  // step (the grid's, and the heads' of the split attention)
-  for (int hh = 0; hh < p.s.n_heads; ++hh) atomicExch(reinterpret_cast<unsigned*>(p.cnt) + hh, 0u);
+  // every CTA is past its last grid barrier: reset the counters for the next step
   atomicExch(p.s.sync, 0u);
   atomicExch(p.s.sync + 1, 0u);
 }
 
+// RMSNorm scale 1/sqrt(mean(x^2) + eps) of the phase's input (llm.c:416-442)
+// by the chain warps from the shared-memory copy, while the compute warps
+// evaluate block values: chain thread t sums the squares of chunks t, t + 96,
+// ... in order, then a butterfly per warp and the three warps in order (the
+// same order in every instance, so a sharded step's scale equals the one-GPU
+// step's).
+__device__ __noinline__ float norm_scale(const Params& p, Hdr* h, const float4* X4) {
+  const int ct = (int)threadIdx.x - 32, lane = threadIdx.x & 31;
+  const int nq = p.s.dim / 4;
+  float acc = 0.0f;
+  for (int q = ct; q < nq; q += 32 * kChain) {
+    const float4 v = X4[xsw(q)];
+    acc = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, acc))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) h->cpart[ct >> 5] = acc;
+  named_sync(B_CHAIN, 32 * kChain);
+  float s2 = 0.0f;
+  for (int c = 0; c < kChain; ++c) s2 += h->cpart[c];
+  named_sync(B_CHAIN, 32 * kChain);   // cpart is read before the next phase writes it
+  return 1.0f / sqrtf(s2 / (float)p.s.dim + p.s.eps);
+}
+
 template <int ESZ, bool kLL>
-__device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float* P, int kind, int layer, int& gs) {
+__device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float* Xs, const float* P, int kind,
+                                           int layer, int& gs) {
   float bv = 0.0f;   // LM head: this lane's running (value, index) of llm_argmax
   int bi = -1;
   const Geo G = geo_regs(p, kind);
@@ -789,6 +770,8 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
   const int j0 = min(G.nb, seg * L), j1 = min(G.nb, seg * L + L);
   const int pos = h->pos;
   const bool pre_res = (kind == K_O || kind == K_D) && re - rb <= kPreRows;
+  const bool nrm = norm_weights(p, kind, layer) != nullptr;
+  float ss = 1.0f;
   {
     const int ct = (int)threadIdx.x - 32;   // 0 .. 32 * kChain - 1
     if (pre_res)
@@ -802,23 +785,19 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
         const int hd = p.s.hd, group = p.s.n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
         const uint32_t rowb = (uint32_t)(hd * ESZ);
         const uint64_t keep = policy_evict_last();
-        const int per = p.split ? kHeadSplit : 1;
-        for (int c = blockIdx.x; c < p.s.n_heads * per; c += gridDim.x) {
-          const int hh = c / per, sp = c % per;
+        for (int hh = blockIdx.x; hh < p.s.n_heads; hh += gridDim.x) {
           const size_t off = (size_t)(hh / group) * hd * ESZ;
-          // this CTA's positions of the head (the whole head without the split)
-          const int ta = (int)(((long long)(pos + 1) * sp) / per);
-          const int tb = min(pos, (int)(((long long)(pos + 1) * (sp + 1)) / per));
-          const int m = max(0, tb - ta);
-          for (int t = ct; t < 2 * m; t += 32 * kChain) {
-            const uint8_t* base = reinterpret_cast<const uint8_t*>(t < m ? Ly.k_cache : Ly.v_cache);
-            prefetch_l2(base + (size_t)(ta + (t < m ? t : t - m)) * kv_dim * ESZ + off, rowb, keep);
+          for (int t = ct; t < 2 * pos; t += 32 * kChain) {
+            const uint8_t* base = reinterpret_cast<const uint8_t*>(t < pos ? Ly.k_cache : Ly.v_cache);
+            prefetch_l2(base + (size_t)(t < pos ? t : t - pos) * kv_dim * ESZ + off, rowb, keep);
           }
         }
       }
     }
     named_sync(B_CHAIN, 32 * kChain);
   }
+  named_sync(B_WORKERS, kWorkers);   // the compute warps have staged the input vector
+  if (nrm) ss = norm_scale(p, h, reinterpret_cast<const float4*>(Xs));
   for (int it = ((cw - gs0) % kChain + kChain) % kChain; it < nst; it += kChain) {
     const int gsi = gs0 + it;
     if (!wait_mb(&h->pfull[cw], (gsi / kChain) & 1, err, 4, &h->abort)) break;
@@ -834,7 +813,8 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
     for (; j < j1; ++j) s0 += Prow[j];
     float t = (s0 + s1) + (s2 + s3);
     for (int o = 1; o < nseg; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    const float y = __shfl_sync(0xffffffffu, t, min(lane, tr - 1) * nseg);
+    float y = __shfl_sync(0xffffffffu, t, min(lane, tr - 1) * nseg);
+    if (nrm) y = __fmul_rn(y, ss);   // RMSNorm's 1/rms (llm.c:416-442), applied to the row
     __syncwarp();
     if (lane == 0) mbar_arrive(&h->pempty[cw]);
     epilogue<ESZ, kLL>(p, h, kind, layer, y, r0, n, lane, pos, rb, pre_res, bv, bi);
@@ -1151,202 +1131,18 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
   }
 }
 
-// Short contexts with the head split: kHeadSplit CTAs share a head, CTA
-// (head, s) taking positions [n*s/kHeadSplit, n*(s+1)/kHeadSplit).  Each
-// scores its positions (as attn_head: eight per warp per pass), publishes
-// its maximum and waits for the head's other CTAs (a per-head counter in
-// global memory, bounded wait; all CTAs are resident); then e_t =
-// llm_expf(s_t - the head's maximum), the partial sum and the partial
-// sum_t e_t v_t, published; the last of the head's CTAs adds the partials in
-// split order (fixed, so results do not depend on which CTA that is) and
-// writes the head's output.  The counter of head h reaches 2 * kHeadSplit
-// per layer; the step's last CTA resets it.
-template <int ESZ, bool kLL>
-__device__ __noinline__ void attn_split(const Params& p, Hdr* h, float* smf, int layer) {
-  const int w = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
-  const int wt = (int)threadIdx.x - 32;
-  const int n = h->pos + 1;
-  const int hd = p.s.hd, n_heads = p.s.n_heads, group = n_heads / p.s.n_kv, kv_dim = p.s.n_kv * hd;
-  int* err = p.s.io + 3;
-  float* sc = smf;                              // [n / kHeadSplit + 1]: scores, then e_t
-  float* part = smf + kHeadMaxN;                // [kNW][kMaxHd] PV partials
-  float* red = part + kNW * kMaxHd;             // [32]
-  int* flag = reinterpret_cast<int*>(red + 24);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].k_cache);
-  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.s.layers[layer].v_cache);
-  const unsigned arrive0 = 2u * kHeadSplit * (unsigned)layer;   // this layer's counts start here
-  for (int c = blockIdx.x; c < n_heads * kHeadSplit; c += gridDim.x) {
-    const int hh = c / kHeadSplit, sp = c % kHeadSplit;
-    const int t0 = (int)(((long long)n * sp) / kHeadSplit), t1 = (int)(((long long)n * (sp + 1)) / kHeadSplit);
-    const int m = t1 - t0;
-    const int kvh = hh / group;
-    const uint8_t* kc = kbase + (size_t)kvh * hd * ESZ;
-    const uint8_t* vc = vbase + (size_t)kvh * hd * ESZ;
-    float4 qv[kMaxHd / 128];
-#pragma unroll
-    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
-      const int d = 128 * sl + 4 * lane;
-      qv[sl] = d < hd ? __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d))
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    // scores of positions t0 + i, eight per warp per pass (llm.c:686-692)
-    for (int i0 = w; i0 < m; i0 += 8 * kNW) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = 0.0f;
-#pragma unroll 1
-      for (int sl = 0; sl < kMaxHd / 128; ++sl) {
-        const int d = 128 * sl + 4 * lane;
-        if (d < hd) {
-          float4 kv[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * kNW;
-            kv[u] = i < m ? ldcg4<ESZ>(kc + ((size_t)(t0 + i) * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            v[u] = fmaf(qv[sl].x, kv[u].x, fmaf(qv[sl].y, kv[u].y, fmaf(qv[sl].z, kv[u].z, fmaf(qv[sl].w, kv[u].w, v[u]))));
-        }
-      }
-#pragma unroll
-      for (int half = 4, o = 16; half >= 1; half >>= 1, o >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-          const float keep = up ? v[half + i] : v[i];
-          const float send = up ? v[i] : v[half + i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-      }
-      float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-      const int i = i0 + ((lane >> 2) & 7) * kNW;
-      if ((lane & 3) == 0 && i < m) sc[i] = dot * scale;
-    }
-    named_sync(B_WORKERS, kWorkers);
-    // this CTA's maximum, published; then the head's (llm.c:509-511)
-    float mx = -INFINITY;
-    for (int i = wt; i < m; i += kWorkers) mx = fmaxf(mx, sc[i]);
-    mx = warp_max_f(mx);
-    if (lane == 0) red[w] = mx;
-    named_sync(B_WORKERS, kWorkers);
-    if (threadIdx.x == 32) {
-      float ms = red[0];
-      for (int i = 1; i < kNW; ++i) ms = fmaxf(ms, red[i]);
-      p.cmax[(size_t)hh * p.maxc + sp] = ms;
-      __threadfence();
-      atomicAdd(reinterpret_cast<unsigned*>(p.cnt) + hh, 1u);
-      const long long tw = clock64();
-      for (int it = 0;; ++it) {
-        if (ld_acquire(reinterpret_cast<const unsigned*>(p.cnt) + hh) >= arrive0 + kHeadSplit) break;
-        if ((it & 7) == 7) {
-          if (*reinterpret_cast<volatile int*>(err)) {
-            h->abort = 1;
-            break;
-          }
-          if (clock64() - tw > kWaitCycles) {
-            atomicCAS(err, 0, 23);
-            h->abort = 1;
-            break;
-          }
-        }
-      }
-      __threadfence();
-      float M = -INFINITY;
-      for (int i = 0; i < kHeadSplit; ++i) M = fmaxf(M, __ldcg(p.cmax + (size_t)hh * p.maxc + i));
-      red[16] = M;
-    }
-    named_sync(B_WORKERS, kWorkers);
-    if (*reinterpret_cast<volatile int*>(&h->abort)) return;
-    const float M = red[16];
-    // e_t = llm_expf(s_t - M) and this CTA's sum (llm.c:514-517)
-    float l = 0.0f;
-    for (int i = wt; i < m; i += kWorkers) {
-      const float e = ref_expf(__fsub_rn(sc[i], M));
-      sc[i] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    named_sync(B_WORKERS, kWorkers);   // every thread has read red[16] and written its e_t
-    if (lane == 0) red[w] = l;
-    // sum_t e_t v_t[d] over this CTA's positions (llm.c:703-712)
-#pragma unroll 1
-    for (int sl = 0; sl < kMaxHd / 128; ++sl) {
-      const int d = 128 * sl + 4 * lane;
-      if (d < hd) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i0 = w; i0 < m; i0 += 8 * kNW) {
-          float4 vv[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * kNW;
-            vv[u] = i < m ? ldcg4<ESZ>(vc + ((size_t)(t0 + i) * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * kNW;
-            const float e = i < m ? sc[i] : 0.0f;
-            acc.x = fmaf(e, vv[u].x, acc.x);
-            acc.y = fmaf(e, vv[u].y, acc.y);
-            acc.z = fmaf(e, vv[u].z, acc.z);
-            acc.w = fmaf(e, vv[u].w, acc.w);
-          }
-        }
-        *reinterpret_cast<float4*>(part + w * kMaxHd + d) = acc;
-      }
-    }
-    named_sync(B_WORKERS, kWorkers);
-    // this CTA's partials (warp order), published; the last of the head's
-    // CTAs combines them in split order
-    float* op = p.opart + ((size_t)hh * p.maxc + sp) * kMaxHd;
-    for (int d = wt; d < hd; d += kWorkers) {
-      float o = part[d];
-      for (int i = 1; i < kNW; ++i) o += part[i * kMaxHd + d];
-      op[d] = o;
-    }
-    if (threadIdx.x == 32) {
-      float L = red[0];
-      for (int i = 1; i < kNW; ++i) L += red[i];
-      p.lsum[(size_t)hh * p.maxc + sp] = L;
-    }
-    __threadfence();
-    named_sync(B_WORKERS, kWorkers);
-    if (threadIdx.x == 32) {
-      *flag = atomicAdd(reinterpret_cast<unsigned*>(p.cnt) + hh, 1u) == arrive0 + 2 * kHeadSplit - 1;
-      __threadfence();
-    }
-    named_sync(B_WORKERS, kWorkers);
-    if (*flag) {
-      const size_t b = (size_t)hh * p.maxc;
-      float Ls = __ldcg(p.lsum + b);
-      for (int i = 1; i < kHeadSplit; ++i) Ls += __ldcg(p.lsum + b + i);
-      const float inv = 1.0f / (Ls + 1e-10f);   // llm.c:519
-      for (int d = wt; d < hd; d += kWorkers) {
-        float o = __ldcg(p.opart + b * kMaxHd + d);
-        for (int i = 1; i < kHeadSplit; ++i) o += __ldcg(p.opart + (b + i) * kMaxHd + d);
-        if (kLL) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
-        else p.s.att[(size_t)hh * hd + d] = o * inv;
-      }
-    }
-    named_sync(B_WORKERS, kWorkers);   // scratch is reused by the next head
-  }
-}
-
 // ---------------------------------------------------------------------------
 // the step
 // ---------------------------------------------------------------------------
 template <int ESZ, bool kLL>
-__device__ __forceinline__ void gemv_phase(const Params& p, Hdr* h, uint32_t* X, float* P, const uint8_t* ring,
+__device__ __forceinline__ void gemv_phase(const Params& p, Hdr* h, float* Xs, float* P, const uint8_t* ring,
                                            int kind, int layer, int& gs) {
   if ((threadIdx.x >> 5) <= kChain)
-    chain_gemv<ESZ, kLL>(p, h, P, kind, layer, gs);
+    chain_gemv<ESZ, kLL>(p, h, Xs, P, kind, layer, gs);
   else if (p.g[kind].qb == 16)
-    compute_gemv<16, kLL>(p, h, X, P, ring, kind, layer, gs);
+    compute_gemv<16, kLL>(p, h, Xs, P, ring, kind, layer, gs);
   else
-    compute_gemv<32, kLL>(p, h, X, P, ring, kind, layer, gs);
+    compute_gemv<32, kLL>(p, h, Xs, P, ring, kind, layer, gs);
 }
 
 template <int ESZ, bool kLL>
@@ -1356,7 +1152,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   // one-GPU step carries none of the exchange code.
   extern __shared__ __align__(1024) uint8_t smem[];
   Hdr* h = reinterpret_cast<Hdr*>(smem);
-  uint32_t* X = reinterpret_cast<uint32_t*>(smem + kHdr);
+  float* A = reinterpret_cast<float*>(smem + kHdr);   // input vector / attention scratch
   float* P = reinterpret_cast<float*>(smem + kHdr + kXBytes);
   uint8_t* ring = smem + kHdr + kXBytes + kPBytes;
   int* err = p.s.io + 3;
@@ -1398,12 +1194,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     const int l = ph / 6, r = ph - 6 * l;
     if (l == p.s.n_layers || r == 0 || r >= 3) {
       const int kind = l == p.s.n_layers ? K_LM : r == 0 ? K_QKV : r == 3 ? K_O : r == 4 ? K_GU : K_D;
-      gemv_phase<ESZ, kLL>(p, h, X, P, ring, kind, l, gs);
+      gemv_phase<ESZ, kLL>(p, h, A, P, ring, kind, l, gs);
       if (kind == K_LM) break;
     } else if (short_ctx) {
       if (r == 2) continue;
-      if (p.split) attn_split<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
-      else attn_head<ESZ, kLL>(p, h, reinterpret_cast<float*>(X), l);
+      attn_head<ESZ, kLL>(p, h, A, l);
     } else if (r == 1) {
       attn_scores<ESZ>(p, h, P, l);
     } else {
@@ -1444,7 +1239,7 @@ static int make_geo(int R, int cols, int qtype, int unit, Geo& G) {
   G.R = R;
   G.nb = cols / 32;
   // a block per compute thread; its fixed-point record in shared memory
-  if (G.nb > 32 * kCompute || G.nb * 128 > kXBytes) return (int)cudaErrorNotSupported;
+  if (G.nb > 32 * kCompute || G.nb * 128 > kXBytes) return (int)cudaErrorNotSupported;   // a block per compute thread
   G.nbp = round_up_i(G.nb, 8);
   G.qb = qtype == TOSK_Q4_0 ? 16 : 32;
   G.unit = unit;
@@ -1511,9 +1306,6 @@ static int plan(const tosk_step_t* s, Params* p) {
   }
   if (t.world == 1 && t.peer_ll[0] && (reinterpret_cast<uintptr_t>(t.peer_ll[0]) & 15)) return (int)cudaErrorInvalidValue;
   p->ll = t.peer_ll[0] != nullptr;
-  // the head split needs kHeadSplit partial slots per head in the attention
-  // workspace and groups of CTAs that stay aligned across the grid
-  p->split = ((s->max_seq + kChunk - 1) / kChunk) >= kHeadSplit && tosk_num_sms() % kHeadSplit == 0;
   int e = make_geo(q_dim + 2 * kv_dim, s->dim, s->wtype, 2, p->g[K_QKV]);
   if (!e) e = make_geo(t.n_rows, t.q_full, s->wtype, 1, p->g[K_O]);
   if (!e) e = make_geo(2 * t.n_ff, s->dim, s->wtype, 2, p->g[K_GU]);

@@ -25,9 +25,12 @@
 //     depend on nothing, so the ring fills before the previous kernel has
 //     finished;
 //   * warps 2..17, two groups of eight taking alternate K chunks, turn the
-//     raw blocks into the fp16 hi / lo A tiles (UMMA K-major SWIZZLE_128B,
-//     one row and one block a thread, consecutive lanes on consecutive rows:
-//     no bank conflicts on either side) in a ring of A stages;
+//     raw blocks into the fp16 hi / lo A operands in tensor memory (one row
+//     and one block a thread, the row in the TMEM lane of that number,
+//     tcgen05.st), a ring of A stages of 64 columns beside the accumulators.
+//     The tensor cores then read only the activations from shared memory:
+//     with A there too, its writes and the MMAs' reads of both operands
+//     (~76 KB a chunk at 16 tokens) made a chunk shared-memory bound;
 //   * warp 22 bulk-copies the prepared activation parts (the B tiles) into
 //     their own ring, ahead of the MMAs: for up to 32 tokens one copy covers
 //     the four chunks of a weight stage (an L2-to-shared copy takes ~1.5 us
@@ -61,7 +64,6 @@ namespace tos {
 constexpr int kWR = 128;                  // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kTok = 128;                 // most tokens per tile (MMA N)
 constexpr int kBK = 64;                   // K per chunk: one 128-byte fp16 row
-constexpr int kAPart = kWR * kBK * 2;     // 16 KB: one weight operand part of a chunk
 constexpr int kRawBlk = 8;                // GGUF blocks a row per raw stage
 constexpr int kRawCh = kRawBlk / 2;       // K chunks per raw stage
 constexpr int kDqWarps = 8;               // dequantising warps per group
@@ -72,7 +74,7 @@ constexpr int kEp0 = kDq0 + kDqGroups * kDqWarps;        // first epilogue warp
 constexpr int kBw = kEp0 + kEpWarps;                     // activation copy warp
 constexpr int kGThreads = 32 * (kBw + 1);                // 736: six warps on some SM
                                                          // sub-partitions, 80 registers a thread
-constexpr int kMaxSA = 4;                 // A stages (weight hi/lo of one chunk)
+constexpr int kMaxSA = 4;                 // A stages in TMEM (weight hi/lo of one chunk)
 constexpr int kMaxSB = 8;                 // B stages (activation hi/lo of one chunk)
 constexpr int kMaxR = 8;                  // raw stages
 constexpr int kHdrBytes = 512;
@@ -107,6 +109,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same MMA with A (128 rows x 16 fp16) in tensor memory: lane m holds
+// row m, column j its K elements 2j and 2j + 1 (low half first).
+__device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -151,6 +165,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers
+// (completion: tmem_st_wait).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Byte offset of 16-byte chunk c (0..7) of row r in a K-major SWIZZLE_128B
 // tile of 128-byte rows.
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
@@ -191,14 +217,17 @@ struct GemmArgs {
   int nb, nbp, N, K, nkc;
   const uint8_t* xa;    // prepared activations [mtiles][nkc][hi, lo][NB rows x 128 B]
   const float* xs;      // per-row inverse activation scales [mtiles * NB]
-  float* y;             // Y [M][N]
+  float* y;             // Y [M][N] (epi 0), the residual stream [M][N] (epi 1) or H [M][N / 2] (epi 2)
+  int epi;              // epilogue: 0 store, 1 add to y (residual), 2 SiLU(row 2j) * row 2j+1 into y
   float* part;          // K-slice partials [splits][M][N]
   int M, NB, mtiles, ntiles, splits, kcps, units;
   int full;             // tiles 0..full-1 run whole; the rest in `splits` K slices each
   int SA, SB, R;        // A, B and raw stages in the rings
   int bcs;              // chunks per B stage: kRawCh (one copy per weight stage) or 1
   int cat;              // 1: [X_hi X_lo] as one operand, accumulators of 2 NB columns
-  uint32_t b_bytes, raw_bytes, tcols;   // b_bytes: one B stage
+  uint32_t b_bytes, raw_bytes, tcols;   // b_bytes: one B stage; tcols: TMEM columns allocated
+  uint32_t acols;       // TMEM columns of one accumulator (NB, or 2 NB with cat)
+  uint32_t aoff;        // first TMEM column of the A stages (64 columns each: hi, lo)
   int* err;
 };
 
@@ -410,8 +439,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   uint64_t* drain = tm_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const uint32_t sbase = (smem_u32(gsm) + kHdrBytes + 1023) & ~1023u;
-  uint8_t* aring = gsm + (sbase - smem_u32(gsm));
-  uint8_t* bring = aring + (size_t)a.SA * (2 * kAPart);
+  uint8_t* bring = gsm + (sbase - smem_u32(gsm));
   uint8_t* raws = bring + (size_t)a.SB * a.b_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -435,7 +463,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
     mbar_init(drain, 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, a.tcols);   // two accumulators of NB fp32 columns
+  if (warp == 0) tmem_alloc(tmem_slot, a.tcols);   // two accumulators, then the A stages
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -510,7 +538,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       if (v >= 2 && !warp_wait(&tm_empty[buf], ((v >> 1) - 1) & 1, a.err, 22)) break;
       tc_fence_after();
       const uint32_t idesc = a.cat ? idesc_n(2 * a.NB) : idesc_n(w.ntok);
-      const uint32_t d = taddr + (uint32_t)(buf * (a.cat ? 2 * a.NB : a.NB));
+      const uint32_t d = taddr + (uint32_t)buf * a.acols;
       int c = 0;   // chunks of this unit so far (run order)
       for (int q = 0; q < w.nst && ok; ++q) {
        const int cn = min(kRawCh, w.nk - stage_c0(w, q));
@@ -524,20 +552,20 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
           break;
         }
         tc_fence_after();
-        const uint32_t ab = smem_u32(aring + (size_t)sa * (2 * kAPart));
+        const uint32_t ah0 = taddr + a.aoff + 64u * (uint32_t)sa, al0 = ah0 + 32u;   // A hi / lo in TMEM
         const uint32_t bh0 = smem_u32(bring + (size_t)sb * a.b_bytes) + (uint32_t)(cc % a.bcs) * 256u * a.NB;
         const uint32_t bl0 = bh0 + (uint32_t)a.NB * 128u;
         if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ah = sw128_desc(ab + 32 * kk), al = sw128_desc(ab + kAPart + 32 * kk);
+            const uint32_t ah = ah0 + 8u * kk, al = al0 + 8u * kk;   // 16 K elements = 8 columns
             const uint64_t bh = sw128_desc(bh0 + 32 * kk), bl = sw128_desc(bl0 + 32 * kk);
-            umma_f16(d, ah, bh, idesc, (c > 0 || kk > 0) ? 1u : 0u);   // c counts chunks in run order
+            umma_f16_ta(d, ah, bh, idesc, (c > 0 || kk > 0) ? 1u : 0u);   // c counts chunks in run order
             if (a.cat) {
-              umma_f16(d, al, bh, idesc, 1u);   // bh spans the hi and the lo rows
+              umma_f16_ta(d, al, bh, idesc, 1u);   // bh spans the hi and the lo rows
             } else {
-              umma_f16(d, ah, bl, idesc, 1u);
-              umma_f16(d, al, bh, idesc, 1u);
+              umma_f16_ta(d, ah, bl, idesc, 1u);
+              umma_f16_ta(d, al, bh, idesc, 1u);
             }
           }
           umma_commit(&a_empty[sa]);   // the chunk's operands may be refilled once read
@@ -559,9 +587,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
     }
   } else if (warp < kEp0) {
     // ---------------- dequantisation: group g takes the chunks i with i % 2 == g ----------------
-    const int g = (warp - kDq0) / kDqWarps;
-    const int tid = (int)threadIdx.x - 32 * (kDq0 + g * kDqWarps);   // 0..255
-    const int r = tid & (kWR - 1), h = tid >> 7;   // weight row in the tile, block of the chunk
+    // a warp reaches only TMEM lanes 32 (warp % 4) .. + 31, so it takes those
+    // rows: warps 0..3 of a group cover the four lane quarters for the
+    // chunk's first block, warps 4..7 for its second
+    const int g = (warp - kDq0) / kDqWarps, wg = (warp - kDq0) % kDqWarps;
+    const int r = 32 * (warp & 3) + lane, h = wg >> 2;   // weight row in the tile, block of the chunk
+    const uint32_t tlane = taddr + ((uint32_t)(32 * (warp & 3)) << 16) + a.aoff + 16u * (uint32_t)h;
     int i = 0, j = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
@@ -584,7 +615,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
             ok = false;
             break;
           }
-          uint8_t* st = aring + (size_t)s * (2 * kAPart);
+          tc_fence_after();   // the MMAs that read this A stage are complete
           uint32_t hi[16], lo[16];
           if (valid) {
             const int blk = 2 * c + h;    // block of the raw stage, 0..7
@@ -600,14 +631,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
 #pragma unroll
             for (int e = 0; e < 16; ++e) hi[e] = lo[e] = 0u;
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t off = sw128_off(r, 4 * h + q);
-            *reinterpret_cast<uint4*>(st + off) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
-            *reinterpret_cast<uint4*>(st + kAPart + off) =
-                make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
-          }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
+          // row r's K elements 32 h .. 32 h + 31 of the chunk: columns 16 h ..
+          // 16 h + 15 of the stage's hi and lo parts
+          const uint32_t ta = tlane + 64u * (uint32_t)s;
+          tmem_st16(ta, hi);
+          tmem_st16(ta + 32u, lo);
+          tmem_st_wait();
+          tc_fence_before();   // ordered before the MMA warp's issue
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[s]);
         }
@@ -632,7 +662,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       const float inv_ws = vn ? 1.0f / a.rws[n] : 0.0f;   // exact: power of two
       const int m0 = w.mt * kTok;
       const int mend = min(a.M, m0 + w.ntok);
-      const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * (a.cat ? 2 * a.NB : a.NB));
+      const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)buf * a.acols;
       // a whole tile goes to Y; a K slice to its partial plane (added by
       // the slice-sum kernel)
       float* dst = w.ns == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
@@ -645,10 +675,32 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
 #pragma unroll
           for (int e = 0; e < 16; ++e) vv[e] = __fadd_rn(vv[e], vl[e]);
         }
+        if (w.ns > 1 || a.epi == 0) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int m = m0 + c0 + e;
-          if (vn && m < mend) dst[(size_t)m * a.N + n] = __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws);
+          for (int e = 0; e < 16; ++e) {
+            const int m = m0 + c0 + e;
+            if (vn && m < mend) dst[(size_t)m * a.N + n] = __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws);
+          }
+        } else if (a.epi == 1) {
+          // residual (llm.c:717-718, 732-733): x + y, as pf_add_kernel
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int m = m0 + c0 + e;
+            if (vn && m < mend) {
+              float* px = a.y + (size_t)m * a.N + n;
+              *px = __fadd_rn(*px, __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws));
+            }
+          }
+        } else {
+          // gate|up rows interleaved (2j gate, 2j + 1 up, in lanes r, r ^ 1):
+          // h = SiLU(gate) * up (llm.c:726-729), as pf_swiglu_kernel
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int m = m0 + c0 + e;
+            const float v = m < mend ? __fmul_rn(__fmul_rn(vv[e], a.xs[m]), inv_ws) : 0.0f;
+            const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+            if (vn && m < mend && (n & 1) == 0) a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = __fmul_rn(ref_silu(v), up);
+          }
         }
       }
       tc_fence_before();
@@ -664,23 +716,30 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   }
 }
 
-// The K slices of the tiles past `full`, added in slice order.
+// The K slices of the tiles past `full`, added in slice order, then the
+// epilogue of gemm_tc_kernel (epi 2: one thread per row pair).
 __global__ void __launch_bounds__(256) gemm_slice_sum_kernel(const float* __restrict__ part, int splits, int M,
                                                              int N, int NB, int full, int ntiles, int rem,
-                                                             float* __restrict__ y) {
+                                                             int epi, float* __restrict__ y) {
   pdl_wait();
   pdl_trigger();
-  const size_t per = (size_t)NB * kWR;   // tokens x columns of one tile
+  const int pw = epi == 2 ? 2 : 1;        // columns a thread covers
+  const size_t per = (size_t)NB * kWR / pw;   // threads of one tile (tokens x columns)
   const size_t total = (size_t)rem * per;
+  auto sum = [&](int m, int n) {
+    float acc = part[(size_t)m * N + n];
+    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[((size_t)s * M + m) * N + n]);
+    return acc;
+  };
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int t = full + (int)(i / per);
     const int wi = (int)(i % per);
-    const int m = (t / ntiles) * kTok + wi / kWR;
-    const int n = (t % ntiles) * kWR + wi % kWR;
+    const int m = (t / ntiles) * kTok + wi / (kWR / pw);
+    const int n = (t % ntiles) * kWR + pw * (wi % (kWR / pw));
     if (m >= M || n >= N) continue;
-    float acc = part[(size_t)m * N + n];
-    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[((size_t)s * M + m) * N + n]);
-    y[(size_t)m * N + n] = acc;
+    if (epi == 0) y[(size_t)m * N + n] = sum(m, n);
+    else if (epi == 1) y[(size_t)m * N + n] = __fadd_rn(y[(size_t)m * N + n], sum(m, n));
+    else y[(size_t)m * (N >> 1) + (n >> 1)] = __fmul_rn(ref_silu(sum(m, n)), sum(m, n + 1));
   }
 }
 
@@ -712,7 +771,7 @@ extern "C" int tosk_qmat_row_scales(tosk_qmat_t* m, cudaStream_t st) {
 namespace {
 struct GemmPlan {
   int mtiles, ntiles, nkc, NB, splits, kcps, units, grid, SA, SB, R, full, bcs, cat;
-  uint32_t b_bytes, raw_bytes, tcols;
+  uint32_t b_bytes, raw_bytes, tcols, acols, aoff;
   size_t off_xs, off_part, bytes, smem;
 };
 
@@ -735,26 +794,28 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   p.raw_bytes = (uint32_t)(16384 * (qb / 16) + 2048);   // quant box(es), then the scale box
   p.bcs = p.NB <= 32 ? kRawCh : 1;
   p.b_bytes = (uint32_t)(2 * p.NB * 128 * p.bcs);
-  p.SA = p.NB <= 32 ? 2 : p.NB <= 64 ? 3 : 2;
+  p.cat = p.NB <= 64 ? 1 : 0;
+  // TMEM (512 columns, one CTA per SM): two accumulators, then the A
+  // stages of 64 columns (hi and lo parts of a 64-wide K chunk)
+  p.tcols = 512;
+  p.acols = (uint32_t)(p.cat ? 2 * p.NB : p.NB);
+  p.aoff = 2 * p.acols;
+  p.SA = (int)min((uint32_t)kMaxSA, (p.tcols - p.aoff) / 64u);
   p.SB = p.NB <= 32 ? 4 : p.NB >= 96 ? 3 : 4;
   const size_t avail = (size_t)kMaxSmem - kHdrBytes - 1024;
   for (;; --p.SB) {
-    const size_t used = (size_t)p.SA * 2 * kAPart + (size_t)p.SB * p.b_bytes;
+    const size_t used = (size_t)p.SB * p.b_bytes;
     p.R = used < avail ? (int)min((size_t)kMaxR, (avail - used) / p.raw_bytes) : 0;
     if (p.R >= 2 || p.SB == 2) break;
   }
-  p.cat = p.NB <= 64 ? 1 : 0;
-  p.tcols = 32;
-  while (p.tcols < (uint32_t)(2 * p.NB * (p.cat ? 2 : 1))) p.tcols <<= 1;
-  p.smem = (size_t)kHdrBytes + 1024 + (size_t)p.SA * 2 * kAPart + (size_t)p.SB * p.b_bytes +
-           (size_t)p.R * p.raw_bytes;
+  p.smem = (size_t)kHdrBytes + 1024 + (size_t)p.SB * p.b_bytes + (size_t)p.R * p.raw_bytes;
 
   const int tiles = p.mtiles * p.ntiles;
   const int sms = tosk_num_sms();
   const double t_mem = 256.0 * (qb + 2) / (6500.0 / sms);
   const double t_mma = 3.0 * kWR * p.NB * kBK / 5600.0;
   const double t_dq = qb == 16 ? 95.0 : 250.0;
-  const double t_issue = (p.cat ? 8 : 12) * 44.0;   // one tcgen05.mma issued every ~85 cycles (measured)
+  const double t_issue = (p.cat ? 8 : 12) * 10.0;   // MMA issue per chunk (estimate, A in TMEM)
   const double tc = fmax(fmax(t_mem, t_issue), fmax(t_mma, t_dq));
   const int rounds = tiles / sms;
   const int rem = tiles - rounds * sms;
@@ -832,10 +893,11 @@ extern "C" size_t tosk_gemm_ws_bytes(int M, int N, int K) {
 }
 
 namespace {
-int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int M, float* y, void* ws,
+int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int M, float* y, int epi, void* ws,
            size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
   if (!w || !x || !y || !ws || M <= 0 || (w->qb != 16 && w->qb != 32)) return (int)cudaErrorInvalidValue;
   const int N = w->rows, K = w->cols;
+  if (epi == 2 && (N & 1)) return (int)cudaErrorInvalidValue;
   if (K % kBK || (reinterpret_cast<uintptr_t>(ws) & 255)) return (int)cudaErrorInvalidValue;
   const GemmPlan p = gemm_plan(M, N, K, w->qb);
   if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
@@ -880,6 +942,7 @@ int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int
   a.xa = xa;
   a.xs = xs;
   a.y = y;
+  a.epi = epi;
   a.part = part;
   a.M = M;
   a.NB = p.NB;
@@ -897,6 +960,8 @@ int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int
   a.b_bytes = p.b_bytes;
   a.raw_bytes = p.raw_bytes;
   a.tcols = p.tcols;
+  a.acols = p.acols;
+  a.aoff = p.aoff;
   a.err = err;
   static bool attr_done[2] = {false, false};
   const int qi = w->qb == 16 ? 0 : 1;
@@ -912,8 +977,8 @@ int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int
                         : launch_ex(gemm_tc_kernel<32>, p.grid, kGThreads, p.smem, pdl, st, gargs);
   const int tiles = p.mtiles * p.ntiles;
   if (e || p.splits == 1 || tiles == p.full) return e;
-  int sp = p.splits, Mi = M, Ni = N, NBi = p.NB, full = p.full, nti = p.ntiles, rem = tiles - p.full;
-  void* rargs[] = {&part, &sp, &Mi, &Ni, &NBi, &full, &nti, &rem, &y};
+  int sp = p.splits, Mi = M, Ni = N, NBi = p.NB, full = p.full, nti = p.ntiles, rem = tiles - p.full, ep = epi;
+  void* rargs[] = {&part, &sp, &Mi, &Ni, &NBi, &full, &nti, &rem, &ep, &y};
   const size_t total = (size_t)rem * p.NB * kWR;
   const int rgrid = (int)min((size_t)tosk_num_sms() * 8, (total + 255) / 256);
   return launch_ex(gemm_slice_sum_kernel, rgrid, 256, 0, pdl, st, rargs);
@@ -922,11 +987,23 @@ int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int
 
 extern "C" int tosk_gemm_q(const tosk_qmat_t* w, const float* x, int M, float* y, void* ws, size_t ws_bytes,
                            int* err, int pdl, cudaStream_t st) {
-  return gemm_q(w, x, nullptr, 0.0f, M, y, ws, ws_bytes, err, pdl, st);
+  return gemm_q(w, x, nullptr, 0.0f, M, y, 0, ws, ws_bytes, err, pdl, st);
 }
 
 extern "C" int tosk_gemm_q_norm(const tosk_qmat_t* w, const float* x, const float* norm_w, float eps, int M,
                                 float* y, void* ws, size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
   if (!norm_w) return (int)cudaErrorInvalidValue;
-  return gemm_q(w, x, norm_w, eps, M, y, ws, ws_bytes, err, pdl, st);
+  return gemm_q(w, x, norm_w, eps, M, y, 0, ws, ws_bytes, err, pdl, st);
+}
+
+extern "C" int tosk_gemm_q_residual(const tosk_qmat_t* w, const float* x, int M, float* res, void* ws,
+                                    size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
+  return gemm_q(w, x, nullptr, 0.0f, M, res, 1, ws, ws_bytes, err, pdl, st);
+}
+
+extern "C" int tosk_gemm_q_norm_swiglu(const tosk_qmat_t* w, const float* x, const float* norm_w, float eps,
+                                       int M, float* h, void* ws, size_t ws_bytes, int* err, int pdl,
+                                       cudaStream_t st) {
+  if (!norm_w) return (int)cudaErrorInvalidValue;
+  return gemm_q(w, x, norm_w, eps, M, h, 2, ws, ws_bytes, err, pdl, st);
 }

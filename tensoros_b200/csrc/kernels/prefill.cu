@@ -9,8 +9,8 @@
 //   pf_attention_kernel  causal single-query attention of every token over
 //                        the cache (llm.c:683-714) with llm_expf weights,
 //                        tree sums (FAST numerics)
-//   pf_add_kernel, pf_swiglu_kernel  residual (llm.c:718, 733) and
-//                        SiLU(gate)*up (llm.c:726-729) with the decode order
+// The residual adds (llm.c:718, 733) and SiLU(gate)*up (llm.c:726-729) run
+// in the GEMMs' epilogues.
 // The rope/store and attention kernels also serve batched decode: n tokens
 // of n different sequences, each at its own position with its own cache.
 #include <cuda_runtime.h>
@@ -176,6 +176,54 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
   if (lane == 0) red[warp] = l;
   __syncthreads();
   const float inv = 1.0f / ((red[0] + red[1]) + (red[2] + red[3]) + 1e-10f);
+  if (hd % 32 == 0 && hd <= 256) {
+    // warp w takes positions 8 w .. 8 w + 7, then 32 further on (eight V rows
+    // in flight); lane l covers d = 4 l .. 4 l + 3 (+ 128); the four warps'
+    // partial sums are added in warp order
+    __shared__ float part[4][256];
+    const bool f16 = kv_type == TOSK_F16;
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int j0 = warp * 8; j0 < n; j0 += 32) {
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int d = 128 * s + 4 * lane;
+        if (d < hd) {
+          float4 v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const size_t idx = (size_t)(j0 + k) * kv_dim + (size_t)kvh * hd + d;
+            if (j0 + k >= n) {
+              v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else if (f16) {
+              const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(vc) + idx);
+              const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+              const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+              v[k] = make_float4(a.x, a.y, b.x, b.y);
+            } else {
+              v[k] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vc) + idx);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float e = j0 + k < n ? sc[j0 + k] : 0.0f;
+            acc[s].x = fmaf(e, v[k].x, acc[s].x);
+            acc[s].y = fmaf(e, v[k].y, acc[s].y);
+            acc[s].z = fmaf(e, v[k].z, acc[s].z);
+            acc[s].w = fmaf(e, v[k].w, acc[s].w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int d = 128 * s + 4 * lane;
+      if (d < hd) *reinterpret_cast<float4*>(&part[warp][d]) = acc[s];
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x)
+      out[((size_t)t * n_heads + h) * hd + d] = (((part[0][d] + part[1][d]) + part[2][d]) + part[3][d]) * inv;
+    return;
+  }
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     // eight independent chains (eight V rows in flight), added in a fixed order
     float a[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -192,21 +240,6 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
     const float s = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
     out[((size_t)t * n_heads + h) * hd + d] = s * inv;
   }
-}
-
-__global__ void pf_add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
-  pdl_wait();
-  pdl_trigger();
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    x[i] = __fadd_rn(x[i], y[i]);
-}
-
-// gu rows interleaved (2j = gate j, 2j+1 = up j) -> h[j] = silu(g) * u
-__global__ void pf_swiglu_kernel(float* __restrict__ h, const float* __restrict__ gu, size_t n) {
-  pdl_wait();
-  pdl_trigger();
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    h[i] = __fmul_rn(ref_silu(gu[2 * i]), gu[2 * i + 1]);
 }
 
 }  // namespace tos
@@ -226,10 +259,6 @@ int launch_pf(const void* func, dim3 grid, dim3 block, size_t smem, void** args,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return (int)cudaLaunchKernelExC(&cfg, func, args);
-}
-int ew_grid(size_t n) {
-  size_t g = (n + 255) / 256;
-  return (int)(g > 4096 ? 4096 : (g < 1 ? 1 : g));
 }
 }  // namespace
 
@@ -295,14 +324,4 @@ extern "C" int tosk_bd_attention(const float* q, const void* kc, const void* vc,
   void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out,
                   (void*)&pos, (void*)&slot, &cstride};
   return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
-}
-
-extern "C" int tosk_pf_add(float* x, const float* y, size_t n, cudaStream_t st) {
-  void* args[] = {&x, (void*)&y, &n};
-  return launch_pf((const void*)pf_add_kernel, dim3(ew_grid(n)), dim3(256), 0, args, st);
-}
-
-extern "C" int tosk_pf_swiglu(float* h, const float* gu, size_t n, cudaStream_t st) {
-  void* args[] = {&h, (void*)&gu, &n};
-  return launch_pf((const void*)pf_swiglu_kernel, dim3(ew_grid(n)), dim3(256), 0, args, st);
 }
