@@ -75,7 +75,8 @@ constexpr int kHeadMaxN = 1024;          // longest context of the one-phase-per
 constexpr int kNW = kWorkers / 32;       // worker warps
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4, K_N = 5 };
 // named barriers (0 is __syncthreads)
-enum { B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4 };
+enum { B_COMPUTE = 1, B_WORKERS = 2, B_CHAIN = 3, B_GROUP0 = 4, B_STAGED = 4 + kWorkers / 32 / 4 };
+static_assert(B_STAGED <= 15, "named barriers");
 
 // Geometry of one projection (the same in every layer).
 struct Geo {
@@ -190,14 +191,21 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Grid barrier for the worker threads of every CTA: the k-th call waits for
-// the counter to reach k * gridDim.x.  Returns false, in every worker thread
-// of the CTA alike, when the step must stop (an error here or elsewhere).
+// the counter to reach k * gridDim.x.  The CTA's writes are ordered before
+// its arrival by the CTA barrier and the release reduction (cumulative), and
+// the acquire load that sees the count orders the other CTAs' writes before
+// everything after the closing CTA barrier.  Returns false, in every worker
+// thread of the CTA alike, when the step must stop (an error here or
+// elsewhere).
 __device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target, int* err) {
   named_sync(B_WORKERS, kWorkers);
   if (threadIdx.x == 32 && !*reinterpret_cast<volatile int*>(&h->abort)) {
-    __threadfence();
-    atomicAdd(bar, 1u);
+    red_release_add(bar, 1u);
     const long long t0 = clock64();
     for (int i = 0;; ++i) {
       if (ld_acquire(bar) >= target) break;
@@ -214,7 +222,6 @@ __device__ __forceinline__ bool grid_sync(Hdr* h, unsigned* bar, unsigned target
         }
       }
     }
-    __threadfence();
   }
   named_sync(B_WORKERS, kWorkers);
   return !*reinterpret_cast<volatile int*>(&h->abort);
@@ -527,7 +534,8 @@ __device__ __forceinline__ void compute_gemv(const Params& p, Hdr* h, float* Xs,
       for (int q = ct; q < nq; q += 32 * kCompute) cp_async16(W4 + xsw(q), reinterpret_cast<const float4*>(nw) + q);
     cp_async_wait_all();
   }
-  named_sync(B_WORKERS, kWorkers);   // the vector is in shared memory (the chain warps read it too)
+  named_sync(B_COMPUTE, 32 * kCompute);   // the vector is in shared memory
+  if (nw) named_arrive(B_STAGED, kWorkers);   // ... for the chain warps' sum of squares too
   XFix xf;
   if (active) {
     float v[32];
@@ -796,8 +804,10 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
     }
     named_sync(B_CHAIN, 32 * kChain);
   }
-  named_sync(B_WORKERS, kWorkers);   // the compute warps have staged the input vector
-  if (nrm) ss = norm_scale(p, h, reinterpret_cast<const float4*>(Xs));
+  if (nrm) {
+    named_sync(B_STAGED, kWorkers);   // the compute warps have staged the input vector
+    ss = norm_scale(p, h, reinterpret_cast<const float4*>(Xs));
+  }
   for (int it = ((cw - gs0) % kChain + kChain) % kChain; it < nst; it += kChain) {
     const int gsi = gs0 + it;
     if (!wait_mb(&h->pfull[cw], (gsi / kChain) & 1, err, 4, &h->abort)) break;

@@ -24,9 +24,9 @@
 //     scale box, into a shared-memory ring (mbarrier complete_tx).  Weights
 //     depend on nothing, so the ring fills before the previous kernel has
 //     finished;
-//   * warps 2..17, two groups of eight taking alternate K chunks, turn the
-//     raw blocks into the fp16 hi / lo A operands in tensor memory (one row
-//     and one block a thread, the row in the TMEM lane of that number,
+//   * warps 2..17, four groups of four each taking every fourth K chunk,
+//     turn the raw blocks into the fp16 hi / lo A operands in tensor memory
+//     (one row a thread, the row in the TMEM lane of that number,
 //     tcgen05.st), a ring of A stages of 64 columns beside the accumulators.
 //     The tensor cores then read only the activations from shared memory:
 //     with A there too, its writes and the MMAs' reads of both operands
@@ -66,15 +66,15 @@ constexpr int kTok = 128;                 // most tokens per tile (MMA N)
 constexpr int kBK = 64;                   // K per chunk: one 128-byte fp16 row
 constexpr int kRawBlk = 8;                // GGUF blocks a row per raw stage
 constexpr int kRawCh = kRawBlk / 2;       // K chunks per raw stage
-constexpr int kDqWarps = 8;               // dequantising warps per group
-constexpr int kDqGroups = 2;
+constexpr int kDqWarps = 4;               // dequantising warps per group (one per TMEM lane quarter)
+constexpr int kDqGroups = 4;              // groups, each on every fourth K chunk
 constexpr int kEpWarps = 4;
 constexpr int kDq0 = 2;                                  // first dequantising warp
 constexpr int kEp0 = kDq0 + kDqGroups * kDqWarps;        // first epilogue warp
 constexpr int kBw = kEp0 + kEpWarps;                     // activation copy warp
 constexpr int kGThreads = 32 * (kBw + 1);                // 736: six warps on some SM
                                                          // sub-partitions, 80 registers a thread
-constexpr int kMaxSA = 4;                 // A stages in TMEM (weight hi/lo of one chunk)
+constexpr int kMaxSA = 7;                 // A stages in TMEM (weight hi/lo of one chunk)
 constexpr int kMaxSB = 8;                 // B stages (activation hi/lo of one chunk)
 constexpr int kMaxR = 8;                  // raw stages
 constexpr int kHdrBytes = 512;
@@ -586,13 +586,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
       mbar_wait(drain, 0, a.err, 27);
     }
   } else if (warp < kEp0) {
-    // ---------------- dequantisation: group g takes the chunks i with i % 2 == g ----------------
+    // ---------------- dequantisation: group g takes the chunks i with i % kDqGroups == g ----------------
     // a warp reaches only TMEM lanes 32 (warp % 4) .. + 31, so it takes those
-    // rows: warps 0..3 of a group cover the four lane quarters for the
-    // chunk's first block, warps 4..7 for its second
-    const int g = (warp - kDq0) / kDqWarps, wg = (warp - kDq0) % kDqWarps;
-    const int r = 32 * (warp & 3) + lane, h = wg >> 2;   // weight row in the tile, block of the chunk
-    const uint32_t tlane = taddr + ((uint32_t)(32 * (warp & 3)) << 16) + a.aoff + 16u * (uint32_t)h;
+    // rows (the group's four warps cover the four lane quarters); a thread
+    // dequantises both blocks of its row in the chunk
+    const int g = (warp - kDq0) / kDqWarps;
+    const int r = 32 * (warp & 3) + lane;   // weight row in the tile
+    const uint32_t tlane = taddr + ((uint32_t)(32 * (warp & 3)) << 16) + a.aoff;
     int i = 0, j = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
@@ -609,33 +609,36 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
         const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + 16384 * (QB / 16));
         const int cn = min(kRawCh, w.nk - stage_c0(w, q));
         for (int c = 0; c < cn; ++c, ++i) {
-          if ((i & 1) != g) continue;
+          if (i % kDqGroups != g) continue;
           const int s = i % a.SA;
           if (i >= a.SA && !warp_wait(&a_empty[s], ((i / a.SA) - 1) & 1, a.err, 25)) {
             ok = false;
             break;
           }
           tc_fence_after();   // the MMAs that read this A stage are complete
-          uint32_t hi[16], lo[16];
-          if (valid) {
-            const int blk = 2 * c + h;    // block of the raw stage, 0..7
-            const float dd = h2f(rs[8 * r + blk]);
-            if constexpr (QB == 16) {
-              dequant_q4(*reinterpret_cast<const uint4*>(rq + sw128_off(r, blk)), dd, ws, hi, lo);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {   // the chunk's two blocks
+            uint32_t hi[16], lo[16];
+            if (valid) {
+              const int blk = 2 * c + h;    // block of the raw stage, 0..7
+              const float dd = h2f(rs[8 * r + blk]);
+              if constexpr (QB == 16) {
+                dequant_q4(*reinterpret_cast<const uint4*>(rq + sw128_off(r, blk)), dd, ws, hi, lo);
+              } else {
+                const uint8_t* box = rq + 16384 * (blk >> 2);
+                dequant_q8(*reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3))),
+                           *reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3) + 1)), dd, ws, hi, lo);
+              }
             } else {
-              const uint8_t* box = rq + 16384 * (blk >> 2);
-              dequant_q8(*reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3))),
-                         *reinterpret_cast<const uint4*>(box + sw128_off(r, 2 * (blk & 3) + 1)), dd, ws, hi, lo);
-            }
-          } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) hi[e] = lo[e] = 0u;
+              for (int e = 0; e < 16; ++e) hi[e] = lo[e] = 0u;
+            }
+            // row r's K elements 32 h .. 32 h + 31 of the chunk: columns 16 h ..
+            // 16 h + 15 of the stage's hi and lo parts
+            const uint32_t ta = tlane + 64u * (uint32_t)s + 16u * (uint32_t)h;
+            tmem_st16(ta, hi);
+            tmem_st16(ta + 32u, lo);
           }
-          // row r's K elements 32 h .. 32 h + 31 of the chunk: columns 16 h ..
-          // 16 h + 15 of the stage's hi and lo parts
-          const uint32_t ta = tlane + 64u * (uint32_t)s;
-          tmem_st16(ta, hi);
-          tmem_st16(ta + 32u, lo);
           tmem_st_wait();
           tc_fence_before();   // ordered before the MMA warp's issue
           __syncwarp();

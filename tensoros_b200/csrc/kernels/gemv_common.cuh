@@ -48,6 +48,13 @@ __device__ __forceinline__ void named_sync(int id, int n) {
   __syncwarp();
   asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+// Arrive on named barrier id (n threads in all) without waiting: the
+// producer side of a producer / consumer hand-off (its earlier writes are
+// visible to the threads that wait on the barrier with named_sync).
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  __syncwarp();
+  asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
 // Output epilogue of one stage, run by a full warp: lane i (< n) holds the
 // row sum y of row r0 + i.  Paired epilogues (RoPE, SiLU*up) rely on stages
