@@ -1022,8 +1022,31 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
 // takes positions w, w + kNW, ... eight at a time (all eight K or V rows in
 // flight); the eight dot products of a warp meet in one reduce-scatter.
 
+// Four consecutive cache elements as loaded (fp16: two packed words) and as
+// floats.
+template <int ESZ> struct RawT { using type = float4; };
+template <> struct RawT<2> { using type = uint2; };
+template <int ESZ>
+__device__ __forceinline__ typename RawT<ESZ>::type ldraw(const uint8_t* p) {
+  return __ldcg(reinterpret_cast<const typename RawT<ESZ>::type*>(p));
+}
+__device__ __forceinline__ float4 unraw2(uint2 u) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <int ESZ>
+__device__ __forceinline__ float4 unraw(typename RawT<ESZ>::type r) {
+  if constexpr (ESZ == 2) return unraw2(r);
+  else return r;
+}
+
 template <int ESZ, bool kLL>
 __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, int layer) {
+  // rows in flight per warp: sixteen fp16 rows (two registers each), eight fp32
+  using KRaw = typename RawT<ESZ>::type;
+  constexpr int kRows = ESZ == 2 ? 16 : 8;
+  constexpr int kLow = ESZ == 2 ? 1 : 2;   // lane bits left to sum after the reduce-scatter
   const int w = (int)(threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
   const int wt = (int)threadIdx.x - 32;
   const int n = h->pos + 1;
@@ -1045,30 +1068,34 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       qv[sl] = d < hd ? __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d))
                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // scores (llm.c:686-692), eight positions per warp per pass
-    for (int t0 = w; t0 < n; t0 += 8 * kNW) {
-      float v[8];
+    // scores (llm.c:686-692), kRows positions per warp per pass (all their
+    // K rows in flight; fp16 rows stay packed until used)
+    for (int t0 = w; t0 < n; t0 += kRows * kNW) {
+      float v[kRows];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+      for (int u = 0; u < kRows; ++u) v[u] = 0.0f;
 #pragma unroll 1
       for (int sl = 0; sl < kMaxHd / 128; ++sl) {
         const int d = 128 * sl + 4 * lane;
         if (d < hd) {
-          float4 kv[8];
+          KRaw kr[kRows];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int u = 0; u < kRows; ++u) {
             const int t = t0 + u * kNW;
-            kv[u] = t < n ? ldcg4<ESZ>(kc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            kr[u] = t < n ? ldraw<ESZ>(kc + ((size_t)t * kv_dim + d) * ESZ) : KRaw{};
           }
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            v[u] = fmaf(qv[sl].x, kv[u].x, fmaf(qv[sl].y, kv[u].y, fmaf(qv[sl].z, kv[u].z, fmaf(qv[sl].w, kv[u].w, v[u]))));
+          for (int u = 0; u < kRows; ++u) {
+            const float4 kv = unraw<ESZ>(kr[u]);
+            v[u] = fmaf(qv[sl].x, kv.x, fmaf(qv[sl].y, kv.y, fmaf(qv[sl].z, kv.z, fmaf(qv[sl].w, kv.w, v[u]))));
+          }
         }
       }
-      // reduce-scatter over lane bits 4, 3, 2: lane l ends with position
-      // (l >> 2) & 7 summed over those bits; bits 1, 0 finish the sum
+      // reduce-scatter over the lane bits from 4 down: lane l ends with
+      // position (l >> kLow) % kRows summed over those bits; the kLow low
+      // bits finish the sum
 #pragma unroll
-      for (int half = 4, o = 16; half >= 1; half >>= 1, o >>= 1) {
+      for (int half = kRows / 2, o = 16; half >= 1; half >>= 1, o >>= 1) {
         const bool up = (lane & o) != 0;
 #pragma unroll
         for (int i = 0; i < half; ++i) {
@@ -1077,10 +1104,11 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
           v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
       }
-      float dot = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-      const int t = t0 + ((lane >> 2) & 7) * kNW;
-      if ((lane & 3) == 0 && t < n) sc[t] = dot * scale;
+      float dot = v[0];
+#pragma unroll
+      for (int o = 1 << (kLow - 1); o >= 1; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const int t = t0 + ((lane >> kLow) & (kRows - 1)) * kNW;
+      if ((lane & ((1 << kLow) - 1)) == 0 && t < n) sc[t] = dot * scale;
     }
     named_sync(B_WORKERS, kWorkers);
     // llm.c:509-521: max, e_t = llm_expf(s_t - max), sum (tree), 1/(sum + 1e-10)
@@ -1107,21 +1135,22 @@ __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, i
       const int d = 128 * sl + 4 * lane;
       if (d < hd) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t0 = w; t0 < n; t0 += 8 * kNW) {
-          float4 vv[8];
+        for (int t0 = w; t0 < n; t0 += kRows * kNW) {
+          KRaw vr[kRows];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int u = 0; u < kRows; ++u) {
             const int t = t0 + u * kNW;
-            vv[u] = t < n ? ldcg4<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vr[u] = t < n ? ldraw<ESZ>(vc + ((size_t)t * kv_dim + d) * ESZ) : KRaw{};
           }
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int u = 0; u < kRows; ++u) {
             const int t = t0 + u * kNW;
             const float e = t < n ? sc[t] : 0.0f;
-            acc.x = fmaf(e, vv[u].x, acc.x);
-            acc.y = fmaf(e, vv[u].y, acc.y);
-            acc.z = fmaf(e, vv[u].z, acc.z);
-            acc.w = fmaf(e, vv[u].w, acc.w);
+            const float4 vv = unraw<ESZ>(vr[u]);
+            acc.x = fmaf(e, vv.x, acc.x);
+            acc.y = fmaf(e, vv.y, acc.y);
+            acc.z = fmaf(e, vv.z, acc.z);
+            acc.w = fmaf(e, vv.w, acc.w);
           }
         }
         *reinterpret_cast<float4*>(part + w * kMaxHd + d) = acc;
