@@ -283,7 +283,9 @@ __global__ void __launch_bounds__(kFThreads) fast_scores_kernel(
   const int items = n_kv * nchunk;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    const int kvh = item / nchunk, c = item % nchunk;
+    // kv head fastest: the CTAs that run together read every head of the
+    // same positions, i.e. whole cache rows
+    const int kvh = item % n_kv, c = item / n_kv;
     const int tw = c * kFChunk + warp * 16;   // this warp's first position
     for (int g = 0; g < group; ++g) {
       const int h = kvh * group + g;
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(kFThreads) fast_pv_kernel(
   const int nchunk = (n + kFChunk - 1) / kFChunk;
   const int items = n_heads * nchunk;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    const int h = item / nchunk, c = item % nchunk;
+    const int h = item % n_heads, c = item / n_heads;   // head fastest (whole cache rows together)
     const int kvh = h / group;
     const int t0 = c * kFChunk, cn = min(kFChunk, n - t0);
     // global max of the head's scores (llm.c:509-511) from the chunk maxima
@@ -422,13 +424,29 @@ __global__ void __launch_bounds__(kFThreads) fast_pv_kernel(
     __syncthreads();
     if (s_last) {
       __threadfence();
+      // chunk order, eight chunks' loads in flight (L2: written by other CTAs)
+      const float* ls = lsum + (size_t)h * maxc;
+      const float* op = opart + (size_t)h * maxc * kFMaxHd;
       float L = 0.0f;
-      for (int i = 0; i < nchunk; ++i) L += *reinterpret_cast<volatile const float*>(&lsum[(size_t)h * maxc + i]);
+      for (int i0 = 0; i0 < nchunk; i0 += 8) {
+        float lv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) lv[k] = i0 + k < nchunk ? __ldcg(ls + i0 + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (i0 + k < nchunk) L += lv[k];
+      }
       const float inv = 1.0f / (L + 1e-10f);   // llm.c:519
       for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
-        for (int i = 0; i < nchunk; ++i)
-          o += *reinterpret_cast<volatile const float*>(&opart[((size_t)h * maxc + i) * kFMaxHd + d]);
+        for (int i0 = 0; i0 < nchunk; i0 += 8) {
+          float ov[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) ov[k] = i0 + k < nchunk ? __ldcg(op + (size_t)(i0 + k) * kFMaxHd + d) : 0.0f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (i0 + k < nchunk) o += ov[k];
+        }
         out[(size_t)h * hd + d] = o * inv;
       }
     }

@@ -857,7 +857,7 @@ __device__ __forceinline__ float warp_max_f(float m) {
 // positions, lane l covering d = 128 s + 4 l .. +3, all 16 rows in flight,
 // then a shuffle reduce-scatter; per-chunk maxima for the softmax pass.
 template <int ESZ>
-__device__ __noinline__ void attn_scores(const Params& p, Hdr* h, float* P, int layer) {
+__device__ __forceinline__ void attn_scores(const Params& p, Hdr* h, float* P, int layer) {
   const int w = (int)(threadIdx.x >> 5) - 1;
   const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
   float* wmax = P + grp * kGroupFloats + kChunk + 4;
@@ -872,7 +872,9 @@ __device__ __noinline__ void attn_scores(const Params& p, Hdr* h, float* P, int 
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const uint8_t* kc = reinterpret_cast<const uint8_t*>(p.s.layers[layer].k_cache);
   for (int item = blockIdx.x * kGroups + grp; item < items; item += gridDim.x * kGroups) {
-    const int kvh = item / nchunk, c = item % nchunk;
+    // kv head fastest: the groups that run together read every head of the
+    // same positions, i.e. whole cache rows
+    const int kvh = item % n_kv, c = item / n_kv;
     const int tw = c * kChunk + gw * 16;
     for (int gi = 0; gi < group; ++gi) {
       const int hh = kvh * group + gi;
@@ -929,7 +931,7 @@ __device__ __noinline__ void attn_scores(const Params& p, Hdr* h, float* P, int 
 // chunk's e-sum and sum_t e_t v_t; the last chunk of a head to finish adds
 // the chunks in order and divides by the sum (llm.c:519-521, 703-712).
 template <int ESZ, bool kLL>
-__device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int layer) {
+__device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int layer) {
   const int w = (int)(threadIdx.x >> 5) - 1;
   const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
   const int gt = gw * 32 + lane;
@@ -945,7 +947,7 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
   const int items = n_heads * nchunk;
   const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.s.layers[layer].v_cache);
   for (int item = blockIdx.x * kGroups + grp; item < items; item += gridDim.x * kGroups) {
-    const int hh = item / nchunk, c = item % nchunk;
+    const int hh = item % n_heads, c = item / n_heads;   // head fastest (whole cache rows together)
     const int kvh = hh / group;
     const int t0 = c * kChunk, cn = min(kChunk, n - t0);
     float m = -INFINITY;
@@ -1002,12 +1004,29 @@ __device__ __noinline__ void attn_pv(const Params& p, Hdr* h, float* P, int laye
     named_sync(B_GROUP0 + grp, 128);
     if (*s_last) {
       __threadfence();
+      // chunk order, eight chunks' loads in flight
+      const float* ls = p.lsum + (size_t)hh * p.maxc;
+      const float* op = p.opart + (size_t)hh * p.maxc * kMaxHd;
       float Ls = 0.0f;
-      for (int i = 0; i < nchunk; ++i) Ls += __ldcg(p.lsum + (size_t)hh * p.maxc + i);
+      for (int i0 = 0; i0 < nchunk; i0 += 8) {
+        float lv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) lv[k] = i0 + k < nchunk ? __ldcg(ls + i0 + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (i0 + k < nchunk) Ls += lv[k];
+      }
       const float inv = 1.0f / (Ls + 1e-10f);
       for (int d = gt; d < hd; d += 128) {
         float o = 0.0f;
-        for (int i = 0; i < nchunk; ++i) o += __ldcg(p.opart + ((size_t)hh * p.maxc + i) * kMaxHd + d);
+        for (int i0 = 0; i0 < nchunk; i0 += 8) {
+          float ov[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) ov[k] = i0 + k < nchunk ? __ldcg(op + (size_t)(i0 + k) * kMaxHd + d) : 0.0f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (i0 + k < nchunk) o += ov[k];
+        }
         if (kLL) ll_store_all(p, X_ATT, p.s.q0 + (size_t)hh * hd + d, o * inv, ll_epoch(h, layer, X_ATT));
         else p.s.att[(size_t)hh * hd + d] = o * inv;
       }
