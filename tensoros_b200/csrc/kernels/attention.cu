@@ -262,11 +262,30 @@ __device__ __forceinline__ float4 load4(const uint8_t* p) {
   }
 }
 
+// Four cache elements as loaded (fp16: two packed words, half the registers
+// of four floats, so more rows stay in flight per SM) and as floats.
+template <int ESZ> struct RawT { using type = float4; };
+template <> struct RawT<2> { using type = uint2; };
+template <int ESZ>
+__device__ __forceinline__ typename RawT<ESZ>::type ldraw(const uint8_t* p) {
+  return *reinterpret_cast<const typename RawT<ESZ>::type*>(p);
+}
+template <int ESZ>
+__device__ __forceinline__ float4 unraw(typename RawT<ESZ>::type r) {
+  if constexpr (ESZ == 2) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    return r;
+  }
+}
+
 // Lane l covers d = 128 s + 4 l .. +3 for slabs s < ceil(hd / 128).
 constexpr int kFSlabs = kFMaxHd / 128;
 
 template <int ESZ>
-__global__ void __launch_bounds__(kFThreads) fast_scores_kernel(
+__global__ void __launch_bounds__(kFThreads, 8) fast_scores_kernel(
     const float* __restrict__ q, const uint8_t* __restrict__ kc, int n_heads, int n_kv, int hd,
     const int* __restrict__ pos_dev, int pos_arg, float* __restrict__ S, float* __restrict__ cmax,
     int* __restrict__ cnt, int max_ctx, int maxc) {
@@ -292,19 +311,21 @@ __global__ void __launch_bounds__(kFThreads) fast_scores_kernel(
       float v[16];
 #pragma unroll
       for (int p = 0; p < 16; ++p) v[p] = 0.0f;
-#pragma unroll
+#pragma unroll 1
       for (int sl = 0; sl < kFSlabs; ++sl) {
         const int d = 128 * sl + 4 * lane;
         if (d < hd) {
           const float4 qv = *reinterpret_cast<const float4*>(q + (size_t)h * hd + d);
-          float4 kv[16];
+          typename RawT<ESZ>::type kr[16];
 #pragma unroll
           for (int p = 0; p < 16; ++p)   // all 16 rows in flight at once
-            kv[p] = tw + p < n ? load4<ESZ>(kc + ((size_t)(tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            kr[p] = tw + p < n ? ldraw<ESZ>(kc + ((size_t)(tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                               : typename RawT<ESZ>::type{};
 #pragma unroll
-          for (int p = 0; p < 16; ++p)
-            v[p] = fmaf(qv.x, kv[p].x, fmaf(qv.y, kv[p].y, fmaf(qv.z, kv[p].z, fmaf(qv.w, kv[p].w, v[p]))));
+          for (int p = 0; p < 16; ++p) {
+            const float4 kv = unraw<ESZ>(kr[p]);
+            v[p] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, v[p]))));
+          }
         }
       }
       // reduce-scatter: after the steps over lane bits 4..1, lane l holds
@@ -341,7 +362,7 @@ __global__ void __launch_bounds__(kFThreads) fast_scores_kernel(
 }
 
 template <int ESZ>
-__global__ void __launch_bounds__(kFThreads) fast_pv_kernel(
+__global__ void __launch_bounds__(kFThreads, 8) fast_pv_kernel(
     const float* __restrict__ S, const float* __restrict__ cmax, const uint8_t* __restrict__ vc, int n_heads,
     int n_kv, int hd, const int* __restrict__ pos_dev, int pos_arg, float* __restrict__ lsum,
     float* __restrict__ opart, int* __restrict__ cnt, float* __restrict__ out, int max_ctx, int maxc) {
@@ -383,23 +404,24 @@ __global__ void __launch_bounds__(kFThreads) fast_pv_kernel(
     if (lane == 0) red[warp] = l;
     // sum_t e_t v_t[d]: warp w takes 16 positions, lane l four consecutive d
     const int tw = warp * 16;
-#pragma unroll
+#pragma unroll 1
     for (int sl = 0; sl < kFSlabs; ++sl) {
       const int d = 128 * sl + 4 * lane;
       if (d < hd) {
-        float4 vv[16];
+        typename RawT<ESZ>::type vr[16];
 #pragma unroll
         for (int p = 0; p < 16; ++p)   // all 16 rows in flight at once
-          vv[p] = tw + p < cn ? load4<ESZ>(vc + ((size_t)(t0 + tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+          vr[p] = tw + p < cn ? ldraw<ESZ>(vc + ((size_t)(t0 + tw + p) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                              : typename RawT<ESZ>::type{};
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
           const float ep = es[tw + p];
-          acc.x = fmaf(ep, vv[p].x, acc.x);
-          acc.y = fmaf(ep, vv[p].y, acc.y);
-          acc.z = fmaf(ep, vv[p].z, acc.z);
-          acc.w = fmaf(ep, vv[p].w, acc.w);
+          const float4 vv = unraw<ESZ>(vr[p]);
+          acc.x = fmaf(ep, vv.x, acc.x);
+          acc.y = fmaf(ep, vv.y, acc.y);
+          acc.z = fmaf(ep, vv.z, acc.z);
+          acc.w = fmaf(ep, vv.w, acc.w);
         }
         *reinterpret_cast<float4*>(&wpart[warp][d]) = acc;
       }

@@ -297,11 +297,23 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
   const int nkc = K / kBK;
   const bool valid = m < M;
   const float* xr = x + (size_t)m * K;
+  // the row in 16-byte pieces, eight per thread in flight (K is a multiple
+  // of 64, rows and norm weights 16-byte aligned)
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  const float4* w4 = reinterpret_cast<const float4*>(nw);
+  const int K4 = K / 4, bd = (int)blockDim.x;
   float ss = 1.0f;
   if (nw) {
     float acc = 0.0f;
     if (valid)
-      for (int i = threadIdx.x; i < K; i += blockDim.x) acc = fmaf(xr[i], xr[i], acc);
+      for (int i0 = threadIdx.x; i0 < K4; i0 += 8 * bd) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = i0 + u * bd < K4 ? x4[i0 + u * bd] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          acc = fmaf(v[u].w, v[u].w, fmaf(v[u].z, v[u].z, fmaf(v[u].y, v[u].y, fmaf(v[u].x, v[u].x, acc))));
+      }
     for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -312,11 +324,23 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
     __syncthreads();
     ss = s_ss;
   }
-  // element i of the (normalised) row
-  auto val = [&](int i) { return nw ? __fmul_rn(__fmul_rn(xr[i], ss), nw[i]) : xr[i]; };
+  // an element of the (normalised) row
+  auto nval = [&](float xv, float wv) { return nw ? __fmul_rn(__fmul_rn(xv, ss), wv) : xv; };
   float mx = 0.0f;
   if (valid)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(val(i)));
+    for (int i0 = threadIdx.x; i0 < K4; i0 += 8 * bd) {
+      float4 v[8], wv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const bool in = i0 + u * bd < K4;
+        v[u] = in ? x4[i0 + u * bd] : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv[u] = in && nw ? w4[i0 + u * bd] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        mx = fmaxf(fmaxf(fmaxf(mx, fabsf(nval(v[u].x, wv[u].x))), fabsf(nval(v[u].y, wv[u].y))),
+                   fmaxf(fabsf(nval(v[u].z, wv[u].z)), fabsf(nval(v[u].w, wv[u].w))));
+    }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
@@ -329,12 +353,20 @@ __global__ void __launch_bounds__(128) gemm_prep_kernel(const float* __restrict_
   // one 16-byte group (8 elements) per thread and step
   for (int q = (int)(((long long)blockIdx.y * ng) / gridDim.y) + threadIdx.x; q < g1; q += blockDim.x) {
     const int kc = q / 8, c = q % 8;
+    float g8[8];   // elements 8q .. 8q + 7, normalised
+    if (valid) {
+      const float4 a = x4[2 * q], b = x4[2 * q + 1];
+      const float4 wa = nw ? w4[2 * q] : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 wb = nw ? w4[2 * q + 1] : make_float4(1.f, 1.f, 1.f, 1.f);
+      g8[0] = nval(a.x, wa.x); g8[1] = nval(a.y, wa.y); g8[2] = nval(a.z, wa.z); g8[3] = nval(a.w, wa.w);
+      g8[4] = nval(b.x, wb.x); g8[5] = nval(b.y, wb.y); g8[6] = nval(b.z, wb.z); g8[7] = nval(b.w, wb.w);
+    }
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i0 = perm ? e : 2 * e, i1 = perm ? e + 4 : 2 * e + 1;
-      const float v0 = valid ? __fmul_rn(val(8 * q + i0), s) : 0.0f;
-      const float v1 = valid ? __fmul_rn(val(8 * q + i1), s) : 0.0f;
+      const float v0 = valid ? __fmul_rn(g8[i0], s) : 0.0f;
+      const float v1 = valid ? __fmul_rn(g8[i1], s) : 0.0f;
       split2(v0, v1, hi[e], lo[e]);
     }
     uint8_t* blk = xa + ((size_t)mt * nkc + kc) * 2 * part;
@@ -818,7 +850,9 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   const double t_mem = 256.0 * (qb + 2) / (6500.0 / sms);
   const double t_mma = 3.0 * kWR * p.NB * kBK / 5600.0;
   const double t_dq = qb == 16 ? 95.0 : 250.0;
-  const double t_issue = (p.cat ? 8 : 12) * 10.0;   // MMA issue per chunk (estimate, A in TMEM)
+  // the tensor core's pace for a chunk's MMAs (measured: ~0.75 us a chunk at
+  // 16 tokens, 8 MMAs of N = 32; ~1.4 us at 128, 12 MMAs of N = 128)
+  const double t_issue = p.cat ? 8 * 90.0 : 12 * 115.0;
   const double tc = fmax(fmax(t_mem, t_issue), fmax(t_mma, t_dq));
   const int rounds = tiles / sms;
   const int rem = tiles - rounds * sms;
