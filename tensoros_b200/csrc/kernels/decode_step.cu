@@ -835,16 +835,23 @@ __device__ __forceinline__ void chain_gemv(const Params& p, Hdr* h, const float*
 // ---------------------------------------------------------------------------
 // attention (llm.c:683-714), FAST: split-K over 64-position chunks
 // ---------------------------------------------------------------------------
+// Four consecutive cache elements as loaded (fp16: two packed words) and as
+// floats.
+template <int ESZ> struct RawT { using type = float4; };
+template <> struct RawT<2> { using type = uint2; };
 template <int ESZ>
-__device__ __forceinline__ float4 ldcg4(const uint8_t* p) {
-  if constexpr (ESZ == 2) {
-    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-    return make_float4(a.x, a.y, b.x, b.y);
-  } else {
-    return __ldcg(reinterpret_cast<const float4*>(p));
-  }
+__device__ __forceinline__ typename RawT<ESZ>::type ldraw(const uint8_t* p) {
+  return __ldcg(reinterpret_cast<const typename RawT<ESZ>::type*>(p));
+}
+__device__ __forceinline__ float4 unraw2(uint2 u) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <int ESZ>
+__device__ __forceinline__ float4 unraw(typename RawT<ESZ>::type r) {
+  if constexpr (ESZ == 2) return unraw2(r);
+  else return r;
 }
 
 __device__ __forceinline__ float warp_max_f(float m) {
@@ -886,17 +893,15 @@ __device__ __forceinline__ void attn_scores(const Params& p, Hdr* h, float* P, i
         const int d = 128 * sl + 4 * lane;
         if (d < hd) {
           const float4 qv = __ldcg(reinterpret_cast<const float4*>(p.s.q + (size_t)hh * hd + d));
+          typename RawT<ESZ>::type kr[16];   // all 16 rows in flight (fp16 packed)
 #pragma unroll
-          for (int hf = 0; hf < 16; hf += 8) {   // eight rows in flight at a time
-            float4 kv[8];
+          for (int q = 0; q < 16; ++q)
+            kr[q] = tw + q < n ? ldraw<ESZ>(kc + ((size_t)(tw + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                               : typename RawT<ESZ>::type{};
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              kv[q] = tw + hf + q < n
-                          ? ldcg4<ESZ>(kc + ((size_t)(tw + hf + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              v[hf + q] = fmaf(qv.x, kv[q].x, fmaf(qv.y, kv[q].y, fmaf(qv.z, kv[q].z, fmaf(qv.w, kv[q].w, v[hf + q]))));
+          for (int q = 0; q < 16; ++q) {
+            const float4 kv = unraw<ESZ>(kr[q]);
+            v[q] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, v[q]))));
           }
         }
       }
@@ -973,22 +978,19 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
       const int d = 128 * sl + 4 * lane;
       if (d < hd) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        typename RawT<ESZ>::type vr[16];   // all 16 rows in flight (fp16 packed)
 #pragma unroll
-        for (int hf = 0; hf < 16; hf += 8) {   // eight rows in flight at a time
-          float4 vv[8];
+        for (int q = 0; q < 16; ++q)
+          vr[q] = tw + q < cn ? ldraw<ESZ>(vc + ((size_t)(t0 + tw + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
+                              : typename RawT<ESZ>::type{};
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            vv[q] = tw + hf + q < cn
-                        ? ldcg4<ESZ>(vc + ((size_t)(t0 + tw + hf + q) * kv_dim + (size_t)kvh * hd + d) * ESZ)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float ep = es[tw + hf + q];
-            acc.x = fmaf(ep, vv[q].x, acc.x);
-            acc.y = fmaf(ep, vv[q].y, acc.y);
-            acc.z = fmaf(ep, vv[q].z, acc.z);
-            acc.w = fmaf(ep, vv[q].w, acc.w);
-          }
+        for (int q = 0; q < 16; ++q) {
+          const float ep = es[tw + q];
+          const float4 vv = unraw<ESZ>(vr[q]);
+          acc.x = fmaf(ep, vv.x, acc.x);
+          acc.y = fmaf(ep, vv.y, acc.y);
+          acc.z = fmaf(ep, vv.z, acc.z);
+          acc.w = fmaf(ep, vv.w, acc.w);
         }
         *reinterpret_cast<float4*>(&wpart[gw * kMaxHd + d]) = acc;
       }
@@ -1040,25 +1042,6 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
 // no grid barrier separates the max from the exponentials.  Worker warp w
 // takes positions w, w + kNW, ... eight at a time (all eight K or V rows in
 // flight); the eight dot products of a warp meet in one reduce-scatter.
-
-// Four consecutive cache elements as loaded (fp16: two packed words) and as
-// floats.
-template <int ESZ> struct RawT { using type = float4; };
-template <> struct RawT<2> { using type = uint2; };
-template <int ESZ>
-__device__ __forceinline__ typename RawT<ESZ>::type ldraw(const uint8_t* p) {
-  return __ldcg(reinterpret_cast<const typename RawT<ESZ>::type*>(p));
-}
-__device__ __forceinline__ float4 unraw2(uint2 u) {
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-template <int ESZ>
-__device__ __forceinline__ float4 unraw(typename RawT<ESZ>::type r) {
-  if constexpr (ESZ == 2) return unraw2(r);
-  else return r;
-}
 
 template <int ESZ, bool kLL>
 __device__ __forceinline__ void attn_head(const Params& p, Hdr* h, float* smf, int layer) {

@@ -98,15 +98,17 @@ __device__ __forceinline__ float kv_load(const void* c, int kv_type, size_t idx)
                              : reinterpret_cast<const float*>(c)[idx];
 }
 
-// One CTA per (head, token): scores over positions 0..pos0+t, llm_expf
-// weights of (s - max), tree sums, sum_j e_j v_j / (sum_j e_j + 1e-10).
-__global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restrict__ q, const void* __restrict__ kc,
+// One CTA of kPfWarps warps per (head, token): scores over positions
+// 0..pos0+t, llm_expf weights of (s - max), tree sums, sum_j e_j v_j /
+// (sum_j e_j + 1e-10).
+constexpr int kPfWarps = 8;
+__global__ void __launch_bounds__(32 * kPfWarps) pf_attention_kernel(const float* __restrict__ q, const void* __restrict__ kc,
                                                            const void* __restrict__ vc, int kv_type, int n_heads,
                                                            int n_kv, int hd, int pos0, float* __restrict__ out,
                                                            const int* __restrict__ pos_arr,
                                                            const int* __restrict__ slot, size_t cstride) {
   extern __shared__ float sc[];   // [pos0 + n] scores, then weights
-  __shared__ float red[4];
+  __shared__ float red[kPfWarps];
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x, t = blockIdx.y;
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
     __syncthreads();
     const int sub = lane & 3, dpl = hd >> 2;
     const float* qs = qsh + sub * dpl;
-    for (int j0 = warp * 8; j0 < n; j0 += 32) {
+    for (int j0 = warp * 8; j0 < n; j0 += 8 * kPfWarps) {
       const int j = j0 + (lane >> 2);
       float acc = 0.0f;
       if (j < n) {
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
       if (sub == 0 && j < n) sc[j] = acc * scale;
     }
   } else {
-    for (int j = warp; j < n; j += 4) {
+    for (int j = warp; j < n; j += kPfWarps) {
       float acc = 0.0f;
       for (int d = lane; d < hd; d += 32) acc = fmaf(qh[d], kv_load(kc, kv_type, (size_t)j * kv_dim + (size_t)kvh * hd + d), acc);
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -164,7 +166,8 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float M = red[0];
+  for (int w = 1; w < kPfWarps; ++w) M = fmaxf(M, red[w]);
   __syncthreads();
   float l = 0.0f;
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
@@ -175,15 +178,17 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
   for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
   if (lane == 0) red[warp] = l;
   __syncthreads();
-  const float inv = 1.0f / ((red[0] + red[1]) + (red[2] + red[3]) + 1e-10f);
+  float L = red[0];
+  for (int w = 1; w < kPfWarps; ++w) L += red[w];
+  const float inv = 1.0f / (L + 1e-10f);
   if (hd % 32 == 0 && hd <= 256) {
-    // warp w takes positions 8 w .. 8 w + 7, then 32 further on (eight V rows
-    // in flight); lane l covers d = 4 l .. 4 l + 3 (+ 128); the four warps'
-    // partial sums are added in warp order
-    __shared__ float part[4][256];
+    // warp w takes positions 8 w .. 8 w + 7, then 8 kPfWarps further on
+    // (eight V rows in flight); lane l covers d = 4 l .. 4 l + 3 (+ 128); the
+    // warps' partial sums are added in warp order
+    __shared__ float part[kPfWarps][256];
     const bool f16 = kv_type == TOSK_F16;
     float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-    for (int j0 = warp * 8; j0 < n; j0 += 32) {
+    for (int j0 = warp * 8; j0 < n; j0 += 8 * kPfWarps) {
 #pragma unroll
       for (int s = 0; s < 2; ++s) {
         const int d = 128 * s + 4 * lane;
@@ -220,8 +225,11 @@ __global__ void __launch_bounds__(128) pf_attention_kernel(const float* __restri
       if (d < hd) *reinterpret_cast<float4*>(&part[warp][d]) = acc[s];
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x)
-      out[((size_t)t * n_heads + h) * hd + d] = (((part[0][d] + part[1][d]) + part[2][d]) + part[3][d]) * inv;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      float o = part[0][d];
+      for (int w = 1; w < kPfWarps; ++w) o += part[w][d];
+      out[((size_t)t * n_heads + h) * hd + d] = o * inv;
+    }
     return;
   }
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
@@ -305,7 +313,7 @@ extern "C" int tosk_pf_attention(const float* q, const void* kc, const void* vc,
   size_t cstride = 0;
   void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out,
                   (void*)&pos_arr, (void*)&slot, &cstride};
-  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
+  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(32 * kPfWarps), smem, args, st);
 }
 
 extern "C" int tosk_bd_attention(const float* q, const void* kc, const void* vc, size_t cstride, int kv_type,
@@ -323,5 +331,5 @@ extern "C" int tosk_bd_attention(const float* q, const void* kc, const void* vc,
   int pos0 = 0;
   void* args[] = {(void*)&q, (void*)&kc, (void*)&vc, &kv_type, &n_heads, &n_kv, &hd, &pos0, &out,
                   (void*)&pos, (void*)&slot, &cstride};
-  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(128), smem, args, st);
+  return launch_pf((const void*)pf_attention_kernel, dim3(n_heads, n), dim3(32 * kPfWarps), smem, args, st);
 }
