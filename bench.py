@@ -58,7 +58,7 @@ METRIC = "decode tokens/sec (Llama-2-7B-shaped, Q4_0, batch 1)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_step_kernel launch
 # of the 32-layer model, from a full-size ncu capture at context 8 (the KV rows
 # of a longer context add 16 KB per position and layer)
-STEP_TRAFFIC = 3721760768 + 13937152
+STEP_TRAFFIC = 3721505024 + 15383296
 
 
 def peaks():
@@ -551,6 +551,31 @@ def time_prefill(model, prompt, prompt_next, torch):
             "next_token_identical_to_stepwise": nxt == prompt_next["token"]}
 
 
+def attention_once(lib, torch, ctx, calls=5):
+    """FAST decode attention, 32 heads x 128, fp16 cache of ctx positions:
+    `calls` calls on one cache (L2-warm after the first), the last timed."""
+    nh, hd = 32, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    k = torch.randn(ctx * nh * hd, generator=g, device="cuda").half()
+    v = torch.randn(ctx * nh * hd, generator=g, device="cuda").half()
+    q = torch.randn(nh * hd, generator=g, device="cuda")
+    out = torch.empty(nh * hd, device="cuda")
+    wsb = lib.tos_attention_workspace_bytes(nh, ctx)
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(calls):
+        if i == calls - 1:
+            e0.record(s)
+        assert lib.tos_attention_dev(out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, nh, nh, hd,
+                                     ctx - 1, ctx, 1, ws.data_ptr(), wsb, s.cuda_stream) == 0
+    e1.record(s)
+    e1.synchronize()
+    return {"kernel": f"FAST attention 32x128 fp16, context {ctx}", "calls": calls,
+            "last_call_us": e0.elapsed_time(e1) * 1000.0}
+
+
 def gemm_roofline(lib, torch, m=128, n=22016, k=4096, reps=10):
     """Isolated tensor-core GEMM of the prefill (gate|up shape)."""
     import ctypes
@@ -893,6 +918,9 @@ def main():
                     help="time only the prefill tensor-core GEMM (128x22016x4096 Q4_0) and print it")
     ap.add_argument("--gemm-m", type=int, default=128,
                     help="--gemm-only: token rows of the gate|up GEMM (16 = a batch-16 decode step)")
+    ap.add_argument("--attention-only", type=int, default=0, metavar="CTX",
+                    help="time only FAST decode attention (32 heads x 128, fp16 cache) at this context: "
+                         "five calls on one cache (the small case for a profiler capture)")
     args = ap.parse_args()
     if args.cpu_batch_worker:
         cpu_batch_worker(*args.cpu_batch_worker)
@@ -900,6 +928,13 @@ def main():
     world, rank, local = dist_setup(args)
     if args.gemv_only:
         run_gemv_only(args, local)
+    elif args.attention_only:
+        import torch
+        from tensoros_b200 import lib as _lib
+        torch.cuda.set_device(local)
+        lib = _lib()
+        assert lib.tos_init(local) == 0, "tos_init failed"
+        print(json.dumps(attention_once(lib, torch, args.attention_only)), flush=True)
     elif args.gemm_only:
         import torch
         from tensoros_b200 import lib as _lib
