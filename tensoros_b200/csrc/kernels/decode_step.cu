@@ -67,8 +67,9 @@ constexpr int kXBytes = 58368;           // the phase's input vector and norm we
 constexpr int kPBytes = 28512;           // partials tile (also attention scratch)
 constexpr int kSmem = kHdr + kXBytes + kPBytes + kSlots * kSlot;
 static_assert(kSmem <= 227 * 1024, "shared memory");
-constexpr int kGroups = kWorkers / 32 / 4;   // attention groups of four worker warps
-constexpr int kChunk = 64;               // attention positions per chunk
+constexpr int kGW = 5;                   // worker warps per long-context attention group
+constexpr int kGroups = kWorkers / 32 / kGW;   // three groups: all fifteen worker warps
+constexpr int kChunk = 16 * kGW;         // attention positions per chunk (16 per warp)
 constexpr int kMaxHd = 256;
 constexpr int kMaxGrid = 1024;
 constexpr int kHeadMaxN = 1024;          // longest context of the one-phase-per-head attention
@@ -115,7 +116,10 @@ struct Hdr {
 static_assert(sizeof(Hdr) <= kHdr, "header");
 
 // Attention scratch of one group inside the partials area (floats).
-constexpr int kGroupFloats = kChunk + 8 + 4 * kMaxHd + 8;
+// es[kChunk] | red[12] (kGW maxima, kGW sums; 16-byte padded) | wpart[kGW][kMaxHd] | s_last
+constexpr int kGroupFloats = kChunk + 12 + kGW * kMaxHd + 8;
+static_assert((kChunk + 12) % 4 == 0 && kGroupFloats % 4 == 0 && 2 * kGW <= 12, "attention scratch alignment");
+static_assert(B_GROUP0 + kGroups <= B_STAGED, "named barriers");
 static_assert(kGroups * kGroupFloats * 4 <= kPBytes, "attention scratch");
 static_assert((1024 + (kWorkers / 32) * kMaxHd + 32) * 4 <= kXBytes, "per-head attention scratch");
 
@@ -860,14 +864,14 @@ __device__ __forceinline__ float warp_max_f(float m) {
   return m;
 }
 
-// Scores of one (kv head, chunk) item per group of four warps: a warp per 16
+// Scores of one (kv head, chunk) item per group of kGW warps: a warp per 16
 // positions, lane l covering d = 128 s + 4 l .. +3, all 16 rows in flight,
 // then a shuffle reduce-scatter; per-chunk maxima for the softmax pass.
 template <int ESZ>
 __device__ __forceinline__ void attn_scores(const Params& p, Hdr* h, float* P, int layer) {
   const int w = (int)(threadIdx.x >> 5) - 1;
-  const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
-  float* wmax = P + grp * kGroupFloats + kChunk + 4;
+  const int grp = w / kGW, gw = w % kGW, lane = threadIdx.x & 31;
+  float* wmax = P + grp * kGroupFloats + kChunk;
   const int n = h->pos + 1;
   const int n_heads = p.s.n_heads, n_kv = p.s.n_kv, hd = p.s.hd;
   if (blockIdx.x == 0)
@@ -923,11 +927,14 @@ __device__ __forceinline__ void attn_scores(const Params& p, Hdr* h, float* P, i
         if ((lane & 1) == 0) p.S[(size_t)hh * p.s.max_seq + t] = m;
       }
       m = warp_max_f(m);
-      named_sync(B_GROUP0 + grp, 128);
+      named_sync(B_GROUP0 + grp, 32 * kGW);
       if (lane == 0) wmax[gw] = m;
-      named_sync(B_GROUP0 + grp, 128);
-      if (gw == 0 && lane == 0)
-        p.cmax[(size_t)hh * p.maxc + c] = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+      named_sync(B_GROUP0 + grp, 32 * kGW);
+      if (gw == 0 && lane == 0) {
+        float cm = wmax[0];
+        for (int i = 1; i < kGW; ++i) cm = fmaxf(cm, wmax[i]);
+        p.cmax[(size_t)hh * p.maxc + c] = cm;
+      }
     }
   }
 }
@@ -937,13 +944,14 @@ __device__ __forceinline__ void attn_scores(const Params& p, Hdr* h, float* P, i
 // the chunks in order and divides by the sum (llm.c:519-521, 703-712).
 template <int ESZ, bool kLL>
 __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int layer) {
+  constexpr int kGT = 32 * kGW;   // threads of a group
   const int w = (int)(threadIdx.x >> 5) - 1;
-  const int grp = w >> 2, gw = w & 3, lane = threadIdx.x & 31;
+  const int grp = w / kGW, gw = w % kGW, lane = threadIdx.x & 31;
   const int gt = gw * 32 + lane;
   float* es = P + grp * kGroupFloats;
   float* red = es + kChunk;
-  float* wpart = es + kChunk + 8;
-  int* s_last = reinterpret_cast<int*>(wpart + 4 * kMaxHd);
+  float* wpart = es + kChunk + 12;
+  int* s_last = reinterpret_cast<int*>(wpart + kGW * kMaxHd);
   if (grp >= kGroups) return;
   const int n = h->pos + 1;
   const int n_heads = p.s.n_heads, n_kv = p.s.n_kv, hd = p.s.hd;
@@ -956,12 +964,13 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
     const int kvh = hh / group;
     const int t0 = c * kChunk, cn = min(kChunk, n - t0);
     float m = -INFINITY;
-    for (int i = gt; i < nchunk; i += 128) m = fmaxf(m, __ldcg(p.cmax + (size_t)hh * p.maxc + i));
+    for (int i = gt; i < nchunk; i += kGT) m = fmaxf(m, __ldcg(p.cmax + (size_t)hh * p.maxc + i));
     m = warp_max_f(m);
-    named_sync(B_GROUP0 + grp, 128);
+    named_sync(B_GROUP0 + grp, kGT);
     if (lane == 0) red[gw] = m;
-    named_sync(B_GROUP0 + grp, 128);
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    named_sync(B_GROUP0 + grp, kGT);
+    float M = red[0];
+    for (int i = 1; i < kGW; ++i) M = fmaxf(M, red[i]);
     float e = 0.0f;
     if (gt < kChunk) {
       if (gt < cn) e = ref_expf(__fsub_rn(__ldcg(p.S + (size_t)hh * p.s.max_seq + t0 + gt), M));
@@ -970,8 +979,8 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
     float l = e;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    named_sync(B_GROUP0 + grp, 128);
-    if (lane == 0) red[4 + gw] = l;
+    named_sync(B_GROUP0 + grp, kGT);
+    if (lane == 0) red[kGW + gw] = l;
     const int tw = gw * 16;
 #pragma unroll
     for (int sl = 0; sl < kMaxHd / 128; ++sl) {
@@ -995,15 +1004,22 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
         *reinterpret_cast<float4*>(&wpart[gw * kMaxHd + d]) = acc;
       }
     }
-    named_sync(B_GROUP0 + grp, 128);
+    named_sync(B_GROUP0 + grp, kGT);
     float* op = p.opart + ((size_t)hh * p.maxc + c) * kMaxHd;
-    for (int d = gt; d < hd; d += 128)
-      op[d] = ((wpart[d] + wpart[kMaxHd + d]) + wpart[2 * kMaxHd + d]) + wpart[3 * kMaxHd + d];
-    if (gt == 0) p.lsum[(size_t)hh * p.maxc + c] = ((red[4] + red[5]) + red[6]) + red[7];
+    for (int d = gt; d < hd; d += kGT) {
+      float o = wpart[d];
+      for (int i = 1; i < kGW; ++i) o += wpart[i * kMaxHd + d];
+      op[d] = o;
+    }
+    if (gt == 0) {
+      float lc = red[kGW];
+      for (int i = 1; i < kGW; ++i) lc += red[kGW + i];
+      p.lsum[(size_t)hh * p.maxc + c] = lc;
+    }
     __threadfence();
-    named_sync(B_GROUP0 + grp, 128);
+    named_sync(B_GROUP0 + grp, kGT);
     if (gt == 0) *s_last = atomicAdd(p.cnt + hh, 1) == nchunk - 1;
-    named_sync(B_GROUP0 + grp, 128);
+    named_sync(B_GROUP0 + grp, kGT);
     if (*s_last) {
       __threadfence();
       // chunk order, eight chunks' loads in flight
@@ -1019,7 +1035,7 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
           if (i0 + k < nchunk) Ls += lv[k];
       }
       const float inv = 1.0f / (Ls + 1e-10f);
-      for (int d = gt; d < hd; d += 128) {
+      for (int d = gt; d < hd; d += kGT) {
         float o = 0.0f;
         for (int i0 = 0; i0 < nchunk; i0 += 8) {
           float ov[8];
@@ -1033,7 +1049,7 @@ __device__ __forceinline__ void attn_pv(const Params& p, Hdr* h, float* P, int l
         else p.s.att[(size_t)hh * hd + d] = o * inv;
       }
     }
-    named_sync(B_GROUP0 + grp, 128);   // es / red / wpart / s_last are reused by the next item
+    named_sync(B_GROUP0 + grp, kGT);   // es / red / wpart / s_last are reused by the next item
   }
 }
 
