@@ -14,9 +14,10 @@
 //     complete_tx).  Weights depend on nothing, so the producer only waits
 //     for free slots: while the other warps wait at a grid barrier or run
 //     attention, the next projection's rows are already landing.
-//   * warps 4..15 (compute): thread (b, g) reads block b of the phase's
-//     input vector from L2 (RMSNorm weight applied), keeps its fixed-point
-//     record in registers and evaluates block b of rows g, g + rg, ... of
+//   * warps 4..15 (compute) stage the phase's input vector in shared memory
+//     (coalesced cp.async, every chunk once per CTA); thread (b, g) then
+//     turns block b (RMSNorm weight applied) into a fixed-point record in
+//     registers and evaluates block b of rows g, g + rg, ... of
 //     each ring stage as the FAST GEMV does (integer dp4a dot products on
 //     24-bit fixed-point x, gemv_fastmath.cuh) into a partials tile;
 //   * warps 1..3 (chain) compute a RMSNorm phase's 1/rms from the whole
@@ -108,8 +109,8 @@ struct Hdr {
   float cpart[kChain];   // the chain warps' partial sums of squares (RMSNorm)
   float av[kChain];
   int ai[kChain];
-  // epilogue operands the chain warps stage while the compute warps build
-  // the input records: this CTA's residual rows, RoPE (cos, sin) of pos
+  // epilogue operands the chain warps stage while the compute warps stage
+  // the input vector: this CTA's residual rows, RoPE (cos, sin) of pos
   float res[kPreRows];
   float2 cs[kMaxHd / 2];
 };
@@ -1295,8 +1296,8 @@ static int make_geo(int R, int cols, int qtype, int unit, Geo& G) {
   if (qtype != TOSK_Q4_0 && qtype != TOSK_Q8_0) return (int)cudaErrorNotSupported;
   G.R = R;
   G.nb = cols / 32;
-  // a block per compute thread; its fixed-point record in shared memory
-  if (G.nb > 32 * kCompute || G.nb * 128 > kXBytes) return (int)cudaErrorNotSupported;   // a block per compute thread
+  // a block per compute thread; the input vector staged in shared memory
+  if (G.nb > 32 * kCompute || G.nb * 128 > kXBytes) return (int)cudaErrorNotSupported;
   G.nbp = round_up_i(G.nb, 8);
   G.qb = qtype == TOSK_Q4_0 ? 16 : 32;
   G.unit = unit;
