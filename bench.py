@@ -800,7 +800,7 @@ def run_ours(args, world, rank, local):
         # row, norms and the small vectors (<1 MB, ignored)
         ctx = args.prefill + warm + K // 2
         step_bytes = weight_bytes + L * 2 * (ctx + 1) * 4096 * 2
-        gemv_rl = {"bound": "hbm", "kernel": f"gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
+        gemv_rl = {"bound": "hbm", "kernel": f"tos_gemv_kernel<Q4_0, {args.math}> 4096x4096 (isolated, L2-cold)",
                    "achieved": achieved, "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                    "frac": achieved / peak,
                    # dram__bytes_read.sum + dram__bytes_write.sum of one launch

@@ -132,7 +132,7 @@ __device__ __forceinline__ float block_value(const uint8_t* stq, const uint16_t*
 // slower than the overlap it buys; one CTA per SM keeps ~85 registers.)
 
 template <int QB, bool kNorm, int kEpi, bool kFast>
-__global__ void __launch_bounds__(704, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(704, 1) tos_gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -593,7 +593,7 @@ template <int QB, bool kNorm, int kEpi, bool kFast>
 static int launch_gemv(const GemvArgs& a, int grid, int threads, size_t smem, int pdl,
                        cudaStream_t st) {
   static bool done = false;
-  auto kern = gemv_kernel<QB, kNorm, kEpi, kFast>;
+  auto kern = tos_gemv_kernel<QB, kNorm, kEpi, kFast>;
   if (!done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return (int)e;
