@@ -51,13 +51,17 @@ __device__ __forceinline__ uint32_t dp4a_ss(uint32_t a, uint32_t b, uint32_t c) 
 // Six dot-product chains per block (each limb split over the low- and
 // high-nibble words, or even and odd words) keep the dependent dp4a runs
 // short; the integer total is the same in any order (mod 2^32).
+// Q4_0: the high nibbles stay in place (byte value 16 n, no shift per
+// word), so the b chains hold 16x their sums.  Each limb's chains are small
+// (|a| < 2^16, |b| < 2^20), so s_l = 16 a_l + b_l is exact and a multiple of
+// 16, and Y = s0/16 + 2^4 s1 + 2^12 s2 + c (mod 2^32, exact since |Y| <= 2^30).
 __device__ __forceinline__ float fast_q4_0(const uint4 q, const float d, const XFix& f) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-  uint32_t a0 = (uint32_t)f.c, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+  uint32_t a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t lo = w[k] & 0x0F0F0F0Fu;
-    const uint32_t hi = (w[k] >> 4) & 0x0F0F0F0Fu;
+    const uint32_t hi = w[k] & 0xF0F0F0F0u;
     a0 = dp4a_uu(lo, f.l[0][2 * k], a0);
     a1 = dp4a_uu(lo, f.l[1][2 * k], a1);
     a2 = dp4a_us(lo, f.l[2][2 * k], a2);
@@ -65,7 +69,8 @@ __device__ __forceinline__ float fast_q4_0(const uint4 q, const float d, const X
     b1 = dp4a_uu(hi, f.l[1][2 * k + 1], b1);
     b2 = dp4a_us(hi, f.l[2][2 * k + 1], b2);
   }
-  const int y = (int)((a0 + b0) + ((a1 + b1) << 8) + ((a2 + b2) << 16));
+  const uint32_t s0 = a0 * 16u + b0, s1 = a1 * 16u + b1, s2 = a2 * 16u + b2;
+  const int y = (int)((s0 >> 4) + (s1 << 4) + (s2 << 12) + (uint32_t)f.c);
   return (float)y * (d * f.s);
 }
 
