@@ -751,6 +751,495 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tc_kernel(const __grid_cons
   }
 }
 
+// ---------------------------------------------------------------------------
+// Q4_0 at up to 16 tokens: exact integer block products on the tensor cores
+// (tcgen05.mma kind::i8).
+//
+// Every 32-element block of an activation row becomes X_i = rint(x_i / s),
+// s a power of two per (token, block) with max |X_i| <= 2^22 (the FAST
+// GEMV's fixed point, gemv_fastmath.cuh), written as three signed byte limbs
+// X = L0 + 2^8 L1 + 2^16 L2.  The weights enter as n - 8 (signed bytes, no
+// scale), so one MMA of K = 32 per block (N = 48: limb l of token t in
+// column 16 l + t) gives the exact sums S_l = sum_k (n_k - 8) L_l,k
+// (|S_l| <= 2^15), and Y = S_0 + 2^8 S_1 + 2^16 S_2 is the block's exact
+// integer value, the FAST GEMV's block value before its two roundings.  The
+// warps that read the accumulators add float(Y) * (d * s) into per-row fp32
+// sums.  Against the fp16 hi / lo form: one MMA per block instead of four,
+// and a weight operand that is a nibble expansion (no scale, no split).
+//
+// Warps: 0 raw weight stages (TMA, as gemm_tc_kernel); 1 MMA issue; 2..17
+// dequantise and accumulate: two groups of eight, group g taking the chunks
+// (4 blocks, K = 128) i with i % 2 == g, each warp its TMEM lane quarter and
+// two blocks (half h) of the chunk; 18 activation chunks (bulk copies).  A
+// group owns one A stage (32 TMEM columns) and one accumulator (4 x 48
+// columns): it reads out chunk i's sums, then writes chunk i + 2's weights,
+// so its A-stage arrival also frees the accumulator.  At the end of a unit
+// the four partial sums of a row (two groups x two halves) are added in a
+// fixed order (deterministic) and the epilogue of gemm_tc_kernel runs.
+// ---------------------------------------------------------------------------
+constexpr int kI8Tok = 16;                                     // tokens (MMA N / 3)
+constexpr int kI8N = 3 * kI8Tok;                               // MMA N
+constexpr int kI8BK = 128;                                     // K per chunk: one 128-byte B row
+constexpr int kI8RawCh = 2;                                    // chunks per raw stage (8 blocks)
+constexpr int kI8W0 = 2;                                       // first dequantising warp
+constexpr int kI8Heavy = 16;                                   // dequantising warps
+constexpr int kI8Bw = kI8W0 + kI8Heavy;                        // activation copy warp
+constexpr int kI8Threads = 32 * (kI8Bw + 1);                   // 608
+constexpr int kI8MaxSB = 8;
+constexpr int kI8MaxR = 8;
+constexpr uint32_t kI8BChunk = kI8N * 128 + 4 * kI8Tok * 4;    // 6400: limb rows, then s[4 blocks][16 tokens]
+constexpr uint32_t kI8BStage = 7168;                           // a B stage in shared memory (1024-aligned)
+constexpr uint32_t kI8RawBytes = 16384 + 2048;                 // quant box, scale box
+constexpr uint32_t kI8Acc = 4 * kI8N;                          // accumulator columns of a chunk (192)
+constexpr uint32_t kI8ACols = 4 * 8;                           // A columns of a chunk (K = 32 bytes a block)
+constexpr uint32_t kI8RedBytes = 3 * kI8Tok * kWR * 4;         // three partial sums [3][16][128]
+static_assert(2 * kI8Acc + 2 * kI8ACols <= 512, "TMEM");
+static_assert((2 * kI8MaxR + 2 * kI8MaxSB + 7) * 8 + 8 <= kHdrBytes, "header");
+
+// Instruction descriptor: s32 accumulate, signed 8-bit A and B, both
+// K-major, M = 128, N = 48.
+constexpr uint32_t kIdescI8 =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kI8N >> 3) << 17) | ((uint32_t)(kWR >> 4) << 24);
+
+// D = A B with A (128 rows x 32 signed bytes) in tensor memory: lane m holds
+// row m, column j its K elements 4j .. 4j + 3 (lowest byte first).
+__device__ __forceinline__ void umma_i8_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(0u)
+      : "memory");
+}
+
+// 16 consecutive 32-bit accumulator columns of this warp's 32 TMEM lanes
+// (completion: tmem_ld_wait).
+__device__ __forceinline__ void tmem_ld16_raw(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// A Q4_0 quant word (bytes b = elements 2b (low nibble) and 2b + 1) as two
+// words of signed bytes n - 8: the low nibbles (elements 0, 2, 4, 6 of the
+// word's eight) and the high ones (1, 3, 5, 7).  n + 120 stays inside its
+// byte; flipping bit 7 then gives n - 8 in two's complement.
+__device__ __forceinline__ void q4_to_s8(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = ((w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+  hi = (((w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+}
+
+struct GemmI8Args {
+  CUtensorMap tq;       // weight quants, as GemmArgs
+  CUtensorMap ts;       // weight scales, as GemmArgs
+  const uint8_t* xb;    // prepared activation chunks [nkc][kI8BChunk]
+  float* y;             // as GemmArgs
+  int epi;
+  float* part;          // K-slice partials [splits][M][N]
+  int N, K, nkc, M, ntiles, splits, kcps, units, full, SB, R;
+  int* err;
+};
+
+// Work unit: a 128-row tile and a K slice (chunks of 128), its raw stages
+// (two chunks each) in the rotated order of unit_of.
+struct UnitI8 {
+  int tile, split, ns, n0, kc0, nk, nst, rot;
+};
+__device__ __forceinline__ UnitI8 unit_i8(const GemmI8Args& a, int u) {
+  UnitI8 w;
+  if (u < a.full) {
+    w.tile = u;
+    w.split = 0;
+    w.ns = 1;
+    w.kc0 = 0;
+    w.nk = a.nkc;
+  } else {
+    const int v = u - a.full;
+    w.tile = a.full + v / a.splits;
+    w.split = v % a.splits;
+    w.ns = a.splits;
+    w.kc0 = w.split * a.kcps;
+    w.nk = min(a.nkc, w.kc0 + a.kcps) - w.kc0;
+  }
+  w.n0 = w.tile * kWR;
+  w.nst = (w.nk + kI8RawCh - 1) / kI8RawCh;
+  w.rot = w.tile % w.nst;
+  return w;
+}
+__device__ __forceinline__ int stage_c0_i8(const UnitI8& w, int q) {
+  const int st = q + w.rot < w.nst ? q + w.rot : q + w.rot - w.nst;
+  return kI8RawCh * st;
+}
+
+// prep for gemm_i8_kernel: X[M][K] fp32 (RMS-normalised first when nw is
+// given, exactly as gemm_prep_kernel) -> chunk c (K elements 128 c ..): 48
+// K-major rows of 128 bytes, SWIZZLE_128B (row 16 l + t: limb l of token t),
+// then s[4 blocks][16 tokens].  Inside each group of eight elements the K
+// order is q4_to_s8's: positions 0..3 hold elements 0, 2, 4, 6 and 4..7 hold
+// 1, 3, 5, 7.  Tokens t >= M are zeros with s = 0; a block holding a
+// non-finite value gets X = 0 and s = NaN (as make_xfix).  Grid (16 tokens,
+// parts of K); four consecutive threads make one block.
+__global__ void __launch_bounds__(128) gemm_prep_i8_kernel(const float* __restrict__ x, int M, int K,
+                                                           uint8_t* __restrict__ xb,
+                                                           const float* __restrict__ nw, float eps) {
+  __shared__ float red[4];
+  __shared__ float s_ss;
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const bool valid = t < M;
+  const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)(valid ? t : 0) * K);
+  const float4* w4 = reinterpret_cast<const float4*>(nw);
+  const int K4 = K / 4, bd = (int)blockDim.x;
+  float ss = 1.0f;
+  if (nw) {
+    float acc = 0.0f;
+    if (valid)
+      for (int i0 = threadIdx.x; i0 < K4; i0 += 8 * bd) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = i0 + u * bd < K4 ? x4[i0 + u * bd] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          acc = fmaf(v[u].w, v[u].w, fmaf(v[u].z, v[u].z, fmaf(v[u].y, v[u].y, fmaf(v[u].x, v[u].x, acc))));
+      }
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float tt = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
+      s_ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tt, (float)K), eps)));
+    }
+    __syncthreads();
+    ss = s_ss;
+  }
+  const int nblk = K / 32;
+  const int g0 = 4 * (int)(((long long)blockIdx.y * nblk) / gridDim.y);
+  const int g1 = 4 * (int)(((long long)(blockIdx.y + 1) * nblk) / gridDim.y);
+  for (int base = g0; base < g1; base += bd) {   // g0 and bd are multiples of 4
+    const int q = base + threadIdx.x;              // 8-element group: elements 8q .. 8q + 7
+    const bool in = q < g1;
+    float g8[8];
+    if (valid && in) {
+      const float4 va = x4[2 * q], vb = x4[2 * q + 1];
+      g8[0] = va.x; g8[1] = va.y; g8[2] = va.z; g8[3] = va.w;
+      g8[4] = vb.x; g8[5] = vb.y; g8[6] = vb.z; g8[7] = vb.w;
+      if (nw) {
+        const float4 wa = w4[2 * q], wb = w4[2 * q + 1];
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g8[e] = __fmul_rn(__fmul_rn(g8[e], ss), wv[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g8[e] = 0.0f;
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(g8[e]));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int eb = (int)((__float_as_uint(m) >> 23) & 0xFF);
+    const int e = max(eb - 127 - 21, -126);   // max / 2^e < 2^22
+    const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+    const bool fin = eb != 255;
+    const float s = !valid ? 0.0f : fin ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(0x7FC00000u);
+    uint32_t lw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int X = valid && fin ? __float_as_int(fmaf(g8[j], inv, 12582912.0f)) - 0x4B400000 : 0;
+      const int l0 = (int)(signed char)(X & 0xFF);
+      const int r1 = (X - l0) >> 8;
+      const int l1 = (int)(signed char)(r1 & 0xFF);
+      const int l2 = (r1 - l1) >> 8;   // |l2| <= 65
+      const int p = (j & 1) ? 4 + (j >> 1) : (j >> 1);   // K position of element j
+      lw[0][p >> 2] |= ((uint32_t)l0 & 0xFFu) << (8 * (p & 3));
+      lw[1][p >> 2] |= ((uint32_t)l1 & 0xFFu) << (8 * (p & 3));
+      lw[2][p >> 2] |= ((uint32_t)l2 & 0xFFu) << (8 * (p & 3));
+    }
+    if (in) {
+      const int kpos = 8 * q;
+      const int o = kpos & (kI8BK - 1);
+      uint8_t* ch = xb + (size_t)(kpos / kI8BK) * kI8BChunk;
+#pragma unroll
+      for (int l = 0; l < 3; ++l)
+        *reinterpret_cast<uint2*>(ch + sw128_off(kI8Tok * l + t, o >> 4) + (o & 15)) = make_uint2(lw[l][0], lw[l][1]);
+      if ((q & 3) == 0) reinterpret_cast<float*>(ch + kI8N * 128)[kI8Tok * (o >> 5) + t] = s;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_constant__ GemmI8Args a) {
+  extern __shared__ uint8_t gsm[];
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(gsm);   // [R]: raw stage landed
+  uint64_t* raw_empty = raw_full + kI8MaxR;                // [R]: every dequantising warp is done with it
+  uint64_t* b_full = raw_empty + kI8MaxR;                  // [SB]: activation chunk landed
+  uint64_t* b_empty = b_full + kI8MaxSB;                   // [SB]: its group has read its sums and scales
+  uint64_t* a_full = b_empty + kI8MaxSB;                   // [2]: group's A stage written, accumulator free
+  uint64_t* acc_full = a_full + 2;                         // [2]: group's chunk MMAs complete
+  uint64_t* red_full = acc_full + 2;                       // partial sums of a unit written
+  uint64_t* red_empty = red_full + 1;                      // ... and read
+  uint64_t* drain = red_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  const uint32_t sbase = (smem_u32(gsm) + kHdrBytes + 1023) & ~1023u;
+  uint8_t* bring = gsm + (sbase - smem_u32(gsm));
+  uint8_t* raws = bring + (size_t)a.SB * kI8BStage;
+  float* red = reinterpret_cast<float*>(raws + (size_t)a.R * kI8RawBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.R; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kI8Heavy);
+    }
+    for (int s = 0; s < a.SB; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], kI8Heavy / 2);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&a_full[g], kI8Heavy / 2);
+      mbar_init(&acc_full[g], 1);
+    }
+    mbar_init(red_full, 12);   // the warps of halves 1..3
+    mbar_init(red_empty, 4);   // the warps of half 0
+    mbar_init(drain, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, 512);   // two accumulators, then two A stages
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- raw weight stages: TMA boxes of 128 rows x 8 blocks ----------------
+    if (lane == 0) {
+      int j = 0;
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+        const UnitI8 w = unit_i8(a, u);
+        bool ok = true;
+        for (int q = 0; q < w.nst; ++q, ++j) {
+          const int slot = j % a.R;
+          if (j >= a.R && !mbar_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 41)) {
+            ok = false;
+            break;
+          }
+          const int b0 = 4 * (w.kc0 + stage_c0_i8(w, q));   // a multiple of 8: 16-byte aligned boxes
+          uint8_t* rq = raws + (size_t)slot * kI8RawBytes;
+          mbar_arrive_expect_tx(&raw_full[slot], kI8RawBytes);
+          tma_load_2d(rq, &a.tq, b0 * 16, w.n0, &raw_full[slot]);
+          tma_load_2d(rq + 16384, &a.ts, b0, w.n0, &raw_full[slot]);
+        }
+        if (!ok) break;
+      }
+      for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 42);
+    }
+  } else if (warp == kI8Bw) {
+    // ---------------- activation chunks: one bulk copy each ----------------
+    if (lane == 0) {
+      pdl_wait();   // the prepared chunks come from the prep kernel
+      int i = 0;
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+        const UnitI8 w = unit_i8(a, u);
+        bool ok = true;
+        for (int q = 0; q < w.nst && ok; ++q) {
+          const int c0 = stage_c0_i8(w, q), cn = min(kI8RawCh, w.nk - c0);
+          for (int c = c0; c < c0 + cn; ++c, ++i) {
+            const int s = i % a.SB;
+            if (i >= a.SB && !mbar_wait(&b_empty[s], ((i / a.SB) - 1) & 1, a.err, 43)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&b_full[s], kI8BChunk);
+            bulk_g2s(bring + (size_t)s * kI8BStage, a.xb + (size_t)(w.kc0 + c) * kI8BChunk, kI8BChunk, &b_full[s]);
+          }
+        }
+        if (!ok) break;
+      }
+      for (int ii = max(0, i - a.SB); ii < i; ++ii) mbar_wait(&b_full[ii % a.SB], (ii / a.SB) & 1, a.err, 44);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue: four MMAs (one a block) a chunk ----------------
+    int i = 0;
+    bool ok = true, issued = false;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+      const UnitI8 w = unit_i8(a, u);
+      for (int q = 0; q < w.nst && ok; ++q) {
+        const int cn = min(kI8RawCh, w.nk - stage_c0_i8(w, q));
+        for (int cc = 0; cc < cn; ++cc, ++i) {
+          const int g = i & 1, sb = i % a.SB;
+          if (!warp_wait(&a_full[g], (i >> 1) & 1, a.err, 45) || !warp_wait(&b_full[sb], (i / a.SB) & 1, a.err, 46)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d0 = taddr + (uint32_t)g * kI8Acc;
+          const uint32_t a0 = taddr + 2u * kI8Acc + (uint32_t)g * kI8ACols;
+          const uint32_t b0 = smem_u32(bring + (size_t)sb * kI8BStage);
+          if (elect_one()) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              umma_i8_ta(d0 + (uint32_t)(kI8N * j), a0 + 8u * (uint32_t)j, sw128_desc(b0 + 32u * (uint32_t)j), kIdescI8);
+            umma_commit(&acc_full[g]);
+          }
+          __syncwarp();
+          issued = true;
+        }
+      }
+    }
+    if (issued) {
+      if (elect_one()) umma_commit(drain);   // nothing of this warp is in flight past here
+      __syncwarp();
+      mbar_wait(drain, 0, a.err, 47);
+    }
+  } else {
+    // ---------------- dequantise, accumulate, epilogue ----------------
+    const int hw = warp - kI8W0;
+    const int g = hw >> 3;             // group: chunks i with i % 2 == g
+    const int h = (hw >> 2) & 1;       // blocks 2h, 2h + 1 of a chunk
+    const int gh = hw >> 2;            // which of a row's four partial sums
+    const int qd = warp & 3;           // TMEM lane quarter
+    const int r = 32 * qd + lane;      // weight row in the tile
+    const uint32_t tl = taddr + ((uint32_t)(32 * qd) << 16);
+    const uint32_t accb = tl + (uint32_t)g * kI8Acc + (uint32_t)(2 * h * kI8N);
+    const uint32_t ab = tl + 2u * kI8Acc + (uint32_t)g * kI8ACols + 16u * (uint32_t)h;
+    float acc[kI8Tok];
+    bool pend = false;
+    int pi = 0;
+    float pd0 = 0.0f, pd1 = 0.0f;
+    // add the pending chunk's two blocks: float(Y) * (d * s) per token
+    auto take = [&]() -> bool {
+      if (!warp_wait(&acc_full[g], (pi >> 1) & 1, a.err, 48)) return false;
+      tc_fence_after();
+      const float* sc = reinterpret_cast<const float*>(bring + (size_t)(pi % a.SB) * kI8BStage + kI8N * 128);
+#pragma unroll
+      for (int jb = 0; jb < 2; ++jb) {
+        uint32_t v[kI8N];
+        tmem_ld16_raw(accb + (uint32_t)(kI8N * jb), v);
+        tmem_ld16_raw(accb + (uint32_t)(kI8N * jb + 16), v + 16);
+        tmem_ld16_raw(accb + (uint32_t)(kI8N * jb + 32), v + 32);
+        tmem_ld_wait();
+        const float dd = jb ? pd1 : pd0;
+        const float4* s4 = reinterpret_cast<const float4*>(sc + kI8Tok * (2 * h + jb));
+#pragma unroll
+        for (int t4 = 0; t4 < kI8Tok / 4; ++t4) {
+          const float4 sv = s4[t4];
+          const float s[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = 4 * t4 + e;
+            const int Y = (int)(v[t] + (v[16 + t] << 8) + (v[32 + t] << 16));
+            acc[t] = fmaf((float)Y, __fmul_rn(dd, s[e]), acc[t]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_empty[pi % a.SB]);
+      return true;
+    };
+    int i = 0, j = 0, v = 0;   // chunks, raw stages, units
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x, ++v) {
+      const UnitI8 w = unit_i8(a, u);
+#pragma unroll
+      for (int t = 0; t < kI8Tok; ++t) acc[t] = 0.0f;
+      for (int q = 0; q < w.nst; ++q, ++j) {
+        const int slot = j % a.R;
+        if (!warp_wait(&raw_full[slot], (j / a.R) & 1, a.err, 49)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* rq = raws + (size_t)slot * kI8RawBytes;
+        const uint16_t* rs = reinterpret_cast<const uint16_t*>(rq + 16384);
+        const int cn = min(kI8RawCh, w.nk - stage_c0_i8(w, q));
+        for (int c = 0; c < cn; ++c, ++i) {
+          if ((i & 1) != g) continue;
+          if (pend && !take()) {
+            ok = false;
+            break;
+          }
+          // blocks 4c + 2h, 4c + 2h + 1 of the raw stage into this group's A stage
+          uint32_t wv[16];
+          float dv[2];
+#pragma unroll
+          for (int jb = 0; jb < 2; ++jb) {
+            const int blk = 4 * c + 2 * h + jb;
+            const uint4 qv = *reinterpret_cast<const uint4*>(rq + sw128_off(r, blk));
+            dv[jb] = h2f(rs[8 * r + blk]);
+            q4_to_s8(qv.x, wv[8 * jb + 0], wv[8 * jb + 1]);
+            q4_to_s8(qv.y, wv[8 * jb + 2], wv[8 * jb + 3]);
+            q4_to_s8(qv.z, wv[8 * jb + 4], wv[8 * jb + 5]);
+            q4_to_s8(qv.w, wv[8 * jb + 6], wv[8 * jb + 7]);
+          }
+          tmem_st16(ab, wv);
+          tmem_st_wait();
+          tc_fence_before();   // ordered before the MMA warp's issue
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[g]);
+          pend = true;
+          pi = i;
+          pd0 = dv[0];
+          pd1 = dv[1];
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[slot]);
+      }
+      if (!ok) break;
+      if (pend) {
+        if (!take()) break;
+        pend = false;
+      }
+      // the row's four partial sums, added in a fixed order, then the epilogue
+      pdl_wait();   // Y and the partial planes: after the previous kernels
+      if (gh != 0) {
+        if (v > 0 && !warp_wait(red_empty, (v - 1) & 1, a.err, 50)) break;
+        float* rp = red + (size_t)(gh - 1) * kI8Tok * kWR;
+#pragma unroll
+        for (int t = 0; t < kI8Tok; ++t) rp[t * kWR + r] = acc[t];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(red_full);
+        continue;
+      }
+      if (!warp_wait(red_full, v & 1, a.err, 51)) break;
+      const int n = w.n0 + r;
+      const bool vn = n < a.N;
+      float* dst = w.ns == 1 ? a.y : a.part + (size_t)w.split * a.M * a.N;
+#pragma unroll
+      for (int t = 0; t < kI8Tok; ++t) {
+        const float y = __fadd_rn(__fadd_rn(__fadd_rn(acc[t], red[t * kWR + r]), red[(kI8Tok + t) * kWR + r]),
+                                  red[(2 * kI8Tok + t) * kWR + r]);
+        if (w.ns > 1 || a.epi == 0) {
+          if (vn && t < a.M) dst[(size_t)t * a.N + n] = y;
+        } else if (a.epi == 1) {
+          if (vn && t < a.M) {
+            float* px = a.y + (size_t)t * a.N + n;
+            *px = __fadd_rn(*px, y);
+          }
+        } else {
+          const float up = __shfl_xor_sync(0xffffffffu, y, 1);
+          if (vn && t < a.M && (n & 1) == 0) a.y[(size_t)t * (a.N >> 1) + (n >> 1)] = __fmul_rn(ref_silu(y), up);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(red_empty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(taddr, 512);
+  }
+}
+
 // The K slices of the tiles past `full`, added in slice order, then the
 // epilogue of gemm_tc_kernel (epi 2: one thread per row pair).
 __global__ void __launch_bounds__(256) gemm_slice_sum_kernel(const float* __restrict__ part, int splits, int M,
@@ -883,6 +1372,53 @@ GemmPlan gemm_plan(int M, int N, int K, int qb) {
   return p;
 }
 
+struct GemmI8Plan {
+  int nkc, ntiles, splits, kcps, units, full, grid, SB, R;
+  size_t off_part, bytes, smem;
+};
+
+// Schedule of gemm_i8_kernel, as gemm_plan: every CTA first runs the same
+// number of whole tiles, the tiles left over are cut into K slices of an
+// even number of chunks.  A chunk (4 blocks of 128 rows) costs about its
+// weight bytes at the per-SM share of HBM bandwidth; a unit adds its
+// pipeline fill (estimates in ns).
+GemmI8Plan gemm_plan_i8(int M, int N, int K) {
+  GemmI8Plan p = {};
+  p.nkc = K / kI8BK;
+  p.ntiles = (N + kWR - 1) / kWR;
+  p.SB = kI8MaxSB;
+  const size_t fixed = (size_t)kHdrBytes + 1024 + (size_t)p.SB * kI8BStage + kI8RedBytes;
+  p.R = (int)min((size_t)kI8MaxR, ((size_t)kMaxSmem - fixed) / kI8RawBytes);
+  p.smem = fixed + (size_t)p.R * kI8RawBytes;
+  const int sms = tosk_num_sms();
+  const double tc = 4.0 * 18.0 * kWR / (6500.0 / sms);
+  const int rounds = p.ntiles / sms;
+  const int rem = p.ntiles - rounds * sms;
+  p.full = rounds * sms;
+  p.kcps = (p.nkc + 1) & ~1;
+  p.splits = 1;
+  double best = 1e300;
+  if (rem > 0) {
+    for (int kcps = 2; kcps <= ((p.nkc + 1) & ~1); kcps += 2) {
+      const int splits = (p.nkc + kcps - 1) / kcps;
+      if (splits > 64) continue;
+      const int last = (rem * splits + sms - 1) / sms;
+      const double red = splits > 1 ? 2500.0 + (splits + 1.0) * rem * kI8Tok * kWR * 4.0 / 6500.0 : 0.0;
+      const double t = last * (min(kcps, p.nkc) * tc + 1000.0) + red;
+      if (t < best * 0.999) {
+        best = t;
+        p.kcps = kcps;
+        p.splits = splits;
+      }
+    }
+  }
+  p.units = p.full + rem * p.splits;
+  p.grid = min(sms, p.units);
+  p.off_part = up256((size_t)p.nkc * kI8BChunk);
+  p.bytes = p.off_part + (p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0);
+  return p;
+}
+
 template <typename Kern>
 int launch_ex(Kern kern, dim3 grid, int threads, size_t smem, int pdl, cudaStream_t st, void** args) {
   cudaLaunchConfig_t cfg = {};
@@ -924,18 +1460,94 @@ extern "C" size_t tosk_gemm_ws_bytes(int M, int N, int K) {
       const size_t b = gemm_plan(mm, N, K, qb).bytes;
       if (b > best) best = b;
     }
+    if (mm <= kI8Tok && K % kI8BK == 0) best = max(best, gemm_plan_i8(mm, N, K).bytes);
     if (mm == M) break;
   }
   return best;
 }
 
 namespace {
+// Tensor maps of the two weight planes (host-side encoding, no device work):
+// quants in 128-byte x 128-row boxes (SWIZZLE_128B), scales in 8 x 128 boxes.
+int weight_maps(const tosk_qmat_t* w, CUtensorMap* tq, CUtensorMap* ts) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return (int)cudaErrorNotSupported;
+  const int N = w->rows;
+  const cuuint32_t es[2] = {1, 1};
+  const cuuint64_t qdim[2] = {(cuuint64_t)w->nb * w->qb, (cuuint64_t)N};
+  const cuuint64_t qstr[1] = {(cuuint64_t)w->nb * w->qb};
+  const cuuint32_t qbox[2] = {128, (cuuint32_t)kWR};
+  const cuuint64_t sdim[2] = {(cuuint64_t)w->nbp, (cuuint64_t)N};
+  const cuuint64_t sstr[1] = {(cuuint64_t)w->nbp * 2};
+  const cuuint32_t sbox[2] = {(cuuint32_t)kRawBlk, (cuuint32_t)kWR};
+  if (enc(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)w->qs, qdim, qstr, qbox, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+      enc(ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void*)w->sc, sdim, sstr, sbox, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return (int)cudaErrorInvalidValue;
+  return 0;
+}
+
+// Q4_0 at up to 16 tokens (gemm_i8_kernel): prep, GEMM, and the slice sum
+// when the last tiles were cut into K slices.
+int gemm_i8(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int M, float* y, int epi, void* ws,
+            size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
+  const int N = w->rows, K = w->cols;
+  const GemmI8Plan p = gemm_plan_i8(M, N, K);
+  if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
+  uint8_t* xb = (uint8_t*)ws;
+  float* part = (float*)((uint8_t*)ws + p.off_part);
+  {
+    int Mi = M, Ki = K;
+    float epsv = eps;
+    void* args[] = {(void*)&x, &Mi, &Ki, &xb, (void*)&nw, &epsv};
+    const int kparts = max(1, min(K / 32 / 32, (4 * tosk_num_sms() + kI8Tok - 1) / kI8Tok));
+    const int e = launch_ex(gemm_prep_i8_kernel, dim3(kI8Tok, kparts), 128, 0, pdl, st, args);
+    if (e) return e;
+  }
+  GemmI8Args a = {};
+  if (const int e = weight_maps(w, &a.tq, &a.ts)) return e;
+  a.xb = xb;
+  a.y = y;
+  a.epi = epi;
+  a.part = part;
+  a.N = N;
+  a.K = K;
+  a.nkc = p.nkc;
+  a.M = M;
+  a.ntiles = p.ntiles;
+  a.splits = p.splits;
+  a.kcps = p.kcps;
+  a.units = p.units;
+  a.full = p.full;
+  a.SB = p.SB;
+  a.R = p.R;
+  a.err = err;
+  static bool attr_done = false;
+  if (!attr_done) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (e != cudaSuccess) return (int)e;
+    attr_done = true;
+  }
+  void* gargs[] = {&a};
+  const int e = launch_ex(gemm_i8_kernel, p.grid, kI8Threads, p.smem, pdl, st, gargs);
+  if (e || p.splits == 1 || p.ntiles == p.full) return e;
+  int sp = p.splits, Mi = M, Ni = N, NBi = kI8Tok, full = p.full, nti = p.ntiles, rem = p.ntiles - p.full, ep = epi;
+  void* rargs[] = {&part, &sp, &Mi, &Ni, &NBi, &full, &nti, &rem, &ep, &y};
+  const size_t total = (size_t)rem * kI8Tok * kWR;
+  const int rgrid = (int)min((size_t)tosk_num_sms() * 8, (total + 255) / 256);
+  return launch_ex(gemm_slice_sum_kernel, rgrid, 256, 0, pdl, st, rargs);
+}
+
 int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int M, float* y, int epi, void* ws,
            size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
   if (!w || !x || !y || !ws || M <= 0 || (w->qb != 16 && w->qb != 32)) return (int)cudaErrorInvalidValue;
   const int N = w->rows, K = w->cols;
   if (epi == 2 && (N & 1)) return (int)cudaErrorInvalidValue;
   if (K % kBK || (reinterpret_cast<uintptr_t>(ws) & 255)) return (int)cudaErrorInvalidValue;
+  if (w->qb == 16 && M <= kI8Tok && K % kI8BK == 0) return gemm_i8(w, x, nw, eps, M, y, epi, ws, ws_bytes, err, pdl, st);
   const GemmPlan p = gemm_plan(M, N, K, w->qb);
   if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
   uint8_t* xa = (uint8_t*)ws;
@@ -951,25 +1563,7 @@ int gemm_q(const tosk_qmat_t* w, const float* x, const float* nw, float eps, int
     if (e) return e;
   }
   GemmArgs a = {};
-  {
-    // tensor maps of the two weight planes (host-side encoding, no device work)
-    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-    if (!enc) return (int)cudaErrorNotSupported;
-    const cuuint32_t es[2] = {1, 1};
-    const cuuint64_t qdim[2] = {(cuuint64_t)w->nb * w->qb, (cuuint64_t)N};
-    const cuuint64_t qstr[1] = {(cuuint64_t)w->nb * w->qb};
-    const cuuint32_t qbox[2] = {128, (cuuint32_t)kWR};
-    const cuuint64_t sdim[2] = {(cuuint64_t)w->nbp, (cuuint64_t)N};
-    const cuuint64_t sstr[1] = {(cuuint64_t)w->nbp * 2};
-    const cuuint32_t sbox[2] = {(cuuint32_t)kRawBlk, (cuuint32_t)kWR};
-    if (enc(&a.tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)w->qs, qdim, qstr, qbox, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-        enc(&a.ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void*)w->sc, sdim, sstr, sbox, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return (int)cudaErrorInvalidValue;
-  }
+  if (const int e = weight_maps(w, &a.tq, &a.ts)) return e;
   a.rws = w->rws;
   a.nb = w->nb;
   a.nbp = w->nbp;

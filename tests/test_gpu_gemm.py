@@ -1,8 +1,9 @@
 """Batched Q4_0 / Q8_0 GEMM on the tcgen05 tensor cores (prefill, batched
 decode): Y = X W^T for M activation rows at once.  No counterpart in the
 reference, which runs M GEMVs (llm.c:329-349); checked against the float64
-product of the dequantised weights (normwise 1e-5; the hi/lo split delivers
-~1e-6) and against the oracle's GEMV rows (the 1e-4 FAST bound)."""
+product of the dequantised weights (normwise 1e-5; the hi/lo split and the
+integer form for Q4_0 at up to 16 rows both deliver ~1e-6) and against the
+oracle's GEMV rows (the 1e-4 FAST bound)."""
 import ctypes
 
 import numpy as np
@@ -47,7 +48,12 @@ def run_gemm(gpu, w, t, n, k, x):
 
 @pytest.mark.parametrize("t,m,n,k", [
     (W.TYPE_Q4_0, 128, 4096, 4096),     # one prefill tile of the 7B q/o projections
-    (W.TYPE_Q4_0, 16, 4096, 4096),      # batch-16 decode
+    (W.TYPE_Q4_0, 16, 4096, 4096),      # batch-16 decode (integer form: Q4_0, <= 16 rows)
+    (W.TYPE_Q4_0, 1, 4096, 4096),       # one row
+    (W.TYPE_Q4_0, 16, 4096, 11008),     # batch-16 down projection
+    (W.TYPE_Q4_0, 3, 19200, 512),       # 150 tiles: two cut into K slices, then the slice sum
+    (W.TYPE_Q4_0, 12, 256, 384),        # three K chunks: a raw stage holding one
+    (W.TYPE_Q4_0, 16, 4096, 4160),      # K not a multiple of 128: the fp16 hi / lo form
     (W.TYPE_Q4_0, 128, 4096, 11008),    # down projection
     (W.TYPE_Q4_0, 130, 2048, 4096),     # two M tiles, ragged
     (W.TYPE_Q4_0, 37, 288, 768),        # ragged N tile, short K
