@@ -841,7 +841,7 @@ struct GemmI8Args {
   float* y;             // as GemmArgs
   int epi;
   float* part;          // K-slice partials [splits][M][N]
-  int N, K, nkc, M, ntiles, splits, kcps, units, full, SB, R;
+  int N, K, nkc, M, ntiles, splits, kcps, units, full;
   int* err;
 };
 
@@ -988,16 +988,16 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const uint32_t sbase = (smem_u32(gsm) + kHdrBytes + 1023) & ~1023u;
   uint8_t* bring = gsm + (sbase - smem_u32(gsm));
-  uint8_t* raws = bring + (size_t)a.SB * kI8BStage;
-  float* red = reinterpret_cast<float*>(raws + (size_t)a.R * kI8RawBytes);
+  uint8_t* raws = bring + (size_t)kI8MaxSB * kI8BStage;
+  float* red = reinterpret_cast<float*>(raws + (size_t)kI8MaxR * kI8RawBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < a.R; ++s) {
+    for (int s = 0; s < kI8MaxR; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kI8Heavy);
     }
-    for (int s = 0; s < a.SB; ++s) {
+    for (int s = 0; s < kI8MaxSB; ++s) {
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], kI8Heavy / 2);
     }
@@ -1025,8 +1025,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         const UnitI8 w = unit_i8(a, u);
         bool ok = true;
         for (int q = 0; q < w.nst; ++q, ++j) {
-          const int slot = j % a.R;
-          if (j >= a.R && !mbar_wait(&raw_empty[slot], ((j / a.R) - 1) & 1, a.err, 41)) {
+          const int slot = j % kI8MaxR;
+          if (j >= kI8MaxR && !mbar_wait(&raw_empty[slot], ((j / kI8MaxR) - 1) & 1, a.err, 41)) {
             ok = false;
             break;
           }
@@ -1038,7 +1038,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         }
         if (!ok) break;
       }
-      for (int jj = max(0, j - a.R); jj < j; ++jj) mbar_wait(&raw_full[jj % a.R], (jj / a.R) & 1, a.err, 42);
+      for (int jj = max(0, j - kI8MaxR); jj < j; ++jj) mbar_wait(&raw_full[jj % kI8MaxR], (jj / kI8MaxR) & 1, a.err, 42);
     }
   } else if (warp == kI8Bw) {
     // ---------------- activation chunks: one bulk copy each ----------------
@@ -1051,8 +1051,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         for (int q = 0; q < w.nst && ok; ++q) {
           const int c0 = stage_c0_i8(w, q), cn = min(kI8RawCh, w.nk - c0);
           for (int c = c0; c < c0 + cn; ++c, ++i) {
-            const int s = i % a.SB;
-            if (i >= a.SB && !mbar_wait(&b_empty[s], ((i / a.SB) - 1) & 1, a.err, 43)) {
+            const int s = i % kI8MaxSB;
+            if (i >= kI8MaxSB && !mbar_wait(&b_empty[s], ((i / kI8MaxSB) - 1) & 1, a.err, 43)) {
               ok = false;
               break;
             }
@@ -1062,7 +1062,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
         }
         if (!ok) break;
       }
-      for (int ii = max(0, i - a.SB); ii < i; ++ii) mbar_wait(&b_full[ii % a.SB], (ii / a.SB) & 1, a.err, 44);
+      for (int ii = max(0, i - kI8MaxSB); ii < i; ++ii) mbar_wait(&b_full[ii % kI8MaxSB], (ii / kI8MaxSB) & 1, a.err, 44);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue: four MMAs (one a block) a chunk ----------------
@@ -1073,8 +1073,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
       for (int q = 0; q < w.nst && ok; ++q) {
         const int cn = min(kI8RawCh, w.nk - stage_c0_i8(w, q));
         for (int cc = 0; cc < cn; ++cc, ++i) {
-          const int g = i & 1, sb = i % a.SB;
-          if (!warp_wait(&a_full[g], (i >> 1) & 1, a.err, 45) || !warp_wait(&b_full[sb], (i / a.SB) & 1, a.err, 46)) {
+          const int g = i & 1, sb = i % kI8MaxSB;
+          if (!warp_wait(&a_full[g], (i >> 1) & 1, a.err, 45) || !warp_wait(&b_full[sb], (i / kI8MaxSB) & 1, a.err, 46)) {
             ok = false;
             break;
           }
@@ -1117,7 +1117,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
     auto take = [&]() -> bool {
       if (!warp_wait(&acc_full[g], (pi >> 1) & 1, a.err, 48)) return false;
       tc_fence_after();
-      const float* sc = reinterpret_cast<const float*>(bring + (size_t)(pi % a.SB) * kI8BStage + kI8N * 128);
+      const float* sc = reinterpret_cast<const float*>(bring + (size_t)(pi % kI8MaxSB) * kI8BStage + kI8N * 128);
 #pragma unroll
       for (int jb = 0; jb < 2; ++jb) {
         uint32_t v[kI8N];
@@ -1141,7 +1141,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&b_empty[pi % a.SB]);
+      if (lane == 0) mbar_arrive(&b_empty[pi % kI8MaxSB]);
       return true;
     };
     int i = 0, j = 0, v = 0;   // chunks, raw stages, units
@@ -1151,8 +1151,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_i8_kernel(const __grid_con
 #pragma unroll
       for (int t = 0; t < kI8Tok; ++t) acc[t] = 0.0f;
       for (int q = 0; q < w.nst; ++q, ++j) {
-        const int slot = j % a.R;
-        if (!warp_wait(&raw_full[slot], (j / a.R) & 1, a.err, 49)) {
+        const int slot = j % kI8MaxR;
+        if (!warp_wait(&raw_full[slot], (j / kI8MaxR) & 1, a.err, 49)) {
           ok = false;
           break;
         }
@@ -1496,7 +1496,9 @@ int gemm_i8(const tosk_qmat_t* w, const float* x, const float* nw, float eps, in
             size_t ws_bytes, int* err, int pdl, cudaStream_t st) {
   const int N = w->rows, K = w->cols;
   const GemmI8Plan p = gemm_plan_i8(M, N, K);
-  if (ws_bytes < p.bytes || p.R < 2 || p.smem > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
+  // the kernel's rings are compile-time sized (no division by a ring size in its loops)
+  if (ws_bytes < p.bytes || p.R != kI8MaxR || p.SB != kI8MaxSB || p.smem > (size_t)kMaxSmem)
+    return (int)cudaErrorInvalidValue;
   uint8_t* xb = (uint8_t*)ws;
   float* part = (float*)((uint8_t*)ws + p.off_part);
   {
@@ -1522,8 +1524,6 @@ int gemm_i8(const tosk_qmat_t* w, const float* x, const float* nw, float eps, in
   a.kcps = p.kcps;
   a.units = p.units;
   a.full = p.full;
-  a.SB = p.SB;
-  a.R = p.R;
   a.err = err;
   static bool attr_done = false;
   if (!attr_done) {
