@@ -658,10 +658,14 @@ def run_ours(args, world, rank, local):
         toks = model.decode(nxt, pos, warm)
         nxt, pos = int(toks[-1]), pos + warm
         stream = torch.cuda.ExternalStream(model.stream())
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # the clock sampler starts (and delivers its first sample) before the
+        # ranks meet: its start-up time differs from rank to rank, and a rank
+        # that starts its steps early waits inside the sharded step for the
+        # others, which the max over ranks would count
         if clk:
             clk.__enter__()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.cudart().cudaProfilerStart()
         e0.record(stream)
         toks = model.decode(nxt, pos, K)
