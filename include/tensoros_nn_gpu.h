@@ -105,8 +105,11 @@ int tos_gemv_mode_dev(const tos_weight_t *w, const float *x, const float *norm_w
  * llm_gemv (llm.c:329-349) at once.  No counterpart in the reference (which
  * runs tokens one by one).  Runs on the tcgen05 tensor cores with an exact
  * fp16 hi/lo split of the dequantised weights and a 22-bit split of the
- * activations, fp32 accumulation: normwise error ~1e-6 against the fp32
- * GEMV.  in_dim a multiple of 64; ws: tos_gemm_workspace_bytes bytes,
+ * activations, fp32 accumulation; Q4_0 at m <= 16 with in_dim a multiple of
+ * 128 instead as exact integer block products (the FAST GEMV's 22-bit
+ * fixed-point activations, 8-bit tensor-core MMAs) scaled and summed in
+ * fp32.  Normwise error ~1e-6 against the fp32 GEMV either way.  in_dim a
+ * multiple of 64; ws: tos_gemm_workspace_bytes bytes,
  * 256-byte aligned.  tos_gemm_workspace_bytes(m, ...) covers every call with
  * at most m rows, so one workspace sized for the longest batch serves the
  * shorter ones.  Results are bit-identical run to run. */
