@@ -8,7 +8,10 @@
 //                        path) and the K/V cache store (llm.c:673-681)
 //   pf_attention_kernel  causal single-query attention of every token over
 //                        the cache (llm.c:683-714) with llm_expf weights,
-//                        tree sums (FAST numerics)
+//                        tree sums (FAST numerics); for an fp16 cache and
+//                        head dimension 128 the prompt pass uses
+//                        pf_attention_tile_kernel (16 tokens of a head per
+//                        CTA, each K / V row read once per tile)
 // The residual adds (llm.c:718, 733) and SiLU(gate)*up (llm.c:726-729) run
 // in the GEMMs' epilogues.
 // The rope/store and attention kernels also serve batched decode: n tokens
@@ -250,6 +253,146 @@ __global__ void __launch_bounds__(32 * kPfWarps) pf_attention_kernel(const float
   }
 }
 
+
+// Prefill attention, a tile of kTT consecutive tokens of one head per CTA
+// (fp16 cache, head dimension 128): each K and V row of the head is read
+// once per tile instead of once per token.  Same arithmetic as
+// pf_attention_kernel: score = (q . k) * (1 / sqrt(hd)) over the token's
+// positions 0..pos0+t, llm_expf(s - max) weights (llm.c:506-532, 683-714),
+// sum_j e_j v_j / (sum_j e_j + 1e-10); only the fp32 summation orders differ
+// (tree sums, FAST numerics).
+//   scores: lane l of warp w takes position j = 32 (w + 8 i) + l and all kTT
+//           tokens (q of the tile in shared memory, read as broadcasts);
+//   softmax: warp w takes tokens 2w, 2w + 1;
+//   softmax * V: warp w takes tokens 2w, 2w + 1, lane l dimensions 4l..4l+3.
+constexpr int kTT = 16;
+constexpr int kTHd = 128;
+__global__ void __launch_bounds__(256) pf_attention_tile_kernel(const float* __restrict__ q,
+                                                                const uint16_t* __restrict__ kc,
+                                                                const uint16_t* __restrict__ vc, int n_heads,
+                                                                int n_kv, int pos0, int n, float* __restrict__ out) {
+  extern __shared__ float tsm[];
+  float* qs = tsm;                  // [kTT][kTHd]
+  float* sc = tsm + kTT * kTHd;     // [kTT][P]: scores, then weights
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, t0 = blockIdx.y * kTT;
+  const int nt = min(kTT, n - t0);
+  const int P = pos0 + t0 + nt;     // positions the tile's last token sees
+  const int kvh = h / (n_heads / n_kv);
+  const int kv_dim = n_kv * kTHd;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kTHd));
+  for (int i = threadIdx.x; i < kTT * kTHd; i += blockDim.x) {
+    const int tt = i / kTHd, d = i % kTHd;
+    qs[i] = tt < nt ? q[((size_t)(t0 + tt) * n_heads + h) * kTHd + d] : 0.0f;
+  }
+  __syncthreads();
+  for (int jb = 32 * warp; jb < P; jb += 32 * 8) {
+    const int j = jb + lane;
+    float acc[kTT];
+#pragma unroll
+    for (int tt = 0; tt < kTT; ++tt) acc[tt] = 0.0f;
+    if (j < P) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)j * kv_dim + (size_t)kvh * kTHd);
+#pragma unroll 2
+      for (int v = 0; v < kTHd / 8; ++v) {
+        const uint4 w = kr[v];
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ww[e]));
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int tt = 0; tt < kTT; ++tt) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + tt * kTHd + 8 * v);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + tt * kTHd + 8 * v + 4);
+          float a = acc[tt];
+          a = fmaf(qa.x, kf[0], a);
+          a = fmaf(qa.y, kf[1], a);
+          a = fmaf(qa.z, kf[2], a);
+          a = fmaf(qa.w, kf[3], a);
+          a = fmaf(qb.x, kf[4], a);
+          a = fmaf(qb.y, kf[5], a);
+          a = fmaf(qb.z, kf[6], a);
+          a = fmaf(qb.w, kf[7], a);
+          acc[tt] = a;
+        }
+      }
+#pragma unroll
+      for (int tt = 0; tt < kTT; ++tt) sc[tt * P + j] = acc[tt] * scale;
+    }
+  }
+  __syncthreads();
+  float inv[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int tt = 2 * warp + u;
+    inv[u] = 0.0f;
+    if (tt >= nt) continue;
+    const int len = pos0 + t0 + tt + 1;
+    float* s = sc + tt * P;
+    float m = -INFINITY;
+    for (int j = lane; j < len; j += 32) m = fmaxf(m, s[j]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.0f;
+    for (int j = lane; j < len; j += 32) {
+      const float e = ref_expf(__fsub_rn(s[j], m));   // llm.c:514-517
+      s[j] = e;
+      l += e;
+    }
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    inv[u] = 1.0f / (l + 1e-10f);
+  }
+  __syncwarp();
+  // softmax * V for this warp's two tokens (its own weights: no CTA barrier)
+  const int ta = 2 * warp, tb = 2 * warp + 1;
+  if (ta >= nt) return;
+  const int la = pos0 + t0 + ta + 1, lb = tb < nt ? la + 1 : 0;
+  const float* sa = sc + ta * P;
+  const float* sb = sc + tb * P;
+  float4 oa = make_float4(0.f, 0.f, 0.f, 0.f), ob = make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint16_t* vcol = vc + (size_t)kvh * kTHd + 4 * lane;
+  int j = 0;
+  for (; j + 8 <= la; j += 8) {
+    float4 vv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint2 u = *reinterpret_cast<const uint2*>(vcol + (size_t)(j + k) * kv_dim);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      vv[k] = make_float4(a.x, a.y, b.x, b.y);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float ea = sa[j + k];
+      const float eb = j + k < lb ? sb[j + k] : 0.0f;
+      oa.x = fmaf(ea, vv[k].x, oa.x); oa.y = fmaf(ea, vv[k].y, oa.y);
+      oa.z = fmaf(ea, vv[k].z, oa.z); oa.w = fmaf(ea, vv[k].w, oa.w);
+      ob.x = fmaf(eb, vv[k].x, ob.x); ob.y = fmaf(eb, vv[k].y, ob.y);
+      ob.z = fmaf(eb, vv[k].z, ob.z); ob.w = fmaf(eb, vv[k].w, ob.w);
+    }
+  }
+  for (; j < max(la, lb); ++j) {
+    const uint2 u = *reinterpret_cast<const uint2*>(vcol + (size_t)j * kv_dim);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    const float ea = j < la ? sa[j] : 0.0f;
+    const float eb = j < lb ? sb[j] : 0.0f;
+    oa.x = fmaf(ea, a.x, oa.x); oa.y = fmaf(ea, a.y, oa.y); oa.z = fmaf(ea, b.x, oa.z); oa.w = fmaf(ea, b.y, oa.w);
+    ob.x = fmaf(eb, a.x, ob.x); ob.y = fmaf(eb, a.y, ob.y); ob.z = fmaf(eb, b.x, ob.z); ob.w = fmaf(eb, b.y, ob.w);
+  }
+  float* oo = out + ((size_t)(t0 + ta) * n_heads + h) * kTHd + 4 * lane;
+  *reinterpret_cast<float4*>(oo) = make_float4(oa.x * inv[0], oa.y * inv[0], oa.z * inv[0], oa.w * inv[0]);
+  if (tb < nt) {
+    float* ob_ = out + ((size_t)(t0 + tb) * n_heads + h) * kTHd + 4 * lane;
+    *reinterpret_cast<float4*>(ob_) = make_float4(ob.x * inv[1], ob.y * inv[1], ob.z * inv[1], ob.w * inv[1]);
+  }
+}
+
 }  // namespace tos
 
 using namespace tos;
@@ -299,6 +442,22 @@ extern "C" int tosk_bd_rope_store(const float* qkv, int q_rows, int kv_rows, int
 
 extern "C" int tosk_pf_attention(const float* q, const void* kc, const void* vc, int kv_type, int n_heads, int n_kv,
                                  int hd, int pos0, int n, float* out, cudaStream_t st) {
+  // fp16 cache, head dimension 128: token tiles (pf_attention_tile_kernel)
+  const size_t tsmem = ((size_t)kTT * kTHd + (size_t)kTT * (pos0 + n)) * 4;
+  if (kv_type == TOSK_F16 && hd == kTHd && tsmem <= 200 * 1024 && n > 0) {
+    static bool tattr = false;
+    if (!tattr) {
+      const cudaError_t e = cudaFuncSetAttribute(pf_attention_tile_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) return (int)e;
+      tattr = true;
+    }
+    const uint16_t* k16 = (const uint16_t*)kc;
+    const uint16_t* v16 = (const uint16_t*)vc;
+    void* args[] = {(void*)&q, (void*)&k16, (void*)&v16, &n_heads, &n_kv, &pos0, &n, &out};
+    return launch_pf((const void*)pf_attention_tile_kernel, dim3(n_heads, (n + kTT - 1) / kTT), dim3(256), tsmem,
+                     args, st);
+  }
   const size_t smem = (size_t)(pos0 + n) * 4;
   if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
   static bool attr = false;
