@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(704, 1) tos_gemv_kernel(const GemvArgs a) {
     const float4* w4 = reinterpret_cast<const float4*>(ws);
     const int nchunk = a.cols >> 2;
     for (int base = threadIdx.x - 32; base - (threadIdx.x - 32) < nchunk; base += nthr) {
-      const int t = base;   // chunk index owned by this thread in this round
+      const int t = base;   // chunk index owned by this thread in this pass
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (t < nchunk) {
         v = x4[t];
