@@ -15,8 +15,8 @@
  *    (llm.c:48-65).  The KV cache is supplied by the harness (llm.h:100-101),
  *    so LLM_KV_FLOATS stays small.
  *  - runtime/jit/x86_jit.c is replaced by a stub returning NULL, so Q8_0 takes
- *    the portable C path of llm_gemv (llm.c:343-348): the JIT emits x86 code
- *    with its own summation order and is replaced on the GPU, not matched.
+ *    the portable C path of llm_gemv (llm.c:343-348): the JIT is x86-only
+ *    code generation, and the GPU path follows the portable C path.
  */
 #define _GNU_SOURCE   /* ucontext register names for the timestamp trap below */
 #include "runtime/nn/llm.h"
